@@ -1,0 +1,346 @@
+"""Benchmark of the FNO spectral block on B200 (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+
+Default workload: one SpectralConv forward, batch 64 per GPU,
+Cin = Cout = 64, grid 256x256, n_modes (64, 64), fp32, synthetic N(0,1) input and seeded
+complex weights.  A step is one forward over the batch; under torchrun every rank runs its
+own batch (weak scaling, no collective on the data path) and the job value is
+sum(samples) / max-over-ranks(time).
+
+* value      : samples/s with x resident in HBM (CUDA events on the launching stream).
+* e2e        : the same through the public API with pinned host buffers, the H2D copy of x
+               and the D2H copy of y inside the timed region.
+* roofline   : the spectral block's algorithmic bytes |x|+|y|+|W|+|bias| per step over its
+               time, against the measured HBM copy bandwidth; traffic comes from an ncu
+               capture summarised under profiles/.
+* cpu_baseline: the oracle (the reference's torch CPU path restated in oracle/) on the
+               host cores over a bounded batch of the same workload.
+--impl reference times that CPU path as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FNO fwd samples/s/GPU at 1–8 B200; spectral block % of HBM/tensor roofline"
+HBM_FALLBACK_GBS = 6533.2  # measured copy bandwidth on this pool (MEASURED_PEAKS.json at round start)
+
+# name -> (description, batch, Ci, Co, grid, n_modes, factorization)
+CONFIGS = {
+    "c1": ("darcy2d_layer", 16, 32, 32, (128, 128), (16, 16), None),
+    "c2": ("spectralconv2d_micro", 64, 64, 64, (256, 256), (64, 64), None),
+    "c3": ("burgers1d_layer", 256, 64, 64, (8192,), (16,), None),
+    "c4": ("tfno2d_ns_layer", 32, 64, 64, (512, 512), (64, 64), "tucker"),
+    "c5": ("fno3d_layer", 8, 32, 32, (256, 256, 256), (32, 32, 32), None),
+}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+    except Exception:  # noqa: BLE001
+        return HBM_FALLBACK_GBS, "measured on this pool (recorded value; MEASURED_PEAKS.json absent)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(cfg, device, seed=0):
+    """Synthetic input and seeded weights with the config's shapes (no dataset is available)."""
+    import neuraloperator_b200 as nb
+    desc, batch, ci, co, grid, modes, fact = cfg
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    kw = {}
+    if fact:
+        kw = dict(factorization=fact, implementation="factorized", rank=0.1)
+    conv = nb.SpectralConv(ci, co, modes, **kw)
+    std = math.sqrt(2.0 / (ci + co))
+    with torch.no_grad():
+        for p in conv.weight.parameters():
+            p.copy_(torch.complex(torch.randn(p.shape, generator=g), torch.randn(p.shape, generator=g)) *
+                    (std if not fact else 0.5))
+        conv.bias.copy_(torch.randn(conv.bias.shape, generator=g) * std)
+    conv = conv.to(device)
+    x = torch.randn((batch, ci, *grid), generator=g).to(device) if device != "cpu" else \
+        torch.randn((batch, ci, *grid), generator=g)
+    return conv, x
+
+
+def bytes_alg(cfg, conv):
+    _, batch, ci, co, grid, _, _ = cfg
+    p = math.prod(grid)
+    w = sum(t.numel() * t.element_size() for t in conv.weight.parameters())
+    return batch * ci * p * 4 + batch * co * p * 4 + w + co * 4
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline(cfg, seconds=12.0):
+    """Oracle (reference torch CPU path) on the host cores, bounded sample of the workload."""
+    import oracle
+    desc, batch, ci, co, grid, modes, fact = cfg
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample_b = max(1, min(batch, 4 if math.prod(grid) <= 512 * 512 else 1))
+    conv, x = make_inputs((desc, sample_b, ci, co, grid, modes, fact), "cpu", seed=1)
+    if fact:
+        w = {"core": conv.weight.core.detach(), "factors": [f.detach() for f in conv.weight.factors]}
+        kind = "tucker"
+    else:
+        w, kind = conv.weight.tensor.detach(), "dense"
+    run = lambda: oracle.spectral_conv(x, w, conv.bias.detach(), modes, weight_kind=kind)
+    with torch.no_grad():
+        run()  # warm-up
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            run()
+            n += 1
+            if time.perf_counter() - t0 >= seconds or n >= 50:
+                break
+        dt = (time.perf_counter() - t0) / n
+    return {"value": sample_b / dt, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_b} of {batch} samples per forward, {n} forwards, torch {torch.__version__} CPU"}
+
+
+def run_reference(args, cfg, world, rank):
+    if rank != 0:
+        return
+    steps, warm = args.steps, args.warmup
+    import oracle
+    desc, batch, ci, co, grid, modes, fact = cfg
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample_b = max(1, min(batch, 4 if math.prod(grid) <= 512 * 512 else 1))
+    conv, x = make_inputs((desc, sample_b, ci, co, grid, modes, fact), "cpu", seed=1)
+    if fact:
+        w = {"core": conv.weight.core.detach(), "factors": [f.detach() for f in conv.weight.factors]}
+        kind = "tucker"
+    else:
+        w, kind = conv.weight.tensor.detach(), "dense"
+    with torch.no_grad():
+        for _ in range(warm):
+            oracle.spectral_conv(x, w, conv.bias.detach(), modes, weight_kind=kind)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            oracle.spectral_conv(x, w, conv.bias.detach(), modes, weight_kind=kind)
+        dt = (time.perf_counter() - t0) / steps
+    value = sample_b / dt
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": desc, "global_batch": batch, "sample_batch": sample_b, "grid": list(grid),
+                       "channels": [ci, co], "n_modes": list(modes), "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
+                             "sample": f"{sample_b} of {batch} samples per step (oracle = reference torch CPU path)"},
+            "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, cfg, world, rank, local):
+    import neuraloperator_b200 as nb  # noqa: F401
+    from neuraloperator_b200 import ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    desc, batch, ci, co, grid, modes, fact = cfg
+    conv, x = make_inputs(cfg, dev, seed=0)
+    conv.engine = args.engine
+    stream = torch.cuda.current_stream(dev)
+    steps, warm = args.steps, args.warmup
+
+    with torch.no_grad():
+        for _ in range(warm):
+            y = conv(x)
+        torch.cuda.synchronize()
+        geo = conv.geometry(list(grid))
+        kind, _, ranks = conv.kernel_operands(geo)
+        desc_c = ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks, engine=args.engine)
+        plan = ops.get_plan(desc_c, local)
+
+        # ---- device-resident timed region ----
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            e0.record(stream)
+            for _ in range(steps):
+                y = conv(x)
+            e1.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        ms = e0.elapsed_time(e1) / steps
+        ms = max_over_ranks(ms, world)
+        value = world * batch / (ms / 1e3)
+
+        # ---- end to end through the public API: pinned host in, pinned host out ----
+        x_host = x.cpu().pin_memory()
+        y_host = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        e2e_steps = max(1, min(steps, 10))
+        barrier(world)
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(e2e_steps):
+            xd = x_host.to(dev, non_blocking=True)
+            yd = conv(xd)
+            y_host.copy_(yd, non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_e2e = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+
+    if rank != 0:
+        return
+    hbm, peak_src = peaks()
+    b_alg = bytes_alg(cfg, conv)
+    achieved = b_alg / (ms / 1e3) / 1e9
+    clk = clocks.summary()
+    line = {
+        "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) input, seeded complex weights; no dataset)",
+        "config": {"workload": desc, "global_batch": batch * world, "per_gpu_batch": batch, "grid": list(grid),
+                   "channels": [ci, co], "n_modes": list(modes), "factorization": fact or "dense",
+                   "parallelism": f"dp{world}" if world > 1 else "single", "engine": "fast" if plan.is_fast else
+                   "generic", "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None, "kernel": "spectral block (all launches of one forward)",
+                     "bytes_alg_per_launch": b_alg, "peak_source": peak_src},
+        "e2e": {"value": world * batch / (ms_e2e / 1e3), "unit": "samples/s",
+                "h2d_bytes_per_step": x.numel() * x.element_size(),
+                "d2h_bytes_per_step": y.numel() * y.element_size()},
+        "gpu_launches": plan.launches_per_forward * steps,
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, seconds=args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--engine", choices=["auto", "fast", "generic"], default="auto")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, cfg, world, rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, cfg, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

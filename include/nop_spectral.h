@@ -1,0 +1,137 @@
+/*
+ * nop_spectral.h — C ABI of the B200 FNO spectral block (libnop_b200.so).
+ *
+ * One SpectralConv forward (neuralop/layers/spectral_convolution.py:417-570) is
+ *   truncated forward real FFT over every spatial axis  ->  per-mode channel contraction
+ *   (dense, separable, Tucker or CP weights)  ->  truncated inverse FFT  ->  + bias
+ * optionally followed by the FNOBlocks epilogue  y = gelu(y + skip)
+ * (neuralop/layers/fno_block.py:356-361).
+ *
+ * Conventions
+ *   - All device pointers are CUDA device memory of the current device.  Complex data are
+ *     interleaved float pairs (complex64).  Every tensor is contiguous, row-major.
+ *   - x   : [B, Ci, n_in[0..ndim-1]]   float32 (complex64 when complex_data)
+ *   - y   : [B, Co, n_out[0..ndim-1]]  float32 (complex64 when complex_data)
+ *   - The caller owns every buffer, including the workspace, whose size the plan reports.
+ *     Forward calls never allocate; plan creation allocates the plan's twiddle tables.
+ *   - Kernels are enqueued on `stream` (a cudaStream_t; NULL = legacy default stream).
+ *   - Functions return NOP_OK (0) or a negative nop_status; nop_last_error() then returns
+ *     a message for the calling thread.  All argument checks run on the host before any
+ *     launch; no kernel traps.
+ *
+ * Geometry: kept mode m of axis j is DFT bin u = (m - fwd_off[j]) mod n_in[j] in the forward
+ * transform and bin index u = (m - inv_off[j]) mod n_in[j] in the inverse, where bins with
+ * u >= n_out[j] are dropped (ifftn with s=n_out truncates / zero-pads at the end).  For real
+ * data the last axis keeps rFFT bins 0..kept-1 (offsets 0) and is inverted with the Hermitian
+ * c2r rule; the bins listed in zero_imag_bins contribute only their real part.  The Python
+ * layer fills these from the reference's fftshift / slice / ifftshift bookkeeping
+ * (spectral_convolution.py:443-559).
+ */
+#ifndef NOP_SPECTRAL_H
+#define NOP_SPECTRAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NOP_ABI_VERSION 1
+#define NOP_MAX_DIMS 4
+
+typedef enum nop_status {
+    NOP_OK = 0,
+    NOP_E_INVALID = -1,      /* malformed descriptor or argument */
+    NOP_E_UNSUPPORTED = -2,  /* well-formed request this library does not implement */
+    NOP_E_ALIGNMENT = -3,    /* a pointer is not aligned as required */
+    NOP_E_WORKSPACE = -4,    /* workspace missing or smaller than nop_spectral_workspace_size */
+    NOP_E_CUDA = -5,         /* CUDA runtime error (message names the call) */
+    NOP_E_NOMEM = -6         /* host or device allocation failed during plan creation */
+} nop_status;
+
+typedef enum nop_weight_kind {
+    NOP_WEIGHT_DENSE = 0,    /* weights[0] = W [Ci, Co, kept...] (separable: [C, kept...])            */
+    NOP_WEIGHT_TUCKER = 1,   /* weights = core, U_in, U_out, U_1..U_ndim (separable: core, U_c, U_j)  */
+    NOP_WEIGHT_CP = 2        /* weights = lambda, U_in, U_out, U_1..U_ndim (separable: lambda, U_c, U_j) */
+} nop_weight_kind;
+
+typedef enum nop_precision {
+    NOP_PRECISION_FP32 = 0,  /* float32 transforms and contraction                                  */
+    NOP_PRECISION_BF16 = 1   /* contraction operands rounded to bfloat16, float32 accumulation        */
+} nop_precision;
+
+typedef enum nop_engine {
+    NOP_ENGINE_AUTO = 0,     /* fused FFT kernels where the shape is supported, else generic         */
+    NOP_ENGINE_GENERIC = 1,  /* direct-DFT kernels: any sizes, any ndim; slower                         */
+    NOP_ENGINE_FAST = 2      /* fused FFT kernels only; NOP_E_UNSUPPORTED when the shape is not covered */
+} nop_engine;
+
+typedef struct nop_spectral_desc {
+    int32_t abi_version;                 /* must be NOP_ABI_VERSION                                 */
+    int32_t ndim;                        /* spatial dims, 1..NOP_MAX_DIMS                            */
+    int32_t complex_data;                /* 1: x and y are complex64                                 */
+    int32_t separable;                   /* 1: diagonal in channels (Ci == Co)                       */
+    int32_t weight_kind;                 /* nop_weight_kind                                          */
+    int32_t precision;                   /* nop_precision                                            */
+    int32_t engine;                      /* nop_engine                                               */
+    int32_t n_zero_imag;                 /* entries used in zero_imag_bins (0..3)                    */
+    int64_t batch;                       /* B (0 is allowed: calls return immediately)               */
+    int64_t in_channels;                 /* Ci                                                       */
+    int64_t out_channels;                /* Co                                                       */
+    int64_t n_in[NOP_MAX_DIMS];          /* input spatial sizes                                      */
+    int64_t n_out[NOP_MAX_DIMS];         /* output spatial sizes                                     */
+    int64_t kept[NOP_MAX_DIMS];          /* kept modes per axis (the weight's mode dims)             */
+    int64_t fwd_off[NOP_MAX_DIMS];       /* forward bin offset per axis                              */
+    int64_t inv_off[NOP_MAX_DIMS];       /* inverse bin offset per axis                              */
+    int64_t ranks[NOP_MAX_DIMS + 2];     /* Tucker: r_in, r_out, r_1..r_ndim (separable: r_c, r_j);
+                                            CP: ranks[0] = R                                         */
+    int64_t zero_imag_bins[3];           /* real data: last-axis bins read as real                   */
+    double fwd_scale;                    /* forward normalisation (1/prod(n_in) for norm="forward")  */
+    double inv_scale;                    /* inverse normalisation (1 for norm="forward")             */
+} nop_spectral_desc;
+
+typedef struct nop_plan nop_plan;        /* opaque, immutable after creation, thread-safe to share  */
+
+/* ABI version of the loaded library (NOP_ABI_VERSION it was built with). */
+int32_t nop_abi_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* nop_last_error(void);
+
+/* Validate `desc`, pick the kernels and upload twiddle tables for the current device.
+ * Replaces the per-call shape bookkeeping of SpectralConv.forward
+ * (neuralop/layers/spectral_convolution.py:429-519). */
+int32_t nop_spectral_plan_create(const nop_spectral_desc* desc, nop_plan** plan_out);
+
+/* Release a plan (frees its device tables).  NULL is ignored. */
+void nop_spectral_plan_destroy(nop_plan* plan);
+
+/* Bytes of device workspace nop_spectral_forward needs (256-byte aligned buffer). */
+int32_t nop_spectral_workspace_size(const nop_plan* plan, size_t* bytes);
+
+/* 1 when the plan runs the fused FFT kernels, 0 when it runs the generic direct-DFT kernels. */
+int32_t nop_spectral_plan_is_fast(const nop_plan* plan);
+
+/* Number of kernel launches one nop_spectral_forward call with this plan enqueues. */
+int32_t nop_spectral_launches_per_forward(const nop_plan* plan);
+
+/* One forward of the spectral block.
+ * Replaces SpectralConv.forward (neuralop/layers/spectral_convolution.py:417-570); with
+ * `addend` / `apply_gelu` it also replaces the skip add and activation of
+ * FNOBlocks.forward_with_postactivation (neuralop/layers/fno_block.py:356-361):
+ *     y = spec(x) + bias;  if addend: y += addend;  if apply_gelu: y = gelu_erf(y)
+ *   weights   : n_weights device pointers, layout per nop_weight_kind (complex64, contiguous)
+ *   bias      : [Co] float32, or NULL
+ *   addend    : [B, Co, n_out...] float32, or NULL (real data only)
+ *   workspace : >= nop_spectral_workspace_size bytes, 256-byte aligned */
+int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* const* weights,
+                             int32_t n_weights, const float* bias, const float* addend,
+                             int32_t apply_gelu, void* y, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NOP_SPECTRAL_H */

@@ -1,0 +1,150 @@
+"""ctypes binding of libnop_b200.so (C ABI declared in include/nop_spectral.h).
+
+The library is loaded from this package directory.  If it is missing or older than its
+sources it is rebuilt with nvcc; if that is impossible the import of the compute path
+fails with a RuntimeError -- there is no CPU or PyTorch fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnop_b200.so")
+
+ABI_VERSION = 1
+MAX_DIMS = 4
+
+NOP_OK = 0
+STATUS_NAMES = {0: "NOP_OK", -1: "NOP_E_INVALID", -2: "NOP_E_UNSUPPORTED", -3: "NOP_E_ALIGNMENT",
+                -4: "NOP_E_WORKSPACE", -5: "NOP_E_CUDA", -6: "NOP_E_NOMEM"}
+
+WEIGHT_DENSE, WEIGHT_TUCKER, WEIGHT_CP = 0, 1, 2
+PRECISION_FP32, PRECISION_BF16 = 0, 1
+ENGINE_AUTO, ENGINE_GENERIC, ENGINE_FAST = 0, 1, 2
+
+EXPORTED_SYMBOLS = (
+    "nop_abi_version", "nop_last_error", "nop_spectral_plan_create", "nop_spectral_plan_destroy",
+    "nop_spectral_workspace_size", "nop_spectral_plan_is_fast", "nop_spectral_launches_per_forward",
+    "nop_spectral_forward",
+)
+
+
+class NopSpectralDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("ndim", ctypes.c_int32),
+        ("complex_data", ctypes.c_int32),
+        ("separable", ctypes.c_int32),
+        ("weight_kind", ctypes.c_int32),
+        ("precision", ctypes.c_int32),
+        ("engine", ctypes.c_int32),
+        ("n_zero_imag", ctypes.c_int32),
+        ("batch", ctypes.c_int64),
+        ("in_channels", ctypes.c_int64),
+        ("out_channels", ctypes.c_int64),
+        ("n_in", ctypes.c_int64 * MAX_DIMS),
+        ("n_out", ctypes.c_int64 * MAX_DIMS),
+        ("kept", ctypes.c_int64 * MAX_DIMS),
+        ("fwd_off", ctypes.c_int64 * MAX_DIMS),
+        ("inv_off", ctypes.c_int64 * MAX_DIMS),
+        ("ranks", ctypes.c_int64 * (MAX_DIMS + 2)),
+        ("zero_imag_bins", ctypes.c_int64 * 3),
+        ("fwd_scale", ctypes.c_double),
+        ("inv_scale", ctypes.c_double),
+    ]
+
+
+class NopError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {message}")
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def _declare(lib):
+    c_plan_p = ctypes.c_void_p
+    lib.nop_abi_version.restype = ctypes.c_int32
+    lib.nop_abi_version.argtypes = []
+    lib.nop_last_error.restype = ctypes.c_char_p
+    lib.nop_last_error.argtypes = []
+    lib.nop_spectral_plan_create.restype = ctypes.c_int32
+    lib.nop_spectral_plan_create.argtypes = [ctypes.POINTER(NopSpectralDesc), ctypes.POINTER(c_plan_p)]
+    lib.nop_spectral_plan_destroy.restype = None
+    lib.nop_spectral_plan_destroy.argtypes = [c_plan_p]
+    lib.nop_spectral_workspace_size.restype = ctypes.c_int32
+    lib.nop_spectral_workspace_size.argtypes = [c_plan_p, ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_spectral_plan_is_fast.restype = ctypes.c_int32
+    lib.nop_spectral_plan_is_fast.argtypes = [c_plan_p]
+    lib.nop_spectral_launches_per_forward.restype = ctypes.c_int32
+    lib.nop_spectral_launches_per_forward.argtypes = [c_plan_p]
+    lib.nop_spectral_forward.restype = ctypes.c_int32
+    lib.nop_spectral_forward.argtypes = [
+        c_plan_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+
+
+def library():
+    """The loaded CDLL (built on first use when the in-tree .so is missing or stale)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if os.environ.get("NOP_SKIP_BUILD") != "1":
+            try:
+                from . import build as _build
+                _build.build()
+            except Exception as exc:  # noqa: BLE001
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(f"libnop_b200.so is not built and building it failed: {exc}") from exc
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError("libnop_b200.so not found; run `python -m neuraloperator_b200.build`")
+        lib = ctypes.CDLL(LIB_PATH)
+        _declare(lib)
+        v = lib.nop_abi_version()
+        if v != ABI_VERSION:
+            raise RuntimeError(f"libnop_b200.so ABI {v} != binding ABI {ABI_VERSION}; rebuild the library")
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return library().nop_last_error().decode(errors="replace")
+
+
+def check(code: int):
+    if code != NOP_OK:
+        raise NopError(code, last_error())
+
+
+class Plan:
+    """Owns one nop_plan (created on the current CUDA device)."""
+
+    def __init__(self, desc: NopSpectralDesc):
+        lib = library()
+        handle = ctypes.c_void_p()
+        check(lib.nop_spectral_plan_create(ctypes.byref(desc), ctypes.byref(handle)))
+        self._lib = lib
+        self.handle = handle
+        self.desc = desc
+        size = ctypes.c_size_t()
+        check(lib.nop_spectral_workspace_size(handle, ctypes.byref(size)))
+        self.workspace_bytes = int(size.value)
+        self.is_fast = bool(lib.nop_spectral_plan_is_fast(handle))
+        self.launches_per_forward = int(lib.nop_spectral_launches_per_forward(handle))
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                self._lib.nop_spectral_plan_destroy(h)
+            except Exception:  # noqa: BLE001  (interpreter shutdown)
+                pass
+            self.handle = None

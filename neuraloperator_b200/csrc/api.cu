@@ -1,0 +1,334 @@
+// C ABI of libnop_b200: descriptor validation, plans (twiddle tables, workspace layout) and
+// dispatch to the fused FFT engine or the generic direct-DFT engine.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "nop_internal.cuh"
+
+namespace nop {
+
+namespace {
+thread_local std::string g_last_error;
+constexpr int64_t kMaxLen = int64_t(1) << 20;     // per-axis transform length limit
+constexpr int64_t kMaxElems = int64_t(1) << 40;   // per-tensor element limit
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+bool mul_ok(int64_t a, int64_t b, int64_t* out) {
+    if (a < 0 || b < 0) return false;
+    if (a != 0 && b > kMaxElems / a) return false;
+    *out = a * b;
+    return true;
+}
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int32_t fail(int32_t code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int32_t cuda_fail(cudaError_t err, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorName(err) + " (" + cudaGetErrorString(err) + ")";
+    return fail(NOP_E_CUDA, m);
+}
+
+// fused engine hooks (fast.cu)
+bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why);
+size_t fast_workspace_bytes(const Plan& p, WorkspaceLayout* ws);
+int32_t fast_launches(const Plan& p);
+int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
+                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+
+namespace {
+
+int expected_weights(const nop_spectral_desc& d) {
+    if (d.weight_kind == NOP_WEIGHT_DENSE) return 1;
+    return 1 + (d.separable ? 1 : 2) + d.ndim;
+}
+
+int32_t validate(const nop_spectral_desc* d) {
+    if (!d) return fail(NOP_E_INVALID, "descriptor is NULL");
+    if (d->abi_version != NOP_ABI_VERSION)
+        return fail(NOP_E_INVALID, "descriptor abi_version " + std::to_string(d->abi_version) +
+                                       " != library " + std::to_string(NOP_ABI_VERSION));
+    if (d->ndim < 1 || d->ndim > NOP_MAX_DIMS)
+        return fail(NOP_E_INVALID, "ndim must be in 1.." + std::to_string(NOP_MAX_DIMS));
+    if (d->batch < 0) return fail(NOP_E_INVALID, "batch must be >= 0");
+    if (d->in_channels < 1 || d->out_channels < 1) return fail(NOP_E_INVALID, "channel counts must be >= 1");
+    if (d->separable && d->in_channels != d->out_channels)
+        return fail(NOP_E_INVALID, "separable contraction needs in_channels == out_channels");
+    if (d->complex_data != 0 && d->complex_data != 1) return fail(NOP_E_INVALID, "complex_data must be 0 or 1");
+    if (d->weight_kind < NOP_WEIGHT_DENSE || d->weight_kind > NOP_WEIGHT_CP)
+        return fail(NOP_E_INVALID, "unknown weight_kind");
+    if (d->precision != NOP_PRECISION_FP32 && d->precision != NOP_PRECISION_BF16)
+        return fail(NOP_E_INVALID, "unknown precision");
+    if (d->engine < NOP_ENGINE_AUTO || d->engine > NOP_ENGINE_FAST) return fail(NOP_E_INVALID, "unknown engine");
+    if (d->n_zero_imag < 0 || d->n_zero_imag > 3) return fail(NOP_E_INVALID, "n_zero_imag must be in 0..3");
+    if (!(std::isfinite(d->fwd_scale) && std::isfinite(d->inv_scale)))
+        return fail(NOP_E_INVALID, "scales must be finite");
+    const int nd = d->ndim;
+    for (int j = 0; j < nd; ++j) {
+        const std::string ax = "axis " + std::to_string(j);
+        if (d->n_in[j] < 1 || d->n_in[j] > kMaxLen || d->n_out[j] < 1 || d->n_out[j] > kMaxLen)
+            return fail(NOP_E_INVALID, ax + ": spatial sizes must be in 1.." + std::to_string(kMaxLen));
+        const bool real_last = !d->complex_data && j == nd - 1;
+        const int64_t spec = real_last ? d->n_in[j] / 2 + 1 : d->n_in[j];
+        if (d->kept[j] < 1 || d->kept[j] > spec)
+            return fail(NOP_E_INVALID, ax + ": kept modes " + std::to_string(d->kept[j]) + " outside 1.." +
+                                           std::to_string(spec));
+        if (d->fwd_off[j] < 0 || d->fwd_off[j] >= d->n_in[j] || d->inv_off[j] < 0 || d->inv_off[j] >= d->n_in[j])
+            return fail(NOP_E_INVALID, ax + ": bin offsets must be in 0..n_in-1");
+        if (real_last && (d->fwd_off[j] != 0 || d->inv_off[j] != 0))
+            return fail(NOP_E_INVALID, "the real last axis keeps rFFT bins from 0 (offsets must be 0)");
+    }
+    if (d->weight_kind != NOP_WEIGHT_DENSE) {
+        const int nr = d->weight_kind == NOP_WEIGHT_CP ? 1 : (d->separable ? 1 : 2) + nd;
+        for (int i = 0; i < nr; ++i)
+            if (d->ranks[i] < 1 || d->ranks[i] > kMaxLen) return fail(NOP_E_INVALID, "factor ranks must be >= 1");
+    }
+    // element-count overflow checks on the largest tensors
+    int64_t px = 1, py = 1, e;
+    for (int j = 0; j < nd; ++j) {
+        if (!mul_ok(px, d->n_in[j], &px) || !mul_ok(py, d->n_out[j], &py))
+            return fail(NOP_E_INVALID, "spatial size product overflows");
+    }
+    if (!mul_ok(d->batch, d->in_channels, &e) || !mul_ok(e, px, &e) || !mul_ok(d->batch, d->out_channels, &e) ||
+        !mul_ok(e, py, &e))
+        return fail(NOP_E_INVALID, "tensor size overflows");
+    return NOP_OK;
+}
+
+int64_t tucker_expansion_elems(const nop_spectral_desc& d, int64_t lead, int r0) {
+    int64_t best = 0;
+    for (int j = 0; j < d.ndim; ++j) {
+        int64_t e = lead;
+        for (int i = 0; i <= j; ++i) e *= d.kept[i];
+        for (int i = j + 1; i < d.ndim; ++i) e *= d.ranks[r0 + i];
+        if (e > best) best = e;
+    }
+    return best;
+}
+
+// Workspace regions of the contraction stage (shared by both engines).
+void contraction_layout(const Plan& p, size_t* off, WorkspaceLayout* ws) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Mt = p.modes_total, B = d.batch, Ci = d.in_channels;
+    int64_t g = 0, xf = 0, z = 0;
+    if (d.weight_kind == NOP_WEIGHT_TUCKER) {
+        if (d.separable) {
+            int64_t q = 1;
+            for (int j = 0; j < d.ndim; ++j) q *= d.ranks[1 + j];
+            xf = Ci * q;
+            g = tucker_expansion_elems(d, Ci, 1);
+        } else {
+            g = tucker_expansion_elems(d, d.ranks[0] * d.ranks[1], 2);
+            xf = B * d.ranks[0] * Mt;
+            z = B * d.ranks[1] * Mt;
+        }
+    } else if (d.weight_kind == NOP_WEIGHT_CP) {
+        g = (d.separable ? Ci : d.ranks[0]) * Mt;
+        if (!d.separable) xf = z = B * d.ranks[0] * Mt;
+    }
+    auto take = [&](int64_t elems) {
+        size_t at = *off;
+        *off += align_up((size_t)elems * sizeof(float2));
+        return at;
+    };
+    ws->g = take(g);
+    ws->g_tmp = take(d.weight_kind == NOP_WEIGHT_TUCKER ? g : 0);
+    ws->xf = take(xf);
+    ws->z = take(z);
+}
+
+int32_t build_tables(Plan* p) {
+    const nop_spectral_desc& d = p->d;
+    std::vector<int64_t> lens;
+    for (int j = 0; j < d.ndim; ++j) {
+        for (int64_t n : {d.n_in[j], d.n_out[j]}) {
+            bool seen = false;
+            for (int64_t v : lens) seen |= (v == n);
+            if (!seen) lens.push_back(n);
+        }
+    }
+    size_t bytes = 0;
+    for (int64_t n : lens) bytes += align_up(n * sizeof(double2)) + align_up(n * sizeof(float2));
+    std::vector<char> host(bytes);
+    size_t at = 0;
+    std::vector<std::pair<size_t, size_t>> offs;
+    for (int64_t n : lens) {
+        double2* dt = reinterpret_cast<double2*>(host.data() + at);
+        size_t dat = at;
+        at += align_up(n * sizeof(double2));
+        float2* ft = reinterpret_cast<float2*>(host.data() + at);
+        size_t fat = at;
+        at += align_up(n * sizeof(float2));
+        const long double two_pi = 6.283185307179586476925286766559005768L;
+        for (int64_t k = 0; k < n; ++k) {
+            // exact values at the quarter points keep the table free of tiny residuals
+            long double a = two_pi * (long double)k / (long double)n;
+            double c = (double)cosl(a), s = (double)sinl(a);
+            if (4 * k == n) { c = 0.0; s = 1.0; }
+            if (2 * k == n) { c = -1.0; s = 0.0; }
+            if (4 * k == 3 * n) { c = 0.0; s = -1.0; }
+            dt[k] = make_double2(c, s);
+            ft[k] = make_float2((float)c, (float)s);
+        }
+        offs.push_back({dat, fat});
+    }
+    void* mem = nullptr;
+    cudaError_t err = cudaMalloc(&mem, bytes ? bytes : 1);
+    if (err != cudaSuccess)
+        return fail(NOP_E_NOMEM, std::string("twiddle table allocation: ") + cudaGetErrorString(err));
+    err = cudaMemcpy(mem, host.data(), bytes, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        cudaFree(mem);
+        return cuda_fail(err, "twiddle table upload");
+    }
+    p->table_mem = mem;
+    for (size_t i = 0; i < lens.size(); ++i) {
+        TwiddleTable t;
+        t.n = lens[i];
+        t.d_table = reinterpret_cast<const double2*>(static_cast<char*>(mem) + offs[i].first);
+        t.f_table = reinterpret_cast<const float2*>(static_cast<char*>(mem) + offs[i].second);
+        p->tables.push_back(t);
+    }
+    return NOP_OK;
+}
+
+}  // namespace
+}  // namespace nop
+
+using namespace nop;
+
+extern "C" {
+
+int32_t nop_abi_version(void) { return NOP_ABI_VERSION; }
+
+const char* nop_last_error(void) { return g_last_error.c_str(); }
+
+int32_t nop_spectral_plan_create(const nop_spectral_desc* desc, nop_plan** plan_out) {
+    if (!plan_out) return fail(NOP_E_INVALID, "plan_out is NULL");
+    *plan_out = nullptr;
+    int32_t rc = validate(desc);
+    if (rc != NOP_OK) return rc;
+    Plan* p = new (std::nothrow) Plan();
+    if (!p) return fail(NOP_E_NOMEM, "plan allocation failed");
+    p->d = *desc;
+    for (int j = 0; j < p->d.ndim; ++j) p->modes_total *= p->d.kept[j];
+    for (int j = p->d.ndim; j < NOP_MAX_DIMS; ++j) {
+        p->d.n_in[j] = p->d.n_out[j] = p->d.kept[j] = 1;
+        p->d.fwd_off[j] = p->d.inv_off[j] = 0;
+    }
+    std::string why;
+    FastKind kind = FastKind::None;
+    const bool fast_ok = fast_supported(p->d, &kind, &why);
+    if (p->d.engine == NOP_ENGINE_FAST && !fast_ok) {
+        delete p;
+        return fail(NOP_E_UNSUPPORTED, "fused FFT engine does not cover this shape: " + why);
+    }
+    cudaError_t err = cudaGetDevice(&p->device);
+    if (err != cudaSuccess) {
+        delete p;
+        return cuda_fail(err, "cudaGetDevice");
+    }
+    p->fast = fast_ok && p->d.engine != NOP_ENGINE_GENERIC;
+    p->fast_kind = p->fast ? kind : FastKind::None;
+
+    size_t off = 0;
+    if (p->fast) {
+        off = fast_workspace_bytes(*p, &p->ws);
+    } else {
+        p->ws.buf_elems = generic_buffer_elems(p->d);
+        p->ws.buf_a = off;
+        off += align_up((size_t)p->ws.buf_elems * sizeof(float2));
+        p->ws.buf_b = off;
+        off += align_up((size_t)p->ws.buf_elems * sizeof(float2));
+    }
+    contraction_layout(*p, &off, &p->ws);
+    p->ws.bytes = off;
+
+    rc = build_tables(p);
+    if (rc != NOP_OK) {
+        delete p;
+        return rc;
+    }
+    *plan_out = reinterpret_cast<nop_plan*>(p);
+    return NOP_OK;
+}
+
+void nop_spectral_plan_destroy(nop_plan* plan) {
+    if (!plan) return;
+    Plan* p = reinterpret_cast<Plan*>(plan);
+    if (p->table_mem) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        if (prev != p->device) cudaSetDevice(p->device);
+        cudaFree(p->table_mem);
+        if (prev >= 0 && prev != p->device) cudaSetDevice(prev);
+    }
+    delete p;
+}
+
+int32_t nop_spectral_workspace_size(const nop_plan* plan, size_t* bytes) {
+    if (!plan || !bytes) return fail(NOP_E_INVALID, "plan and bytes must be non-NULL");
+    *bytes = reinterpret_cast<const Plan*>(plan)->ws.bytes;
+    return NOP_OK;
+}
+
+int32_t nop_spectral_plan_is_fast(const nop_plan* plan) {
+    return plan && reinterpret_cast<const Plan*>(plan)->fast ? 1 : 0;
+}
+
+int32_t nop_spectral_launches_per_forward(const nop_plan* plan) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    return p.fast ? fast_launches(p) : generic_launches(p);
+}
+
+int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* const* weights, int32_t n_weights,
+                             const float* bias, const float* addend, int32_t apply_gelu, void* y, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    const nop_spectral_desc& d = p.d;
+    if (n_weights != expected_weights(d))
+        return fail(NOP_E_INVALID, "expected " + std::to_string(expected_weights(d)) + " weight pointers, got " +
+                                       std::to_string(n_weights));
+    if (d.batch == 0) return NOP_OK;
+    if (!x || !y) return fail(NOP_E_INVALID, "x and y must be non-NULL");
+    if (!weights) return fail(NOP_E_INVALID, "weights array is NULL");
+    for (int i = 0; i < n_weights; ++i)
+        if (!weights[i]) return fail(NOP_E_INVALID, "weight pointer " + std::to_string(i) + " is NULL");
+    if (addend && d.complex_data) return fail(NOP_E_UNSUPPORTED, "addend / fused skip needs real data");
+    if (apply_gelu && d.complex_data) return fail(NOP_E_UNSUPPORTED, "fused GELU needs real data");
+    const size_t elem_align = d.complex_data ? 8 : 4;
+    if ((uintptr_t)x % elem_align || (uintptr_t)y % elem_align || (bias && (uintptr_t)bias % 4) ||
+        (addend && (uintptr_t)addend % 4))
+        return fail(NOP_E_ALIGNMENT, "x / y / bias / addend are not aligned to their element size");
+    for (int i = 0; i < n_weights; ++i)
+        if ((uintptr_t)weights[i] % 8) return fail(NOP_E_ALIGNMENT, "weights must be 8-byte aligned (complex64)");
+    if (p.ws.bytes > 0) {
+        if (!workspace) return fail(NOP_E_WORKSPACE, "workspace is NULL");
+        if (workspace_bytes < p.ws.bytes)
+            return fail(NOP_E_WORKSPACE, "workspace has " + std::to_string(workspace_bytes) + " bytes, plan needs " +
+                                             std::to_string(p.ws.bytes));
+        if ((uintptr_t)workspace % kAlign) return fail(NOP_E_ALIGNMENT, "workspace must be 256-byte aligned");
+    }
+    int dev = -1;
+    NOP_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != p.device)
+        return fail(NOP_E_INVALID, "plan was created on device " + std::to_string(p.device) +
+                                       " but the current device is " + std::to_string(dev));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* ws = static_cast<char*>(workspace);
+    if (p.fast) return fast_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s);
+    return generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+// Internal declarations shared by the libnop_b200 translation units.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "nop_spectral.h"
+
+namespace nop {
+
+// ------------------------------------------------------------------------------------------
+// error reporting (thread-local message behind nop_last_error)
+// ------------------------------------------------------------------------------------------
+void set_error(const std::string& msg);
+int32_t fail(int32_t code, const std::string& msg);
+int32_t cuda_fail(cudaError_t err, const char* what);
+
+#define NOP_CUDA_TRY(call)                                         \
+    do {                                                           \
+        cudaError_t e_ = (call);                                   \
+        if (e_ != cudaSuccess) return ::nop::cuda_fail(e_, #call); \
+    } while (0)
+
+// ------------------------------------------------------------------------------------------
+// plan
+// ------------------------------------------------------------------------------------------
+struct TwiddleTable {
+    int64_t n = 0;
+    const double2* d_table = nullptr;  // (cos 2 pi k / n, sin 2 pi k / n), k < n   (generic path)
+    const float2* f_table = nullptr;   // same values rounded to float               (fused path)
+};
+
+struct WorkspaceLayout {
+    size_t bytes = 0;
+    size_t buf_a = 0, buf_b = 0;       // ping-pong spectra (complex64)
+    size_t g = 0, g_tmp = 0;           // factorized weight expansions
+    size_t xf = 0, z = 0;              // factorized contraction intermediates
+    int64_t buf_elems = 0;
+};
+
+enum class FastKind : int32_t { None = 0, Plane2D = 1, Row1D = 2, Vol3D = 3 };
+
+struct Plan {
+    nop_spectral_desc d{};
+    int device = 0;
+    bool fast = false;
+    FastKind fast_kind = FastKind::None;
+    int64_t modes_total = 1;           // prod(kept)
+    std::vector<TwiddleTable> tables;  // one per distinct transform length
+    void* table_mem = nullptr;         // single device allocation holding every table
+    WorkspaceLayout ws;
+
+    const TwiddleTable* table(int64_t n) const {
+        for (const auto& t : tables)
+            if (t.n == n) return &t;
+        return nullptr;
+    }
+};
+
+// ------------------------------------------------------------------------------------------
+// generic direct-DFT engine (any sizes, any ndim): generic.cu
+// ------------------------------------------------------------------------------------------
+int64_t generic_buffer_elems(const nop_spectral_desc& d);
+int32_t generic_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
+                        const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+
+int32_t generic_launches(const Plan& p);
+int32_t contract_launches(const Plan& p);
+
+// contraction stage shared by both engines: X [B, Ci, Mt] -> Y [B, Co, Mt]
+int32_t contract_stage(const Plan& p, const float2* X, const void* const* weights, float2* Y, char* ws,
+                       cudaStream_t s);
+
+// ------------------------------------------------------------------------------------------
+// small device helpers
+// ------------------------------------------------------------------------------------------
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+__device__ __forceinline__ float gelu_erf(float v) {
+    // exact GELU, as torch.nn.functional.gelu(approximate="none")
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+}
+
+__device__ __forceinline__ float round_bf16(float v) {
+    // value after rounding to bfloat16 (round to nearest even), as float
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+}  // namespace nop

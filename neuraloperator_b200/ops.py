@@ -1,0 +1,115 @@
+"""Torch-facing wrapper of the C ABI: descriptor assembly, plan cache, launch.
+
+PyTorch provides device memory (including the workspace, from its caching allocator) and
+the current stream; all arithmetic runs in libnop_b200's CUDA kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from .geometry import Geometry
+
+_KIND = {"dense": _lib.WEIGHT_DENSE, "tucker": _lib.WEIGHT_TUCKER, "cp": _lib.WEIGHT_CP}
+_PREC = {"fp32": _lib.PRECISION_FP32, "bf16": _lib.PRECISION_BF16}
+_ENGINE = {"auto": _lib.ENGINE_AUTO, "generic": _lib.ENGINE_GENERIC, "fast": _lib.ENGINE_FAST}
+
+_plans = {}
+_plans_lock = threading.Lock()
+
+
+def make_desc(geo: Geometry, batch: int, in_channels: int, out_channels: int, *, weight_kind: str = "dense",
+              ranks: Sequence[int] = (), separable: bool = False, precision: str = "fp32",
+              engine: str = "auto") -> _lib.NopSpectralDesc:
+    d = _lib.NopSpectralDesc()
+    d.abi_version = _lib.ABI_VERSION
+    d.ndim = geo.order
+    d.complex_data = int(geo.complex_data)
+    d.separable = int(separable)
+    d.weight_kind = _KIND[weight_kind]
+    d.precision = _PREC[precision]
+    d.engine = _ENGINE[engine]
+    d.batch = int(batch)
+    d.in_channels = int(in_channels)
+    d.out_channels = int(out_channels)
+    for j in range(_lib.MAX_DIMS):
+        if j < geo.order:
+            d.n_in[j], d.n_out[j], d.kept[j] = geo.n_in[j], geo.n_out[j], geo.kept[j]
+            d.fwd_off[j], d.inv_off[j] = geo.fwd_off[j], geo.inv_off[j]
+        else:
+            d.n_in[j] = d.n_out[j] = d.kept[j] = 1
+    for i, r in enumerate(ranks):
+        d.ranks[i] = int(r)
+    zb = list(geo.zero_imag_bins)
+    if len(zb) > 3:
+        raise ValueError("at most three last-axis bins can be forced real")
+    d.n_zero_imag = len(zb)
+    for i, b in enumerate(zb):
+        d.zero_imag_bins[i] = int(b)
+    d.fwd_scale = float(geo.fwd_scale)
+    d.inv_scale = float(geo.inv_scale)
+    return d
+
+
+def get_plan(desc: _lib.NopSpectralDesc, device_index: int) -> _lib.Plan:
+    key = (device_index, bytes(desc))
+    plan = _plans.get(key)
+    if plan is None:
+        with _plans_lock:
+            plan = _plans.get(key)
+            if plan is None:
+                with torch.cuda.device(device_index):
+                    plan = _lib.Plan(desc)
+                _plans[key] = plan
+    return plan
+
+
+def clear_plans():
+    with _plans_lock:
+        _plans.clear()
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor], *, out_channels: int,
+                     weight_kind: str = "dense", ranks: Sequence[int] = (), separable: bool = False,
+                     bias: Optional[torch.Tensor] = None, addend: Optional[torch.Tensor] = None,
+                     apply_gelu: bool = False, precision: str = "fp32", engine: str = "auto",
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Run one spectral-block forward through nop_spectral_forward on x's device/stream."""
+    if not x.is_cuda:
+        raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path); "
+                           f"got a tensor on {x.device}")
+    dev = x.device
+    want = torch.complex64 if geo.complex_data else torch.float32
+    if x.dtype != want:
+        raise TypeError(f"expected {want} input, got {x.dtype}")
+    x = x.contiguous()
+    ws = [w.detach().to(device=dev, dtype=torch.complex64).contiguous() for w in weights]
+    b = None if bias is None else bias.detach().reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    a = None if addend is None else addend.detach().to(device=dev, dtype=torch.float32).contiguous()
+    batch, ci = x.shape[0], x.shape[1]
+    y_shape = (batch, out_channels, *geo.n_out)
+    if a is not None and tuple(a.shape) != y_shape:
+        raise ValueError(f"addend shape {tuple(a.shape)} != output shape {y_shape}")
+    if b is not None and b.numel() != out_channels:
+        raise ValueError(f"bias has {b.numel()} entries, expected {out_channels}")
+    y = out if out is not None else torch.empty(y_shape, device=dev, dtype=want)
+    desc = make_desc(geo, batch, ci, out_channels, weight_kind=weight_kind, ranks=ranks, separable=separable,
+                     precision=precision, engine=engine)
+    plan = get_plan(desc, dev.index if dev.index is not None else torch.cuda.current_device())
+    workspace = torch.empty(max(plan.workspace_bytes, 1), device=dev, dtype=torch.uint8)
+    arr = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        _lib.check(_lib.library().nop_spectral_forward(
+            plan.handle, _ptr(x), arr, len(ws), _ptr(b), _ptr(a), int(bool(apply_gelu)), _ptr(y),
+            _ptr(workspace), plan.workspace_bytes, ctypes.c_void_p(stream)))
+    return y

@@ -1,0 +1,205 @@
+"""SpectralConv: drop-in for neuralop.layers.spectral_convolution.SpectralConv on B200.
+
+Same constructor signature, parameters, ``n_modes`` property and ``forward`` /
+``transform`` methods as the reference (neuralop/layers/spectral_convolution.py:183-570).
+The forward runs entirely in libnop_b200's CUDA kernels: truncated forward FFT, per-mode
+contraction, truncated inverse FFT and bias, with no full spectrum ever stored.  Inputs
+must be CUDA tensors; there is no CPU path.
+
+Two keyword arguments are added after the reference's:
+``contraction_precision`` ("fp32" or "bf16": contraction operands rounded to bfloat16 with
+float32 accumulation) and ``engine`` ("auto", "fast", "generic").
+
+Differences that raise instead of silently diverging: ``fno_block_precision`` "half" /
+"mixed" (complex-half einsum, neuralop/layers/einsum_utils.py) raises NotImplementedError;
+calling ``backward`` through the block raises NotImplementedError (forward only).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Tuple, Union
+
+import torch
+from torch import nn
+
+from . import ops
+from .factorized import CPTensor, DenseTensor, FactorizedTensor, TTTensor, TuckerTensor
+from .geometry import Geometry, active_modes, compute_geometry, output_sizes
+from .utils import validate_scaling_factor
+
+Number = Union[int, float]
+
+
+class BaseSpectralConv(nn.Module):
+    """Plugin base (neuralop/layers/base_spectral_conv.py:4-27)."""
+
+    def __init__(self, device=None, dtype=None):
+        super().__init__()
+        self.dtype = dtype
+        self.device = device
+
+    def transform(self, x, output_shape=None):
+        return x
+
+
+class _SpectralFn(torch.autograd.Function):
+    """Forward through the CUDA kernels; backward is not implemented (raises)."""
+
+    @staticmethod
+    def forward(ctx, x, bias, addend, runner, *weights):
+        return runner(x, list(weights), bias, addend)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError("backward of the neuraloperator_b200 spectral block is not implemented "
+                                  "(the CUDA kernels are forward-only)")
+
+
+class SpectralConv(BaseSpectralConv):
+    """Fourier layer: rFFT -> keep n_modes -> per-mode channel contraction -> irFFT -> + bias."""
+
+    def __init__(self, in_channels, out_channels, n_modes, complex_data=False, max_n_modes=None, bias=True,
+                 separable=False, resolution_scaling_factor: Optional[Union[Number, List[Number]]] = None,
+                 fno_block_precision="full", rank=1.0, factorization=None, implementation="reconstructed",
+                 enforce_hermitian_symmetry=True, fixed_rank_modes=False, decomposition_kwargs: Optional[dict] = None,
+                 init_std="auto", fft_norm="forward", device=None, contraction_precision="fp32", engine="auto"):
+        super().__init__(device=device)
+        self.in_channels = in_channels
+        self.out_channels = out_channels
+        self.complex_data = complex_data
+        self.n_modes = n_modes
+        self.order = len(self.n_modes)
+        if max_n_modes is None:
+            max_n_modes = self.n_modes
+        elif isinstance(max_n_modes, int):
+            max_n_modes = [max_n_modes]
+        self.max_n_modes = max_n_modes
+        self.fno_block_precision = fno_block_precision
+        self.rank = rank
+        self.factorization = factorization
+        self.implementation = implementation
+        self.enforce_hermitian_symmetry = enforce_hermitian_symmetry
+        self.resolution_scaling_factor = validate_scaling_factor(resolution_scaling_factor, self.order)
+        if contraction_precision not in ("fp32", "bf16"):
+            raise ValueError("contraction_precision must be 'fp32' or 'bf16'")
+        self.contraction_precision = contraction_precision
+        self.engine = engine
+        if init_std == "auto":
+            init_std = (2 / (in_channels + out_channels)) ** 0.5
+        if isinstance(fixed_rank_modes, bool):
+            fixed_rank_modes = [0] if fixed_rank_modes else None
+        self.fft_norm = fft_norm
+        if factorization is None:
+            factorization = "Dense"
+        if separable:
+            if in_channels != out_channels:
+                raise ValueError("To use separable Fourier Conv, in_channels must be equal to out_channels, "
+                                 f"but got in_channels={in_channels} and out_channels={out_channels}")
+            weight_shape = (in_channels, *max_n_modes)
+        else:
+            weight_shape = (in_channels, out_channels, *max_n_modes)
+        self.separable = separable
+        if implementation not in ("reconstructed", "factorized"):
+            raise ValueError(f'Got implementation={implementation}, expected "reconstructed" or "factorized"')
+        kwargs = decomposition_kwargs if decomposition_kwargs is not None else {}
+        self.weight = FactorizedTensor.new(weight_shape, rank=self.rank, factorization=factorization,
+                                           fixed_rank_modes=fixed_rank_modes, **kwargs, dtype=torch.cfloat,
+                                           device=device)
+        self.weight.normal_(0, init_std)
+        if bias:
+            self.bias = nn.Parameter(init_std * torch.randn(*((self.out_channels,) + (1,) * self.order),
+                                                            device=device))
+        else:
+            self.bias = None
+
+    # -- reference API -------------------------------------------------------------------------
+    @property
+    def n_modes(self):
+        return self._n_modes
+
+    @n_modes.setter
+    def n_modes(self, n_modes):
+        self._n_modes = active_modes(n_modes, self.complex_data)
+
+    def transform(self, x, output_shape=None):
+        """Resample a skip connection to the output resolution (spectral_convolution.py:383-398)."""
+        in_shape = list(x.shape[2:])
+        if self.resolution_scaling_factor is not None and output_shape is None:
+            out_shape = tuple(round(s * r) for s, r in zip(in_shape, self.resolution_scaling_factor))
+        elif output_shape is not None:
+            out_shape = output_shape
+        else:
+            out_shape = in_shape
+        if list(in_shape) == list(out_shape):
+            return x
+        from .layers import resample
+        return resample(x, 1.0, list(range(2, x.ndim)), output_shape=out_shape)
+
+    # -- geometry and kernel operands -------------------------------------------------------------
+    def geometry(self, in_sizes, output_shape=None) -> Geometry:
+        out = output_sizes(in_sizes, self.resolution_scaling_factor, output_shape)
+        return compute_geometry(in_sizes, self.n_modes, self.max_n_modes, complex_data=self.complex_data,
+                                enforce_hermitian_symmetry=self.enforce_hermitian_symmetry, fft_norm=self.fft_norm,
+                                out_sizes=out)
+
+    def kernel_operands(self, geo: Geometry):
+        """(weight_kind, [tensors], ranks) for the kernels: the weight slice of :465-489."""
+        lead = (slice(None),) * (1 if self.separable else 2)
+        idx = lead + geo.weight_slices
+        w = self.weight
+        factorized = self.implementation == "factorized"
+        if isinstance(w, DenseTensor):
+            return "dense", [w.tensor[idx]], ()
+        if isinstance(w, TuckerTensor):
+            core, facs = w.sliced(idx)
+            if factorized:
+                return "tucker", [core] + facs, tuple(core.shape)
+            return "dense", [_tucker_full(core, facs)], ()
+        if isinstance(w, CPTensor):
+            lam, facs = w.sliced(idx)
+            if factorized:
+                return "cp", [lam] + facs, (lam.shape[0],)
+            return "dense", [_cp_full(lam, facs)], ()
+        if isinstance(w, TTTensor):
+            # tensor-train weights run as the reconstructed dense weight (same math, other rounding)
+            return "dense", [w.to_tensor(w.sliced(idx))], ()
+        if torch.is_tensor(w):
+            return "dense", [w[idx]], ()
+        raise ValueError(f"unexpected weight type {type(w).__name__}")
+
+    def _run(self, x, weights, bias, addend, *, geo, kind, ranks, apply_gelu):
+        return ops.spectral_forward(x, geo, weights, out_channels=self.out_channels, weight_kind=kind, ranks=ranks,
+                                    separable=self.separable, bias=bias, addend=addend, apply_gelu=apply_gelu,
+                                    precision=self.contraction_precision, engine=self.engine)
+
+    def forward(self, x: torch.Tensor, output_shape: Optional[Tuple[int]] = None, *, addend=None,
+                apply_gelu: bool = False):
+        """Spectral convolution of x (batch, channels, d1, ..., dN).
+
+        ``addend`` / ``apply_gelu`` fuse FNOBlocks' skip add and activation into the same
+        kernel: returns gelu(conv(x) + addend) (neuralop/layers/fno_block.py:356-361).
+        """
+        if self.fno_block_precision in ("half", "mixed"):
+            raise NotImplementedError("fno_block_precision='half'/'mixed' is not implemented; use "
+                                      "contraction_precision='bf16' for a reduced-precision contraction")
+        if not x.is_cuda:
+            raise RuntimeError("neuraloperator_b200.SpectralConv needs CUDA tensors; there is no CPU path")
+        geo = self.geometry(list(x.shape[2:]), output_shape)
+        kind, weights, ranks = self.kernel_operands(geo)
+        bias = None if self.bias is None else self.bias
+        runner = lambda xx, ww, bb, aa: self._run(xx, ww, bb, aa, geo=geo, kind=kind, ranks=ranks,
+                                                   apply_gelu=apply_gelu)
+        return _SpectralFn.apply(x, bias, addend, runner, *weights)
+
+
+def _tucker_full(core, factors):
+    t = core
+    for mode, u in enumerate(factors):
+        t = torch.tensordot(u, t.movedim(mode, 0), dims=([1], [0])).movedim(0, mode)
+    return t
+
+
+def _cp_full(lam, factors):
+    sy = "abcdefghijklmnop"
+    eq = "z," + ",".join(sy[i] + "z" for i in range(len(factors))) + "->" + sy[: len(factors)]
+    return torch.einsum(eq, lam, *factors)

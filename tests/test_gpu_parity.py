@@ -1,0 +1,178 @@
+"""Parity of the CUDA spectral block with the reference (golden vectors) and the oracle.
+
+Tolerances: relative L2 <= 1e-5 in fp32, <= 2e-2 with the bf16
+contraction.  TF32 is switched off in torch so the host-side ChannelMLP / skip GEMMs run in
+full fp32 like the reference's CPU path.
+"""
+
+import os
+
+import pytest
+import torch
+
+import neuraloperator_b200 as nb
+import oracle
+from conftest import GOLDEN, rel_l2
+from helpers import build_fno, build_spectral_conv, case_scaling
+from neuraloperator_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP32 = 1e-5
+TOL_BF16 = 2e-2
+
+SPECTRAL = torch.load(os.path.join(GOLDEN, "spectral_cases.pt"), weights_only=False)
+CONFIG = torch.load(os.path.join(GOLDEN, "config_layers.pt"), weights_only=False)
+FNO_CASES = torch.load(os.path.join(GOLDEN, "fno_cases.pt"), weights_only=False)
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _fp32_torch():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def _run(case, **extra):
+    conv = build_spectral_conv(case, **extra)
+    x = case["x"].cuda()
+    with torch.no_grad():
+        y = conv(x, **case["forward_kwargs"])
+    torch.cuda.synchronize()
+    return y
+
+
+@pytest.mark.parametrize("engine", ["auto", "generic"])
+@pytest.mark.parametrize("case", SPECTRAL, ids=[c["name"] for c in SPECTRAL])
+def test_spectral_conv_golden(case, engine):
+    y = _run(case, engine=engine)
+    assert y.shape == case["y"].shape and y.dtype == case["y"].dtype
+    assert rel_l2(y, case["y"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("engine", ["auto", "generic"])
+@pytest.mark.parametrize("case", CONFIG, ids=[c["name"] for c in CONFIG])
+def test_config_layers_golden(case, engine):
+    y = _run(case, engine=engine)
+    assert rel_l2(y, case["y"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("case", [c for c in SPECTRAL + CONFIG if not c["kwargs"].get("complex_data")],
+                         ids=[c["name"] for c in SPECTRAL + CONFIG if not c["kwargs"].get("complex_data")])
+def test_bf16_contraction_tolerance(case):
+    y = _run(case, contraction_precision="bf16")
+    assert rel_l2(y, case["y"]) <= TOL_BF16
+
+
+@pytest.mark.parametrize("case", [c for c in FNO_CASES if c["model"] != "FNOBlocks"],
+                         ids=[c["name"] for c in FNO_CASES if c["model"] != "FNOBlocks"])
+def test_fno_end_to_end_golden(case):
+    model = build_fno(case)
+    with torch.no_grad():
+        y = model(case["x"].cuda())
+    assert rel_l2(y, case["y"]) <= TOL_FP32
+
+
+def test_fnoblocks_fused_epilogue_golden():
+    """Skip add + GELU fused into the inverse epilogue (fno_block.py:356-361)."""
+    case = [c for c in FNO_CASES if c["model"] == "FNOBlocks"][0]
+    from helpers import load_block
+    fb = nb.FNOBlocks(**case["kwargs"])
+    for i, blk in enumerate(case["params"]["blocks"]):
+        load_block(fb, i, blk, "dense")
+    fb = fb.cuda()
+    h = case["x"].cuda()
+    with torch.no_grad():
+        for i in range(2):
+            assert fb._fusable(i, h, None)
+            h = fb(h, i)
+            assert rel_l2(h, case["y"][i]) <= TOL_FP32
+
+
+def _oracle_case(shape, modes, ci, co, batch, seed, **kw):
+    g = torch.Generator().manual_seed(seed)
+    conv = nb.SpectralConv(ci, co, modes, **kw)
+    with torch.no_grad():
+        conv.weight.tensor.copy_(torch.complex(torch.randn(conv.weight.shape, generator=g),
+                                               torch.randn(conv.weight.shape, generator=g)) * 0.2)
+        conv.bias.copy_(torch.randn(conv.bias.shape, generator=g))
+    x = torch.randn((batch, ci, *shape), generator=g)
+    ref = oracle.spectral_conv(x, conv.weight.tensor.detach(), conv.bias.detach(), modes)
+    return conv, x, ref
+
+
+@pytest.mark.parametrize("shape, modes, ci, co, batch", [
+    ((256, 256), (64, 64), 8, 8, 2),      # micro config grid / modes
+    ((512, 512), (64, 64), 4, 4, 1),      # TFNO config grid / modes
+    ((8192,), (16,), 8, 8, 4),            # Burgers config
+    ((128, 128), (16, 16), 8, 8, 3),      # Darcy config
+    ((64, 64, 64), (32, 32, 32), 2, 3, 1),
+    ((32, 48), (12, 20), 3, 5, 2),        # non-square
+    ((1, 16), (1, 8), 2, 2, 1),           # degenerate axis of length 1
+])
+def test_random_against_oracle(shape, modes, ci, co, batch):
+    conv, x, ref = _oracle_case(shape, modes, ci, co, batch, seed=sum(shape) + ci)
+    conv = conv.cuda()
+    with torch.no_grad():
+        y = conv(x.cuda())
+    assert rel_l2(y, ref) <= TOL_FP32
+
+
+def test_linearity_and_bias():
+    """Size-independent property: conv(a x1 + b x2) - bias = a (conv(x1)-bias) + b (conv(x2)-bias)."""
+    conv = nb.SpectralConv(8, 8, (64, 64)).cuda()
+    x1 = torch.randn(2, 8, 256, 256, device="cuda")
+    x2 = torch.randn(2, 8, 256, 256, device="cuda")
+    with torch.no_grad():
+        b = conv.bias
+        y1, y2, y12 = conv(x1) - b, conv(x2) - b, conv(0.5 * x1 - 2.0 * x2) - b
+    assert rel_l2(y12, 0.5 * y1 - 2.0 * y2) <= 1e-5
+
+
+def test_batch_zero_and_errors():
+    conv = nb.SpectralConv(2, 3, (4, 4)).cuda()
+    with torch.no_grad():
+        y = conv(torch.empty(0, 2, 8, 8, device="cuda"))
+    assert y.shape == (0, 3, 8, 8)
+    with pytest.raises(TypeError):
+        conv(torch.randn(1, 2, 8, 8, device="cuda", dtype=torch.float64))
+
+
+def test_backward_raises():
+    conv = nb.SpectralConv(2, 2, (4, 4)).cuda()
+    y = conv(torch.randn(1, 2, 8, 8, device="cuda", requires_grad=True))
+    with pytest.raises(NotImplementedError):
+        y.sum().backward()
+
+
+def test_nonzero_stream_and_repeat():
+    """Launches go on torch's current stream; repeated calls give identical results."""
+    conv = nb.SpectralConv(4, 4, (16, 16)).cuda()
+    x = torch.randn(2, 4, 64, 64, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.no_grad():
+        y0 = conv(x)
+        with torch.cuda.stream(s):
+            y1 = conv(x)
+        s.synchronize()
+    assert torch.equal(y0, y1)
+
+
+def test_workspace_too_small_is_rejected():
+    geo = nb.SpectralConv(2, 2, (4, 4)).geometry([8, 8])
+    desc = ops.make_desc(geo, 1, 2, 2)
+    plan = _lib.Plan(desc)
+    import ctypes
+    x = torch.randn(1, 2, 8, 8, device="cuda")
+    w = torch.zeros(2, 2, 4, 3, dtype=torch.complex64, device="cuda")
+    y = torch.empty_like(x)
+    ws = torch.empty(16, dtype=torch.uint8, device="cuda")
+    arr = (ctypes.c_void_p * 1)(w.data_ptr())
+    rc = _lib.library().nop_spectral_forward(plan.handle, ctypes.c_void_p(x.data_ptr()), arr, 1, None, None, 0,
+                                             ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(ws.data_ptr()), 16, None)
+    if plan.workspace_bytes > 16:
+        assert rc == -4 and "workspace" in _lib.last_error()

@@ -1,0 +1,101 @@
+"""CPU checks of the C ABI: the library loads, exports every declared symbol, and rejects
+malformed descriptors on the host (no GPU needed: validation runs before any CUDA call)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from neuraloperator_b200 import _lib
+from neuraloperator_b200.geometry import active_modes, compute_geometry
+from neuraloperator_b200.ops import make_desc
+
+
+def declared_functions():
+    names = []
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            names += re.findall(r"^\s*(?:int32_t|void|const char\*)\s+(nop_\w+)\s*\(", text, re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.library()
+    names = declared_functions()
+    assert names, "no declarations found in include/*.h"
+    for n in names:
+        assert hasattr(lib, n), f"{n} is declared in include/ but not exported"
+    assert set(_lib.EXPORTED_SYMBOLS) <= set(names)
+
+
+def test_abi_version_and_struct_layout():
+    lib = _lib.library()
+    assert lib.nop_abi_version() == _lib.ABI_VERSION
+    # 8 int32 + 3 int64 + 5*4 int64 + 6 int64 + 3 int64 + 2 double
+    assert ctypes.sizeof(_lib.NopSpectralDesc) == 8 * 4 + 3 * 8 + 20 * 8 + 6 * 8 + 3 * 8 + 2 * 8
+
+
+def _desc(**over):
+    geo = compute_geometry([16, 16], active_modes((8, 8), False), active_modes((8, 8), False))
+    d = make_desc(geo, 2, 3, 4)
+    for k, v in over.items():
+        if isinstance(v, tuple):
+            arr = getattr(d, k)
+            for i, e in enumerate(v):
+                arr[i] = e
+        else:
+            setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("over, msg", [
+    (dict(abi_version=99), "abi_version"),
+    (dict(ndim=0), "ndim"),
+    (dict(ndim=5), "ndim"),
+    (dict(batch=-1), "batch"),
+    (dict(in_channels=0), "channel"),
+    (dict(separable=1), "separable"),
+    (dict(weight_kind=7), "weight_kind"),
+    (dict(precision=3), "precision"),
+    (dict(engine=9), "engine"),
+    (dict(kept=(17, 5)), "kept modes"),
+    (dict(kept=(8, 10)), "kept modes"),
+    (dict(fwd_off=(16, 0)), "offsets"),
+    (dict(fwd_off=(4, 1)), "real last axis"),
+    (dict(n_in=(0, 16)), "spatial sizes"),
+    (dict(n_zero_imag=4), "n_zero_imag"),
+    (dict(weight_kind=1), "ranks"),
+])
+def test_plan_create_rejects_bad_descriptors(over, msg):
+    lib = _lib.library()
+    d = _desc(**over)
+    h = ctypes.c_void_p()
+    rc = lib.nop_spectral_plan_create(ctypes.byref(d), ctypes.byref(h))
+    assert rc == -1, (rc, _lib.last_error())
+    assert msg in _lib.last_error()
+    assert not h.value
+
+
+def test_null_arguments():
+    lib = _lib.library()
+    h = ctypes.c_void_p()
+    assert lib.nop_spectral_plan_create(None, ctypes.byref(h)) == -1
+    assert "NULL" in _lib.last_error()
+    assert lib.nop_spectral_forward(None, None, None, 0, None, None, 0, None, None, 0, None) == -1
+    size = ctypes.c_size_t()
+    assert lib.nop_spectral_workspace_size(None, ctypes.byref(size)) == -1
+    lib.nop_spectral_plan_destroy(None)  # no-op
+
+
+def test_fast_engine_request_reports_unsupported_shape():
+    """engine=FAST on a shape the fused kernels do not cover fails before any CUDA call."""
+    lib = _lib.library()
+    geo = compute_geometry([9, 7], active_modes((4, 4), False), active_modes((4, 4), False))
+    d = make_desc(geo, 1, 2, 2, engine="fast")
+    h = ctypes.c_void_p()
+    rc = lib.nop_spectral_plan_create(ctypes.byref(d), ctypes.byref(h))
+    assert rc == -2, _lib.last_error()
+    assert "fused FFT engine" in _lib.last_error()
