@@ -130,6 +130,22 @@ int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* co
                              int32_t apply_gelu, void* y, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Allocation-free forward.  No counterpart in the reference: it exists for callers that may not
+ * allocate device memory at all -- code hosted by a runtime that owns every byte of device memory
+ * and hands a plugin only its input and output buffers, or a latency-bound loop that cannot afford
+ * a cudaMalloc, which may synchronise the device.  It takes the descriptor directly (no plan, no
+ * workspace), runs the generic direct-DFT kernels and keeps their twiddle tables and intermediate
+ * spectra in a 16 MiB scratch area compiled into the library (held by every GPU that loads the
+ * library until the process exits).  Problems that need more scratch fail with NOP_E_WORKSPACE.
+ * The first call on each device looks up that area's device address; make it before any stream
+ * capture starts.  All calls on a device share the area and leave their contents in it (every
+ * region is fully rewritten before it is read); calls that run concurrently on the GPU race on it,
+ * so order them on one stream.  Arguments are those of nop_spectral_forward minus plan and
+ * workspace; it never calls cudaMalloc or cudaFree. */
+int32_t nop_spectral_forward_static(const nop_spectral_desc* desc, const void* x, const void* const* weights,
+                                    int32_t n_weights, const float* bias, const float* addend,
+                                    int32_t apply_gelu, void* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -45,8 +45,6 @@ int32_t fast_launches(const Plan& p);
 int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
                      const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
 
-namespace {
-
 int expected_weights(const nop_spectral_desc& d) {
     if (d.weight_kind == NOP_WEIGHT_DENSE) return 1;
     return 1 + (d.separable ? 1 : 2) + d.ndim;
@@ -104,7 +102,7 @@ int32_t validate(const nop_spectral_desc* d) {
     return NOP_OK;
 }
 
-int64_t tucker_expansion_elems(const nop_spectral_desc& d, int64_t lead, int r0) {
+static int64_t tucker_expansion_elems(const nop_spectral_desc& d, int64_t lead, int r0) {
     int64_t best = 0;
     for (int j = 0; j < d.ndim; ++j) {
         int64_t e = lead;
@@ -145,6 +143,8 @@ void contraction_layout(const Plan& p, size_t* off, WorkspaceLayout* ws) {
     ws->xf = take(xf);
     ws->z = take(z);
 }
+
+namespace {
 
 int32_t build_tables(Plan* p) {
     const nop_spectral_desc& d = p->d;

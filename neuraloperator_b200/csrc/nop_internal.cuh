@@ -61,6 +61,11 @@ struct Plan {
     }
 };
 
+// descriptor checks and contraction workspace regions (api.cu)
+int expected_weights(const nop_spectral_desc& d);
+int32_t validate(const nop_spectral_desc* d);
+void contraction_layout(const Plan& p, size_t* off, WorkspaceLayout* ws);
+
 // ------------------------------------------------------------------------------------------
 // generic direct-DFT engine (any sizes, any ndim): generic.cu
 // ------------------------------------------------------------------------------------------
