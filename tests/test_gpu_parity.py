@@ -176,3 +176,49 @@ def test_workspace_too_small_is_rejected():
                                              ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(ws.data_ptr()), 16, None)
     if plan.workspace_bytes > 16:
         assert rc == -4 and "workspace" in _lib.last_error()
+
+
+@pytest.mark.parametrize("n, modes, ci, co, batch", [
+    (128, (16, 16), 3, 70, 17),     # Darcy grid; Co > 64 (two output tiles), batch not a multiple of 16
+    (256, (64, 64), 8, 8, 2),       # micro config grid / modes
+    (512, (64, 64), 4, 5, 1),       # TFNO grid / modes
+    (256, (30, 20), 5, 3, 3),       # odd kept counts (My=30, Kx=11)
+    (128, (128, 64), 2, 2, 1),      # every y bin kept (offset 64), Kx = 33
+    (256, (8, 2), 2, 2, 1),         # tiny mode counts (Kx = 2)
+])
+def test_fast_engine_against_oracle(n, modes, ci, co, batch):
+    conv, x, ref = _oracle_case((n, n), modes, ci, co, batch, seed=n + ci + co)
+    conv.engine = "fast"
+    conv = conv.cuda()
+    with torch.no_grad():
+        y = conv(x.cuda())
+    assert rel_l2(y, ref) <= TOL_FP32
+
+
+@pytest.mark.parametrize("n", [128, 256, 512])
+def test_fast_engine_fused_epilogue(n):
+    conv, x, ref = _oracle_case((n, n), (32, 32), 4, 4, 2, seed=n)
+    g = torch.Generator().manual_seed(n + 1)
+    skip = torch.randn(ref.shape, generator=g)
+    conv.engine = "fast"
+    conv = conv.cuda()
+    with torch.no_grad():
+        y = conv(x.cuda(), addend=skip.cuda(), apply_gelu=True)
+    assert rel_l2(y, torch.nn.functional.gelu(ref + skip)) <= TOL_FP32
+
+
+def test_fast_engine_bf16_contraction():
+    conv, x, ref = _oracle_case((256, 256), (64, 64), 16, 16, 2, seed=5)
+    conv.engine = "fast"
+    conv.contraction_precision = "bf16"
+    conv = conv.cuda()
+    with torch.no_grad():
+        y = conv(x.cuda())
+    err = rel_l2(y, ref)
+    assert 1e-5 < err <= TOL_BF16  # visibly reduced precision, inside the bf16 bound
+
+
+def test_fast_engine_rejects_uncovered_shape():
+    conv = nb.SpectralConv(2, 2, (6, 6), engine="fast").cuda()
+    with pytest.raises(_lib.NopError):
+        conv(torch.randn(1, 2, 12, 12, device="cuda"))
