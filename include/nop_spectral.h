@@ -130,6 +130,27 @@ int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* co
                              int32_t apply_gelu, void* y, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Bytes of the packed-weight buffer of a fused-engine plan; 0 when the plan takes weights unpacked
+ * (generic engine).  Packing moves the per-forward weight reformatting (mode-blocked layout, Tucker
+ * core expansion) out of the forward, as the reference's weights are fixed between updates. */
+int32_t nop_spectral_packed_size(const nop_plan* plan, size_t* bytes);
+
+/* Pack `weights` (layout as for nop_spectral_forward) into `packed` (>= nop_spectral_packed_size
+ * bytes, 256-byte aligned).  Weight-only work on `stream`; redo it whenever the weights change.
+ * Replaces the weight slicing / factor handling of SpectralConv.forward
+ * (neuralop/layers/spectral_convolution.py:465-489) and the weight side of _contract_tucker (:76-103). */
+int32_t nop_spectral_pack_weights(const nop_plan* plan, const void* const* weights, int32_t n_weights,
+                                  void* packed, size_t packed_bytes, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* nop_spectral_forward with weights packed by nop_spectral_pack_weights.
+ * Replaces SpectralConv.forward (neuralop/layers/spectral_convolution.py:417-570) and, with
+ * addend / apply_gelu, the skip add + activation of neuralop/layers/fno_block.py:356-361. */
+int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const void* packed,
+                                    size_t packed_bytes, const float* bias, const float* addend,
+                                    int32_t apply_gelu, void* y, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* Allocation-free forward.  No counterpart in the reference: it exists for callers that may not
  * allocate device memory at all -- code hosted by a runtime that owns every byte of device memory
  * and hands a plugin only its input and output buffers, or a latency-bound loop that cannot afford

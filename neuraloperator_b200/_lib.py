@@ -28,7 +28,8 @@ ENGINE_AUTO, ENGINE_GENERIC, ENGINE_FAST = 0, 1, 2
 EXPORTED_SYMBOLS = (
     "nop_abi_version", "nop_last_error", "nop_spectral_plan_create", "nop_spectral_plan_destroy",
     "nop_spectral_workspace_size", "nop_spectral_plan_is_fast", "nop_spectral_launches_per_forward",
-    "nop_spectral_forward",
+    "nop_spectral_forward", "nop_spectral_packed_size", "nop_spectral_pack_weights",
+    "nop_spectral_forward_packed",
 )
 
 
@@ -83,6 +84,16 @@ def _declare(lib):
     lib.nop_spectral_plan_is_fast.argtypes = [c_plan_p]
     lib.nop_spectral_launches_per_forward.restype = ctypes.c_int32
     lib.nop_spectral_launches_per_forward.argtypes = [c_plan_p]
+    lib.nop_spectral_packed_size.restype = ctypes.c_int32
+    lib.nop_spectral_packed_size.argtypes = [c_plan_p, ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_spectral_pack_weights.restype = ctypes.c_int32
+    lib.nop_spectral_pack_weights.argtypes = [
+        c_plan_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nop_spectral_forward_packed.restype = ctypes.c_int32
+    lib.nop_spectral_forward_packed.argtypes = [
+        c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.nop_spectral_forward.restype = ctypes.c_int32
     lib.nop_spectral_forward.argtypes = [
         c_plan_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p,
@@ -139,6 +150,8 @@ class Plan:
         self.workspace_bytes = int(size.value)
         self.is_fast = bool(lib.nop_spectral_plan_is_fast(handle))
         self.launches_per_forward = int(lib.nop_spectral_launches_per_forward(handle))
+        check(lib.nop_spectral_packed_size(handle, ctypes.byref(size)))
+        self.packed_bytes = int(size.value)
 
     def __del__(self):
         h = getattr(self, "handle", None)

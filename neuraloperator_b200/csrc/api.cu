@@ -38,12 +38,6 @@ int32_t cuda_fail(cudaError_t err, const char* what) {
     return fail(NOP_E_CUDA, m);
 }
 
-// fused engine hooks (fast.cu)
-bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why);
-size_t fast_workspace_bytes(const Plan& p, WorkspaceLayout* ws);
-int32_t fast_launches(const Plan& p);
-int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
-                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
 
 int expected_weights(const nop_spectral_desc& d) {
     if (d.weight_kind == NOP_WEIGHT_DENSE) return 1;
@@ -249,8 +243,8 @@ int32_t nop_spectral_plan_create(const nop_spectral_desc* desc, nop_plan** plan_
         off += align_up((size_t)p->ws.buf_elems * sizeof(float2));
         p->ws.buf_b = off;
         off += align_up((size_t)p->ws.buf_elems * sizeof(float2));
+        contraction_layout(*p, &off, &p->ws);
     }
-    contraction_layout(*p, &off, &p->ws);
     p->ws.bytes = off;
 
     rc = build_tables(p);
@@ -329,6 +323,75 @@ int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* co
     char* ws = static_cast<char*>(workspace);
     if (p.fast) return fast_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s);
     return generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s);
+}
+
+int32_t nop_spectral_packed_size(const nop_plan* plan, size_t* bytes) {
+    if (!plan || !bytes) return fail(NOP_E_INVALID, "plan and bytes must be non-NULL");
+    *bytes = reinterpret_cast<const Plan*>(plan)->packed_bytes;
+    return NOP_OK;
+}
+
+static int32_t check_workspace(const Plan& p, const void* workspace, size_t workspace_bytes) {
+    if (p.ws.bytes == 0) return NOP_OK;
+    if (!workspace) return fail(NOP_E_WORKSPACE, "workspace is NULL");
+    if (workspace_bytes < p.ws.bytes)
+        return fail(NOP_E_WORKSPACE, "workspace has " + std::to_string(workspace_bytes) + " bytes, plan needs " +
+                                         std::to_string(p.ws.bytes));
+    if ((uintptr_t)workspace % kAlign) return fail(NOP_E_ALIGNMENT, "workspace must be 256-byte aligned");
+    return NOP_OK;
+}
+
+static int32_t check_device(const Plan& p) {
+    int dev = -1;
+    NOP_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != p.device)
+        return fail(NOP_E_INVALID, "plan was created on device " + std::to_string(p.device) +
+                                       " but the current device is " + std::to_string(dev));
+    return NOP_OK;
+}
+
+int32_t nop_spectral_pack_weights(const nop_plan* plan, const void* const* weights, int32_t n_weights, void* packed,
+                                  size_t packed_bytes, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    if (p.packed_bytes == 0) return fail(NOP_E_UNSUPPORTED, "this plan takes its weights unpacked");
+    if (n_weights != expected_weights(p.d))
+        return fail(NOP_E_INVALID, "expected " + std::to_string(expected_weights(p.d)) + " weight pointers, got " +
+                                       std::to_string(n_weights));
+    if (!weights) return fail(NOP_E_INVALID, "weights array is NULL");
+    for (int i = 0; i < n_weights; ++i) {
+        if (!weights[i]) return fail(NOP_E_INVALID, "weight pointer " + std::to_string(i) + " is NULL");
+        if ((uintptr_t)weights[i] % 8) return fail(NOP_E_ALIGNMENT, "weights must be 8-byte aligned (complex64)");
+    }
+    if (!packed || packed_bytes < p.packed_bytes)
+        return fail(NOP_E_WORKSPACE, "packed-weight buffer missing or smaller than nop_spectral_packed_size");
+    if ((uintptr_t)packed % kAlign) return fail(NOP_E_ALIGNMENT, "packed-weight buffer must be 256-byte aligned");
+    int32_t rc = check_workspace(p, workspace, workspace_bytes);
+    if (rc != NOP_OK) return rc;
+    if ((rc = check_device(p)) != NOP_OK) return rc;
+    return fast_pack(p, weights, static_cast<char*>(packed), static_cast<char*>(workspace),
+                     static_cast<cudaStream_t>(stream));
+}
+
+int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const void* packed, size_t packed_bytes,
+                                    const float* bias, const float* addend, int32_t apply_gelu, void* y,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    const nop_spectral_desc& d = p.d;
+    if (p.packed_bytes == 0) return fail(NOP_E_UNSUPPORTED, "this plan takes its weights unpacked");
+    if (d.batch == 0) return NOP_OK;
+    if (!x || !y) return fail(NOP_E_INVALID, "x and y must be non-NULL");
+    if (!packed || packed_bytes < p.packed_bytes)
+        return fail(NOP_E_WORKSPACE, "packed-weight buffer missing or smaller than nop_spectral_packed_size");
+    if ((uintptr_t)packed % kAlign) return fail(NOP_E_ALIGNMENT, "packed-weight buffer must be 256-byte aligned");
+    if ((uintptr_t)x % 4 || (uintptr_t)y % 4 || (bias && (uintptr_t)bias % 4) || (addend && (uintptr_t)addend % 4))
+        return fail(NOP_E_ALIGNMENT, "x / y / bias / addend are not aligned to their element size");
+    int32_t rc = check_workspace(p, workspace, workspace_bytes);
+    if (rc != NOP_OK) return rc;
+    if ((rc = check_device(p)) != NOP_OK) return rc;
+    return fast_forward_packed(p, x, static_cast<const char*>(packed), bias, addend, apply_gelu, y,
+                               static_cast<char*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -4,7 +4,9 @@
 //   k_plane_fwd  : one CTA per (batch, channel) plane.  Row transforms (two real rows packed as one
 //                  complex line) keep rFFT bins 0..Kx-1 in a shared-memory column store; column
 //                  transforms keep the My bins (m - off) mod N.  Only the kept modes reach HBM.
-//   k_mix_dense  : per-mode complex Cin x Cout contraction, 8-mode x 16-batch x 64-out tiles (fp32 FMA).
+//   k_mix        : per-mode complex contraction on the mode-blocked spectrum [Q][B][C][8]
+//                  (modes in blocks of 8), weights pre-packed once per weight version; Tucker
+//                  weights run as three such contractions (input factor, core, output factor).
 //   k_plane_inv  : column inverses of the kept modes, then row inverses (two real rows per complex
 //                  line) with the epilogue bias (+ skip) (+ GELU) fused into the final pass.
 // Other shapes fall back to the generic engine (plan-time decision).
@@ -12,6 +14,7 @@
 
 #include "fft_core.cuh"
 #include "nop_internal.cuh"
+#include "plane256.cuh"
 
 namespace nop {
 namespace {
@@ -43,7 +46,7 @@ size_t plane_smem_bytes(int Kx, int My) {
 template <int N>
 __global__ void __launch_bounds__(PlaneCfg<N>::THREADS, PlaneCfg<N>::MIN_BLOCKS)
 k_plane_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __restrict__ twg, int Kx, int My,
-            int off_y, float scale) {
+            int off_y, float scale, int64_t blk_stride) {
     using C = PlaneCfg<N>;
     extern __shared__ float2 smem[];
     float2* tw = smem;
@@ -85,7 +88,9 @@ k_plane_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2*
     __syncthreads();
     // ---- columns: complex transform along y, keep My bins (m - off_y) mod N ----
     float2* stage = X;
+    const int warp_first_group = (threadIdx.x & ~31) / C::G;
     for (int base = 0; base < Kx; base += C::GROUPS) {
+        if (base + warp_first_group >= Kx) break;  // warp-uniform: no column left for this warp
         const int c = base + g;
         const bool active = c < Kx;
         float2* col = T + (active ? c : 0) * C::TPITCH;
@@ -98,8 +103,16 @@ k_plane_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2*
             });
     }
     __syncthreads();
-    float2* op = out + plane * (int64_t)My * Kx;
-    for (int i = threadIdx.x; i < My * Kx; i += C::THREADS) op[i] = stage[i];
+    // kept modes -> mode-blocked spectrum [Q][L][8] (zero padding beyond Mt)
+    const int Mt = My * Kx;
+    const int Q = (Mt + 7) >> 3;
+    float2* op = out + plane * 8;
+    for (int e = threadIdx.x; e < Q * 4; e += C::THREADS) {
+        const int q = e >> 2, m = 8 * q + 2 * (e & 3);
+        const float2 a = m < Mt ? stage[m] : make_float2(0.f, 0.f);
+        const float2 b = m + 1 < Mt ? stage[m + 1] : make_float2(0.f, 0.f);
+        *reinterpret_cast<float4*>(op + q * blk_stride + 2 * (e & 3)) = make_float4(a.x, a.y, b.x, b.y);
+    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -117,7 +130,7 @@ struct Epilogue {
 template <int N>
 __global__ void __launch_bounds__(PlaneCfg<N>::THREADS, PlaneCfg<N>::MIN_BLOCKS)
 k_plane_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __restrict__ twg, int Kx, int My,
-            int off_y, float scale, Epilogue ep) {
+            int off_y, float scale, int64_t blk_stride, Epilogue ep) {
     using C = PlaneCfg<N>;
     extern __shared__ float2 smem[];
     float2* tw = smem;
@@ -128,11 +141,22 @@ k_plane_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* 
     const int t = threadIdx.x % C::G;
     for (int i = threadIdx.x; i < N; i += C::THREADS) tw[i] = twg[i];
     float2* stage = X;
-    const float2* ip = in + plane * (int64_t)My * Kx;
-    for (int i = threadIdx.x; i < My * Kx; i += C::THREADS) stage[i] = ip[i];
+    {  // mode-blocked spectrum [Q][L][8] -> kept modes of this plane
+        const int Mt = My * Kx;
+        const int Q = (Mt + 7) >> 3;
+        const float2* ip = in + plane * 8;
+        for (int e = threadIdx.x; e < Q * 4; e += C::THREADS) {
+            const int q = e >> 2, m = 8 * q + 2 * (e & 3);
+            const float4 v = __ldg(reinterpret_cast<const float4*>(ip + q * blk_stride + 2 * (e & 3)));
+            if (m < Mt) stage[m] = make_float2(v.x, v.y);
+            if (m + 1 < Mt) stage[m + 1] = make_float2(v.z, v.w);
+        }
+    }
     __syncthreads();
     // ---- columns: kept bins -> full y lines in the column store ----
+    const int warp_first_group = (threadIdx.x & ~31) / C::G;
     for (int base = 0; base < Kx; base += C::GROUPS) {
+        if (base + warp_first_group >= Kx) break;  // warp-uniform: no column left for this warp
         const int c = base + g;
         const bool active = c < Kx;
         float2* col = T + (active ? c : 0) * C::TPITCH;
@@ -198,62 +222,97 @@ k_plane_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* 
 }
 
 // ------------------------------------------------------------------------------------------
-// dense contraction  Y[b, o, m] = sum_i X[b, i, m] W[i, o, m]   (fp32 FMA, optional bf16 operands)
-// CTA tile: 8 modes x 16 batch x 64 out; K loop over Ci in chunks of 16.
-// Thread (og, mp, bg): o = o0 + og + 16 j (j < 4), modes m0 + 2 mp + {0,1}, b = b0 + 4 bg + {0..3}.
+// per-mode contraction on the mode-blocked spectrum
+//   Y[q][b][o][j] = sum_i X[q][b][i][j] W_q[i][o][8 q + j]      (j < 8: mode 8 q + j)
+// Packed weights: W_q[i][p][o] = float4(mode 8q+2p, mode 8q+2p+1), q stride `wq` float4 (0 when
+// the weight is the same for every mode).  CTA tile: one mode block x 16 batch x 64 out; the Ci
+// loop runs in chunks of 8 with cp.async double buffering.  Thread (og, mp, bg): o = o0 + og + 16 j,
+// modes 2 mp, 2 mp + 1, batch b0 + 4 bg + {0..3}.
 // ------------------------------------------------------------------------------------------
 constexpr int kMixThreads = 256;
-constexpr int kMixKC = 8;  // Ci chunk
+constexpr int kMixKC = 8;
+constexpr int kMixXs = kMixKC * 16 * 8;   // float2 per X stage
+constexpr int kMixWs = kMixKC * 4 * 64;   // float4 per W stage
+constexpr size_t kMixSmem = 2 * (kMixXs * sizeof(float2) + kMixWs * sizeof(float4));
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ float4 bf16x4(float4 v) {
+    return make_float4(round_bf16(v.x), round_bf16(v.y), round_bf16(v.z), round_bf16(v.w));
+}
 
 template <bool BF16>
 __global__ void __launch_bounds__(kMixThreads, 2)
-k_mix_dense(const float2* __restrict__ X, const float2* __restrict__ W, float2* __restrict__ Y, int B, int Ci,
-            int Co, int64_t Mt) {
-    __shared__ __align__(16) float2 Xs[kMixKC][16][8];  // [i][b][m]
-    __shared__ __align__(16) float4 Ws[kMixKC][4][64];  // [i][m pair][o] -> (m even, m odd)
+k_mix(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq, float2* __restrict__ Y, int B, int Ci,
+      int Co) {
+    extern __shared__ float4 mix_smem[];
+    float4* Ws = mix_smem;                                          // [2][KC][4][64]
+    float2* Xs = reinterpret_cast<float2*>(mix_smem + 2 * kMixWs);  // [2][KC][16][8]
     const int tid = threadIdx.x;
     const int og = tid & 15, mp = (tid >> 4) & 3, bg = tid >> 6;
-    const int64_t m0 = (int64_t)blockIdx.x * 8;
+    const int64_t q = blockIdx.x;
     const int b0 = blockIdx.y * 16;
     const int o0 = blockIdx.z * 64;
+    const float2* Xq = X + q * (int64_t)B * Ci * 8;
+    const float4* Wq = Wp + q * wq;
+    const int nchunks = (Ci + kMixKC - 1) / kMixKC;
+
+    auto load_chunk = [&](int c, int buf) {
+        const int i0 = c * kMixKC;
+        float2* xs = Xs + buf * kMixXs;
+        for (int e = tid; e < kMixKC * 16 * 4; e += kMixThreads) {  // 16-byte pieces of X
+            const int piece = e & 3, i = (e >> 2) % kMixKC, b = (e >> 2) / kMixKC;
+            const bool ok = b0 + b < B && i0 + i < Ci;
+            const float2* src = ok ? Xq + ((int64_t)(b0 + b) * Ci + i0 + i) * 8 + 2 * piece : Xq;
+            cp_async16(xs + (i * 16 + b) * 8 + 2 * piece, src, ok);
+        }
+        float4* ws = Ws + buf * kMixWs;
+        for (int e = tid; e < kMixWs; e += kMixThreads) {
+            const int o = e & 63, p = (e >> 6) & 3, i = e >> 8;
+            const bool ok = i0 + i < Ci && o0 + o < Co;
+            const float4* src = ok ? Wq + ((int64_t)(i0 + i) * 4 + p) * Co + o0 + o : Wq;
+            cp_async16(ws + (i * 4 + p) * 64 + o, src, ok);
+        }
+        cp_async_commit();
+    };
+
     float2 acc[4][4][2];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[a][j][0] = acc[a][j][1] = make_float2(0.f, 0.f);
 
-    for (int i0 = 0; i0 < Ci; i0 += kMixKC) {
-        // X chunk: 16 i x 16 b x 8 m  (m fastest in global memory)
-        for (int e = tid; e < kMixKC * 16 * 8; e += kMixThreads) {
-            const int m = e & 7, i = (e >> 3) % kMixKC, b = (e >> 3) / kMixKC;
-            float2 v = make_float2(0.f, 0.f);
-            if (b0 + b < B && i0 + i < Ci && m0 + m < Mt) v = __ldg(X + ((int64_t)(b0 + b) * Ci + i0 + i) * Mt + m0 + m);
-            if constexpr (BF16) v = make_float2(round_bf16(v.x), round_bf16(v.y));
-            Xs[i][b][m] = v;
-        }
-        // W chunk: 16 i x 64 o x 8 m
-        for (int e = tid; e < kMixKC * 64 * 4; e += kMixThreads) {
-            const int p = e & 3, o = (e >> 2) & 63, i = e >> 8;  // i < kMixKC
-            float2 v0 = make_float2(0.f, 0.f), v1 = v0;
-            if (i0 + i < Ci && o0 + o < Co) {
-                const float2* src = W + ((int64_t)(i0 + i) * Co + o0 + o) * Mt + m0 + 2 * p;
-                if (m0 + 2 * p < Mt) v0 = __ldg(src);
-                if (m0 + 2 * p + 1 < Mt) v1 = __ldg(src + 1);
-            }
-            if constexpr (BF16) {
-                v0 = make_float2(round_bf16(v0.x), round_bf16(v0.y));
-                v1 = make_float2(round_bf16(v1.x), round_bf16(v1.y));
-            }
-            Ws[i][p][o] = make_float4(v0.x, v0.y, v1.x, v1.y);
+    load_chunk(0, 0);
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + 1 < nchunks) {
+            load_chunk(c + 1, (c + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const float2* xs = Xs + (c & 1) * kMixXs;
+        const float4* ws = Ws + (c & 1) * kMixWs;
 #pragma unroll 2
         for (int i = 0; i < kMixKC; ++i) {
             float4 xv[4], wv[4];
 #pragma unroll
-            for (int a = 0; a < 4; ++a) xv[a] = *reinterpret_cast<const float4*>(&Xs[i][4 * bg + a][2 * mp]);
+            for (int a = 0; a < 4; ++a) xv[a] = *reinterpret_cast<const float4*>(xs + (i * 16 + 4 * bg + a) * 8 + 2 * mp);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) wv[j] = Ws[i][mp][og + 16 * j];
+            for (int j = 0; j < 4; ++j) wv[j] = ws[(i * 4 + mp) * 64 + og + 16 * j];
+            if constexpr (BF16) {
+#pragma unroll
+                for (int a = 0; a < 4; ++a) xv[a] = bf16x4(xv[a]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) wv[j] = bf16x4(wv[j]);
+            }
 #pragma unroll
             for (int a = 0; a < 4; ++a) {
 #pragma unroll
@@ -273,6 +332,7 @@ k_mix_dense(const float2* __restrict__ X, const float2* __restrict__ W, float2* 
         }
         __syncthreads();
     }
+    float2* Yq = Y + q * (int64_t)B * Co * 8;
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
         const int b = b0 + 4 * bg + a;
@@ -281,31 +341,146 @@ k_mix_dense(const float2* __restrict__ X, const float2* __restrict__ W, float2* 
         for (int j = 0; j < 4; ++j) {
             const int o = o0 + og + 16 * j;
             if (o >= Co) continue;
-            float2* dst = Y + ((int64_t)b * Co + o) * Mt + m0 + 2 * mp;
-            if (m0 + 2 * mp < Mt) dst[0] = acc[a][j][0];
-            if (m0 + 2 * mp + 1 < Mt) dst[1] = acc[a][j][1];
+            *reinterpret_cast<float4*>(Yq + ((int64_t)b * Co + o) * 8 + 2 * mp) =
+                make_float4(acc[a][j][0].x, acc[a][j][0].y, acc[a][j][1].x, acc[a][j][1].y);
         }
     }
+}
+
+// ------------------------------------------------------------------------------------------
+// weight packing (weight-only work, redone when the weights change)
+// ------------------------------------------------------------------------------------------
+// per-mode weight, element (i, o, m) at W[i * s_i + o * s_o + m]  ->  [Q][I][4][O] float4
+__global__ void k_pack_modes(const float2* __restrict__ W, float4* __restrict__ Wp, int I, int O, int64_t Mt,
+                             int64_t Q, int64_t s_i, int64_t s_o) {
+    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (idx >= Q * I * 4 * O) return;
+    const int o = (int)(idx % O);
+    const int p = (int)((idx / O) & 3);
+    const int i = (int)((idx / (4 * (int64_t)O)) % I);
+    const int64_t q = idx / (4 * (int64_t)O * I);
+    const int64_t m = 8 * q + 2 * p;
+    const float2* src = W + i * s_i + o * s_o;
+    const float2 a = m < Mt ? src[m] : make_float2(0.f, 0.f);
+    const float2 b = m + 1 < Mt ? src[m + 1] : make_float2(0.f, 0.f);
+    Wp[idx] = make_float4(a.x, a.y, b.x, b.y);
+}
+
+// mode-independent weight, element (i, o) at U[i * s_i + o * s_o]  ->  [I][4][O] float4
+__global__ void k_pack_broadcast(const float2* __restrict__ U, float4* __restrict__ Up, int I, int O, int64_t s_i,
+                                 int64_t s_o) {
+    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)I * 4 * O) return;
+    const int o = (int)(idx % O);
+    const int i = (int)(idx / (4 * (int64_t)O));
+    const float2 v = U[i * s_i + o * s_o];
+    Up[idx] = make_float4(v.x, v.y, v.x, v.y);
 }
 
 constexpr size_t kSmemLimit = 227 * 1024;
 
 // per-device "dynamic shared memory limit raised" bits, one word per kernel instantiation
-std::atomic<uint64_t> g_attr_done[8];
+std::atomic<uint64_t> g_attr_done[16];
 
 template <class K>
-cudaError_t ensure_smem_attr(K kernel, int slot, int device) {
+cudaError_t ensure_smem_attr(K kernel, int slot, int device, size_t bytes = kSmemLimit) {
     const uint64_t bit = uint64_t(1) << (device & 63);
     if (g_attr_done[slot].load() & bit) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e == cudaSuccess) g_attr_done[slot].fetch_or(bit);
     return e;
 }
 
-template <int N>
-int32_t run_plane_2d(const Plan& p, const void* x, const void* const* weights, const float* bias,
-                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
+inline size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+inline int64_t mode_blocks(const Plan& p) { return (p.modes_total + 7) / 8; }
+
+cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t wq, float2* Y, int Ci, int Co,
+                       cudaStream_t s) {
+    cudaError_t err = ensure_smem_attr(p.d.precision == NOP_PRECISION_BF16 ? k_mix<true> : k_mix<false>,
+                                       p.d.precision == NOP_PRECISION_BF16 ? 14 : 15, p.device, kMixSmem);
+    if (err != cudaSuccess) return err;
+    dim3 grid((unsigned)mode_blocks(p), (unsigned)ceil_div(p.d.batch, 16), (unsigned)ceil_div(Co, 64));
+    if (p.d.precision == NOP_PRECISION_BF16)
+        k_mix<true><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co);
+    else
+        k_mix<false><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co);
+    return cudaGetLastError();
+}
+
+// contraction on the mode-blocked spectrum with packed weights
+int32_t mix_stage(const Plan& p, const float2* Xh, const char* packed, float2* Yh, char* ws, cudaStream_t s) {
     const nop_spectral_desc& d = p.d;
+    const int Ci = (int)d.in_channels, Co = (int)d.out_channels;
+    cudaError_t err;
+    if (d.weight_kind == NOP_WEIGHT_DENSE) {
+        const float4* W = reinterpret_cast<const float4*>(packed + p.pk_w);
+        err = launch_mix(p, Xh, W, (int64_t)Ci * 4 * Co, Yh, Ci, Co, s);
+        return err == cudaSuccess ? NOP_OK : cuda_fail(err, "mix launch");
+    }
+    // Tucker: xf = X . U_in, z = xf . G (per mode), Y = z . U_out^T
+    const int rin = (int)d.ranks[0], rout = (int)d.ranks[1];
+    float2* xf = reinterpret_cast<float2*>(ws + p.ws.xf);
+    float2* z = reinterpret_cast<float2*>(ws + p.ws.z);
+    if ((err = launch_mix(p, Xh, reinterpret_cast<const float4*>(packed + p.pk_uin), 0, xf, Ci, rin, s)) !=
+        cudaSuccess)
+        return cuda_fail(err, "mix launch (input factor)");
+    if ((err = launch_mix(p, xf, reinterpret_cast<const float4*>(packed + p.pk_w), (int64_t)rin * 4 * rout, z, rin,
+                          rout, s)) != cudaSuccess)
+        return cuda_fail(err, "mix launch (core)");
+    if ((err = launch_mix(p, z, reinterpret_cast<const float4*>(packed + p.pk_uout), 0, Yh, rout, Co, s)) !=
+        cudaSuccess)
+        return cuda_fail(err, "mix launch (output factor)");
+    return NOP_OK;
+}
+
+// kept-mode specialisations of the 256 x 256 plane kernels (see plane256.cuh)
+template <int KX, int MY>
+bool p256_applies(const nop_spectral_desc& d) {
+    if (d.n_in[0] != 256 || d.kept[1] != KX || d.kept[0] != MY || d.fwd_off[0] != MY / 2 || d.inv_off[0] != MY / 2)
+        return false;
+    // the inverse forces only bin 0 real; every other forced bin must lie outside the kept range
+    bool has0 = false;
+    for (int i = 0; i < d.n_zero_imag; ++i) {
+        if (d.zero_imag_bins[i] == 0) has0 = true;
+        else if (d.zero_imag_bins[i] < KX) return false;
+    }
+    return has0;
+}
+
+template <int KX, int MY>
+int32_t run_p256(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
+                 int apply_gelu, void* y, char* ws, cudaStream_t s, int slot) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
+    constexpr size_t smem = p256::smem_bytes<KX, MY>();
+    const TwiddleTable* tt = p.table(256);
+    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
+    cudaError_t err;
+    if ((err = ensure_smem_attr(p256::k_fwd<KX, MY>, slot, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p256 fwd)");
+    if ((err = ensure_smem_attr(p256::k_inv<KX, MY>, slot + 1, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p256 inv)");
+    p256::k_fwd<KX, MY><<<(unsigned)Lin, p256::THREADS, smem, s>>>(static_cast<const float*>(x), Xh, tt->f_table,
+                                                                     (float)d.fwd_scale, Lin * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p256 fwd launch");
+    int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
+    if (rc != NOP_OK) return rc;
+    p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, 1};
+    p256::k_inv<KX, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Yh, static_cast<float*>(y), tt->f_table,
+                                                                      (float)d.inv_scale, Lout * 8, ep);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p256 inv launch");
+    return NOP_OK;
+}
+
+template <int N>
+int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
+                     int apply_gelu, void* y, char* ws, cudaStream_t s) {
+    const nop_spectral_desc& d = p.d;
+    if constexpr (N == 256) {
+        if (p256_applies<33, 64>(d)) return run_p256<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 6);
+        if (p256_applies<17, 32>(d)) return run_p256<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 8);
+    }
     const int Kx = (int)d.kept[1], My = (int)d.kept[0];
     const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
     const size_t smem = plane_smem_bytes<N>(Kx, My);
@@ -319,24 +494,10 @@ int32_t run_plane_2d(const Plan& p, const void* x, const void* const* weights, c
     if ((err = ensure_smem_attr(k_plane_inv<N>, 2 * slot + 1, p.device)) != cudaSuccess)
         return cuda_fail(err, "cudaFuncSetAttribute(plane_inv)");
     k_plane_fwd<N><<<(unsigned)Lin, PlaneCfg<N>::THREADS, smem, s>>>(
-        static_cast<const float*>(x), Xh, tt->f_table, Kx, My, (int)d.fwd_off[0], (float)d.fwd_scale);
+        static_cast<const float*>(x), Xh, tt->f_table, Kx, My, (int)d.fwd_off[0], (float)d.fwd_scale, Lin * 8);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "plane_fwd launch");
-    if (d.weight_kind == NOP_WEIGHT_DENSE && !d.separable) {
-        dim3 grid((unsigned)ceil_div(p.modes_total, 8), (unsigned)ceil_div(d.batch, 16),
-                  (unsigned)ceil_div(d.out_channels, 64));
-        if (d.precision == NOP_PRECISION_BF16)
-            k_mix_dense<true><<<grid, kMixThreads, 0, s>>>(Xh, static_cast<const float2*>(weights[0]), Yh,
-                                                           (int)d.batch, (int)d.in_channels, (int)d.out_channels,
-                                                           p.modes_total);
-        else
-            k_mix_dense<false><<<grid, kMixThreads, 0, s>>>(Xh, static_cast<const float2*>(weights[0]), Yh,
-                                                            (int)d.batch, (int)d.in_channels, (int)d.out_channels,
-                                                            p.modes_total);
-        if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "mix_dense launch");
-    } else {
-        int32_t rc = contract_stage(p, Xh, weights, Yh, ws, s);
-        if (rc != NOP_OK) return rc;
-    }
+    int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
+    if (rc != NOP_OK) return rc;
     Epilogue ep{};
     ep.bias = bias;
     ep.addend = addend;
@@ -349,7 +510,7 @@ int32_t run_plane_2d(const Plan& p, const void* x, const void* const* weights, c
     if (d.n_zero_imag > 2) ep.z2 = (int)d.zero_imag_bins[2];
     k_plane_inv<N><<<(unsigned)Lout, PlaneCfg<N>::THREADS, smem, s>>>(Yh, static_cast<float*>(y), tt->f_table, Kx,
                                                                        My, (int)d.inv_off[0], (float)d.inv_scale,
-                                                                       ep);
+                                                                       Lout * 8, ep);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "plane_inv launch");
     return NOP_OK;
 }
@@ -370,11 +531,15 @@ bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why
     if (d.complex_data) return *why = "complex data", false;
     for (int j = 0; j < d.ndim; ++j)
         if (d.n_out[j] != d.n_in[j]) return *why = "output resampling", false;
+    if (d.separable) return *why = "separable contraction", false;
+    if (d.weight_kind != NOP_WEIGHT_DENSE && d.weight_kind != NOP_WEIGHT_TUCKER)
+        return *why = "weight kind other than dense / Tucker", false;
     if (d.ndim != 2) return *why = "only 2D planes are fused so far", false;
     const int64_t N = d.n_in[0];
     if (d.n_in[1] != N) return *why = "non-square plane", false;
     if (N != 128 && N != 256 && N != 512) return *why = "plane size not in {128, 256, 512}", false;
-    if (d.batch * d.in_channels > 0x7fffffffLL || d.batch * d.out_channels > 0x7fffffffLL)
+    if (d.batch * d.in_channels > 0x7fffffffLL || d.batch * d.out_channels > 0x7fffffffLL ||
+        (d.batch + 15) / 16 > 65535)
         return *why = "too many planes for one launch", false;
     const size_t smem = plane_smem_for(N, (int)d.kept[1], (int)d.kept[0]);
     if (smem > kSmemLimit) return *why = "kept modes need more shared memory than a CTA has", false;
@@ -382,29 +547,101 @@ bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why
     return true;
 }
 
-size_t fast_workspace_bytes(const Plan& p, WorkspaceLayout* ws) {
-    const size_t a = (size_t)p.d.batch * p.d.in_channels * p.modes_total * sizeof(float2);
-    const size_t b = (size_t)p.d.batch * p.d.out_channels * p.modes_total * sizeof(float2);
-    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
-    ws->buf_a = 0;
-    ws->buf_b = up(a);
+// Workspace: mode-blocked X^ and Y^, Tucker intermediates, packing temporaries, packed weights
+// (the latter only used by the unpacked forward).  Also fixes the packed-weight layout.
+size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Q = mode_blocks(p), B = d.batch, Ci = d.in_channels, Co = d.out_channels;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = off;
+        off += up256(bytes);
+        return at;
+    };
+    ws->buf_a = take((size_t)Q * 8 * B * Ci * sizeof(float2));
+    ws->buf_b = take((size_t)Q * 8 * B * Co * sizeof(float2));
     ws->buf_elems = 0;
-    return up(a) + up(b);
+    size_t pk = 0;
+    auto pk_take = [&](size_t bytes) {
+        size_t at = pk;
+        pk += up256(bytes);
+        return at;
+    };
+    if (d.weight_kind == NOP_WEIGHT_DENSE) {
+        p.pk_w = pk_take((size_t)Q * Ci * 4 * Co * sizeof(float4));
+        ws->xf = ws->z = ws->g = ws->g_tmp = 0;
+    } else {
+        const int64_t rin = d.ranks[0], rout = d.ranks[1];
+        p.pk_w = pk_take((size_t)Q * rin * 4 * rout * sizeof(float4));
+        p.pk_uin = pk_take((size_t)Ci * 4 * rin * sizeof(float4));
+        p.pk_uout = pk_take((size_t)rout * 4 * Co * sizeof(float4));
+        ws->xf = take((size_t)Q * 8 * B * rin * sizeof(float2));
+        ws->z = take((size_t)Q * 8 * B * rout * sizeof(float2));
+        int64_t g = 0;
+        for (int j = 0; j < d.ndim; ++j) {
+            int64_t e = rin * rout;
+            for (int i = 0; i <= j; ++i) e *= d.kept[i];
+            for (int i = j + 1; i < d.ndim; ++i) e *= d.ranks[2 + i];
+            if (e > g) g = e;
+        }
+        ws->g = take((size_t)g * sizeof(float2));
+        ws->g_tmp = take((size_t)g * sizeof(float2));
+    }
+    p.packed_bytes = pk;
+    ws->packed = take(pk);
+    return off;
 }
 
-int32_t fast_launches(const Plan& p) {
-    const bool dense = p.d.weight_kind == NOP_WEIGHT_DENSE && !p.d.separable;
-    return 2 + (dense ? 1 : contract_launches(p));
+int32_t fast_launches(const Plan& p) { return 2 + (p.d.weight_kind == NOP_WEIGHT_DENSE ? 1 : 3); }
+
+int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Q = mode_blocks(p), Mt = p.modes_total, Ci = d.in_channels, Co = d.out_channels;
+    cudaError_t err;
+    if (d.weight_kind == NOP_WEIGHT_DENSE) {
+        const int64_t n = Q * Ci * 4 * Co;
+        k_pack_modes<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(weights[0]),
+                                                                reinterpret_cast<float4*>(packed + p.pk_w), (int)Ci,
+                                                                (int)Co, Mt, Q, Co * Mt, Mt);
+        return (err = cudaGetLastError()) == cudaSuccess ? NOP_OK : cuda_fail(err, "pack launch");
+    }
+    const int64_t rin = d.ranks[0], rout = d.ranks[1];
+    // G[f][g][m] = core x_2 U_1 x_3 U_2 ... (per-mode r_in x r_out matrices)
+    float2* G = expand_tucker_core(p, static_cast<const float2*>(weights[0]), weights, 3, rin * rout, ws, &err, s);
+    if (!G) return cuda_fail(err, "tucker core expansion");
+    int64_t n = Q * rin * 4 * rout;
+    k_pack_modes<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(G, reinterpret_cast<float4*>(packed + p.pk_w), (int)rin,
+                                                            (int)rout, Mt, Q, rout * Mt, Mt);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "pack launch (core)");
+    // U_in [Ci][r_in]: xf[f] = sum_i x[i] U_in[i][f]
+    n = Ci * 4 * rin;
+    k_pack_broadcast<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(weights[1]),
+                                                                reinterpret_cast<float4*>(packed + p.pk_uin), (int)Ci,
+                                                                (int)rin, rin, 1);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "pack launch (input factor)");
+    // U_out [Co][r_out]: y[o] = sum_g z[g] U_out[o][g]
+    n = rout * 4 * Co;
+    k_pack_broadcast<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(weights[2]),
+                                                                reinterpret_cast<float4*>(packed + p.pk_uout),
+                                                                (int)rout, (int)Co, 1, rout);
+    return (err = cudaGetLastError()) == cudaSuccess ? NOP_OK : cuda_fail(err, "pack launch (output factor)");
+}
+
+int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
+                            const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
+    switch (p.d.n_in[0]) {
+        case 128: return run_plane_2d<128>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        case 256: return run_plane_2d<256>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        case 512: return run_plane_2d<512>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        default: return fail(NOP_E_UNSUPPORTED, "fused engine: unsupported plane size");
+    }
 }
 
 int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
                      const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
-    switch (p.d.n_in[0]) {
-        case 128: return run_plane_2d<128>(p, x, weights, bias, addend, apply_gelu, y, ws, s);
-        case 256: return run_plane_2d<256>(p, x, weights, bias, addend, apply_gelu, y, ws, s);
-        case 512: return run_plane_2d<512>(p, x, weights, bias, addend, apply_gelu, y, ws, s);
-        default: return fail(NOP_E_UNSUPPORTED, "fused engine: unsupported plane size");
-    }
+    int32_t rc = fast_pack(p, weights, ws + p.ws.packed, ws, s);
+    if (rc != NOP_OK) return rc;
+    return fast_forward_packed(p, x, ws + p.ws.packed, bias, addend, apply_gelu, y, ws, s);
 }
 
 }  // namespace nop

@@ -246,6 +246,8 @@ inline cudaError_t launch_mix(const float2* X, const float2* W, float2* Y, int64
     return cudaGetLastError();
 }
 
+}  // namespace
+
 // Tucker core expanded along the spatial modes: core [lead..., r_1..r_d] -> [lead..., kept_1..kept_d]
 // (lead = r_in*r_out, or C for the separable layout), by successive mode products that alternate
 // between the g and g_tmp workspace regions.
@@ -272,8 +274,6 @@ float2* expand_tucker_core(const Plan& p, const float2* core, const void* const*
     }
     return const_cast<float2*>(cur);
 }
-
-}  // namespace
 
 int32_t contract_stage(const Plan& p, const float2* X, const void* const* weights, float2* Y, char* ws,
                        cudaStream_t s) {

@@ -39,6 +39,7 @@ struct WorkspaceLayout {
     size_t buf_a = 0, buf_b = 0;       // ping-pong spectra (complex64)
     size_t g = 0, g_tmp = 0;           // factorized weight expansions
     size_t xf = 0, z = 0;              // factorized contraction intermediates
+    size_t packed = 0;                 // packed weights (fused engine, unpacked forward only)
     int64_t buf_elems = 0;
 };
 
@@ -53,6 +54,8 @@ struct Plan {
     std::vector<TwiddleTable> tables;  // one per distinct transform length
     void* table_mem = nullptr;         // single device allocation holding every table
     WorkspaceLayout ws;
+    size_t packed_bytes = 0;           // fused engine: packed-weight buffer size (0: no packing)
+    size_t pk_w = 0, pk_uin = 0, pk_uout = 0;  // offsets inside the packed-weight buffer
 
     const TwiddleTable* table(int64_t n) const {
         for (const auto& t : tables)
@@ -74,11 +77,24 @@ int32_t generic_forward(const Plan& p, const void* x, const void* const* weights
                         const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
 
 int32_t generic_launches(const Plan& p);
+// Tucker core expanded along the spatial modes into the g / g_tmp workspace regions
+float2* expand_tucker_core(const Plan& p, const float2* core, const void* const* weights, int first_spatial_w,
+                           int64_t lead, char* ws, cudaError_t* err, cudaStream_t s);
 int32_t contract_launches(const Plan& p);
 
 // contraction stage shared by both engines: X [B, Ci, Mt] -> Y [B, Co, Mt]
 int32_t contract_stage(const Plan& p, const float2* X, const void* const* weights, float2* Y, char* ws,
                        cudaStream_t s);
+
+// fused FFT engine: fast.cu
+bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why);
+size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws);
+int32_t fast_launches(const Plan& p);
+int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s);
+int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
+                            const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
+                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
 
 // ------------------------------------------------------------------------------------------
 // small device helpers

@@ -78,12 +78,21 @@ def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+def _weight_key(ws):
+    return tuple((w.data_ptr(), w._version, tuple(w.shape), tuple(w.stride())) for w in ws)
+
+
 def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor], *, out_channels: int,
                      weight_kind: str = "dense", ranks: Sequence[int] = (), separable: bool = False,
                      bias: Optional[torch.Tensor] = None, addend: Optional[torch.Tensor] = None,
                      apply_gelu: bool = False, precision: str = "fp32", engine: str = "auto",
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Run one spectral-block forward through nop_spectral_forward on x's device/stream."""
+                     out: Optional[torch.Tensor] = None, cache: Optional[dict] = None) -> torch.Tensor:
+    """Run one spectral-block forward on x's device and current stream.
+
+    Fused-engine plans use packed weights (nop_spectral_pack_weights).  With ``cache`` (a dict
+    owned by the calling module) the packed buffer is kept and reused while the weight tensors
+    keep their storage and version counter; any in-place update or replacement repacks.
+    """
     if not x.is_cuda:
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path); "
                            f"got a tensor on {x.device}")
@@ -107,9 +116,25 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
     plan = get_plan(desc, dev.index if dev.index is not None else torch.cuda.current_device())
     workspace = torch.empty(max(plan.workspace_bytes, 1), device=dev, dtype=torch.uint8)
     arr = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    lib = _lib.library()
     with torch.cuda.device(dev):
-        _lib.check(_lib.library().nop_spectral_forward(
-            plan.handle, _ptr(x), arr, len(ws), _ptr(b), _ptr(a), int(bool(apply_gelu)), _ptr(y),
-            _ptr(workspace), plan.workspace_bytes, ctypes.c_void_p(stream)))
+        if plan.packed_bytes > 0:
+            key = (bytes(desc), _weight_key(ws))
+            entry = cache.get("packed") if cache is not None else None
+            if entry is None or entry[0] != key:
+                packed = torch.empty(plan.packed_bytes, device=dev, dtype=torch.uint8)
+                _lib.check(lib.nop_spectral_pack_weights(plan.handle, arr, len(ws), _ptr(packed), plan.packed_bytes,
+                                                         _ptr(workspace), plan.workspace_bytes, stream))
+                if cache is not None:
+                    cache["packed"] = (key, packed)
+            else:
+                packed = entry[1]
+            _lib.check(lib.nop_spectral_forward_packed(
+                plan.handle, _ptr(x), _ptr(packed), plan.packed_bytes, _ptr(b), _ptr(a), int(bool(apply_gelu)),
+                _ptr(y), _ptr(workspace), plan.workspace_bytes, stream))
+        else:
+            _lib.check(lib.nop_spectral_forward(
+                plan.handle, _ptr(x), arr, len(ws), _ptr(b), _ptr(a), int(bool(apply_gelu)), _ptr(y),
+                _ptr(workspace), plan.workspace_bytes, stream))
     return y

@@ -168,9 +168,10 @@ class SpectralConv(BaseSpectralConv):
         raise ValueError(f"unexpected weight type {type(w).__name__}")
 
     def _run(self, x, weights, bias, addend, *, geo, kind, ranks, apply_gelu):
+        cache = self.__dict__.setdefault("_nop_pack_cache", {})
         return ops.spectral_forward(x, geo, weights, out_channels=self.out_channels, weight_kind=kind, ranks=ranks,
                                     separable=self.separable, bias=bias, addend=addend, apply_gelu=apply_gelu,
-                                    precision=self.contraction_precision, engine=self.engine)
+                                    precision=self.contraction_precision, engine=self.engine, cache=cache)
 
     def forward(self, x: torch.Tensor, output_shape: Optional[Tuple[int]] = None, *, addend=None,
                 apply_gelu: bool = False):

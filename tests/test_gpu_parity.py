@@ -222,3 +222,59 @@ def test_fast_engine_rejects_uncovered_shape():
     conv = nb.SpectralConv(2, 2, (6, 6), engine="fast").cuda()
     with pytest.raises(_lib.NopError):
         conv(torch.randn(1, 2, 12, 12, device="cuda"))
+
+
+def test_fast_plan_unpacked_entry_matches_packed():
+    """nop_spectral_forward on a fused plan packs internally; same result as the packed path."""
+    import ctypes
+    conv, x, ref = _oracle_case((256, 256), (64, 64), 4, 6, 3, seed=11)
+    conv = conv.cuda()
+    xd = x.cuda()
+    with torch.no_grad():
+        y_mod = conv(xd)
+    geo = conv.geometry([256, 256])
+    _, weights, _ = conv.kernel_operands(geo)
+    w = weights[0].detach().contiguous()
+    b = conv.bias.detach().reshape(-1).contiguous()
+    plan = ops.get_plan(ops.make_desc(geo, 3, 4, 6), 0)
+    assert plan.is_fast and plan.packed_bytes > 0
+    ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device="cuda")
+    y = torch.empty_like(y_mod)
+    arr = (ctypes.c_void_p * 1)(w.data_ptr())
+    rc = _lib.library().nop_spectral_forward(plan.handle, ctypes.c_void_p(xd.data_ptr()), arr, 1,
+                                             ctypes.c_void_p(b.data_ptr()), None, 0, ctypes.c_void_p(y.data_ptr()),
+                                             ctypes.c_void_p(ws.data_ptr()), plan.workspace_bytes,
+                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_mod)
+    assert rel_l2(y, ref) <= TOL_FP32
+
+
+def test_packed_weights_follow_in_place_updates():
+    conv, x, _ = _oracle_case((128, 128), (16, 16), 4, 4, 2, seed=3)
+    conv = conv.cuda()
+    xd = x.cuda()
+    with torch.no_grad():
+        y0 = conv(xd)
+        conv.weight.tensor.mul_(2.0)   # in-place update bumps the version counter -> repack
+        y1 = conv(xd)
+    b = conv.bias.detach()
+    assert rel_l2(y1 - b, 2.0 * (y0 - b)) <= 1e-6
+
+
+@pytest.mark.parametrize("n, modes, ranks", [(256, (64, 64), 0.1), (128, (16, 16), 0.5)])
+def test_fast_tucker_against_oracle(n, modes, ranks):
+    g = torch.Generator().manual_seed(n)
+    conv = nb.SpectralConv(8, 8, modes, factorization="tucker", implementation="factorized", rank=ranks)
+    with torch.no_grad():
+        for prm in conv.weight.parameters():
+            prm.copy_(torch.complex(torch.randn(prm.shape, generator=g), torch.randn(prm.shape, generator=g)) * 0.5)
+    x = torch.randn((2, 8, n, n), generator=g)
+    w = {"core": conv.weight.core.detach(), "factors": [f.detach() for f in conv.weight.factors]}
+    ref = oracle.spectral_conv(x, w, conv.bias.detach(), modes, weight_kind="tucker")
+    conv.engine = "fast"
+    conv = conv.cuda()
+    with torch.no_grad():
+        y = conv(x.cuda())
+    assert rel_l2(y, ref) <= TOL_FP32
