@@ -14,7 +14,9 @@
 
 #include "fft_core.cuh"
 #include "nop_internal.cuh"
+#include "axis.cuh"
 #include "plane256.cuh"
+#include "row1d.cuh"
 
 namespace nop {
 namespace {
@@ -515,6 +517,95 @@ int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const flo
     return NOP_OK;
 }
 
+// ---- 1D: long lines, few kept bins ----
+template <int N, int K>
+int32_t run_row1d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
+                  int apply_gelu, void* y, char* ws, cudaStream_t s) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
+    const TwiddleTable* tt = p.table(N);
+    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
+    cudaError_t err;
+    r1d::k_fwd<N, K><<<(unsigned)ceil_div(Lin, r1d::LINES), r1d::THREADS, 0, s>>>(
+        static_cast<const float*>(x), Xh, tt->f_table, Lin, (float)d.fwd_scale, Lin * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "row1d fwd launch");
+    int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
+    if (rc != NOP_OK) return rc;
+    r1d::Epi1 ep{bias, addend, apply_gelu, (int)d.out_channels};
+    r1d::k_inv<N, K><<<(unsigned)ceil_div(Lout, r1d::LINES), r1d::THREADS, 0, s>>>(
+        Yh, static_cast<float*>(y), tt->f_table, Lout, (float)d.inv_scale, Lout * 8, ep);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "row1d inv launch");
+    return NOP_OK;
+}
+
+template <int N>
+int32_t run_row1d_k(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
+                    int apply_gelu, void* y, char* ws, cudaStream_t s) {
+    switch (p.d.kept[0]) {
+        case 9: return run_row1d<N, 9>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        case 17: return run_row1d<N, 17>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        default: return fail(NOP_E_UNSUPPORTED, "fused 1D engine: unsupported kept-bin count");
+    }
+}
+
+// ---- 3D: (y, z) plane kernels, outer-axis transforms along x, contraction ----
+template <int KZ, int MY, int MX>
+int32_t run_vol3d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
+                  int apply_gelu, void* y, char* ws, cudaStream_t s, int slot) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Nx = d.n_in[0];
+    const int64_t BCi = d.batch * d.in_channels, BCo = d.batch * d.out_channels;
+    const int64_t Lin = BCi * Nx, Lout = BCo * Nx;
+    constexpr int QP = MY * KZ / 8;
+    constexpr size_t smem = p256::smem_bytes<KZ, MY>();
+    float2* Pa = reinterpret_cast<float2*>(ws + p.ws.pl_a);
+    float2* Pb = reinterpret_cast<float2*>(ws + p.ws.pl_b);
+    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
+    const float2* tw256 = p.table(256)->f_table;
+    cudaError_t err;
+    if ((err = ensure_smem_attr(p256::k_fwd<KZ, MY>, slot, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p256 fwd)");
+    if ((err = ensure_smem_attr(p256::k_inv<KZ, MY>, slot + 1, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p256 inv)");
+    p256::k_fwd<KZ, MY><<<(unsigned)Lin, p256::THREADS, smem, s>>>(static_cast<const float*>(x), Pa, tw256,
+                                                                     (float)d.fwd_scale, Lin * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane fwd launch");
+    axis::k_fwd<MX><<<(unsigned)(QP * BCi), axis::THREADS, 0, s>>>(Pa, Xh, tw256, QP, BCi);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis fwd launch");
+    int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
+    if (rc != NOP_OK) return rc;
+    axis::k_inv<MX><<<(unsigned)(QP * BCo), axis::THREADS, 0, s>>>(Yh, Pb, tw256, QP, BCo);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis inv launch");
+    p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, Nx};
+    p256::k_inv<KZ, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Pb, static_cast<float*>(y), tw256,
+                                                                      (float)d.inv_scale, Lout * 8, ep);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane inv launch");
+    return NOP_OK;
+}
+
+bool vol3d_shape(const nop_spectral_desc& d, int* which) {
+    // x-axis 256 with MX centred bins; (y, z) planes 256 x 256 specialised on (kept y, kept z)
+    if (d.ndim != 3 || d.n_in[0] != 256 || d.n_in[1] != 256 || d.n_in[2] != 256) return false;
+    if (d.fwd_off[0] != d.kept[0] / 2 || d.inv_off[0] != d.kept[0] / 2) return false;
+    nop_spectral_desc plane = d;  // view the last two axes as a 2D plane for the p256 check
+    plane.n_in[0] = 256;
+    plane.kept[0] = d.kept[1];
+    plane.kept[1] = d.kept[2];
+    plane.fwd_off[0] = d.fwd_off[1];
+    plane.inv_off[0] = d.inv_off[1];
+    if (d.kept[0] == 32 && p256_applies<17, 32>(plane)) {
+        *which = 0;
+        return true;
+    }
+    if (d.kept[0] == 64 && p256_applies<33, 64>(plane)) {
+        *which = 1;
+        return true;
+    }
+    return false;
+}
+
 size_t plane_smem_for(int64_t N, int Kx, int My) {
     switch (N) {
         case 128: return plane_smem_bytes<128>(Kx, My);
@@ -534,7 +625,29 @@ bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why
     if (d.separable) return *why = "separable contraction", false;
     if (d.weight_kind != NOP_WEIGHT_DENSE && d.weight_kind != NOP_WEIGHT_TUCKER)
         return *why = "weight kind other than dense / Tucker", false;
-    if (d.ndim != 2) return *why = "only 2D planes are fused so far", false;
+    if (d.batch * d.in_channels > 0x7fffffffLL || d.batch * d.out_channels > 0x7fffffffLL ||
+        (d.batch + 15) / 16 > 65535)
+        return *why = "too many lines for one launch", false;
+    bool forced_ok = true;  // only bin 0 may be forced real inside the kept range of the last axis
+    for (int i = 0; i < d.n_zero_imag; ++i)
+        if (d.zero_imag_bins[i] != 0 && d.zero_imag_bins[i] < d.kept[d.ndim - 1]) forced_ok = false;
+    if (d.ndim == 1) {
+        const int64_t N = d.n_in[0];
+        if (N != 2048 && N != 4096 && N != 8192 && N != 16384) return *why = "1D length not in {2048..16384}", false;
+        if (d.kept[0] != 9 && d.kept[0] != 17) return *why = "1D kept bins not in {9, 17}", false;
+        if (!forced_ok) return *why = "forced-real bins inside the kept range", false;
+        *kind = FastKind::Row1D;
+        return true;
+    }
+    if (d.ndim == 3) {
+        int which;
+        if (!vol3d_shape(d, &which)) return *why = "3D shape not covered (256^3 with (32,32,17) or (64,64,33) modes)", false;
+        if (d.batch * d.in_channels * 256 > 0x7fffffffLL || d.batch * d.out_channels * 256 > 0x7fffffffLL)
+            return *why = "too many planes for one launch", false;
+        *kind = FastKind::Vol3D;
+        return true;
+    }
+    if (d.ndim != 2) return *why = "4D is not fused", false;
     const int64_t N = d.n_in[0];
     if (d.n_in[1] != N) return *why = "non-square plane", false;
     if (N != 128 && N != 256 && N != 512) return *why = "plane size not in {128, 256, 512}", false;
@@ -560,6 +673,11 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
     };
     ws->buf_a = take((size_t)Q * 8 * B * Ci * sizeof(float2));
     ws->buf_b = take((size_t)Q * 8 * B * Co * sizeof(float2));
+    if (p.fast_kind == FastKind::Vol3D) {
+        const size_t plane_modes = (size_t)d.kept[1] * d.kept[2];
+        ws->pl_a = take(plane_modes * B * Ci * d.n_in[0] * sizeof(float2));
+        ws->pl_b = take(plane_modes * B * Co * d.n_in[0] * sizeof(float2));
+    }
     ws->buf_elems = 0;
     size_t pk = 0;
     auto pk_take = [&](size_t bytes) {
@@ -592,7 +710,10 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
     return off;
 }
 
-int32_t fast_launches(const Plan& p) { return 2 + (p.d.weight_kind == NOP_WEIGHT_DENSE ? 1 : 3); }
+int32_t fast_launches(const Plan& p) {
+    const int transforms = p.fast_kind == FastKind::Vol3D ? 4 : 2;
+    return transforms + (p.d.weight_kind == NOP_WEIGHT_DENSE ? 1 : 3);
+}
 
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s) {
     const nop_spectral_desc& d = p.d;
@@ -629,6 +750,21 @@ int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char*
 
 int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
                             const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
+    if (p.fast_kind == FastKind::Row1D) {
+        switch (p.d.n_in[0]) {
+            case 2048: return run_row1d_k<2048>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+            case 4096: return run_row1d_k<4096>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+            case 8192: return run_row1d_k<8192>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+            case 16384: return run_row1d_k<16384>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+            default: return fail(NOP_E_UNSUPPORTED, "fused 1D engine: unsupported length");
+        }
+    }
+    if (p.fast_kind == FastKind::Vol3D) {
+        int which = -1;
+        vol3d_shape(p.d, &which);
+        if (which == 0) return run_vol3d<17, 32, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 10);
+        return run_vol3d<33, 64, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 12);
+    }
     switch (p.d.n_in[0]) {
         case 128: return run_plane_2d<128>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
         case 256: return run_plane_2d<256>(p, x, packed, bias, addend, apply_gelu, y, ws, s);

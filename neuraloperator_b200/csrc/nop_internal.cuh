@@ -40,6 +40,7 @@ struct WorkspaceLayout {
     size_t g = 0, g_tmp = 0;           // factorized weight expansions
     size_t xf = 0, z = 0;              // factorized contraction intermediates
     size_t packed = 0;                 // packed weights (fused engine, unpacked forward only)
+    size_t pl_a = 0, pl_b = 0;         // 3D: plane spectra before / after the outer-axis transform
     int64_t buf_elems = 0;
 };
 

@@ -18,7 +18,7 @@ constexpr int N = 256;
 constexpr int G = 16;             // lanes per line
 constexpr int THREADS = 256;      // 16 groups
 constexpr int GROUPS = THREADS / G;
-constexpr int LINE = 272;         // padded line (index i -> i + i/16)
+constexpr int LINE = 288;         // per-group exchange line (index i -> i + 2 (i / 16), 16-byte aligned rows)
 constexpr int TPITCH = 273;       // odd pitch of the column store
 constexpr int TWP = 18;           // per-lane twiddle row pitch (float2), 16-byte multiple
 
@@ -57,11 +57,18 @@ __host__ __device__ constexpr unsigned row_in_mask(int KX) {
 
 __host__ __device__ constexpr int ipad(int i) { return i + (i >> 4); }
 
+// float2 offset of the exchange / stage region: after tw, twp and the column store, rounded up to
+// an even count so the region is 16-byte aligned (128-bit stores into the exchange lines)
+template <int KX>
+__host__ __device__ constexpr size_t x_offset() {
+    return ((size_t)N + (size_t)G * TWP + (size_t)KX * TPITCH + 1) & ~(size_t)1;
+}
+
 template <int KX, int MY>
 __host__ __device__ constexpr size_t smem_bytes() {
     constexpr size_t stage = (size_t)MY * KX;
     constexpr size_t x = (size_t)GROUPS * LINE;
-    return sizeof(float2) * ((size_t)N + (size_t)G * TWP + (size_t)KX * TPITCH + (x > stage ? x : stage));
+    return sizeof(float2) * (x_offset<KX>() + (x > stage ? x : stage));
 }
 
 // per-lane pass-2 twiddles W^(r t) of a 256-point transform, conjugated for the forward direction
@@ -98,7 +105,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
     float2* tw = smem;
     float2* twp = tw + N;
     float2* T = twp + G * TWP;
-    float2* X = T + (size_t)KX * TPITCH;
+    float2* X = smem + x_offset<KX>();
     const int64_t plane = blockIdx.x;
     const int g = threadIdx.x / G;
     const int t = threadIdx.x % G;
@@ -108,20 +115,32 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
     float2* buf = X + g * LINE;
 
     // ---- rows: pairs (2p, 2p+1) as one complex line, kept bins to the column store ----
+    // The next pair's 32 loads are issued before the current pair is transformed.
+    float2 nxt[16];
+    {
+        const float* ra = xp + (int64_t)(2 * g) * N + t;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) nxt[r] = make_float2(__ldg(ra + 16 * r), __ldg(ra + N + 16 * r));
+    }
 #pragma unroll 1
     for (int base = 0; base < N / 2; base += GROUPS) {
         const int pr = base + g;
-        const float* ra = xp + (int64_t)(2 * pr) * N + t;
         float2 v[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = make_float2(__ldg(ra + 16 * r), __ldg(ra + N + 16 * r));
+        for (int r = 0; r < 16; ++r) v[r] = nxt[r];
+        if (base + GROUPS < N / 2) {
+            const float* ra = xp + (int64_t)(2 * (pr + GROUPS)) * N + t;
+#pragma unroll
+            for (int r = 0; r < 16; ++r) nxt[r] = make_float2(__ldg(ra + 16 * r), __ldg(ra + N + 16 * r));
+        }
         fft::dft16<false>(v);
         __syncwarp();
 #pragma unroll
-        for (int r = 0; r < 16; ++r) buf[17 * t + r] = v[r];
+        for (int r = 0; r < 16; r += 2)
+            *reinterpret_cast<float4*>(buf + 18 * t + r) = make_float4(v[r].x, v[r].y, v[r + 1].x, v[r + 1].y);
         __syncwarp();
 #pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = buf[t + 17 * r];
+        for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
         pass2_twiddle<false>(v, twl);
         fft::dft16_m<false, 0xFFFFu, OUT_ROW>(v);
         // separate the two real rows: A[k] = (Z_k + conj Z_{N-k}) / 2, B[k] = (Z_k - conj Z_{N-k}) / 2i
@@ -206,7 +225,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
     float2* tw = smem;
     float2* twp = tw + N;
     float2* T = twp + G * TWP;
-    float2* X = T + (size_t)KX * TPITCH;
+    float2* X = smem + x_offset<KX>();
     const int64_t plane = blockIdx.x;
     const int g = threadIdx.x / G;
     const int t = threadIdx.x % G;
@@ -298,10 +317,11 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
         fft::dft16_m<true, IN_ROW, 0xFFFFu>(v);
         __syncwarp();
 #pragma unroll
-        for (int r = 0; r < 16; ++r) buf[17 * t + r] = v[r];
+        for (int r = 0; r < 16; r += 2)
+            *reinterpret_cast<float4*>(buf + 18 * t + r) = make_float4(v[r].x, v[r].y, v[r + 1].x, v[r + 1].y);
         __syncwarp();
 #pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = buf[t + 17 * r];
+        for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
         pass2_twiddle<true>(v, twl);
         fft::dft16<true>(v);
 #pragma unroll

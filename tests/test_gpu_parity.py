@@ -278,3 +278,61 @@ def test_fast_tucker_against_oracle(n, modes, ranks):
     with torch.no_grad():
         y = conv(x.cuda())
     assert rel_l2(y, ref) <= TOL_FP32
+
+
+def _assert_fast(conv, x):
+    geo = conv.geometry(list(x.shape[2:]))
+    kind, _, ranks = conv.kernel_operands(geo)
+    plan = ops.get_plan(ops.make_desc(geo, x.shape[0], conv.in_channels, conv.out_channels, weight_kind=kind,
+                                      ranks=ranks), 0)
+    assert plan.is_fast
+
+
+@pytest.mark.parametrize("n, modes, ci, co, batch", [
+    (8192, (16,), 8, 6, 5),    # Burgers config length / modes (9 kept bins)
+    (2048, (32,), 3, 4, 3),    # 17 kept bins (fold of bin 16 onto the 16-point transform)
+    (16384, (16,), 2, 2, 2),
+])
+def test_fast_1d_against_oracle(n, modes, ci, co, batch):
+    conv, x, ref = _oracle_case((n,), modes, ci, co, batch, seed=n + ci)
+    g = torch.Generator().manual_seed(n)
+    skip = torch.randn(ref.shape, generator=g)
+    conv.engine = "fast"
+    conv = conv.cuda()
+    _assert_fast(conv, x)
+    with torch.no_grad():
+        y = conv(x.cuda())
+        yf = conv(x.cuda(), addend=skip.cuda(), apply_gelu=True)
+    assert rel_l2(y, ref) <= TOL_FP32
+    assert rel_l2(yf, torch.nn.functional.gelu(ref + skip)) <= TOL_FP32
+
+
+@pytest.mark.parametrize("modes, ci, co", [((32, 32, 32), 2, 3), ((64, 64, 64), 1, 2)])
+def test_fast_3d_against_oracle(modes, ci, co):
+    conv, x, ref = _oracle_case((256, 256, 256), modes, ci, co, 1, seed=sum(modes) + co)
+    conv.engine = "fast"
+    conv = conv.cuda()
+    _assert_fast(conv, x)
+    with torch.no_grad():
+        y = conv(x.cuda())
+    assert rel_l2(y, ref) <= TOL_FP32
+    skip = torch.randn(ref.shape, generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        yf = conv(x.cuda(), addend=skip.cuda(), apply_gelu=True)
+    assert rel_l2(yf, torch.nn.functional.gelu(ref + skip)) <= TOL_FP32
+
+
+def test_fast_3d_tucker():
+    g = torch.Generator().manual_seed(9)
+    conv = nb.SpectralConv(4, 4, (32, 32, 32), factorization="tucker", implementation="factorized", rank=0.2)
+    with torch.no_grad():
+        for prm in conv.weight.parameters():
+            prm.copy_(torch.complex(torch.randn(prm.shape, generator=g), torch.randn(prm.shape, generator=g)) * 0.5)
+    x = torch.randn((1, 4, 256, 256, 256), generator=g)
+    w = {"core": conv.weight.core.detach(), "factors": [f.detach() for f in conv.weight.factors]}
+    ref = oracle.spectral_conv(x, w, conv.bias.detach(), (32, 32, 32), weight_kind="tucker")
+    conv.engine = "fast"
+    conv = conv.cuda()
+    with torch.no_grad():
+        y = conv(x.cuda())
+    assert rel_l2(y, ref) <= TOL_FP32
