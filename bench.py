@@ -38,6 +38,15 @@ sys.path.insert(0, ROOT)
 METRIC = "FNO fwd samples/s/GPU at 1–8 B200; spectral block % of HBM/tensor roofline"
 HBM_FALLBACK_GBS = 6533.2  # measured copy bandwidth on this pool (MEASURED_PEAKS.json at round start)
 
+# DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures summarised under
+# profiles/ (small-batch capture scaled to the full batch; traffic grows with the number of planes)
+TRAFFIC = {
+    # profiles/plane_kernels_c2_b8_full.md: batch-8 capture x 8 (reads + writes during the kernel)
+    ("c2", "plane_inv"): 8 * (8.697344e6 + 79.776e6),
+    ("c2", "plane_fwd"): 8 * (134.24e6 + 4.466176e6),
+    ("c2", "contraction"): None,
+}
+
 # name -> (description, batch, Ci, Co, grid, n_modes, factorization)
 CONFIGS = {
     "c1": ("darcy2d_layer", 16, 32, 32, (128, 128), (16, 16), None),
@@ -237,6 +246,41 @@ def run_reference(args, cfg, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def kernel_names(plan, cfg):
+    """Names of the kernels one forward launches, in launch order (fused engine layouts)."""
+    fact = cfg[6]
+    mix = ["contraction"] if not fact else ["contraction_in_factor", "contraction_core", "contraction_out_factor"]
+    nd = len(cfg[4])
+    if not plan.is_fast:
+        return [f"kernel_{i}" for i in range(plan.launches_per_forward)]
+    if nd == 3:
+        return ["plane_fwd", "axis_fwd"] + mix + ["axis_inv", "plane_inv"]
+    if nd == 1:
+        return ["row_fwd"] + mix + ["row_inv"]
+    return ["plane_fwd"] + mix + ["plane_inv"]
+
+
+def kernel_bytes(name, cfg, conv):
+    """Compulsory HBM bytes of one kernel launch: its inputs and outputs, each touched once."""
+    _, batch, ci, co, grid, modes, _ = cfg
+    p = math.prod(grid)
+    geo = conv.geometry(list(grid))
+    mt = geo.n_modes_total
+    xs, ys = batch * ci * mt * 8, batch * co * mt * 8
+    w = sum(t.numel() * t.element_size() for t in conv.weight.parameters())
+    plane_modes = mt // geo.kept[0] if len(grid) == 3 else mt
+    table = {
+        "plane_fwd": batch * ci * p * 4 + (batch * ci * grid[0] * plane_modes * 8 if len(grid) == 3 else xs),
+        "row_fwd": batch * ci * p * 4 + xs,
+        "plane_inv": (batch * co * grid[0] * plane_modes * 8 if len(grid) == 3 else ys) + batch * co * p * 4,
+        "row_inv": ys + batch * co * p * 4,
+        "axis_fwd": batch * ci * grid[0] * plane_modes * 8 + xs,
+        "axis_inv": ys + batch * co * grid[0] * plane_modes * 8,
+        "contraction": xs + w + ys,
+    }
+    return table.get(name)
+
+
 def run_ours(args, cfg, world, rank, local):
     import neuraloperator_b200 as nb  # noqa: F401
     from neuraloperator_b200 import ops
@@ -258,21 +302,31 @@ def run_ours(args, cfg, world, rank, local):
         desc_c = ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks, engine=args.engine)
         plan = ops.get_plan(desc_c, local)
 
-        # ---- device-resident timed region ----
+        # ---- device-resident timed region (per-kernel CUDA events on the launching stream) ----
+        from neuraloperator_b200 import _lib
+        nk = plan.launches_per_forward
+        marks = [_lib.LaunchEvents(nk) for _ in range(steps)]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier(world)
         torch.cuda.synchronize()
         with ClockSampler(local) as clocks:
             e0.record(stream)
-            for _ in range(steps):
-                y = conv(x)
+            for k in range(steps):
+                with marks[k]:
+                    y = conv(x)
             e1.record(stream)
             torch.cuda.synchronize()
         barrier(world)
         ms = e0.elapsed_time(e1) / steps
         ms = max_over_ranks(ms, world)
         value = world * batch / (ms / 1e3)
+        per_kernel = [statistics.mean(m.durations_ms()[i] for m in marks) for i in range(nk)]
 
+        if args.no_e2e:
+            ms_e2e = float("nan")
+        else:
+            ms_e2e = None
+    if ms_e2e is None:
         # ---- end to end through the public API: pinned host in, pinned host out ----
         x_host = x.cpu().pin_memory()
         y_host = torch.empty(y.shape, dtype=y.dtype).pin_memory()
@@ -280,12 +334,13 @@ def run_ours(args, cfg, world, rank, local):
         barrier(world)
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for _ in range(e2e_steps):
-            xd = x_host.to(dev, non_blocking=True)
-            yd = conv(xd)
-            y_host.copy_(yd, non_blocking=True)
-        f1.record(stream)
+        with torch.no_grad():
+            f0.record(stream)
+            for _ in range(e2e_steps):
+                xd = x_host.to(dev, non_blocking=True)
+                yd = conv(xd)
+                y_host.copy_(yd, non_blocking=True)
+            f1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         ms_e2e = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
@@ -294,8 +349,16 @@ def run_ours(args, cfg, world, rank, local):
         return
     hbm, peak_src = peaks()
     b_alg = bytes_alg(cfg, conv)
-    achieved = b_alg / (ms / 1e3) / 1e9
+    block_gbs = b_alg / (ms / 1e3) / 1e9
     clk = clocks.summary()
+    names = kernel_names(plan, cfg)
+    kernels = []
+    for name, kms in zip(names, per_kernel):
+        kb = kernel_bytes(name, cfg, conv)
+        kernels.append({"name": name, "ms": kms, "bytes_alg": kb,
+                        "gbs": kb / (kms / 1e3) / 1e9 if kb else None,
+                        "frac": kb / (kms / 1e3) / 1e9 / hbm if kb else None})
+    dom = max(kernels, key=lambda k: k["ms"])
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -304,12 +367,17 @@ def run_ours(args, cfg, world, rank, local):
                    "channels": [ci, co], "n_modes": list(modes), "factorization": fact or "dense",
                    "parallelism": f"dp{world}" if world > 1 else "single", "engine": "fast" if plan.is_fast else
                    "generic", "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB > 126 MB L2 (no flush needed)"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": None, "kernel": "spectral block (all launches of one forward)",
-                     "bytes_alg_per_launch": b_alg, "peak_source": peak_src},
-        "e2e": {"value": world * batch / (ms_e2e / 1e3), "unit": "samples/s",
-                "h2d_bytes_per_step": x.numel() * x.element_size(),
-                "d2h_bytes_per_step": y.numel() * y.element_size()},
+        "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm, "unit": "GB/s", "frac": dom["frac"],
+                     "traffic": TRAFFIC.get((args.config, dom["name"])), "kernel": dom["name"],
+                     "bytes_alg_per_launch": dom["bytes_alg"], "ms_per_launch": dom["ms"],
+                     "peak_source": peak_src + " (copy bandwidth, burst)"},
+        "block_roofline": {"bound": "hbm", "achieved": block_gbs, "peak": hbm, "unit": "GB/s",
+                           "frac": block_gbs / hbm, "bytes_alg_per_step": b_alg,
+                           "definition": "|x| + |y| + |W| + |bias| per forward over the step time"},
+        "kernels": kernels,
+        "e2e": ({"value": world * batch / (ms_e2e / 1e3), "unit": "samples/s",
+                 "h2d_bytes_per_step": x.numel() * x.element_size(),
+                 "d2h_bytes_per_step": y.numel() * y.element_size()} if not args.no_e2e else None),
         "gpu_launches": plan.launches_per_forward * steps,
         "clocks": clk,
     }
@@ -326,12 +394,16 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--engine", choices=["auto", "fast", "generic"], default="auto")
+    ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (default: the config's)")
+    ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = CONFIGS[args.config]
+    if args.batch is not None:
+        cfg = (cfg[0], args.batch) + tuple(cfg[2:])
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

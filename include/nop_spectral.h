@@ -151,6 +151,13 @@ int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const v
                                     int32_t apply_gelu, void* y, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/* Measurement hook (no counterpart in the reference, which has no kernels of its own): while n > 0
+ * on the calling thread, every forward call records events[0] on its stream before its first
+ * kernel and events[i] after its i-th kernel launch (i = 1 .. n-1).  `events` are cudaEvent_t
+ * created by the caller; n = 0 disables.  Lets a caller time each kernel of the block with CUDA
+ * events on the launching stream. */
+int32_t nop_set_launch_events(void* const* events, int32_t n);
+
 /* Allocation-free forward.  No counterpart in the reference: it exists for callers that may not
  * allocate device memory at all -- code hosted by a runtime that owns every byte of device memory
  * and hands a plugin only its input and output buffers, or a latency-bound loop that cannot afford

@@ -29,7 +29,7 @@ EXPORTED_SYMBOLS = (
     "nop_abi_version", "nop_last_error", "nop_spectral_plan_create", "nop_spectral_plan_destroy",
     "nop_spectral_workspace_size", "nop_spectral_plan_is_fast", "nop_spectral_launches_per_forward",
     "nop_spectral_forward", "nop_spectral_packed_size", "nop_spectral_pack_weights",
-    "nop_spectral_forward_packed",
+    "nop_spectral_forward_packed", "nop_set_launch_events",
 )
 
 
@@ -94,6 +94,8 @@ def _declare(lib):
     lib.nop_spectral_forward_packed.argtypes = [
         c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nop_set_launch_events.restype = ctypes.c_int32
+    lib.nop_set_launch_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32]
     lib.nop_spectral_forward.restype = ctypes.c_int32
     lib.nop_spectral_forward.argtypes = [
         c_plan_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p,
@@ -124,6 +126,32 @@ def library():
             raise RuntimeError(f"libnop_b200.so ABI {v} != binding ABI {ABI_VERSION}; rebuild the library")
         _lib = lib
         return lib
+
+
+class LaunchEvents:
+    """Context manager: time every kernel of the forward calls made inside it with CUDA events.
+
+    ``LaunchEvents(n_kernels)`` records events[0] before the first kernel and events[i] after the
+    i-th; ``durations_ms()`` returns the per-kernel times of the last forward.
+    """
+
+    def __init__(self, n_kernels: int):
+        import torch
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(n_kernels + 1)]
+        for e in self.events:  # torch creates the underlying cudaEvent_t on first record
+            e.record()
+
+    def __enter__(self):
+        arr = (ctypes.c_void_p * len(self.events))(*[e.cuda_event for e in self.events])
+        check(library().nop_set_launch_events(arr, len(self.events)))
+        return self
+
+    def __exit__(self, *exc):
+        library().nop_set_launch_events(None, 0)
+        return False
+
+    def durations_ms(self):
+        return [self.events[i].elapsed_time(self.events[i + 1]) for i in range(len(self.events) - 1)]
 
 
 def last_error() -> str:

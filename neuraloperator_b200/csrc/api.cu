@@ -26,6 +26,31 @@ bool mul_ok(int64_t a, int64_t b, int64_t* out) {
 }
 }  // namespace
 
+namespace {
+struct LaunchEvents {
+    cudaEvent_t ev[32];
+    int n = 0;
+    int next = 0;
+};
+thread_local LaunchEvents g_events;
+}  // namespace
+
+void launch_mark_begin(cudaStream_t s) {
+    if (g_events.n > 0) {
+        cudaEventRecord(g_events.ev[0], s);
+        g_events.next = 1;
+    }
+}
+
+void launch_mark(cudaStream_t s) {
+    if (g_events.next > 0 && g_events.next < g_events.n) cudaEventRecord(g_events.ev[g_events.next++], s);
+}
+
+static int32_t launch_mark_end(int32_t rc) {
+    g_events.next = 0;  // marks only follow the launches of one forward call
+    return rc;
+}
+
 void set_error(const std::string& msg) { g_last_error = msg; }
 
 int32_t fail(int32_t code, const std::string& msg) {
@@ -321,8 +346,18 @@ int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* co
                                        " but the current device is " + std::to_string(dev));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     char* ws = static_cast<char*>(workspace);
-    if (p.fast) return fast_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s);
-    return generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s);
+    launch_mark_begin(s);
+    if (p.fast) return launch_mark_end(fast_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s));
+    return launch_mark_end(generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s));
+}
+
+int32_t nop_set_launch_events(void* const* events, int32_t n) {
+    if (n < 0 || n > 32) return fail(NOP_E_INVALID, "event count must be in 0..32");
+    if (n > 0 && !events) return fail(NOP_E_INVALID, "events is NULL");
+    for (int i = 0; i < n; ++i) g_events.ev[i] = static_cast<cudaEvent_t>(events[i]);
+    g_events.n = n;
+    g_events.next = 0;
+    return NOP_OK;
 }
 
 int32_t nop_spectral_packed_size(const nop_plan* plan, size_t* bytes) {
@@ -390,8 +425,9 @@ int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const v
     int32_t rc = check_workspace(p, workspace, workspace_bytes);
     if (rc != NOP_OK) return rc;
     if ((rc = check_device(p)) != NOP_OK) return rc;
-    return fast_forward_packed(p, x, static_cast<const char*>(packed), bias, addend, apply_gelu, y,
-                               static_cast<char*>(workspace), static_cast<cudaStream_t>(stream));
+    launch_mark_begin(static_cast<cudaStream_t>(stream));
+    return launch_mark_end(fast_forward_packed(p, x, static_cast<const char*>(packed), bias, addend, apply_gelu, y,
+                                               static_cast<char*>(workspace), static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

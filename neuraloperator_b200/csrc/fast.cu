@@ -406,7 +406,9 @@ cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t 
         k_mix<true><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co);
     else
         k_mix<false><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co);
-    return cudaGetLastError();
+    err = cudaGetLastError();
+    if (err == cudaSuccess) launch_mark(s);
+    return err;
 }
 
 // contraction on the mode-blocked spectrum with packed weights
@@ -466,12 +468,14 @@ int32_t run_p256(const Plan& p, const void* x, const char* packed, const float* 
     p256::k_fwd<KX, MY><<<(unsigned)Lin, p256::THREADS, smem, s>>>(static_cast<const float*>(x), Xh, tt->f_table,
                                                                      (float)d.fwd_scale, Lin * 8);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p256 fwd launch");
+    launch_mark(s);
     int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
     if (rc != NOP_OK) return rc;
     p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, 1};
     p256::k_inv<KX, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Yh, static_cast<float*>(y), tt->f_table,
                                                                       (float)d.inv_scale, Lout * 8, ep);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p256 inv launch");
+    launch_mark(s);
     return NOP_OK;
 }
 
@@ -498,6 +502,7 @@ int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const flo
     k_plane_fwd<N><<<(unsigned)Lin, PlaneCfg<N>::THREADS, smem, s>>>(
         static_cast<const float*>(x), Xh, tt->f_table, Kx, My, (int)d.fwd_off[0], (float)d.fwd_scale, Lin * 8);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "plane_fwd launch");
+    launch_mark(s);
     int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
     if (rc != NOP_OK) return rc;
     Epilogue ep{};
@@ -514,6 +519,7 @@ int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const flo
                                                                        My, (int)d.inv_off[0], (float)d.inv_scale,
                                                                        Lout * 8, ep);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "plane_inv launch");
+    launch_mark(s);
     return NOP_OK;
 }
 
@@ -530,12 +536,14 @@ int32_t run_row1d(const Plan& p, const void* x, const char* packed, const float*
     r1d::k_fwd<N, K><<<(unsigned)ceil_div(Lin, r1d::LINES), r1d::THREADS, 0, s>>>(
         static_cast<const float*>(x), Xh, tt->f_table, Lin, (float)d.fwd_scale, Lin * 8);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "row1d fwd launch");
+    launch_mark(s);
     int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
     if (rc != NOP_OK) return rc;
     r1d::Epi1 ep{bias, addend, apply_gelu, (int)d.out_channels};
     r1d::k_inv<N, K><<<(unsigned)ceil_div(Lout, r1d::LINES), r1d::THREADS, 0, s>>>(
         Yh, static_cast<float*>(y), tt->f_table, Lout, (float)d.inv_scale, Lout * 8, ep);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "row1d inv launch");
+    launch_mark(s);
     return NOP_OK;
 }
 
@@ -572,16 +580,20 @@ int32_t run_vol3d(const Plan& p, const void* x, const char* packed, const float*
     p256::k_fwd<KZ, MY><<<(unsigned)Lin, p256::THREADS, smem, s>>>(static_cast<const float*>(x), Pa, tw256,
                                                                      (float)d.fwd_scale, Lin * 8);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane fwd launch");
+    launch_mark(s);
     axis::k_fwd<MX><<<(unsigned)(QP * BCi), axis::THREADS, 0, s>>>(Pa, Xh, tw256, QP, BCi);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis fwd launch");
+    launch_mark(s);
     int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
     if (rc != NOP_OK) return rc;
     axis::k_inv<MX><<<(unsigned)(QP * BCo), axis::THREADS, 0, s>>>(Yh, Pb, tw256, QP, BCo);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis inv launch");
+    launch_mark(s);
     p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, Nx};
     p256::k_inv<KZ, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Pb, static_cast<float*>(y), tw256,
                                                                       (float)d.inv_scale, Lout * 8, ep);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane inv launch");
+    launch_mark(s);
     return NOP_OK;
 }
 
@@ -734,12 +746,14 @@ int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char*
     k_pack_modes<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(G, reinterpret_cast<float4*>(packed + p.pk_w), (int)rin,
                                                             (int)rout, Mt, Q, rout * Mt, Mt);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "pack launch (core)");
+    launch_mark(s);
     // U_in [Ci][r_in]: xf[f] = sum_i x[i] U_in[i][f]
     n = Ci * 4 * rin;
     k_pack_broadcast<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(weights[1]),
                                                                 reinterpret_cast<float4*>(packed + p.pk_uin), (int)Ci,
                                                                 (int)rin, rin, 1);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "pack launch (input factor)");
+    launch_mark(s);
     // U_out [Co][r_out]: y[o] = sum_g z[g] U_out[o][g]
     n = rout * 4 * Co;
     k_pack_broadcast<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(weights[2]),

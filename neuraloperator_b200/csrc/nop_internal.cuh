@@ -65,6 +65,10 @@ struct Plan {
     }
 };
 
+// measurement hook: record the caller's events around kernel launches (api.cu)
+void launch_mark_begin(cudaStream_t s);
+void launch_mark(cudaStream_t s);
+
 // descriptor checks and contraction workspace regions (api.cu)
 int expected_weights(const nop_spectral_desc& d);
 int32_t validate(const nop_spectral_desc* d);
