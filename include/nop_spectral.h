@@ -151,6 +151,47 @@ int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const v
                                     int32_t apply_gelu, void* y, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/* ---- 3D slab decomposition over the first spatial axis (one process per GPU) ------------------
+ * Replaces the unused all-to-all transpose helper of the reference's model-parallel layer
+ * (neuralop/mpu/helpers.py:81-99) with a data path that exchanges only kept modes.  Every rank holds
+ * x planes [x_begin, x_begin + x_count) of a 3D input (all batch entries and channels) and the full
+ * weights.  One forward is:
+ *   nop_spectral_slab_forward_planes  local (y, z) transforms -> send1
+ *   all-to-all #1 (send1 -> recv1, per-peer byte counts in nop_slab_info)
+ *   nop_spectral_slab_modes           x transforms, contraction, inverse x transforms -> send2
+ *   all-to-all #2 (send2 -> recv2)
+ *   nop_spectral_slab_inverse_planes  local inverse (y, z) transforms + epilogue -> y planes
+ * Rank r contracts plane-mode blocks [block_begin[r], block_begin[r] + block_count[r]) for every
+ * kept x mode.  Buffers are caller-owned device memory (256-byte aligned). */
+#define NOP_MAX_SLAB_RANKS 64
+
+typedef struct nop_slab_info {
+    int32_t rank, world;
+    int64_t x_begin, x_count;                      /* this rank's first-axis planes              */
+    int64_t plane_blocks;                          /* blocks of 8 kept (y, z) modes               */
+    int64_t block_begin[NOP_MAX_SLAB_RANKS];       /* plane-mode blocks contracted by each rank   */
+    int64_t block_count[NOP_MAX_SLAB_RANKS];
+    size_t send1_bytes, recv1_bytes, send2_bytes, recv2_bytes;
+    size_t send1_split[NOP_MAX_SLAB_RANKS];        /* bytes to / from each peer, in rank order     */
+    size_t recv1_split[NOP_MAX_SLAB_RANKS];
+    size_t send2_split[NOP_MAX_SLAB_RANKS];
+    size_t recv2_split[NOP_MAX_SLAB_RANKS];
+} nop_slab_info;
+
+/* Plan for rank `rank` of `world`; `desc` describes the whole (global) problem. */
+int32_t nop_spectral_slab_plan_create(const nop_spectral_desc* desc, int32_t rank, int32_t world,
+                                      nop_plan** plan_out);
+int32_t nop_spectral_slab_info(const nop_plan* plan, nop_slab_info* info);
+/* x: [B, Ci, x_count, n_in[1], n_in[2]] float32; send1: send1_bytes. */
+int32_t nop_spectral_slab_forward_planes(const nop_plan* plan, const float* x, void* send1, void* stream);
+/* recv1: recv1_bytes; packed: nop_spectral_pack_weights of the same plan; send2: send2_bytes. */
+int32_t nop_spectral_slab_modes(const nop_plan* plan, const void* recv1, const void* packed,
+                                size_t packed_bytes, void* send2, void* workspace, size_t workspace_bytes,
+                                void* stream);
+/* recv2: recv2_bytes; y: [B, Co, x_count, n_out[1], n_out[2]]; epilogue as nop_spectral_forward. */
+int32_t nop_spectral_slab_inverse_planes(const nop_plan* plan, const void* recv2, const float* bias,
+                                         const float* addend, int32_t apply_gelu, float* y, void* stream);
+
 /* Measurement hook (no counterpart in the reference, which has no kernels of its own): while n > 0
  * on the calling thread, every forward call records events[0] on its stream before its first
  * kernel and events[i] after its i-th kernel launch (i = 1 .. n-1).  `events` are cudaEvent_t

@@ -29,8 +29,12 @@ EXPORTED_SYMBOLS = (
     "nop_abi_version", "nop_last_error", "nop_spectral_plan_create", "nop_spectral_plan_destroy",
     "nop_spectral_workspace_size", "nop_spectral_plan_is_fast", "nop_spectral_launches_per_forward",
     "nop_spectral_forward", "nop_spectral_packed_size", "nop_spectral_pack_weights",
-    "nop_spectral_forward_packed", "nop_set_launch_events",
+    "nop_spectral_forward_packed", "nop_set_launch_events", "nop_spectral_slab_plan_create",
+    "nop_spectral_slab_info", "nop_spectral_slab_forward_planes", "nop_spectral_slab_modes",
+    "nop_spectral_slab_inverse_planes",
 )
+
+MAX_SLAB_RANKS = 64
 
 
 class NopSpectralDesc(ctypes.Structure):
@@ -55,6 +59,26 @@ class NopSpectralDesc(ctypes.Structure):
         ("zero_imag_bins", ctypes.c_int64 * 3),
         ("fwd_scale", ctypes.c_double),
         ("inv_scale", ctypes.c_double),
+    ]
+
+
+class NopSlabInfo(ctypes.Structure):
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("x_begin", ctypes.c_int64),
+        ("x_count", ctypes.c_int64),
+        ("plane_blocks", ctypes.c_int64),
+        ("block_begin", ctypes.c_int64 * 64),
+        ("block_count", ctypes.c_int64 * 64),
+        ("send1_bytes", ctypes.c_size_t),
+        ("recv1_bytes", ctypes.c_size_t),
+        ("send2_bytes", ctypes.c_size_t),
+        ("recv2_bytes", ctypes.c_size_t),
+        ("send1_split", ctypes.c_size_t * 64),
+        ("recv1_split", ctypes.c_size_t * 64),
+        ("send2_split", ctypes.c_size_t * 64),
+        ("recv2_split", ctypes.c_size_t * 64),
     ]
 
 
@@ -96,6 +120,19 @@ def _declare(lib):
         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.nop_set_launch_events.restype = ctypes.c_int32
     lib.nop_set_launch_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32]
+    lib.nop_spectral_slab_plan_create.restype = ctypes.c_int32
+    lib.nop_spectral_slab_plan_create.argtypes = [ctypes.POINTER(NopSpectralDesc), ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.POINTER(c_plan_p)]
+    lib.nop_spectral_slab_info.restype = ctypes.c_int32
+    lib.nop_spectral_slab_info.argtypes = [c_plan_p, ctypes.POINTER(NopSlabInfo)]
+    lib.nop_spectral_slab_forward_planes.restype = ctypes.c_int32
+    lib.nop_spectral_slab_forward_planes.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.nop_spectral_slab_modes.restype = ctypes.c_int32
+    lib.nop_spectral_slab_modes.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nop_spectral_slab_inverse_planes.restype = ctypes.c_int32
+    lib.nop_spectral_slab_inverse_planes.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                     ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
     lib.nop_spectral_forward.restype = ctypes.c_int32
     lib.nop_spectral_forward.argtypes = [
         c_plan_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p,
@@ -164,12 +201,22 @@ def check(code: int):
 
 
 class Plan:
-    """Owns one nop_plan (created on the current CUDA device)."""
+    """Owns one nop_plan (created on the current CUDA device).  With ``slab=(rank, world)`` the plan
+    is a 3D slab-decomposition plan (nop_spectral_slab_plan_create) and ``slab_info`` is filled."""
 
-    def __init__(self, desc: NopSpectralDesc):
+    def __init__(self, desc: NopSpectralDesc, slab=None):
         lib = library()
         handle = ctypes.c_void_p()
-        check(lib.nop_spectral_plan_create(ctypes.byref(desc), ctypes.byref(handle)))
+        if slab is None:
+            check(lib.nop_spectral_plan_create(ctypes.byref(desc), ctypes.byref(handle)))
+        else:
+            check(lib.nop_spectral_slab_plan_create(ctypes.byref(desc), int(slab[0]), int(slab[1]),
+                                                    ctypes.byref(handle)))
+        self.slab_info = None
+        if slab is not None:
+            info = NopSlabInfo()
+            check(lib.nop_spectral_slab_info(handle, ctypes.byref(info)))
+            self.slab_info = info
         self._lib = lib
         self.handle = handle
         self.desc = desc

@@ -351,21 +351,6 @@ int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* co
     return launch_mark_end(generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s));
 }
 
-int32_t nop_set_launch_events(void* const* events, int32_t n) {
-    if (n < 0 || n > 32) return fail(NOP_E_INVALID, "event count must be in 0..32");
-    if (n > 0 && !events) return fail(NOP_E_INVALID, "events is NULL");
-    for (int i = 0; i < n; ++i) g_events.ev[i] = static_cast<cudaEvent_t>(events[i]);
-    g_events.n = n;
-    g_events.next = 0;
-    return NOP_OK;
-}
-
-int32_t nop_spectral_packed_size(const nop_plan* plan, size_t* bytes) {
-    if (!plan || !bytes) return fail(NOP_E_INVALID, "plan and bytes must be non-NULL");
-    *bytes = reinterpret_cast<const Plan*>(plan)->packed_bytes;
-    return NOP_OK;
-}
-
 static int32_t check_workspace(const Plan& p, const void* workspace, size_t workspace_bytes) {
     if (p.ws.bytes == 0) return NOP_OK;
     if (!workspace) return fail(NOP_E_WORKSPACE, "workspace is NULL");
@@ -382,6 +367,139 @@ static int32_t check_device(const Plan& p) {
     if (dev != p.device)
         return fail(NOP_E_INVALID, "plan was created on device " + std::to_string(p.device) +
                                        " but the current device is " + std::to_string(dev));
+    return NOP_OK;
+}
+
+int32_t nop_spectral_slab_plan_create(const nop_spectral_desc* desc, int32_t rank, int32_t world,
+                                      nop_plan** plan_out) {
+    if (!plan_out) return fail(NOP_E_INVALID, "plan_out is NULL");
+    *plan_out = nullptr;
+    if (world < 1 || world > NOP_MAX_SLAB_RANKS || rank < 0 || rank >= world)
+        return fail(NOP_E_INVALID, "rank / world outside 0 <= rank < world <= " + std::to_string(NOP_MAX_SLAB_RANKS));
+    int32_t rc = validate(desc);
+    if (rc != NOP_OK) return rc;
+    FastKind kind;
+    std::string why;
+    if (!fast_supported(*desc, &kind, &why) || kind != FastKind::Vol3D)
+        return fail(NOP_E_UNSUPPORTED, "slab decomposition needs a fused 3D shape: " + why);
+    if (desc->n_in[0] % world)
+        return fail(NOP_E_INVALID, "first-axis size must be a multiple of the number of ranks");
+    Plan* p = new (std::nothrow) Plan();
+    if (!p) return fail(NOP_E_NOMEM, "plan allocation failed");
+    p->d = *desc;
+    for (int j = 0; j < p->d.ndim; ++j) p->modes_total *= p->d.kept[j];
+    for (int j = p->d.ndim; j < NOP_MAX_DIMS; ++j) {
+        p->d.n_in[j] = p->d.n_out[j] = p->d.kept[j] = 1;
+        p->d.fwd_off[j] = p->d.inv_off[j] = 0;
+    }
+    p->fast = true;
+    p->fast_kind = FastKind::Vol3DSlab;
+    p->slab_rank = rank;
+    p->slab_world = world;
+    p->slab_nx = p->d.n_in[0] / world;
+    const int64_t qp = p->d.kept[1] * p->d.kept[2] / 8;  // fused 3D shapes keep a multiple of 8 plane modes
+    for (int r = 0; r < world; ++r) {  // balanced split of the plane-mode blocks
+        p->slab_qcount[r] = qp / world + (r < qp % world ? 1 : 0);
+        p->slab_qbegin[r] = r * (qp / world) + (r < qp % world ? r : qp % world);
+    }
+    cudaError_t err = cudaGetDevice(&p->device);
+    if (err != cudaSuccess) {
+        delete p;
+        return cuda_fail(err, "cudaGetDevice");
+    }
+    p->ws.bytes = fast_workspace_bytes(*p, &p->ws);
+    rc = build_tables(p);
+    if (rc != NOP_OK) {
+        delete p;
+        return rc;
+    }
+    *plan_out = reinterpret_cast<nop_plan*>(p);
+    return NOP_OK;
+}
+
+int32_t nop_spectral_slab_info(const nop_plan* plan, nop_slab_info* info) {
+    if (!plan || !info) return fail(NOP_E_INVALID, "plan and info must be non-NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    if (p.fast_kind != FastKind::Vol3DSlab) return fail(NOP_E_INVALID, "not a slab plan");
+    *info = nop_slab_info{};
+    const nop_spectral_desc& d = p.d;
+    const int64_t nx = p.slab_nx, r = p.slab_rank;
+    const size_t blk_in = (size_t)d.batch * d.in_channels * nx * 8 * sizeof(float2);   // one block, one slab
+    const size_t blk_out = (size_t)d.batch * d.out_channels * nx * 8 * sizeof(float2);
+    info->rank = p.slab_rank;
+    info->world = p.slab_world;
+    info->x_begin = r * nx;
+    info->x_count = nx;
+    info->plane_blocks = d.kept[1] * d.kept[2] / 8;
+    for (int s = 0; s < p.slab_world; ++s) {
+        info->block_begin[s] = p.slab_qbegin[s];
+        info->block_count[s] = p.slab_qcount[s];
+        info->send1_split[s] = p.slab_qcount[s] * blk_in;   // my planes of s's blocks
+        info->recv1_split[s] = p.slab_qcount[r] * blk_in;   // s's planes of my blocks
+        info->send2_split[s] = p.slab_qcount[r] * blk_out;  // my blocks on s's planes
+        info->recv2_split[s] = p.slab_qcount[s] * blk_out;  // s's blocks on my planes
+        info->send1_bytes += info->send1_split[s];
+        info->recv1_bytes += info->recv1_split[s];
+        info->send2_bytes += info->send2_split[s];
+        info->recv2_bytes += info->recv2_split[s];
+    }
+    return NOP_OK;
+}
+
+static int32_t slab_plan(const nop_plan* plan, const Plan** out) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan* p = reinterpret_cast<const Plan*>(plan);
+    if (p->fast_kind != FastKind::Vol3DSlab) return fail(NOP_E_INVALID, "not a slab plan");
+    *out = p;
+    return check_device(*p);
+}
+
+int32_t nop_spectral_slab_forward_planes(const nop_plan* plan, const float* x, void* send1, void* stream) {
+    const Plan* p;
+    int32_t rc = slab_plan(plan, &p);
+    if (rc != NOP_OK) return rc;
+    if (!x || !send1) return fail(NOP_E_INVALID, "x and send1 must be non-NULL");
+    if ((uintptr_t)send1 % 16 || (uintptr_t)x % 4) return fail(NOP_E_ALIGNMENT, "send1 must be 16-byte aligned");
+    return fast_slab_planes_fwd(*p, x, send1, static_cast<cudaStream_t>(stream));
+}
+
+int32_t nop_spectral_slab_modes(const nop_plan* plan, const void* recv1, const void* packed, size_t packed_bytes,
+                                void* send2, void* workspace, size_t workspace_bytes, void* stream) {
+    const Plan* p;
+    int32_t rc = slab_plan(plan, &p);
+    if (rc != NOP_OK) return rc;
+    if (!recv1 || !send2) return fail(NOP_E_INVALID, "recv1 and send2 must be non-NULL");
+    if (!packed || packed_bytes < p->packed_bytes)
+        return fail(NOP_E_WORKSPACE, "packed-weight buffer missing or smaller than nop_spectral_packed_size");
+    if ((uintptr_t)recv1 % 16 || (uintptr_t)send2 % 16 || (uintptr_t)packed % 16)
+        return fail(NOP_E_ALIGNMENT, "exchange and packed buffers must be 16-byte aligned");
+    if ((rc = check_workspace(*p, workspace, workspace_bytes)) != NOP_OK) return rc;
+    return fast_slab_modes(*p, recv1, static_cast<const char*>(packed), send2, static_cast<char*>(workspace),
+                           static_cast<cudaStream_t>(stream));
+}
+
+int32_t nop_spectral_slab_inverse_planes(const nop_plan* plan, const void* recv2, const float* bias,
+                                         const float* addend, int32_t apply_gelu, float* y, void* stream) {
+    const Plan* p;
+    int32_t rc = slab_plan(plan, &p);
+    if (rc != NOP_OK) return rc;
+    if (!recv2 || !y) return fail(NOP_E_INVALID, "recv2 and y must be non-NULL");
+    if ((uintptr_t)recv2 % 16) return fail(NOP_E_ALIGNMENT, "recv2 must be 16-byte aligned");
+    return fast_slab_planes_inv(*p, recv2, bias, addend, apply_gelu, y, static_cast<cudaStream_t>(stream));
+}
+
+int32_t nop_set_launch_events(void* const* events, int32_t n) {
+    if (n < 0 || n > 32) return fail(NOP_E_INVALID, "event count must be in 0..32");
+    if (n > 0 && !events) return fail(NOP_E_INVALID, "events is NULL");
+    for (int i = 0; i < n; ++i) g_events.ev[i] = static_cast<cudaEvent_t>(events[i]);
+    g_events.n = n;
+    g_events.next = 0;
+    return NOP_OK;
+}
+
+int32_t nop_spectral_packed_size(const nop_plan* plan, size_t* bytes) {
+    if (!plan || !bytes) return fail(NOP_E_INVALID, "plan and bytes must be non-NULL");
+    *bytes = reinterpret_cast<const Plan*>(plan)->packed_bytes;
     return NOP_OK;
 }
 

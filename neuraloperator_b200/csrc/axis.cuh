@@ -1,9 +1,12 @@
 // Outer-axis transforms of the 3D spectral block.  After the (y, z) plane kernels, the kept plane
 // modes of every x-plane sit in the mode-blocked layout P[qp][(bc, x)][j] (8 modes per block).
-// For one (qp, bc) the 8 lines (j) over x are a contiguous block of N * 8 complex values; these
-// kernels transform them along x (keeping MX centred bins forward, expanding them inverse) and
-// write / read the contraction's mode-blocked layout with total mode (mx, plane mode):
-//     X^[(mx * QP + qp)][bc][j]        QP = plane modes / 8
+// For one (qp, bc) the 8 lines (j) over x are N * 8 complex values; these kernels transform them
+// along x (keeping MX centred bins forward, expanding them inverse) and write / read the
+// contraction's mode-blocked layout with total mode (mx, plane mode):
+//     X^[(mx * QP + qp)][bc][j]        QP = plane-mode blocks handled here
+// The x lines may be split into segments of nx_seg planes that lie seg_stride complex values apart
+// (one segment per source rank after the slab exchange); element (qp, bc, x, j) is at
+//     seg(x) * seg_stride + ((qp * BC + bc) * nx_seg + x mod nx_seg) * 8 + j.
 #pragma once
 
 #include "fft_core.cuh"
@@ -19,7 +22,8 @@ constexpr int LINE = N + N / 16;
 
 template <int MX>
 __global__ void __launch_bounds__(THREADS)
-k_fwd(const float2* __restrict__ P, float2* __restrict__ Xh, const float2* __restrict__ twg, int QP, int64_t BC) {
+k_fwd(const float2* __restrict__ P, float2* __restrict__ Xh, const float2* __restrict__ twg, int QP, int64_t BC,
+      int nx_seg, int64_t seg_stride) {
     __shared__ float2 tw[N];
     __shared__ __align__(16) float2 lines[8][LINE];
     __shared__ __align__(16) float2 stage[MX][8];
@@ -27,10 +31,10 @@ k_fwd(const float2* __restrict__ P, float2* __restrict__ Xh, const float2* __res
     const int64_t bc = blockIdx.x / QP;
     const int j = threadIdx.x / LANES, t = threadIdx.x % LANES;
     for (int i = threadIdx.x; i < N; i += THREADS) tw[i] = twg[i];
-    const float4* blk = reinterpret_cast<const float4*>(P + (qp * BC * N + bc * N) * 8);
+    const float2* blk = P + (qp * BC + bc) * nx_seg * 8;
     for (int e = threadIdx.x; e < N * 4; e += THREADS) {  // (x, j pair)
-        const float4 v = __ldg(blk + e);
         const int x = e >> 2, jj = 2 * (e & 3);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(blk + (x / nx_seg) * seg_stride + (x % nx_seg) * 8 + jj));
         lines[jj][fft::pad(x)] = make_float2(v.x, v.y);
         lines[jj + 1][fft::pad(x)] = make_float2(v.z, v.w);
     }
@@ -53,7 +57,8 @@ k_fwd(const float2* __restrict__ P, float2* __restrict__ Xh, const float2* __res
 
 template <int MX>
 __global__ void __launch_bounds__(THREADS)
-k_inv(const float2* __restrict__ Yh, float2* __restrict__ P, const float2* __restrict__ twg, int QP, int64_t BC) {
+k_inv(const float2* __restrict__ Yh, float2* __restrict__ P, const float2* __restrict__ twg, int QP, int64_t BC,
+      int nx_seg, int64_t seg_stride) {
     __shared__ float2 tw[N];
     __shared__ __align__(16) float2 lines[8][LINE];
     __shared__ __align__(16) float2 stage[MX][8];
@@ -77,11 +82,12 @@ k_inv(const float2* __restrict__ Yh, float2* __restrict__ P, const float2* __res
         },
         [&](int x, float2 v) { buf[fft::pad(x)] = v; });
     __syncthreads();
-    float4* blk = reinterpret_cast<float4*>(P + (qp * BC * N + bc * N) * 8);
+    float2* blk = P + (qp * BC + bc) * nx_seg * 8;
     for (int e = threadIdx.x; e < N * 4; e += THREADS) {
         const int x = e >> 2, jj = 2 * (e & 3);
         const float2 a = lines[jj][fft::pad(x)], b = lines[jj + 1][fft::pad(x)];
-        blk[e] = make_float4(a.x, a.y, b.x, b.y);
+        *reinterpret_cast<float4*>(blk + (x / nx_seg) * seg_stride + (x % nx_seg) * 8 + jj) =
+            make_float4(a.x, a.y, b.x, b.y);
     }
 }
 

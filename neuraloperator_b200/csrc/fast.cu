@@ -253,7 +253,7 @@ __device__ __forceinline__ float4 bf16x4(float4 v) {
 template <bool BF16>
 __global__ void __launch_bounds__(kMixThreads, 2)
 k_mix(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq, float2* __restrict__ Y, int B, int Ci,
-      int Co) {
+      int Co, int qpl, int qtot, int qbeg) {
     extern __shared__ float4 mix_smem[];
     float4* Ws = mix_smem;                                          // [2][KC][4][64]
     float2* Xs = reinterpret_cast<float2*>(mix_smem + 2 * kMixWs);  // [2][KC][16][8]
@@ -263,7 +263,9 @@ k_mix(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq, f
     const int b0 = blockIdx.y * 16;
     const int o0 = blockIdx.z * 64;
     const float2* Xq = X + q * (int64_t)B * Ci * 8;
-    const float4* Wq = Wp + q * wq;
+    // local mode block q -> weight block: (q / qpl) * qtot + qbeg + q mod qpl (identity unless the
+    // plane-mode blocks are split across ranks)
+    const float4* Wq = Wp + ((q / qpl) * qtot + qbeg + q % qpl) * wq;
     const int nchunks = (Ci + kMixKC - 1) / kMixKC;
 
     auto load_chunk = [&](int c, int buf) {
@@ -396,16 +398,35 @@ cudaError_t ensure_smem_attr(K kernel, int slot, int device, size_t bytes = kSme
 inline size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 inline int64_t mode_blocks(const Plan& p) { return (p.modes_total + 7) / 8; }
 
+// mode blocks this rank contracts and their position in the packed weights
+struct BlockMap {
+    int64_t local;   // mode blocks in the local spectrum
+    int qpl, qtot, qbeg;
+};
+
+BlockMap block_map(const Plan& p) {
+    const int64_t Q = mode_blocks(p);
+    if (p.fast_kind != FastKind::Vol3DSlab) return {Q, (int)Q, (int)Q, 0};
+    const int mx = (int)p.d.kept[0];
+    const int qtot = (int)(Q / mx);
+    return {(int64_t)mx * p.slab_qcount[p.slab_rank], (int)p.slab_qcount[p.slab_rank], qtot,
+            (int)p.slab_qbegin[p.slab_rank]};
+}
+
 cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t wq, float2* Y, int Ci, int Co,
                        cudaStream_t s) {
     cudaError_t err = ensure_smem_attr(p.d.precision == NOP_PRECISION_BF16 ? k_mix<true> : k_mix<false>,
                                        p.d.precision == NOP_PRECISION_BF16 ? 14 : 15, p.device, kMixSmem);
     if (err != cudaSuccess) return err;
-    dim3 grid((unsigned)mode_blocks(p), (unsigned)ceil_div(p.d.batch, 16), (unsigned)ceil_div(Co, 64));
+    const BlockMap bm = block_map(p);
+    if (bm.local == 0) return cudaSuccess;
+    dim3 grid((unsigned)bm.local, (unsigned)ceil_div(p.d.batch, 16), (unsigned)ceil_div(Co, 64));
     if (p.d.precision == NOP_PRECISION_BF16)
-        k_mix<true><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co);
+        k_mix<true><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
+                                                         bm.qbeg);
     else
-        k_mix<false><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co);
+        k_mix<false><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
+                                                          bm.qbeg);
     err = cudaGetLastError();
     if (err == cudaSuccess) launch_mark(s);
     return err;
@@ -581,18 +602,75 @@ int32_t run_vol3d(const Plan& p, const void* x, const char* packed, const float*
                                                                      (float)d.fwd_scale, Lin * 8);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane fwd launch");
     launch_mark(s);
-    axis::k_fwd<MX><<<(unsigned)(QP * BCi), axis::THREADS, 0, s>>>(Pa, Xh, tw256, QP, BCi);
+    axis::k_fwd<MX><<<(unsigned)(QP * BCi), axis::THREADS, 0, s>>>(Pa, Xh, tw256, QP, BCi, (int)Nx, 0);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis fwd launch");
     launch_mark(s);
     int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
     if (rc != NOP_OK) return rc;
-    axis::k_inv<MX><<<(unsigned)(QP * BCo), axis::THREADS, 0, s>>>(Yh, Pb, tw256, QP, BCo);
+    axis::k_inv<MX><<<(unsigned)(QP * BCo), axis::THREADS, 0, s>>>(Yh, Pb, tw256, QP, BCo, (int)Nx, 0);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis inv launch");
     launch_mark(s);
     p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, Nx};
     p256::k_inv<KZ, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Pb, static_cast<float*>(y), tw256,
                                                                       (float)d.inv_scale, Lout * 8, ep);
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane inv launch");
+    launch_mark(s);
+    return NOP_OK;
+}
+
+// ---- 3D slab stages (first axis split across ranks; exchanges run between the stages) ----
+template <int KZ, int MY>
+int32_t slab_planes_fwd_t(const Plan& p, const float* x, float2* send1, cudaStream_t s, int slot) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t L = d.batch * d.in_channels * p.slab_nx;
+    if (L == 0) return NOP_OK;
+    cudaError_t err;
+    if ((err = ensure_smem_attr(p256::k_fwd<KZ, MY>, slot, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p256 fwd)");
+    p256::k_fwd<KZ, MY><<<(unsigned)L, p256::THREADS, p256::smem_bytes<KZ, MY>(), s>>>(
+        x, send1, p.table(256)->f_table, (float)d.fwd_scale, L * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "slab plane fwd launch");
+    launch_mark(s);
+    return NOP_OK;
+}
+
+template <int MX>
+int32_t slab_modes_t(const Plan& p, const float2* recv1, const char* packed, float2* send2, char* ws,
+                     cudaStream_t s) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t qc = p.slab_qcount[p.slab_rank], nx = p.slab_nx;
+    if (qc == 0) return NOP_OK;
+    const int64_t BCi = d.batch * d.in_channels, BCo = d.batch * d.out_channels;
+    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
+    const float2* tw256 = p.table(256)->f_table;
+    cudaError_t err;
+    axis::k_fwd<MX><<<(unsigned)(qc * BCi), axis::THREADS, 0, s>>>(recv1, Xh, tw256, (int)qc, BCi, (int)nx,
+                                                                    qc * BCi * nx * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "slab axis fwd launch");
+    launch_mark(s);
+    int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
+    if (rc != NOP_OK) return rc;
+    axis::k_inv<MX><<<(unsigned)(qc * BCo), axis::THREADS, 0, s>>>(Yh, send2, tw256, (int)qc, BCo, (int)nx,
+                                                                    qc * BCo * nx * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "slab axis inv launch");
+    launch_mark(s);
+    return NOP_OK;
+}
+
+template <int KZ, int MY>
+int32_t slab_planes_inv_t(const Plan& p, const float2* recv2, const float* bias, const float* addend,
+                          int apply_gelu, float* y, cudaStream_t s, int slot) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t L = d.batch * d.out_channels * p.slab_nx;
+    if (L == 0) return NOP_OK;
+    cudaError_t err;
+    if ((err = ensure_smem_attr(p256::k_inv<KZ, MY>, slot, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p256 inv)");
+    p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, p.slab_nx};
+    p256::k_inv<KZ, MY><<<(unsigned)L, p256::THREADS, p256::smem_bytes<KZ, MY>(), s>>>(
+        recv2, y, p.table(256)->f_table, (float)d.inv_scale, L * 8, ep);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "slab plane inv launch");
     launch_mark(s);
     return NOP_OK;
 }
@@ -685,7 +763,7 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
     };
     ws->buf_a = take((size_t)Q * 8 * B * Ci * sizeof(float2));
     ws->buf_b = take((size_t)Q * 8 * B * Co * sizeof(float2));
-    if (p.fast_kind == FastKind::Vol3D) {
+    if (p.fast_kind == FastKind::Vol3D) {  // (slab plans keep their plane spectra in caller buffers)
         const size_t plane_modes = (size_t)d.kept[1] * d.kept[2];
         ws->pl_a = take(plane_modes * B * Ci * d.n_in[0] * sizeof(float2));
         ws->pl_b = take(plane_modes * B * Co * d.n_in[0] * sizeof(float2));
@@ -773,6 +851,8 @@ int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, co
             default: return fail(NOP_E_UNSUPPORTED, "fused 1D engine: unsupported length");
         }
     }
+    if (p.fast_kind == FastKind::Vol3DSlab)
+        return fail(NOP_E_UNSUPPORTED, "slab plans run through the nop_spectral_slab_* stage calls");
     if (p.fast_kind == FastKind::Vol3D) {
         int which = -1;
         vol3d_shape(p.d, &which);
@@ -785,6 +865,30 @@ int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, co
         case 512: return run_plane_2d<512>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
         default: return fail(NOP_E_UNSUPPORTED, "fused engine: unsupported plane size");
     }
+}
+
+int32_t fast_slab_planes_fwd(const Plan& p, const float* x, void* send1, cudaStream_t s) {
+    int which = -1;
+    vol3d_shape(p.d, &which);
+    if (which == 0) return slab_planes_fwd_t<17, 32>(p, x, static_cast<float2*>(send1), s, 10);
+    return slab_planes_fwd_t<33, 64>(p, x, static_cast<float2*>(send1), s, 12);
+}
+
+int32_t fast_slab_modes(const Plan& p, const void* recv1, const char* packed, void* send2, char* ws,
+                        cudaStream_t s) {
+    int which = -1;
+    vol3d_shape(p.d, &which);
+    if (which == 0) return slab_modes_t<32>(p, static_cast<const float2*>(recv1), packed, static_cast<float2*>(send2), ws, s);
+    return slab_modes_t<64>(p, static_cast<const float2*>(recv1), packed, static_cast<float2*>(send2), ws, s);
+}
+
+int32_t fast_slab_planes_inv(const Plan& p, const void* recv2, const float* bias, const float* addend,
+                             int apply_gelu, float* y, cudaStream_t s) {
+    int which = -1;
+    vol3d_shape(p.d, &which);
+    if (which == 0)
+        return slab_planes_inv_t<17, 32>(p, static_cast<const float2*>(recv2), bias, addend, apply_gelu, y, s, 11);
+    return slab_planes_inv_t<33, 64>(p, static_cast<const float2*>(recv2), bias, addend, apply_gelu, y, s, 13);
 }
 
 int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,

@@ -44,7 +44,9 @@ struct WorkspaceLayout {
     int64_t buf_elems = 0;
 };
 
-enum class FastKind : int32_t { None = 0, Plane2D = 1, Row1D = 2, Vol3D = 3 };
+enum class FastKind : int32_t { None = 0, Plane2D = 1, Row1D = 2, Vol3D = 3, Vol3DSlab = 4 };
+
+constexpr int kMaxSlabRanks = 64;
 
 struct Plan {
     nop_spectral_desc d{};
@@ -56,6 +58,10 @@ struct Plan {
     void* table_mem = nullptr;         // single device allocation holding every table
     WorkspaceLayout ws;
     size_t packed_bytes = 0;           // fused engine: packed-weight buffer size (0: no packing)
+    // 3D slab decomposition (FastKind::Vol3DSlab): this rank's x planes and everyone's mode blocks
+    int slab_rank = 0, slab_world = 1;
+    int64_t slab_nx = 0;                                   // x planes per rank
+    int64_t slab_qbegin[kMaxSlabRanks] = {}, slab_qcount[kMaxSlabRanks] = {};
     size_t pk_w = 0, pk_uin = 0, pk_uout = 0;  // offsets inside the packed-weight buffer
 
     const TwiddleTable* table(int64_t n) const {
@@ -100,6 +106,11 @@ int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, co
                             const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
 int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
                      const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+int32_t fast_slab_planes_fwd(const Plan& p, const float* x, void* send1, cudaStream_t s);
+int32_t fast_slab_modes(const Plan& p, const void* recv1, const char* packed, void* send2, char* ws,
+                        cudaStream_t s);
+int32_t fast_slab_planes_inv(const Plan& p, const void* recv2, const float* bias, const float* addend,
+                             int apply_gelu, float* y, cudaStream_t s);
 
 // ------------------------------------------------------------------------------------------
 // small device helpers
