@@ -97,19 +97,19 @@ class SlabSpectralConv:
         self.group = group
         self._plans = {}
 
-    def layout(self, x_slab: torch.Tensor) -> SlabLayout:
-        world = dist.get_world_size(self.group)
-        rank = dist.get_rank(self.group)
+    def layout(self, x_slab: torch.Tensor, rank: Optional[int] = None, world: Optional[int] = None) -> SlabLayout:
+        """Split of this rank (or of ``rank`` of ``world`` when given, without a process group)."""
+        world = dist.get_world_size(self.group) if world is None else world
+        rank = dist.get_rank(self.group) if rank is None else rank
         geo = self.conv.geometry([x_slab.shape[2] * world, *x_slab.shape[3:]])
         blocks = geo.kept[1] * geo.kept[2] // 8
         return SlabLayout(rank, world, x_slab.shape[2] * world, blocks, x_slab.shape[0], self.conv.in_channels,
                           self.conv.out_channels)
 
     # -- the three compute stages (overridable, e.g. by a host emulation in tests) --------------------
-    def _plan(self, x_slab):
-        world = dist.get_world_size(self.group)
-        rank = dist.get_rank(self.group)
-        geo = self.conv.geometry([x_slab.shape[2] * world, *x_slab.shape[3:]])
+    def _plan(self, x_slab, lay: SlabLayout):
+        rank, world = lay.rank, lay.world
+        geo = self.conv.geometry([lay.nx_total, *x_slab.shape[3:]])
         kind, weights, ranks = self.conv.kernel_operands(geo)
         desc = ops.make_desc(geo, x_slab.shape[0], self.conv.in_channels, self.conv.out_channels,
                              weight_kind=kind, ranks=ranks, precision=self.conv.contraction_precision,
@@ -140,7 +140,7 @@ class SlabSpectralConv:
         return packed
 
     def stage_planes_fwd(self, x_slab: torch.Tensor, lay: SlabLayout) -> torch.Tensor:
-        plan, _, _ = self._plan(x_slab)
+        plan, _, _ = self._plan(x_slab, lay)
         send1 = torch.empty(sum(lay.send1_split()), dtype=torch.uint8, device=x_slab.device)
         stream = ctypes.c_void_p(torch.cuda.current_stream(x_slab.device).cuda_stream)
         _lib.check(_lib.library().nop_spectral_slab_forward_planes(plan.handle, ctypes.c_void_p(x_slab.data_ptr()),
@@ -148,7 +148,7 @@ class SlabSpectralConv:
         return send1
 
     def stage_modes(self, recv1: torch.Tensor, x_slab: torch.Tensor, lay: SlabLayout) -> torch.Tensor:
-        plan, desc, weights = self._plan(x_slab)
+        plan, desc, weights = self._plan(x_slab, lay)
         packed = self._packed(plan, desc, weights, x_slab.device)
         send2 = torch.empty(sum(lay.send2_split()), dtype=torch.uint8, device=x_slab.device)
         workspace = torch.empty(max(plan.workspace_bytes, 1), dtype=torch.uint8, device=x_slab.device)
@@ -160,7 +160,7 @@ class SlabSpectralConv:
 
     def stage_planes_inv(self, recv2: torch.Tensor, x_slab: torch.Tensor, lay: SlabLayout, addend=None,
                          apply_gelu=False) -> torch.Tensor:
-        plan, _, _ = self._plan(x_slab)
+        plan, _, _ = self._plan(x_slab, lay)
         y = torch.empty((x_slab.shape[0], self.conv.out_channels, *x_slab.shape[2:]), dtype=torch.float32,
                         device=x_slab.device)
         b = self.conv.bias
