@@ -35,6 +35,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+E2E_STREAMS = 3
 METRIC = "FNO fwd samples/s/GPU at 1–8 B200; spectral block % of HBM/tensor roofline"
 HBM_FALLBACK_GBS = 6533.2  # measured copy bandwidth on this pool (MEASURED_PEAKS.json at round start)
 
@@ -322,28 +323,33 @@ def run_ours(args, cfg, world, rank, local):
         value = world * batch / (ms / 1e3)
         per_kernel = [statistics.mean(m.durations_ms()[i] for m in marks) for i in range(nk)]
 
+        e2e_how = None
         if args.no_e2e:
             ms_e2e = float("nan")
         else:
             ms_e2e = None
     if ms_e2e is None:
-        # ---- end to end through the public API: pinned host in, pinned host out ----
+        # ---- end to end through the public API: pinned host in, pinned host out.  forward_host
+        # (nop_spectral_forward_host) cuts the batch into chunks whose H2D copy, kernels and D2H copy
+        # overlap across streams; every byte of x and y still crosses PCIe inside the timed region.
         x_host = x.cpu().pin_memory()
         y_host = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        chunk = ops.default_chunk(batch)
         e2e_steps = max(1, min(steps, 10))
-        barrier(world)
-        torch.cuda.synchronize()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.no_grad():
+            conv.forward_host(x_host, out=y_host, chunk=chunk, n_streams=E2E_STREAMS)  # plan + packing
+            barrier(world)
+            torch.cuda.synchronize()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             f0.record(stream)
             for _ in range(e2e_steps):
-                xd = x_host.to(dev, non_blocking=True)
-                yd = conv(xd)
-                y_host.copy_(yd, non_blocking=True)
+                conv.forward_host(x_host, out=y_host, chunk=chunk, n_streams=E2E_STREAMS, synchronize=False)
             f1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         ms_e2e = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+        e2e_how = (f"SpectralConv.forward_host (nop_spectral_forward_host): {batch // chunk} chunks of {chunk} "
+                   f"samples over {E2E_STREAMS} streams, pinned host buffers")
 
     if rank != 0:
         return
@@ -377,7 +383,7 @@ def run_ours(args, cfg, world, rank, local):
         "kernels": kernels,
         "e2e": ({"value": world * batch / (ms_e2e / 1e3), "unit": "samples/s",
                  "h2d_bytes_per_step": x.numel() * x.element_size(),
-                 "d2h_bytes_per_step": y.numel() * y.element_size()} if not args.no_e2e else None),
+                 "d2h_bytes_per_step": y.numel() * y.element_size(), "path": e2e_how} if not args.no_e2e else None),
         "gpu_launches": plan.launches_per_forward * steps,
         "clocks": clk,
     }

@@ -215,6 +215,29 @@ int32_t nop_spectral_forward_static(const nop_spectral_desc* desc, const void* x
                                     int32_t n_weights, const float* bias, const float* addend,
                                     int32_t apply_gelu, void* y, void* stream);
 
+/* ---- forward from host memory, copies overlapped with the kernels ---------------------------
+ * The reference's SpectralConv.forward runs wherever its input lives; a serving caller that holds
+ * inputs in host memory would copy the whole batch in, run, and copy the whole batch out, so the
+ * two PCIe transfers and the kernels follow one another.  nop_spectral_forward_host cuts a batch of
+ * `total_batch` samples (a multiple of desc.batch) into chunks of desc.batch samples and runs each
+ * chunk's host-to-device copy, forward and device-to-host copy on one of `n_streams` (1..8)
+ * internal streams, so the copies of neighbouring chunks in both directions overlap each other and
+ * the kernels.  x_host / addend_host / y_host: host buffers laid out like x / addend / y of
+ * nop_spectral_forward with batch total_batch; page-locked memory is needed for the copies to
+ * overlap (pageable memory gives the same result, serialised).  Weights: `packed` (from
+ * nop_spectral_pack_weights, device) for plans with a packed form, else `weights` / `n_weights`
+ * (device pointers as for nop_spectral_forward), which fused plans pack once into the workspace.
+ * bias: device pointer or NULL.  workspace: device memory of nop_spectral_host_workspace_size
+ * bytes, 256-byte aligned.  Ordering: the chunks start after work already queued on `stream`, and
+ * work queued on `stream` after the call waits for every chunk; the call itself does not block the
+ * host.  Returns without touching the buffers when total_batch is 0. */
+int32_t nop_spectral_host_workspace_size(const nop_plan* plan, int32_t n_streams, size_t* bytes);
+int32_t nop_spectral_forward_host(const nop_plan* plan, const void* x_host, int64_t total_batch,
+                                  const void* const* weights, int32_t n_weights, const void* packed,
+                                  size_t packed_bytes, const float* bias, const float* addend_host,
+                                  int32_t apply_gelu, void* y_host, void* workspace, size_t workspace_bytes,
+                                  int32_t n_streams, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

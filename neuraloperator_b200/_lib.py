@@ -31,7 +31,7 @@ EXPORTED_SYMBOLS = (
     "nop_spectral_forward", "nop_spectral_packed_size", "nop_spectral_pack_weights",
     "nop_spectral_forward_packed", "nop_set_launch_events", "nop_spectral_slab_plan_create",
     "nop_spectral_slab_info", "nop_spectral_slab_forward_planes", "nop_spectral_slab_modes",
-    "nop_spectral_slab_inverse_planes",
+    "nop_spectral_slab_inverse_planes", "nop_spectral_host_workspace_size", "nop_spectral_forward_host",
 )
 
 MAX_SLAB_RANKS = 64
@@ -133,6 +133,13 @@ def _declare(lib):
     lib.nop_spectral_slab_inverse_planes.restype = ctypes.c_int32
     lib.nop_spectral_slab_inverse_planes.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                      ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+    lib.nop_spectral_host_workspace_size.restype = ctypes.c_int32
+    lib.nop_spectral_host_workspace_size.argtypes = [c_plan_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_spectral_forward_host.restype = ctypes.c_int32
+    lib.nop_spectral_forward_host.argtypes = [
+        c_plan_p, ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.c_int32, ctypes.c_void_p]
     lib.nop_spectral_forward.restype = ctypes.c_int32
     lib.nop_spectral_forward.argtypes = [
         c_plan_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p,

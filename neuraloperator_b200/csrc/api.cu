@@ -548,4 +548,166 @@ int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const v
                                                static_cast<char*>(workspace), static_cast<cudaStream_t>(stream)));
 }
 
+/* ---- forward from host memory ------------------------------------------------------------- */
+
+struct HostChunkLayout {
+    size_t x_bytes, y_bytes;   // one chunk of desc.batch samples
+    size_t x_off, y_off, a_off, ws_off, per_stream;
+};
+
+static HostChunkLayout host_layout(const Plan& p) {
+    const nop_spectral_desc& d = p.d;
+    const size_t esz = d.complex_data ? 8 : 4;
+    int64_t pin = 1, pout = 1;
+    for (int j = 0; j < d.ndim; ++j) {
+        pin *= d.n_in[j];
+        pout *= d.n_out[j];
+    }
+    HostChunkLayout h{};
+    h.x_bytes = (size_t)d.batch * d.in_channels * pin * esz;
+    h.y_bytes = (size_t)d.batch * d.out_channels * pout * esz;
+    h.x_off = 0;
+    h.y_off = align_up(h.x_bytes);
+    h.a_off = h.y_off + align_up(h.y_bytes);
+    h.ws_off = h.a_off + align_up(h.y_bytes);
+    h.per_stream = h.ws_off + align_up(p.ws.bytes);
+    return h;
+}
+
+int32_t nop_spectral_host_workspace_size(const nop_plan* plan, int32_t n_streams, size_t* bytes) {
+    if (!plan || !bytes) return fail(NOP_E_INVALID, "plan and bytes must be non-NULL");
+    if (n_streams < 1 || n_streams > 8) return fail(NOP_E_INVALID, "n_streams must be in 1..8");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    if (p.fast_kind == FastKind::Vol3DSlab) return fail(NOP_E_INVALID, "slab plans have no host forward");
+    // [packed weights][stream 0 region][stream 1 region]...
+    *bytes = align_up(p.packed_bytes) + (size_t)n_streams * host_layout(p).per_stream;
+    return NOP_OK;
+}
+
+int32_t nop_spectral_forward_host(const nop_plan* plan, const void* x_host, int64_t total_batch,
+                                  const void* const* weights, int32_t n_weights, const void* packed,
+                                  size_t packed_bytes, const float* bias, const float* addend_host,
+                                  int32_t apply_gelu, void* y_host, void* workspace, size_t workspace_bytes,
+                                  int32_t n_streams, void* stream) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    const nop_spectral_desc& d = p.d;
+    size_t need = 0;
+    int32_t rc = nop_spectral_host_workspace_size(plan, n_streams, &need);
+    if (rc != NOP_OK) return rc;
+    if (total_batch < 0) return fail(NOP_E_INVALID, "total_batch is negative");
+    if (total_batch == 0) return NOP_OK;
+    if (d.batch == 0 || total_batch % d.batch)
+        return fail(NOP_E_INVALID, "total_batch (" + std::to_string(total_batch) +
+                                       ") must be a multiple of the plan's batch (" + std::to_string(d.batch) + ")");
+    if (!x_host || !y_host) return fail(NOP_E_INVALID, "x_host and y_host must be non-NULL");
+    if ((addend_host || apply_gelu) && d.complex_data)
+        return fail(NOP_E_UNSUPPORTED, "addend / fused GELU need real data");
+    if (bias && (uintptr_t)bias % 4) return fail(NOP_E_ALIGNMENT, "bias must be 4-byte aligned");
+    const bool use_packed = packed != nullptr;
+    if (use_packed) {
+        if (p.packed_bytes == 0) return fail(NOP_E_UNSUPPORTED, "this plan takes its weights unpacked");
+        if (packed_bytes < p.packed_bytes)
+            return fail(NOP_E_WORKSPACE, "packed-weight buffer smaller than nop_spectral_packed_size");
+        if ((uintptr_t)packed % kAlign) return fail(NOP_E_ALIGNMENT, "packed-weight buffer must be 256-byte aligned");
+    } else {
+        if (n_weights != expected_weights(d))
+            return fail(NOP_E_INVALID, "expected " + std::to_string(expected_weights(d)) +
+                                           " weight pointers, got " + std::to_string(n_weights));
+        if (!weights) return fail(NOP_E_INVALID, "give either packed weights or the weights array");
+        for (int i = 0; i < n_weights; ++i) {
+            if (!weights[i]) return fail(NOP_E_INVALID, "weight pointer " + std::to_string(i) + " is NULL");
+            if ((uintptr_t)weights[i] % 8) return fail(NOP_E_ALIGNMENT, "weights must be 8-byte aligned (complex64)");
+        }
+    }
+    if (!workspace || workspace_bytes < need)
+        return fail(NOP_E_WORKSPACE, "host-forward workspace has " + std::to_string(workspace_bytes) +
+                                         " bytes, nop_spectral_host_workspace_size gives " + std::to_string(need));
+    if ((uintptr_t)workspace % kAlign) return fail(NOP_E_ALIGNMENT, "workspace must be 256-byte aligned");
+    if ((rc = check_device(p)) != NOP_OK) return rc;
+
+    const HostChunkLayout h = host_layout(p);
+    char* base = static_cast<char*>(workspace);
+    char* packed_ws = base;
+    char* regions = base + align_up(p.packed_bytes);
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+
+    // Streams and events live for this call only: destroying them with work still queued is legal
+    // (their resources are released once that work completes), so nothing outlives the call.
+    cudaStream_t st[8] = {};
+    cudaEvent_t ev[9] = {};
+    auto release = [&]() {
+        for (auto& e : ev)
+            if (e) cudaEventDestroy(e);
+        for (auto& q : st)
+            if (q) cudaStreamDestroy(q);
+    };
+    auto cuda_err = [&](cudaError_t err, const char* what) {
+        release();
+        return cuda_fail(err, what);
+    };
+    cudaError_t err;
+    for (int i = 0; i <= n_streams; ++i)
+        if ((err = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming)) != cudaSuccess)
+            return cuda_err(err, "cudaEventCreateWithFlags");
+    for (int i = 0; i < n_streams; ++i)
+        if ((err = cudaStreamCreateWithFlags(&st[i], cudaStreamNonBlocking)) != cudaSuccess)
+            return cuda_err(err, "cudaStreamCreateWithFlags");
+    if ((err = cudaEventRecord(ev[n_streams], caller)) != cudaSuccess) return cuda_err(err, "cudaEventRecord");
+    for (int i = 0; i < n_streams; ++i)
+        if ((err = cudaStreamWaitEvent(st[i], ev[n_streams], 0)) != cudaSuccess)
+            return cuda_err(err, "cudaStreamWaitEvent");
+
+    // Fused plans given unpacked weights pack them once; every stream then waits for the packing.
+    const char* pk = static_cast<const char*>(packed);
+    if (!use_packed && p.fast) {
+        if ((rc = fast_pack(p, weights, packed_ws, regions + h.ws_off, st[0])) != NOP_OK) {
+            release();
+            return rc;
+        }
+        if ((err = cudaEventRecord(ev[n_streams], st[0])) != cudaSuccess) return cuda_err(err, "cudaEventRecord");
+        for (int i = 1; i < n_streams; ++i)
+            if ((err = cudaStreamWaitEvent(st[i], ev[n_streams], 0)) != cudaSuccess)
+                return cuda_err(err, "cudaStreamWaitEvent");
+        pk = packed_ws;
+    }
+
+    const int64_t chunks = total_batch / d.batch;
+    const char* xh = static_cast<const char*>(x_host);
+    const char* ah = reinterpret_cast<const char*>(addend_host);
+    char* yh = static_cast<char*>(y_host);
+    for (int64_t c = 0; c < chunks; ++c) {
+        const int i = (int)(c % n_streams);
+        cudaStream_t s = st[i];
+        char* r = regions + (size_t)i * h.per_stream;
+        if ((err = cudaMemcpyAsync(r + h.x_off, xh + c * h.x_bytes, h.x_bytes, cudaMemcpyHostToDevice, s)) !=
+            cudaSuccess)
+            return cuda_err(err, "cudaMemcpyAsync (x chunk)");
+        const float* a_dev = nullptr;
+        if (ah) {
+            if ((err = cudaMemcpyAsync(r + h.a_off, ah + c * h.y_bytes, h.y_bytes, cudaMemcpyHostToDevice, s)) !=
+                cudaSuccess)
+                return cuda_err(err, "cudaMemcpyAsync (addend chunk)");
+            a_dev = reinterpret_cast<const float*>(r + h.a_off);
+        }
+        if (p.fast)
+            rc = fast_forward_packed(p, r + h.x_off, pk, bias, a_dev, apply_gelu, r + h.y_off, r + h.ws_off, s);
+        else
+            rc = generic_forward(p, r + h.x_off, weights, bias, a_dev, apply_gelu, r + h.y_off, r + h.ws_off, s);
+        if (rc != NOP_OK) {
+            release();
+            return rc;
+        }
+        if ((err = cudaMemcpyAsync(yh + c * h.y_bytes, r + h.y_off, h.y_bytes, cudaMemcpyDeviceToHost, s)) !=
+            cudaSuccess)
+            return cuda_err(err, "cudaMemcpyAsync (y chunk)");
+    }
+    for (int i = 0; i < n_streams; ++i) {
+        if ((err = cudaEventRecord(ev[i], st[i])) != cudaSuccess) return cuda_err(err, "cudaEventRecord");
+        if ((err = cudaStreamWaitEvent(caller, ev[i], 0)) != cudaSuccess) return cuda_err(err, "cudaStreamWaitEvent");
+    }
+    release();
+    return NOP_OK;
+}
+
 }  // extern "C"

@@ -82,6 +82,21 @@ def _weight_key(ws):
     return tuple((w.data_ptr(), w._version, tuple(w.shape), tuple(w.stride())) for w in ws)
 
 
+def _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream):
+    """Packed weight buffer of a fused plan: reused from ``cache`` while the weight tensors keep
+    their storage and version counter, else packed now (nop_spectral_pack_weights)."""
+    key = (bytes(desc), _weight_key(ws))
+    entry = cache.get("packed") if cache is not None else None
+    if entry is not None and entry[0] == key:
+        return entry[1]
+    packed = torch.empty(plan.packed_bytes, device=dev, dtype=torch.uint8)
+    _lib.check(_lib.library().nop_spectral_pack_weights(plan.handle, arr, len(ws), _ptr(packed), plan.packed_bytes,
+                                                        _ptr(workspace), plan.workspace_bytes, stream))
+    if cache is not None:
+        cache["packed"] = (key, packed)
+    return packed
+
+
 def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor], *, out_channels: int,
                      weight_kind: str = "dense", ranks: Sequence[int] = (), separable: bool = False,
                      bias: Optional[torch.Tensor] = None, addend: Optional[torch.Tensor] = None,
@@ -120,16 +135,7 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
     lib = _lib.library()
     with torch.cuda.device(dev):
         if plan.packed_bytes > 0:
-            key = (bytes(desc), _weight_key(ws))
-            entry = cache.get("packed") if cache is not None else None
-            if entry is None or entry[0] != key:
-                packed = torch.empty(plan.packed_bytes, device=dev, dtype=torch.uint8)
-                _lib.check(lib.nop_spectral_pack_weights(plan.handle, arr, len(ws), _ptr(packed), plan.packed_bytes,
-                                                         _ptr(workspace), plan.workspace_bytes, stream))
-                if cache is not None:
-                    cache["packed"] = (key, packed)
-            else:
-                packed = entry[1]
+            packed = _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream)
             _lib.check(lib.nop_spectral_forward_packed(
                 plan.handle, _ptr(x), _ptr(packed), plan.packed_bytes, _ptr(b), _ptr(a), int(bool(apply_gelu)),
                 _ptr(y), _ptr(workspace), plan.workspace_bytes, stream))
@@ -137,4 +143,73 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
             _lib.check(lib.nop_spectral_forward(
                 plan.handle, _ptr(x), arr, len(ws), _ptr(b), _ptr(a), int(bool(apply_gelu)), _ptr(y),
                 _ptr(workspace), plan.workspace_bytes, stream))
+    return y
+
+
+def default_chunk(batch: int, target_chunks: int = 8) -> int:
+    """Largest divisor of ``batch`` that cuts it into at least ``target_chunks`` chunks (or 1)."""
+    limit = max(1, batch // target_chunks)
+    return max(c for c in range(1, limit + 1) if batch % c == 0)
+
+
+def spectral_forward_host(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor], *, out_channels: int,
+                          device: torch.device, weight_kind: str = "dense", ranks: Sequence[int] = (),
+                          separable: bool = False, bias: Optional[torch.Tensor] = None,
+                          addend: Optional[torch.Tensor] = None, apply_gelu: bool = False, precision: str = "fp32",
+                          engine: str = "auto", chunk: Optional[int] = None, n_streams: int = 3,
+                          out: Optional[torch.Tensor] = None, cache: Optional[dict] = None,
+                          synchronize: bool = True) -> torch.Tensor:
+    """Forward of a batch held in HOST memory (nop_spectral_forward_host).
+
+    The batch is cut into chunks of ``chunk`` samples; each chunk's host-to-device copy, kernels and
+    device-to-host copy run on one of ``n_streams`` streams so that transfers in both directions
+    overlap with each other and with the kernels.  ``x`` / ``addend`` / ``out`` are CPU tensors
+    (page-locked for the overlap; the returned tensor is page-locked when ``out`` is None); the
+    weights and bias live on ``device``.  With ``synchronize=False`` the call returns once the work
+    is queued on the current stream of ``device`` and the caller synchronises before reading the result.
+    """
+    if x.is_cuda:
+        raise ValueError("spectral_forward_host takes a host tensor; use spectral_forward for device tensors")
+    dev = torch.device(device)
+    want = torch.complex64 if geo.complex_data else torch.float32
+    if x.dtype != want:
+        raise TypeError(f"expected {want} input, got {x.dtype}")
+    x = x.contiguous()
+    batch, ci = x.shape[0], x.shape[1]
+    chunk = default_chunk(batch) if chunk is None else int(chunk)
+    if chunk < 1 or batch % chunk:
+        raise ValueError(f"chunk {chunk} does not divide the batch {batch}")
+    y_shape = (batch, out_channels, *geo.n_out)
+    a = None
+    if addend is not None:
+        if addend.is_cuda or tuple(addend.shape) != y_shape:
+            raise ValueError(f"addend must be a host tensor of shape {y_shape}")
+        a = addend.detach().to(torch.float32).contiguous()
+    ws = [w.detach().to(device=dev, dtype=torch.complex64).contiguous() for w in weights]
+    b = None if bias is None else bias.detach().reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    if b is not None and b.numel() != out_channels:
+        raise ValueError(f"bias has {b.numel()} entries, expected {out_channels}")
+    y = out if out is not None else torch.empty(y_shape, dtype=want, pin_memory=True)
+    if y.is_cuda or tuple(y.shape) != y_shape or not y.is_contiguous():
+        raise ValueError(f"out must be a contiguous host tensor of shape {y_shape}")
+    desc = make_desc(geo, chunk, ci, out_channels, weight_kind=weight_kind, ranks=ranks, separable=separable,
+                     precision=precision, engine=engine)
+    plan = get_plan(desc, dev.index if dev.index is not None else torch.cuda.current_device())
+    lib = _lib.library()
+    size = ctypes.c_size_t()
+    _lib.check(lib.nop_spectral_host_workspace_size(plan.handle, int(n_streams), ctypes.byref(size)))
+    arr = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+    with torch.cuda.device(dev):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        workspace = torch.empty(max(int(size.value), 1), device=dev, dtype=torch.uint8)
+        packed = None
+        if plan.packed_bytes > 0:
+            pack_ws = torch.empty(max(plan.workspace_bytes, 1), device=dev, dtype=torch.uint8)
+            packed = _packed_weights(plan, desc, ws, arr, dev, pack_ws, cache, stream)
+        _lib.check(lib.nop_spectral_forward_host(
+            plan.handle, _ptr(x), batch, None if packed is not None else arr, 0 if packed is not None else len(ws),
+            _ptr(packed), plan.packed_bytes if packed is not None else 0, _ptr(b), _ptr(a), int(bool(apply_gelu)),
+            _ptr(y), _ptr(workspace), int(size.value), int(n_streams), stream))
+        if synchronize:
+            torch.cuda.current_stream(dev).synchronize()
     return y

@@ -192,6 +192,25 @@ class SpectralConv(BaseSpectralConv):
                                                    apply_gelu=apply_gelu)
         return _SpectralFn.apply(x, bias, addend, runner, *weights)
 
+    @torch.no_grad()
+    def forward_host(self, x: torch.Tensor, output_shape: Optional[Tuple[int]] = None, *, addend=None,
+                     apply_gelu: bool = False, chunk: Optional[int] = None, n_streams: int = 3, out=None,
+                     synchronize: bool = True):
+        """``forward`` for a batch held in host memory, with the PCIe copies of one chunk of the batch
+        overlapped with the kernels and copies of the others (nop_spectral_forward_host).  ``x``,
+        ``addend`` and ``out`` are CPU tensors (page-locked for the overlap); this module's parameters
+        stay on their CUDA device.  Inference only (no autograd graph)."""
+        if self.fno_block_precision in ("half", "mixed"):
+            raise NotImplementedError("fno_block_precision='half'/'mixed' is not implemented")
+        geo = self.geometry(list(x.shape[2:]), output_shape)
+        kind, weights, ranks = self.kernel_operands(geo)
+        cache = self.__dict__.setdefault("_nop_pack_cache", {})
+        return ops.spectral_forward_host(x, geo, weights, out_channels=self.out_channels, device=weights[0].device,
+                                         weight_kind=kind, ranks=ranks, separable=self.separable, bias=self.bias,
+                                         addend=addend, apply_gelu=apply_gelu, precision=self.contraction_precision,
+                                         engine=self.engine, chunk=chunk, n_streams=n_streams, out=out, cache=cache,
+                                         synchronize=synchronize)
+
 
 def _tucker_full(core, factors):
     t = core
