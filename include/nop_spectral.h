@@ -199,6 +199,14 @@ int32_t nop_spectral_slab_inverse_planes(const nop_plan* plan, const void* recv2
  * events on the launching stream. */
 int32_t nop_set_launch_events(void* const* events, int32_t n);
 
+/* Device status word (no counterpart in the reference).  The tensor-core contraction bounds every
+ * wait for its MMAs (about one second); a wait that expires makes the kernel stop, free its tensor
+ * memory and record NOP_DEVICE_MMA_TIMEOUT here instead of hanging the GPU.  Reads the word of the
+ * current device into *status (0: nothing recorded) and resets it when `clear` is non-zero.
+ * Synchronises with the device. */
+#define NOP_DEVICE_MMA_TIMEOUT 1
+int32_t nop_device_status(int32_t* status, int32_t clear);
+
 /* Allocation-free forward.  No counterpart in the reference: it exists for callers that may not
  * allocate device memory at all -- code hosted by a runtime that owns every byte of device memory
  * and hands a plugin only its input and output buffers, or a latency-bound loop that cannot afford

@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "nop_spectral_forward_packed", "nop_set_launch_events", "nop_spectral_slab_plan_create",
     "nop_spectral_slab_info", "nop_spectral_slab_forward_planes", "nop_spectral_slab_modes",
     "nop_spectral_slab_inverse_planes", "nop_spectral_host_workspace_size", "nop_spectral_forward_host",
+    "nop_device_status",
 )
 
 MAX_SLAB_RANKS = 64
@@ -133,6 +134,8 @@ def _declare(lib):
     lib.nop_spectral_slab_inverse_planes.restype = ctypes.c_int32
     lib.nop_spectral_slab_inverse_planes.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                      ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+    lib.nop_device_status.restype = ctypes.c_int32
+    lib.nop_device_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]
     lib.nop_spectral_host_workspace_size.restype = ctypes.c_int32
     lib.nop_spectral_host_workspace_size.argtypes = [c_plan_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]
     lib.nop_spectral_forward_host.restype = ctypes.c_int32
@@ -243,3 +246,11 @@ class Plan:
             except Exception:  # noqa: BLE001  (interpreter shutdown)
                 pass
             self.handle = None
+
+
+def device_status(clear: bool = True) -> int:
+    """Status word the tensor-core kernels set when a bounded wait expires (0: none); see
+    nop_device_status.  Synchronises with the current device."""
+    v = ctypes.c_int32()
+    check(library().nop_device_status(ctypes.byref(v), int(bool(clear))))
+    return int(v.value)

@@ -1,6 +1,7 @@
 // C ABI of libnop_b200: descriptor validation, plans (twiddle tables, workspace layout) and
 // dispatch to the fused FFT engine or the generic direct-DFT engine.
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -15,6 +16,13 @@ thread_local std::string g_last_error;
 constexpr int64_t kMaxLen = int64_t(1) << 20;     // per-axis transform length limit
 constexpr int64_t kMaxElems = int64_t(1) << 40;   // per-tensor element limit
 constexpr size_t kAlign = 256;
+
+// NOP_CONTRACTION=simt selects the CUDA-core contraction kernel instead of the tcgen05 one (A/B
+// measurements of the two); read once per plan.
+bool mix_on_tensor_cores() {
+    const char* v = getenv("NOP_CONTRACTION");
+    return !(v && strcmp(v, "simt") == 0);
+}
 
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
@@ -258,6 +266,7 @@ int32_t nop_spectral_plan_create(const nop_spectral_desc* desc, nop_plan** plan_
     }
     p->fast = fast_ok && p->d.engine != NOP_ENGINE_GENERIC;
     p->fast_kind = p->fast ? kind : FastKind::None;
+    p->mix_tc = mix_on_tensor_cores();
 
     size_t off = 0;
     if (p->fast) {
@@ -394,6 +403,7 @@ int32_t nop_spectral_slab_plan_create(const nop_spectral_desc* desc, int32_t ran
     }
     p->fast = true;
     p->fast_kind = FastKind::Vol3DSlab;
+    p->mix_tc = mix_on_tensor_cores();
     p->slab_rank = rank;
     p->slab_world = world;
     p->slab_nx = p->d.n_in[0] / world;
@@ -486,6 +496,14 @@ int32_t nop_spectral_slab_inverse_planes(const nop_plan* plan, const void* recv2
     if (!recv2 || !y) return fail(NOP_E_INVALID, "recv2 and y must be non-NULL");
     if ((uintptr_t)recv2 % 16) return fail(NOP_E_ALIGNMENT, "recv2 must be 16-byte aligned");
     return fast_slab_planes_inv(*p, recv2, bias, addend, apply_gelu, y, static_cast<cudaStream_t>(stream));
+}
+
+int32_t nop_device_status(int32_t* status, int32_t clear) {
+    if (!status) return fail(NOP_E_INVALID, "status is NULL");
+    int v = 0;
+    int32_t rc = fast_device_status(&v, clear != 0);
+    if (rc == NOP_OK) *status = v;
+    return rc;
 }
 
 int32_t nop_set_launch_events(void* const* events, int32_t n) {

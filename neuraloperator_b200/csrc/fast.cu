@@ -17,6 +17,7 @@
 #include "axis.cuh"
 #include "plane256.cuh"
 #include "row1d.cuh"
+#include "mix_tc.cuh"
 
 namespace nop {
 namespace {
@@ -384,7 +385,7 @@ __global__ void k_pack_broadcast(const float2* __restrict__ U, float4* __restric
 constexpr size_t kSmemLimit = 227 * 1024;
 
 // per-device "dynamic shared memory limit raised" bits, one word per kernel instantiation
-std::atomic<uint64_t> g_attr_done[16];
+std::atomic<uint64_t> g_attr_done[24];
 
 template <class K>
 cudaError_t ensure_smem_attr(K kernel, int slot, int device, size_t bytes = kSmemLimit) {
@@ -413,21 +414,61 @@ BlockMap block_map(const Plan& p) {
             (int)p.slab_qbegin[p.slab_rank]};
 }
 
+// status word of the tensor-core kernels (bounded waits that expired), per device
+__device__ int g_device_status;
+
+int* device_status_ptr(int device) {
+    static std::atomic<int*> ptrs[64];
+    int* ptr = ptrs[device & 63].load();
+    if (!ptr) {
+        void* addr = nullptr;
+        if (cudaGetSymbolAddress(&addr, g_device_status) != cudaSuccess) return nullptr;
+        ptr = static_cast<int*>(addr);
+        ptrs[device & 63].store(ptr);
+    }
+    return ptr;
+}
+
+template <int CO, bool BF16>
+cudaError_t launch_mix_tc(const Plan& p, const BlockMap& bm, const float2* X, const float4* W, int64_t wq, float2* Y,
+                          int Ci, int Co, int slot, cudaStream_t s) {
+    using C = tc::Cfg<CO, BF16>;
+    cudaError_t err = ensure_smem_attr(tc::k_mix_tc<CO, BF16>, slot, p.device, C::SMEM);
+    if (err != cudaSuccess) return err;
+    int* status = device_status_ptr(p.device);
+    if (!status) return cudaErrorInvalidSymbol;
+    dim3 grid((unsigned)(2 * bm.local), (unsigned)ceil_div(p.d.batch, tc::BT), (unsigned)ceil_div(Co, CO));
+    tc::k_mix_tc<CO, BF16><<<grid, tc::THREADS, C::SMEM, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
+                                                              bm.qbeg, status);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t wq, float2* Y, int Ci, int Co,
                        cudaStream_t s) {
-    cudaError_t err = ensure_smem_attr(p.d.precision == NOP_PRECISION_BF16 ? k_mix<true> : k_mix<false>,
-                                       p.d.precision == NOP_PRECISION_BF16 ? 14 : 15, p.device, kMixSmem);
-    if (err != cudaSuccess) return err;
     const BlockMap bm = block_map(p);
     if (bm.local == 0) return cudaSuccess;
-    dim3 grid((unsigned)bm.local, (unsigned)ceil_div(p.d.batch, 16), (unsigned)ceil_div(Co, 64));
-    if (p.d.precision == NOP_PRECISION_BF16)
-        k_mix<true><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
-                                                         bm.qbeg);
-    else
-        k_mix<false><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
-                                                          bm.qbeg);
-    err = cudaGetLastError();
+    cudaError_t err;
+    const bool bf16 = p.d.precision == NOP_PRECISION_BF16;
+    if (p.mix_tc) {
+        // 64-wide output tiles (N = 128) unless the channels fit a 32-wide tile
+        if (Co > 32)
+            err = bf16 ? launch_mix_tc<64, true>(p, bm, X, W, wq, Y, Ci, Co, 16, s)
+                       : launch_mix_tc<64, false>(p, bm, X, W, wq, Y, Ci, Co, 17, s);
+        else
+            err = bf16 ? launch_mix_tc<32, true>(p, bm, X, W, wq, Y, Ci, Co, 18, s)
+                       : launch_mix_tc<32, false>(p, bm, X, W, wq, Y, Ci, Co, 19, s);
+    } else {
+        err = ensure_smem_attr(bf16 ? k_mix<true> : k_mix<false>, bf16 ? 14 : 15, p.device, kMixSmem);
+        if (err != cudaSuccess) return err;
+        dim3 grid((unsigned)bm.local, (unsigned)ceil_div(p.d.batch, 16), (unsigned)ceil_div(Co, 64));
+        if (bf16)
+            k_mix<true><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
+                                                             bm.qbeg);
+        else
+            k_mix<false><<<grid, kMixThreads, kMixSmem, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, bm.qpl, bm.qtot,
+                                                              bm.qbeg);
+        err = cudaGetLastError();
+    }
     if (err == cudaSuccess) launch_mark(s);
     return err;
 }
@@ -798,6 +839,19 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
     p.packed_bytes = pk;
     ws->packed = take(pk);
     return off;
+}
+
+int32_t fast_device_status(int* status, bool clear) {
+    int v = 0;
+    cudaError_t err = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+    if (err != cudaSuccess) return cuda_fail(err, "cudaMemcpyFromSymbol(status)");
+    if (clear && v != 0) {
+        const int zero = 0;
+        if ((err = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int))) != cudaSuccess)
+            return cuda_fail(err, "cudaMemcpyToSymbol(status)");
+    }
+    *status = v;
+    return NOP_OK;
 }
 
 int32_t fast_launches(const Plan& p) {

@@ -58,6 +58,7 @@ struct Plan {
     void* table_mem = nullptr;         // single device allocation holding every table
     WorkspaceLayout ws;
     size_t packed_bytes = 0;           // fused engine: packed-weight buffer size (0: no packing)
+    bool mix_tc = true;                // fused engine: contraction on the tensor cores (tcgen05)
     // 3D slab decomposition (FastKind::Vol3DSlab): this rank's x planes and everyone's mode blocks
     int slab_rank = 0, slab_world = 1;
     int64_t slab_nx = 0;                                   // x planes per rank
@@ -101,6 +102,8 @@ int32_t contract_stage(const Plan& p, const float2* X, const void* const* weight
 bool fast_supported(const nop_spectral_desc& d, FastKind* kind, std::string* why);
 size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws);
 int32_t fast_launches(const Plan& p);
+// status word of the tensor-core kernels on the current device (synchronous read, optional reset)
+int32_t fast_device_status(int* status, bool clear);
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s);
 int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
                             const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
