@@ -260,9 +260,10 @@ int32_t nop_spectral_plan_create(const nop_spectral_desc* desc, nop_plan** plan_
         return fail(NOP_E_UNSUPPORTED, "fused FFT engine does not cover this shape: " + why);
     }
     cudaError_t err = cudaGetDevice(&p->device);
+    if (err == cudaSuccess) err = cudaDeviceGetAttribute(&p->sm_count, cudaDevAttrMultiProcessorCount, p->device);
     if (err != cudaSuccess) {
         delete p;
-        return cuda_fail(err, "cudaGetDevice");
+        return cuda_fail(err, "cudaGetDevice / multiprocessor count");
     }
     p->fast = fast_ok && p->d.engine != NOP_ENGINE_GENERIC;
     p->fast_kind = p->fast ? kind : FastKind::None;
@@ -413,9 +414,10 @@ int32_t nop_spectral_slab_plan_create(const nop_spectral_desc* desc, int32_t ran
         p->slab_qbegin[r] = r * (qp / world) + (r < qp % world ? r : qp % world);
     }
     cudaError_t err = cudaGetDevice(&p->device);
+    if (err == cudaSuccess) err = cudaDeviceGetAttribute(&p->sm_count, cudaDevAttrMultiProcessorCount, p->device);
     if (err != cudaSuccess) {
         delete p;
-        return cuda_fail(err, "cudaGetDevice");
+        return cuda_fail(err, "cudaGetDevice / multiprocessor count");
     }
     p->ws.bytes = fast_workspace_bytes(*p, &p->ws);
     rc = build_tables(p);

@@ -3,30 +3,32 @@
 //   Y[q][b][o][j] = sum_i X[q][b][i][j] W_q[i][o][j]        (complex, mode 8 q + j)
 //
 // on the mode-blocked spectrum [Q][B][C][8] with weights packed as W_q[i][p][o] = float4(mode 8q+2p,
-// mode 8q+2p+1).  One CTA takes four modes (half a mode block), 64 batch entries and CO output
-// channels.  For each mode the complex product becomes ONE real GEMM with M = 128, N = 2 CO:
+// mode 8q+2p+1).  A tile is four modes (half a mode block), 64 batch entries and CO output channels.
+// For each mode the complex product is ONE real GEMM with M = 128, N = 2 CO, K = input channels:
 //
-//   A = [Xr ; Xi]  (rows 0..63: real parts of the 64 batch rows, rows 64..127: imaginary parts)
-//   B = [Wr | Wi]  (columns 0..CO-1: real parts, CO..2CO-1: imaginary parts),  K = input channels
-//   D = A B = [[Xr Wr, Xr Wi], [Xi Wr, Xi Wi]]   ->   Yr = D[b][o] - D[64+b][CO+o],
-//                                                      Yi = D[b][CO+o] + D[64+b][o].
+//   A rows: in every 32-row quadrant, 16 batch rows of Xr followed by the same 16 rows of Xi
+//   B = [Wr | Wi]  (columns 0..CO-1: real parts, CO..2CO-1: imaginary parts)
+//   D row (Xr of b) = [Xr Wr, Xr Wi],  D row (Xi of b) = [Xi Wr, Xi Wi], 16 lanes apart in one warp's
+//   tensor-memory quadrant, so Yr = Xr Wr - Xi Wi and Yi = Xr Wi + Xi Wr combine with lane shuffles.
 //
 // fp32 accuracy from tf32 operands (three-pass split): every operand x = hi + lo with
 // hi = tf32(x), lo = tf32(x - hi), and D = A_hi B_hi + A_hi B_lo + A_lo B_hi (the dropped lo*lo term
 // is below 2^-22 relative), accumulated in fp32 in tensor memory.  With the bf16 contraction the
 // operands are rounded to bf16 and one kind::f16 MMA per K step replaces the three tf32 ones.
 //
-// Pipeline per CTA (256 threads, one CTA per SM): the K loop runs over 8 input channels (tf32) or
-// 16 (bf16) at a time.  All threads load the next step's X and W into registers while the current
-// step is converted and stored into a shared-memory stage in the canonical no-swizzle K-major layout
-// (8-row x 16-byte core matrices); thread 0 issues the MMAs for the four modes and commits them to
-// the stage's mbarrier, which the threads wait on before they overwrite that stage two steps later.
-// The four modes' accumulators (4 x 2 CO fp32 columns) live in tensor memory for the whole K loop.
-// Epilogue: tensor memory -> registers (tcgen05.ld) -> padded shared memory -> combined complex
-// outputs, 32 contiguous bytes (four modes) per (b, o).
-//
+// Warp-specialised persistent CTAs (one per SM), connected by mbarriers:
+//   producer warps 4..11 : global X / W -> registers (next step prefetched) -> tf32 hi/lo or bf16 ->
+//                          shared-memory stage (ring of NS) in the canonical no-swizzle K-major layout
+//                          (8-row x 16-byte core matrices) -> arrive `full[s]`
+//   MMA warp 12 (lane 0) : wait `full[s]`, issue the step's MMAs for the four modes, commit to
+//                          `empty[s]`; after a tile's last step commit to `acc_full[a]`
+//   epilogue warps 0..3  : wait `acc_full[a]`, tcgen05.ld their lane quadrant, release the
+//                          accumulator (`acc_empty[a]`), combine re / im with shuffles, store 32
+//                          contiguous bytes (four modes) per (b, o)
+// Accumulators: 4 modes x 2 CO fp32 columns per tile; with CO = 32 two tiles' accumulators alternate.
 // Every wait is bounded (about one second of clock cycles): on expiry the kernel records a status
-// word (nop_device_status), stops issuing, waits (bounded) for its MMAs and frees its tensor memory.
+// word (nop_device_status), all roles leave their loops, the issued MMAs are drained (bounded) and
+// the tensor memory is freed.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -37,9 +39,13 @@
 namespace nop {
 namespace tc {
 
-constexpr int THREADS = 256;
-constexpr int MODES = 4;   // modes per CTA
-constexpr int BT = 64;     // batch rows per CTA (A has 2 BT = 128 rows)
+constexpr int EPI_WARPS = 4;                 // warps 0..3
+constexpr int PROD_WARPS = 8;                // warps 4..11
+constexpr int MMA_WARP = EPI_WARPS + PROD_WARPS;
+constexpr int THREADS = 32 * (MMA_WARP + 1); // 416
+constexpr int PROD_THREADS = 32 * PROD_WARPS;
+constexpr int MODES = 4;   // modes per tile
+constexpr int BT = 64;     // batch rows per tile (A has 2 BT = 128 rows)
 constexpr int M = 128;
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
 
@@ -54,16 +60,20 @@ struct Cfg {
     static constexpr int A_TILE = M * 32;               // bytes of one mode's A for one K step
     static constexpr int B_TILE = N * 32;
     static constexpr int STAGE = MODES * SPLITS * (A_TILE + B_TILE);
-    static constexpr int DUMP_PITCH = 33;               // floats per dumped row (32 columns + pad)
-    static constexpr int DUMP = MODES * M * DUMP_PITCH * 4;
-    static constexpr int TMEM_COLS = MODES * N;         // 256 or 512
-    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "tensor-memory allocation must be a power of 2");
-    // a CTA holding all 512 columns must be alone on its SM (more than half the shared memory), so
-    // that no second CTA blocks in tcgen05.alloc; two 256-column CTAs share an SM
-    static constexpr int MIN_BODY = TMEM_COLS == 512 ? 117 * 1024 : 0;
-    static constexpr int BODY0 = 2 * STAGE > DUMP ? 2 * STAGE : DUMP;
-    static constexpr int BODY = BODY0 > MIN_BODY ? BODY0 : MIN_BODY;
-    static constexpr int SMEM = BODY + 64;              // + two mbarriers + tensor-memory address
+    static constexpr int NS0 = (192 * 1024) / STAGE;
+    static constexpr int NS = NS0 > 6 ? 6 : NS0;         // stages in the ring
+    static constexpr int ACC_COLS = MODES * N;          // tensor-memory columns of one tile
+    static constexpr int NACC = ACC_COLS <= 256 ? 2 : 1;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int BODY = NS * STAGE;
+    // after the stages: full[NS], empty[NS], acc_full[2], acc_empty[2], drain (8 bytes each), then the
+    // tensor-memory address and the abort flag (4 bytes each)
+    static constexpr int TAIL = (2 * NS + 5) * 8 + 8;
+    static constexpr int SMEM = BODY + 256;
+    static_assert(TAIL <= 256, "barrier area overflows its reservation");
+    static_assert(NS >= 2, "at least two stages");
+    static_assert(ACC_COLS * NACC <= TMEM_COLS, "accumulators exceed tensor memory");
+    static_assert(SMEM > 116 * 1024, "one CTA per SM: the whole tensor memory is allocated");
     // instruction descriptor: D f32, A/B tf32 (2) or bf16 (1), both K-major, N >> 3, M >> 4
     static constexpr uint32_t IDESC = (1u << 4) | ((BF16 ? 1u : 2u) << 7) | ((BF16 ? 1u : 2u) << 10) |
                                       ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -73,6 +83,9 @@ struct Cfg {
 // 8 rows x 16 bytes stored contiguously; K-adjacent core matrices 128 B apart (LBO), 8-row groups
 // 256 B apart (SBO)
 __device__ __forceinline__ uint32_t tile_off(int r, int kh) { return (r >> 3) * 256 + kh * 128 + (r & 7) * 16; }
+
+// A row of batch entry b (0..63), real (e = 0) or imaginary (e = 1) part
+__device__ __forceinline__ int a_row(int b, int e) { return (b >> 4) * 32 + e * 16 + (b & 15); }
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
@@ -87,7 +100,21 @@ __device__ __forceinline__ float tf32_round(float x) {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+
+// bounded wait for the completion of the phase with parity `parity`; gives up early when `abort`
+// (if given) is set
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    const uint32_t addr = smem_u32(bar);
     const long long t0 = clock64();
     while (true) {
         uint32_t done;
@@ -96,10 +123,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
             "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(done)
-            : "r"(bar), "r"(parity)
+            : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if (clock64() - t0 > kWaitCycles) return false;
+        if ((abort && *abort) || clock64() - t0 > kWaitCycles) return false;
     }
 }
 
@@ -123,16 +150,18 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t da, uint64_t db
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -140,75 +169,97 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Operand staging for one K step.  X unit (thread t < 128): batch row b = t / 2, K quarter kq = t % 2
-// (tf32: 4 channels = 16 bytes; bf16: 8 channels = 16 bytes), all four modes.  W unit
-// (128 <= t < 128 + 2 CO): output channel o = (t - 128) % CO, K quarter (t - 128) / CO.
-template <int CO, bool BF16>
+// Tile of the contraction: mode half h of local mode block q, batch rows b0.., output channels o0..
+struct Tile {
+    int h, b0, o0;
+    const float2* Xq;
+    const float4* Wq;
+    float2* Yq;
+};
+
+struct Problem {
+    const float2* X;
+    const float4* Wp;
+    int64_t wq;
+    float2* Y;
+    int B, Ci, Co;
+    int local;  // local mode blocks (< 2^31; the host checks the tile count fits an int)
+    int qpl, qtot, qbeg;
+    int bt;
+};
+
+// decode of tile t (done once per tile; 32-bit divisions)
+__device__ __forceinline__ Tile tile_at(const Problem& pr, int t, int co_tile) {
+    Tile r;
+    r.h = t & 1;
+    int rest = t >> 1;
+    const int q = rest % pr.local;
+    rest /= pr.local;
+    r.b0 = (rest % pr.bt) * BT;
+    r.o0 = (rest / pr.bt) * co_tile;
+    r.Xq = pr.X + (int64_t)q * pr.B * pr.Ci * 8;
+    // local mode block q -> weight block (identity unless plane-mode blocks are split across ranks)
+    r.Wq = pr.Wp + (int64_t)((q / pr.qpl) * pr.qtot + pr.qbeg + q % pr.qpl) * pr.wq;
+    r.Yq = pr.Y + (int64_t)q * pr.B * pr.Co * 8;
+    return r;
+}
+
+// Producer unit for one K step.  X unit (p < 128): batch row b = p / 2, K half kh = p % 2, all four
+// modes.  W unit (128 <= p < 128 + 2 CO): output channel o = u % CO, K half u / CO (u = p - 128).
+// A K half is 16 bytes of K: 4 tf32 or 8 bf16 channels; per channel two float4 (four modes, complex).
+template <bool BF16>
 struct Step {
-    static constexpr int KQ = BF16 ? 8 : 4;  // channels per unit
-    float4 v[BF16 ? 16 : 8];                 // [channel][mode pair] raw complex values
+    static constexpr int KH = BF16 ? 8 : 4;
+    float4 v[2 * KH];
 };
 
 template <int CO, bool BF16>
-__device__ __forceinline__ void load_step(Step<CO, BF16>& st, const float2* __restrict__ Xq,
-                                          const float4* __restrict__ Wq, int B, int Ci, int Co, int b0, int o0, int h,
-                                          int k0) {
-    constexpr int KQ = Step<CO, BF16>::KQ;
-    const int t = threadIdx.x;
-    if (t < 128) {
-        const int b = t >> 1, kq = t & 1;
-        const bool bok = b0 + b < B;
+__device__ __forceinline__ void load_step(Step<BF16>& st, const Problem& pr, const Tile& tl, int k0, int p) {
+    constexpr int KH = Step<BF16>::KH;
+    if (p < 128) {
+        const int b = p >> 1, kh = p & 1;
+        const bool bok = tl.b0 + b < pr.B;
+        const float2* src = tl.Xq + ((int64_t)(tl.b0 + b) * pr.Ci + k0 + kh * KH) * 8 + 4 * tl.h;
 #pragma unroll
-        for (int c = 0; c < KQ; ++c) {
-            const int i = k0 + kq * KQ + c;
-            const bool ok = bok && i < Ci;
-            const float4* src = reinterpret_cast<const float4*>(Xq + ((int64_t)(b0 + b) * Ci + i) * 8 + 4 * h);
-            st.v[2 * c] = ok ? __ldg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
-            st.v[2 * c + 1] = ok ? __ldg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < KH; ++c) {
+            const bool ok = bok && k0 + kh * KH + c < pr.Ci;
+            const float4* s4 = reinterpret_cast<const float4*>(src + c * 8);
+            st.v[2 * c] = ok ? __ldg(s4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            st.v[2 * c + 1] = ok ? __ldg(s4 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-    } else if (t < 128 + 2 * CO) {
-        const int o = (t - 128) % CO, kq = (t - 128) / CO;
-        const bool ook = o0 + o < Co;
+    } else if (p < 128 + 2 * CO) {
+        const int u = p - 128;
+        const int o = u % CO, kh = u / CO;
+        const bool ook = tl.o0 + o < pr.Co;
 #pragma unroll
-        for (int c = 0; c < KQ; ++c) {
-            const int i = k0 + kq * KQ + c;
-            const bool ok = ook && i < Ci;
-#pragma unroll
-            for (int pp = 0; pp < 2; ++pp) {
-                const float4* src = Wq + ((int64_t)i * 4 + 2 * h + pp) * Co + o0 + o;
-                st.v[2 * c + pp] = ok ? __ldg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+        for (int c = 0; c < KH; ++c) {
+            const int i = k0 + kh * KH + c;
+            const bool ok = ook && i < pr.Ci;
+            const float4* s4 = tl.Wq + ((int64_t)i * 4 + 2 * tl.h) * pr.Co + tl.o0 + o;
+            st.v[2 * c] = ok ? __ldg(s4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            st.v[2 * c + 1] = ok ? __ldg(s4 + pr.Co) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 }
 
-// component e (0: re, 1: im) of local mode jl from a unit's raw values for channel c
 template <int CO, bool BF16>
-__device__ __forceinline__ float comp(const Step<CO, BF16>& st, int c, int jl, int e) {
-    const float4 v = st.v[2 * c + (jl >> 1)];
-    return (jl & 1) ? (e ? v.w : v.z) : (e ? v.y : v.x);
-}
-
-template <int CO, bool BF16>
-__device__ __forceinline__ void store_step(const Step<CO, BF16>& st, char* stage) {
+__device__ __forceinline__ void store_step(const Step<BF16>& st, char* stage, int p) {
     using C = Cfg<CO, BF16>;
-    const int t = threadIdx.x;
-    char* a_base = stage;                                          // [mode][split] A tiles
-    char* b_base = stage + MODES * C::SPLITS * C::A_TILE;          // [mode][split] B tiles
-    int row[2], kq;
+    constexpr int KH = Step<BF16>::KH;
+    int rows[2], kh, tile_bytes;
     char* base;
-    int tile_bytes;
-    if (t < 128) {
-        row[0] = t >> 1;          // real parts
-        row[1] = (t >> 1) + BT;   // imaginary parts
-        kq = t & 1;
-        base = a_base;
+    if (p < 128) {
+        rows[0] = a_row(p >> 1, 0);
+        rows[1] = a_row(p >> 1, 1);
+        kh = p & 1;
+        base = stage;
         tile_bytes = C::A_TILE;
-    } else if (t < 128 + 2 * CO) {
-        row[0] = (t - 128) % CO;        // columns of Wr
-        row[1] = (t - 128) % CO + CO;   // columns of Wi
-        kq = (t - 128) / CO;
-        base = b_base;
+    } else if (p < 128 + 2 * CO) {
+        const int u = p - 128;
+        rows[0] = u % CO;       // columns of Wr
+        rows[1] = u % CO + CO;  // columns of Wi
+        kh = u / CO;
+        base = stage + MODES * C::SPLITS * C::A_TILE;
         tile_bytes = C::B_TILE;
     } else {
         return;
@@ -217,21 +268,26 @@ __device__ __forceinline__ void store_step(const Step<CO, BF16>& st, char* stage
     for (int jl = 0; jl < MODES; ++jl) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const uint32_t off = tile_off(row[e], kq);
+            const uint32_t off = tile_off(rows[e], kh);
+            float x[KH];
+#pragma unroll
+            for (int c = 0; c < KH; ++c) {
+                const float4 v = st.v[2 * c + (jl >> 1)];
+                x[c] = (jl & 1) ? (e ? v.w : v.z) : (e ? v.y : v.x);
+            }
             if constexpr (BF16) {
                 uint4 w;
-                w.x = pack_bf16(comp(st, 0, jl, e), comp(st, 1, jl, e));
-                w.y = pack_bf16(comp(st, 2, jl, e), comp(st, 3, jl, e));
-                w.z = pack_bf16(comp(st, 4, jl, e), comp(st, 5, jl, e));
-                w.w = pack_bf16(comp(st, 6, jl, e), comp(st, 7, jl, e));
+                w.x = pack_bf16(x[0], x[1]);
+                w.y = pack_bf16(x[2], x[3]);
+                w.z = pack_bf16(x[4], x[5]);
+                w.w = pack_bf16(x[6], x[7]);
                 *reinterpret_cast<uint4*>(base + jl * tile_bytes + off) = w;
             } else {
                 float hi[4], lo[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const float x = comp(st, c, jl, e);
-                    hi[c] = tf32_round(x);
-                    lo[c] = tf32_round(x - hi[c]);
+                    hi[c] = tf32_round(x[c]);
+                    lo[c] = tf32_round(x[c] - hi[c]);
                 }
                 *reinterpret_cast<float4*>(base + (jl * 2 + 0) * tile_bytes + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
                 *reinterpret_cast<float4*>(base + (jl * 2 + 1) * tile_bytes + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
@@ -240,28 +296,42 @@ __device__ __forceinline__ void store_step(const Step<CO, BF16>& st, char* stage
     }
 }
 
-// grid: x = 2 * local mode blocks (mode half fastest), y = batch tiles of 64, z = output tiles of CO
+// Persistent: CTA c takes tiles c, c + gridDim.x, ...; tiles ordered mode half fastest, then local
+// mode block, batch tile, output tile.  Global K step g of the CTA = (its tile g / nk, step g % nk).
 template <int CO, bool BF16>
-__global__ void __launch_bounds__(THREADS, 1)
+// 13 warps: the SM's four register banks hold at most 4 warps each at 128 registers per thread
+__global__ void __maxnreg__(128)
 k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq, float2* __restrict__ Y, int B,
-         int Ci, int Co, int qpl, int qtot, int qbeg, int* __restrict__ status) {
+         int Ci, int Co, int local, int qpl, int qtot, int qbeg, int* __restrict__ status) {
     using C = Cfg<CO, BF16>;
+    constexpr int NS = C::NS, NACC = C::NACC;
     extern __shared__ __align__(1024) char smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BODY);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BODY + 16);
-    int* abort_flag = reinterpret_cast<int*>(smem + C::BODY + 20);
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int h = blockIdx.x & 1;
-    const int64_t q = blockIdx.x >> 1;
-    const int b0 = blockIdx.y * BT;
-    const int o0 = blockIdx.z * CO;
-    const float2* Xq = X + q * (int64_t)B * Ci * 8;
-    const float4* Wq = Wp + ((q / qpl) * qtot + qbeg + q % qpl) * wq;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BODY);
+    uint64_t* empty = full + NS;
+    uint64_t* acc_full = empty + NS;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    Problem pr{X, Wp, wq, Y, B, Ci, Co, local, qpl, qtot, qbeg, (B + BT - 1) / BT};
+    const int ot = (Co + CO - 1) / CO;
+    const int tiles = 2 * local * pr.bt * ot;
+    const int my_tiles = tiles > (int)blockIdx.x ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int nk = (Ci + C::KS - 1) / C::KS;
+    auto tile_k = [&](int k) { return tile_at(pr, (int)blockIdx.x + k * (int)gridDim.x, CO); };
 
     if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[0])) : "memory");
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[1])) : "memory");
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], PROD_THREADS);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 32 * EPI_WARPS);
+        }
+        mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *abort_flag = 0;
     }
@@ -276,99 +346,167 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    Step<CO, BF16> cur, nxt;
-    load_step<CO, BF16>(cur, Xq, Wq, B, Ci, Co, b0, o0, h, 0);
-    bool aborted = false;
-    int issued = 0;  // K steps whose MMAs were committed
-    for (int kc = 0; kc < nk; ++kc) {
-        if (kc + 1 < nk) load_step<CO, BF16>(nxt, Xq, Wq, B, Ci, Co, b0, o0, h, (kc + 1) * C::KS);
-        const int s = kc & 1;
-        char* stage = smem + s * C::STAGE;
-        if (kc >= 2 && !mbar_wait(smem_u32(&bars[s]), ((kc >> 1) - 1) & 1)) *abort_flag = 1;
-        store_step<CO, BF16>(cur, stage);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (*abort_flag) {
-            aborted = true;
-            break;
-        }
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a0 = smem_u32(stage);
-            const uint32_t bq = a0 + MODES * C::SPLITS * C::A_TILE;
-#pragma unroll
-            for (int jl = 0; jl < MODES; ++jl) {
-                const uint32_t d = tmem + jl * C::N;
-                if constexpr (BF16) {
-                    mma_bf16(d, smem_desc(a0 + jl * C::A_TILE), smem_desc(bq + jl * C::B_TILE), C::IDESC, kc > 0);
-                } else {
-                    const uint64_t ahi = smem_desc(a0 + (jl * 2) * C::A_TILE);
-                    const uint64_t alo = smem_desc(a0 + (jl * 2 + 1) * C::A_TILE);
-                    const uint64_t bhi = smem_desc(bq + (jl * 2) * C::B_TILE);
-                    const uint64_t blo = smem_desc(bq + (jl * 2 + 1) * C::B_TILE);
-                    mma_tf32(d, ahi, bhi, C::IDESC, kc > 0);
-                    mma_tf32(d, ahi, blo, C::IDESC, 1);
-                    mma_tf32(d, alo, bhi, C::IDESC, 1);
-                }
-            }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             smem_u32(&bars[s]))
-                         : "memory");
-        }
-        issued = kc + 1;
-        if (kc + 1 < nk) cur = nxt;
-    }
-    // every committed MMA has finished once the last commit's phase completes
-    bool ok = true;
-    if (issued > 0) {
-        const int kl = issued - 1;
-        ok = mbar_wait(smem_u32(&bars[kl & 1]), (kl >> 1) & 1);
-    }
-    const int bad = __syncthreads_or(!ok || aborted);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (bad && tid == 0) atomicExch(status, kStatusMmaTimeout);
+    auto give_up = [&]() {
+        *abort_flag = 1;
+        atomicExch(status, kStatusMmaTimeout);
+    };
 
-    if (!bad) {
-        // ---- epilogue: 16 output channels per pass; warpgroup g dumps modes 2g, 2g+1 ----
-        float* dump = reinterpret_cast<float*>(smem);
-        const int lane_base = (warp & 3) * 32;
-        const int row = lane_base + (tid & 31);
-        const int g = warp >> 2;
-        float2* Yq = Y + q * (int64_t)B * Co * 8;
-        for (int ob = 0; ob < CO; ob += 16) {
-#pragma unroll
-            for (int mm = 0; mm < 2; ++mm) {
-                const int jl = 2 * g + mm;
-                float pv[16], qv[16];
-                const uint32_t ta = tmem + ((uint32_t)lane_base << 16) + jl * C::N + ob;
-                tmem_ld16(ta, pv);
-                tmem_ld16(ta + CO, qv);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                float* drow = dump + ((size_t)jl * M + row) * C::DUMP_PITCH;
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    drow[c] = pv[c];
-                    drow[16 + c] = qv[c];
+    if (warp >= EPI_WARPS && warp < MMA_WARP) {
+        // ------------------------------ producers ------------------------------
+        const int p = tid - 32 * EPI_WARPS;
+        // tf32: the next step's loads are issued before the current step is stored (two register
+        // sets); bf16 units are twice as large, so they load and store one step at a time
+        constexpr bool PREFETCH = !BF16;
+        Step<BF16> cur, nxt;
+        int lk = 0, lkc = 0;              // tile and K step of the next load
+        Tile ltile;
+        if (my_tiles > 0) ltile = tile_k(0);
+        auto load_next = [&](Step<BF16>& dst) {
+            load_step<CO, BF16>(dst, pr, ltile, lkc * C::KS, p);
+            if (++lkc == nk) {
+                lkc = 0;
+                if (++lk < my_tiles) ltile = tile_k(lk);
+            }
+        };
+        if (PREFETCH && my_tiles > 0) load_next(cur);
+        int s = 0;
+        uint32_t upar = 0;                // parity of the current use of stage s
+        bool reuse = false;               // stage s held an earlier step
+        for (int k = 0; k < my_tiles; ++k) {
+            for (int kc = 0; kc < nk; ++kc) {
+                if (!PREFETCH)
+                    load_next(cur);
+                else if (lk < my_tiles)
+                    load_next(nxt);
+                if (reuse && !mbar_wait(&empty[s], upar ^ 1, abort_flag)) {
+                    give_up();
+                    k = my_tiles;
+                    break;
+                }
+                store_step<CO, BF16>(cur, smem + s * C::STAGE, p);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&full[s]);
+                if (PREFETCH) cur = nxt;
+                if (++s == NS) {
+                    s = 0;
+                    upar ^= 1;
+                    reuse = true;
                 }
             }
-            __syncthreads();
-            for (int e = tid; e < BT * 16; e += THREADS) {
-                const int b = e >> 4, oo = e & 15;
-                const int o = o0 + ob + oo;
-                if (b0 + b >= B || o >= Co) continue;
-                float out[8];
+        }
+    } else if (warp == MMA_WARP) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            int s = 0;
+            uint32_t upar = 0;
+            bool ok = true;
+            for (int k = 0; k < my_tiles && ok; ++k) {
+                const int a = k % NACC;
+                const int v = k / NACC;
+                if (v > 0 && !mbar_wait(&acc_empty[a], (uint32_t)((v - 1) & 1), abort_flag)) {
+                    give_up();
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t dacc = tmem + a * C::ACC_COLS;
+                for (int kc = 0; kc < nk; ++kc) {
+                    if (!mbar_wait(&full[s], upar, abort_flag)) {
+                        give_up();
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a0 = smem_u32(smem + s * C::STAGE);
+                    const uint32_t bq = a0 + MODES * C::SPLITS * C::A_TILE;
+#pragma unroll
+                    for (int jl = 0; jl < MODES; ++jl) {
+                        const uint32_t d = dacc + jl * C::N;
+                        if constexpr (BF16) {
+                            mma_bf16(d, smem_desc(a0 + jl * C::A_TILE), smem_desc(bq + jl * C::B_TILE), C::IDESC,
+                                     kc > 0);
+                        } else {
+                            const uint64_t ahi = smem_desc(a0 + (jl * 2) * C::A_TILE);
+                            const uint64_t alo = smem_desc(a0 + (jl * 2 + 1) * C::A_TILE);
+                            const uint64_t bhi = smem_desc(bq + (jl * 2) * C::B_TILE);
+                            const uint64_t blo = smem_desc(bq + (jl * 2 + 1) * C::B_TILE);
+                            mma_tf32(d, ahi, bhi, C::IDESC, kc > 0);
+                            mma_tf32(d, ahi, blo, C::IDESC, 1);
+                            mma_tf32(d, alo, bhi, C::IDESC, 1);
+                        }
+                    }
+                    mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                    if (++s == NS) {
+                        s = 0;
+                        upar ^= 1;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[a]);   // the tile's accumulators are complete
+            }
+            // drain: every MMA issued so far has finished once this commit lands (also after an
+            // abort, so the tensor memory is never freed under a running MMA)
+            mma_commit(drain);
+            if (!mbar_wait(drain, 0, nullptr)) give_up();
+        }
+    } else {
+        // ------------------------------ epilogue (warps 0..3) ------------------------------
+        const int qd = warp;                   // tensor-memory lane quadrant
+        const bool im = lane >= 16;            // this lane holds the Xi row of its batch entry
+        const int bl = qd * 16 + (lane & 15);  // batch entry within the tile
+        for (int k = 0; k < my_tiles; ++k) {
+            const int a = k % NACC;
+            if (!mbar_wait(&acc_full[a], (uint32_t)((k / NACC) & 1), abort_flag)) {
+                give_up();
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const Tile tl = tile_k(k);
+            const uint32_t tbase = tmem + ((uint32_t)(qd * 32) << 16) + a * C::ACC_COLS;
+            const bool bok = tl.b0 + bl < B;
+            for (int cb = 0; cb < CO; cb += 8) {
+                float P[MODES][8], Qv[MODES][8];
 #pragma unroll
                 for (int jl = 0; jl < MODES; ++jl) {
-                    const float* top = dump + ((size_t)jl * M + b) * C::DUMP_PITCH;
-                    const float* bot = dump + ((size_t)jl * M + BT + b) * C::DUMP_PITCH;
-                    out[2 * jl] = top[oo] - bot[16 + oo];      // Xr Wr - Xi Wi
-                    out[2 * jl + 1] = top[16 + oo] + bot[oo];  // Xr Wi + Xi Wr
+                    tmem_ld8(tbase + jl * C::N + cb, P[jl]);
+                    tmem_ld8(tbase + jl * C::N + CO + cb, Qv[jl]);
                 }
-                float4* dst = reinterpret_cast<float4*>(Yq + ((int64_t)(b0 + b) * Co + o) * 8 + 4 * h);
-                dst[0] = make_float4(out[0], out[1], out[2], out[3]);
-                dst[1] = make_float4(out[4], out[5], out[6], out[7]);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (cb + 8 >= CO) {
+                    // accumulators read: the next tile using this buffer may start
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    mbar_arrive(&acc_empty[a]);
+                }
+                // re lanes finish columns 0..3 of this group, im lanes columns 4..7
+                float out[4][2 * MODES];
+#pragma unroll
+                for (int jl = 0; jl < MODES; ++jl) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const float sp = im ? P[jl][c] : P[jl][4 + c];
+                        const float sq = im ? Qv[jl][c] : Qv[jl][4 + c];
+                        const float rp = __shfl_xor_sync(0xffffffffu, sp, 16);
+                        const float rq = __shfl_xor_sync(0xffffffffu, sq, 16);
+                        if (!im) {  // own Xr row: P = Xr Wr, Q = Xr Wi; partner: Xi Wr, Xi Wi
+                            out[c][2 * jl] = P[jl][c] - rq;
+                            out[c][2 * jl + 1] = Qv[jl][c] + rp;
+                        } else {    // own Xi row; partner: Xr Wr, Xr Wi of columns 4..7
+                            out[c][2 * jl] = rp - Qv[jl][4 + c];
+                            out[c][2 * jl + 1] = rq + P[jl][4 + c];
+                        }
+                    }
+                }
+                if (bok) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int o = tl.o0 + cb + (im ? 4 : 0) + c;
+                        if (o >= Co) continue;
+                        float4* dst = reinterpret_cast<float4*>(tl.Yq + ((int64_t)(tl.b0 + bl) * Co + o) * 8 + 4 * tl.h);
+                        dst[0] = make_float4(out[c][0], out[c][1], out[c][2], out[c][3]);
+                        dst[1] = make_float4(out[c][4], out[c][5], out[c][6], out[c][7]);
+                    }
+                }
             }
-            __syncthreads();
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -51,6 +51,7 @@ constexpr int kMaxSlabRanks = 64;
 struct Plan {
     nop_spectral_desc d{};
     int device = 0;
+    int sm_count = 148;                // multiprocessors of `device` (persistent grids)
     bool fast = false;
     FastKind fast_kind = FastKind::None;
     int64_t modes_total = 1;           // prod(kept)
