@@ -437,7 +437,7 @@ cudaError_t launch_mix_tc(const Plan& p, const BlockMap& bm, const float2* X, co
     if (err != cudaSuccess) return err;
     int* status = device_status_ptr(p.device);
     if (!status) return cudaErrorInvalidSymbol;
-    const int64_t tiles = 2 * bm.local * ceil_div(p.d.batch, tc::BT) * ceil_div(Co, CO);
+    const int64_t tiles = 2 * bm.local * ceil_div(p.d.batch, tc::BT) * ceil_div(Co, CO);  // 2 mode halves per block
     if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;  // tile indices are 32-bit
     const unsigned grid = (unsigned)(tiles < p.sm_count ? tiles : p.sm_count);  // persistent, one CTA per SM
     tc::k_mix_tc<CO, BF16><<<grid, tc::THREADS, C::SMEM, s>>>(X, W, wq, Y, (int)p.d.batch, Ci, Co, (int)bm.local,

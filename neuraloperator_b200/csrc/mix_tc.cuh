@@ -164,6 +164,19 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32-byte global load / store (one sector per request)
+__device__ __forceinline__ void ldg32B(const void* p, float4& a, float4& b) {
+    asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(a.x), "=f"(a.y), "=f"(a.z), "=f"(a.w), "=f"(b.x), "=f"(b.y), "=f"(b.z), "=f"(b.w)
+                 : "l"(p));
+}
+
+__device__ __forceinline__ void stg32B(void* p, const float4& a, const float4& b) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(a.x), "f"(a.y), "f"(a.z),
+                 "f"(a.w), "f"(b.x), "f"(b.y), "f"(b.z), "f"(b.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
@@ -185,18 +198,20 @@ struct Problem {
     int B, Ci, Co;
     int local;  // local mode blocks (< 2^31; the host checks the tile count fits an int)
     int qpl, qtot, qbeg;
-    int bt;
+    int bt, ot;  // batch tiles, output tiles
 };
 
-// decode of tile t (done once per tile; 32-bit divisions)
+// decode of tile t (done once per tile; 32-bit divisions).  Order: mode half fastest, then output
+// tile, local mode block, batch tile -- the tiles that read the same X run on neighbouring CTAs at
+// the same time, so X comes from L2 after its first read.
 __device__ __forceinline__ Tile tile_at(const Problem& pr, int t, int co_tile) {
     Tile r;
     r.h = t & 1;
     int rest = t >> 1;
+    r.o0 = (rest % pr.ot) * co_tile;
+    rest /= pr.ot;
     const int q = rest % pr.local;
-    rest /= pr.local;
-    r.b0 = (rest % pr.bt) * BT;
-    r.o0 = (rest / pr.bt) * co_tile;
+    r.b0 = (rest / pr.local) * BT;
     r.Xq = pr.X + (int64_t)q * pr.B * pr.Ci * 8;
     // local mode block q -> weight block (identity unless plane-mode blocks are split across ranks)
     r.Wq = pr.Wp + (int64_t)((q / pr.qpl) * pr.qtot + pr.qbeg + q % pr.qpl) * pr.wq;
@@ -223,9 +238,11 @@ __device__ __forceinline__ void load_step(Step<BF16>& st, const Problem& pr, con
 #pragma unroll
         for (int c = 0; c < KH; ++c) {
             const bool ok = bok && k0 + kh * KH + c < pr.Ci;
-            const float4* s4 = reinterpret_cast<const float4*>(src + c * 8);
-            st.v[2 * c] = ok ? __ldg(s4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            st.v[2 * c + 1] = ok ? __ldg(s4 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ok) {
+                ldg32B(src + c * 8, st.v[2 * c], st.v[2 * c + 1]);
+            } else {
+                st.v[2 * c] = st.v[2 * c + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
     } else if (p < 128 + 2 * CO) {
         const int u = p - 128;
@@ -315,21 +332,20 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    Problem pr{X, Wp, wq, Y, B, Ci, Co, local, qpl, qtot, qbeg, (B + BT - 1) / BT};
-    const int ot = (Co + CO - 1) / CO;
-    const int tiles = 2 * local * pr.bt * ot;
+    Problem pr{X, Wp, wq, Y, B, Ci, Co, local, qpl, qtot, qbeg, (B + BT - 1) / BT, (Co + CO - 1) / CO};
+    const int tiles = 2 * local * pr.bt * pr.ot;
     const int my_tiles = tiles > (int)blockIdx.x ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int nk = (Ci + C::KS - 1) / C::KS;
     auto tile_k = [&](int k) { return tile_at(pr, (int)blockIdx.x + k * (int)gridDim.x, CO); };
 
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
-            mbar_init(&full[i], PROD_THREADS);
+            mbar_init(&full[i], PROD_WARPS);  // one arrival per producer warp
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 32 * EPI_WARPS);
+            mbar_init(&acc_empty[i], EPI_WARPS);
         }
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -354,8 +370,8 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
     if (warp >= EPI_WARPS && warp < MMA_WARP) {
         // ------------------------------ producers ------------------------------
         const int p = tid - 32 * EPI_WARPS;
-        // tf32: the next step's loads are issued before the current step is stored (two register
-        // sets); bf16 units are twice as large, so they load and store one step at a time
+        // tf32: the next step's loads are in flight while the current step is stored (two register
+        // sets; a third spills); bf16 units are twice as large, so they load and store one step at a time
         constexpr bool PREFETCH = !BF16;
         Step<BF16> cur, nxt;
         int lk = 0, lkc = 0;              // tile and K step of the next load
@@ -385,7 +401,8 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
                 }
                 store_step<CO, BF16>(cur, smem + s * C::STAGE, p);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&full[s]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
                 if (PREFETCH) cur = nxt;
                 if (++s == NS) {
                     s = 0;
@@ -475,7 +492,8 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
                 if (cb + 8 >= CO) {
                     // accumulators read: the next tile using this buffer may start
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                    mbar_arrive(&acc_empty[a]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[a]);
                 }
                 // re lanes finish columns 0..3 of this group, im lanes columns 4..7
                 float out[4][2 * MODES];
@@ -501,9 +519,9 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
                     for (int c = 0; c < 4; ++c) {
                         const int o = tl.o0 + cb + (im ? 4 : 0) + c;
                         if (o >= Co) continue;
-                        float4* dst = reinterpret_cast<float4*>(tl.Yq + ((int64_t)(tl.b0 + bl) * Co + o) * 8 + 4 * tl.h);
-                        dst[0] = make_float4(out[c][0], out[c][1], out[c][2], out[c][3]);
-                        dst[1] = make_float4(out[c][4], out[c][5], out[c][6], out[c][7]);
+                        stg32B(tl.Yq + ((int64_t)(tl.b0 + bl) * Co + o) * 8 + 4 * tl.h,
+                               make_float4(out[c][0], out[c][1], out[c][2], out[c][3]),
+                               make_float4(out[c][4], out[c][5], out[c][6], out[c][7]));
                     }
                 }
             }
