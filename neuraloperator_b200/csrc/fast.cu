@@ -501,6 +501,18 @@ int32_t mix_stage(const Plan& p, const float2* Xh, const char* packed, float2* Y
     return NOP_OK;
 }
 
+// planes per CTA of the 256 x 256 inverse plane kernel: two, so each CTA prefetches one plane's
+// spectrum across planes, once the grid still fills the 2 CTAs x SMs slots several times over
+// (measured on B200 with 4096 planes: 1 -> 307 us, 2 -> 301 us, 3 -> 322 us, 4 -> 302 us)
+inline int planes_per_cta(const Plan& p, int64_t planes) {
+    return planes >= 8 * (int64_t)p.sm_count ? 2 : 1;
+}
+
+inline unsigned plane_ctas(const Plan& p, int64_t planes) {
+    const int ppc = planes_per_cta(p, planes);
+    return (unsigned)((planes + ppc - 1) / ppc);
+}
+
 // kept-mode specialisations of the 256 x 256 plane kernels (see plane256.cuh)
 template <int KX, int MY>
 bool p256_applies(const nop_spectral_desc& d) {
@@ -536,8 +548,9 @@ int32_t run_p256(const Plan& p, const void* x, const char* packed, const float* 
     int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
     if (rc != NOP_OK) return rc;
     p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, 1};
-    p256::k_inv<KX, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Yh, static_cast<float*>(y), tt->f_table,
-                                                                      (float)d.inv_scale, Lout * 8, ep);
+    p256::k_inv<KX, MY><<<plane_ctas(p, Lout), p256::THREADS, smem, s>>>(Yh, static_cast<float*>(y), tt->f_table,
+                                                                           (float)d.inv_scale, Lout * 8, ep, Lout,
+                                                                           planes_per_cta(p, Lout));
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p256 inv launch");
     launch_mark(s);
     return NOP_OK;
@@ -654,8 +667,9 @@ int32_t run_vol3d(const Plan& p, const void* x, const char* packed, const float*
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d axis inv launch");
     launch_mark(s);
     p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, Nx};
-    p256::k_inv<KZ, MY><<<(unsigned)Lout, p256::THREADS, smem, s>>>(Pb, static_cast<float*>(y), tw256,
-                                                                      (float)d.inv_scale, Lout * 8, ep);
+    p256::k_inv<KZ, MY><<<plane_ctas(p, Lout), p256::THREADS, smem, s>>>(Pb, static_cast<float*>(y), tw256,
+                                                                           (float)d.inv_scale, Lout * 8, ep, Lout,
+                                                                           planes_per_cta(p, Lout));
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "vol3d plane inv launch");
     launch_mark(s);
     return NOP_OK;
@@ -711,8 +725,8 @@ int32_t slab_planes_inv_t(const Plan& p, const float2* recv2, const float* bias,
     if ((err = ensure_smem_attr(p256::k_inv<KZ, MY>, slot, p.device)) != cudaSuccess)
         return cuda_fail(err, "cudaFuncSetAttribute(p256 inv)");
     p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, p.slab_nx};
-    p256::k_inv<KZ, MY><<<(unsigned)L, p256::THREADS, p256::smem_bytes<KZ, MY>(), s>>>(
-        recv2, y, p.table(256)->f_table, (float)d.inv_scale, L * 8, ep);
+    p256::k_inv<KZ, MY><<<plane_ctas(p, L), p256::THREADS, p256::smem_bytes<KZ, MY>(), s>>>(
+        recv2, y, p.table(256)->f_table, (float)d.inv_scale, L * 8, ep, L, planes_per_cta(p, L));
     if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "slab plane inv launch");
     launch_mark(s);
     return NOP_OK;

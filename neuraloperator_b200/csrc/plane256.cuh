@@ -4,7 +4,11 @@
 //   * forward: the last radix-16 pass of every line computes only the outputs that are kept (and
 //     their Hermitian partners); the two packed real rows are separated with warp shuffles;
 //   * inverse: the first radix-16 pass reads only the non-zero (kept) inputs;
-//   * per-lane pass-2 twiddles come from a padded per-lane table (two per 16-byte load).
+//   * pass-2 twiddles: the forward kernel keeps its lane's 16 in registers; the inverse reads them
+//     from a padded per-lane table (two per 16-byte load);
+//   * the forward kernel issues its first row loads before it builds the twiddle tables; an inverse
+//     CTA transforms `ppc` consecutive planes, with the kept spectrum of its next plane in flight
+//     while it finishes the current one (the first one's while the tables are built).
 // Lane t of a 16-lane group owns elements t + 16 r (first pass) and outputs t + 16 r (last pass).
 #pragma once
 
@@ -82,6 +86,13 @@ __device__ __forceinline__ void pass2_twiddle(float2* v, const float2* twp_lane)
     }
 }
 
+// the same with the lane's 16 twiddles held in registers
+template <bool INV>
+__device__ __forceinline__ void pass2_twiddle_reg(float2* v, const float2* w) {
+#pragma unroll
+    for (int r = 1; r < 16; ++r) v[r] = fft::cmul(v[r], INV ? w[r] : make_float2(w[r].x, -w[r].y));
+}
+
 __device__ __forceinline__ void init_tables(float2* tw, float2* twp, const float2* twg) {
     for (int i = threadIdx.x; i < N; i += THREADS) tw[i] = twg[i];
     __syncthreads();
@@ -109,19 +120,22 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
     const int64_t plane = blockIdx.x;
     const int g = threadIdx.x / G;
     const int t = threadIdx.x % G;
-    init_tables(tw, twp, twg);
-    const float2* twl = twp + t * TWP;
     const float* xp = x + plane * (int64_t)N * N;
     float2* buf = X + g * LINE;
 
     // ---- rows: pairs (2p, 2p+1) as one complex line, kept bins to the column store ----
-    // The next pair's 32 loads are issued before the current pair is transformed.
+    // The next pair's 32 loads are issued before the current pair is transformed; the first pair's
+    // loads are in flight while the twiddle tables are built.
     float2 nxt[16];
     {
         const float* ra = xp + (int64_t)(2 * g) * N + t;
 #pragma unroll
         for (int r = 0; r < 16; ++r) nxt[r] = make_float2(__ldg(ra + 16 * r), __ldg(ra + N + 16 * r));
     }
+    init_tables(tw, twp, twg);
+    float2 twr[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) twr[r] = twp[t * TWP + r];
 #pragma unroll 1
     for (int base = 0; base < N / 2; base += GROUPS) {
         const int pr = base + g;
@@ -141,7 +155,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
         __syncwarp();
 #pragma unroll
         for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
-        pass2_twiddle<false>(v, twl);
+        pass2_twiddle_reg<false>(v, twr);
         fft::dft16_m<false, 0xFFFFu, OUT_ROW>(v);
         // separate the two real rows: A[k] = (Z_k + conj Z_{N-k}) / 2, B[k] = (Z_k - conj Z_{N-k}) / 2i
 #pragma unroll
@@ -181,7 +195,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
         __syncwarp();
 #pragma unroll
         for (int r = 0; r < 16; ++r) v[r] = col[t + 17 * r];
-        pass2_twiddle<false>(v, twl);
+        pass2_twiddle_reg<false>(v, twr);
         fft::dft16_m<false, 0xFFFFu, OUT_COL>(v);
         if (active) {
 #pragma unroll
@@ -218,129 +232,147 @@ struct Epi {
 template <int KX, int MY>
 __global__ void __launch_bounds__(THREADS, 2)
 k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __restrict__ twg, float scale,
-      int64_t blk_stride, Epi ep) {
+      int64_t blk_stride, Epi ep, int64_t L, int ppc) {
     constexpr unsigned IN_COL = col_mask(MY);
     constexpr unsigned IN_ROW = row_in_mask(KX);
+    constexpr int Mt = MY * KX;
+    constexpr int Q = (Mt + 7) / 8;
+    constexpr int NPF = (Q * 4 + THREADS - 1) / THREADS;  // 16-byte pieces of the spectrum per thread
     extern __shared__ float2 smem[];
     float2* tw = smem;
     float2* twp = tw + N;
     float2* T = twp + G * TWP;
     float2* X = smem + x_offset<KX>();
-    const int64_t plane = blockIdx.x;
     const int g = threadIdx.x / G;
     const int t = threadIdx.x % G;
+    const int64_t first = (int64_t)blockIdx.x * ppc;
+    const int64_t last = first + ppc < L ? first + ppc : L;  // planes [first, last)
     float2* stage = X;
-    {
-        constexpr int Mt = MY * KX;
-        constexpr int Q = (Mt + 7) / 8;
-        const float2* ip = in + plane * 8;
-        for (int e = threadIdx.x; e < Q * 4; e += THREADS) {
-            const int q = e >> 2, m = 8 * q + 2 * (e & 3);
-            const float4 v = __ldg(reinterpret_cast<const float4*>(ip + q * blk_stride + 2 * (e & 3)));
-            if (m < Mt) stage[m] = make_float2(v.x, v.y);
-            if (m + 1 < Mt) stage[m + 1] = make_float2(v.z, v.w);
+    float4 pf[NPF];  // the next plane's kept spectrum, in flight
+    auto fetch = [&](int64_t pl) {
+        const float2* ip = in + pl * 8;
+#pragma unroll
+        for (int k = 0; k < NPF; ++k) {
+            const int e = threadIdx.x + k * THREADS;
+            if (e < Q * 4) pf[k] = __ldg(reinterpret_cast<const float4*>(ip + (e >> 2) * blk_stride + 2 * (e & 3)));
         }
-    }
-    init_tables(tw, twp, twg);  // includes the barrier that publishes `stage`
+    };
+    auto put = [&]() {
+#pragma unroll
+        for (int k = 0; k < NPF; ++k) {
+            const int e = threadIdx.x + k * THREADS;
+            const int m = 8 * (e >> 2) + 2 * (e & 3);
+            if (e < Q * 4 && m < Mt) stage[m] = make_float2(pf[k].x, pf[k].y);
+            if (e < Q * 4 && m + 1 < Mt) stage[m + 1] = make_float2(pf[k].z, pf[k].w);
+        }
+    };
+    if (first < last) fetch(first);  // overlaps the table set-up
+    init_tables(tw, twp, twg);
     const float2* twl = twp + t * TWP;
-
-    // ---- columns: kept bins -> full y lines ----
     const int warp_first_group = (threadIdx.x & ~31) / G;
-#pragma unroll 1
-    for (int base = 0; base < KX; base += GROUPS) {
-        if (base + warp_first_group >= KX) break;
-        const int c = base + g;
-        const bool active = c < KX;
-        float2* col = T + (active ? c : 0) * TPITCH;
-        float2 v[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            if (!((IN_COL >> r) & 1)) continue;
-            const int m = (t + 16 * r + MY / 2) & (N - 1);
-            v[r] = active ? stage[m * KX + c] : make_float2(0.f, 0.f);
-        }
-        fft::dft16_m<true, IN_COL, 0xFFFFu>(v);
-        if (active) {
-#pragma unroll
-            for (int r = 0; r < 16; ++r) col[17 * t + r] = v[r];
-        }
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = col[t + 17 * r];
-        pass2_twiddle<true>(v, twl);
-        fft::dft16<true>(v);
-        __syncwarp();
-        if (active) {
-#pragma unroll
-            for (int r = 0; r < 16; ++r) col[t + 17 * r] = v[r];
-        }
-    }
-    __syncthreads();
-
-    // ---- rows: Z = A + iB (k < KX), conj(A) + i conj(B) at 256 - k; inverse; epilogue ----
-    const float bias = ep.bias ? ep.bias[(plane / ep.chan_div) % ep.C] : 0.f;
-    float* yp = y + plane * (int64_t)N * N;
-    const float* ap = ep.addend ? ep.addend + plane * (int64_t)N * N : nullptr;
     float2* buf = X + g * LINE;
 #pragma unroll 1
-    for (int base = 0; base < N / 2; base += GROUPS) {
-        const int pr = base + g;
-        const int na = 2 * pr, nb = 2 * pr + 1;
-        float2 v[16];
+    for (int64_t plane = first; plane < last; ++plane) {
+        put();
+        __syncthreads();
+        // ---- columns: kept bins -> full y lines ----
+#pragma unroll 1
+        for (int base = 0; base < KX; base += GROUPS) {
+            if (base + warp_first_group >= KX) break;
+            const int c = base + g;
+            const bool active = c < KX;
+            float2* col = T + (active ? c : 0) * TPITCH;
+            float2 v[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            if (!((IN_ROW >> r) & 1)) continue;
-            const int i = t + 16 * r;
-            if (16 * r < KX) {  // direct bins
-                float2 z = make_float2(0.f, 0.f);
-                if (16 * r + 15 < KX || i < KX) {
-                    float2 A = T[i * TPITCH + ipad(na)];
-                    float2 B = T[i * TPITCH + ipad(nb)];
-                    if (i == 0) {
-                        A.y = 0.f;
-                        B.y = 0.f;
+            for (int r = 0; r < 16; ++r) {
+                if (!((IN_COL >> r) & 1)) continue;
+                const int m = (t + 16 * r + MY / 2) & (N - 1);
+                v[r] = active ? stage[m * KX + c] : make_float2(0.f, 0.f);
+            }
+            fft::dft16_m<true, IN_COL, 0xFFFFu>(v);
+            if (active) {
+#pragma unroll
+                for (int r = 0; r < 16; ++r) col[17 * t + r] = v[r];
+            }
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < 16; ++r) v[r] = col[t + 17 * r];
+            pass2_twiddle<true>(v, twl);
+            fft::dft16<true>(v);
+            __syncwarp();
+            if (active) {
+#pragma unroll
+                for (int r = 0; r < 16; ++r) col[t + 17 * r] = v[r];
+            }
+        }
+        __syncthreads();
+        if (plane + 1 < last) fetch(plane + 1);
+
+        // ---- rows: Z = A + iB (k < KX), conj(A) + i conj(B) at 256 - k; inverse; epilogue ----
+        const float bias = ep.bias ? ep.bias[(plane / ep.chan_div) % ep.C] : 0.f;
+        float* yp = y + plane * (int64_t)N * N;
+        const float* ap = ep.addend ? ep.addend + plane * (int64_t)N * N : nullptr;
+#pragma unroll 1
+        for (int base = 0; base < N / 2; base += GROUPS) {
+            const int pr = base + g;
+            const int na = 2 * pr, nb = 2 * pr + 1;
+            float2 v[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                if (!((IN_ROW >> r) & 1)) continue;
+                const int i = t + 16 * r;
+                if (16 * r < KX) {  // direct bins
+                    float2 z = make_float2(0.f, 0.f);
+                    if (16 * r + 15 < KX || i < KX) {
+                        float2 A = T[i * TPITCH + ipad(na)];
+                        float2 B = T[i * TPITCH + ipad(nb)];
+                        if (i == 0) {
+                            A.y = 0.f;
+                            B.y = 0.f;
+                        }
+                        z = make_float2(A.x - B.y, A.y + B.x);
                     }
-                    z = make_float2(A.x - B.y, A.y + B.x);
+                    v[r] = z;
+                } else {  // mirrored bins k = 256 - i
+                    const int k = N - i;
+                    float2 z = make_float2(0.f, 0.f);
+                    if (k < KX) {
+                        const float2 A = T[k * TPITCH + ipad(na)];
+                        const float2 B = T[k * TPITCH + ipad(nb)];
+                        z = make_float2(A.x + B.y, B.x - A.y);
+                    }
+                    v[r] = z;
                 }
-                v[r] = z;
-            } else {  // mirrored bins k = 256 - i
-                const int k = N - i;
-                float2 z = make_float2(0.f, 0.f);
-                if (k < KX) {
-                    const float2 A = T[k * TPITCH + ipad(na)];
-                    const float2 B = T[k * TPITCH + ipad(nb)];
-                    z = make_float2(A.x + B.y, B.x - A.y);
+            }
+            fft::dft16_m<true, IN_ROW, 0xFFFFu>(v);
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < 16; r += 2)
+                *reinterpret_cast<float4*>(buf + 18 * t + r) = make_float4(v[r].x, v[r].y, v[r + 1].x, v[r + 1].y);
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
+            pass2_twiddle<true>(v, twl);
+            fft::dft16<true>(v);
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                const int n = t + 16 * r;
+                float va = v[r].x * scale + bias;
+                float vb = v[r].y * scale + bias;
+                if (ap) {
+                    va += __ldg(ap + (int64_t)na * N + n);
+                    vb += __ldg(ap + (int64_t)nb * N + n);
                 }
-                v[r] = z;
+                if (ep.apply_gelu) {
+                    va = gelu_erf(va);
+                    vb = gelu_erf(vb);
+                }
+                yp[(int64_t)na * N + n] = va;
+                yp[(int64_t)nb * N + n] = vb;
             }
+            __syncwarp();  // buf is rewritten by the next iteration
         }
-        fft::dft16_m<true, IN_ROW, 0xFFFFu>(v);
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 16; r += 2)
-            *reinterpret_cast<float4*>(buf + 18 * t + r) = make_float4(v[r].x, v[r].y, v[r + 1].x, v[r + 1].y);
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
-        pass2_twiddle<true>(v, twl);
-        fft::dft16<true>(v);
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int n = t + 16 * r;
-            float va = v[r].x * scale + bias;
-            float vb = v[r].y * scale + bias;
-            if (ap) {
-                va += __ldg(ap + (int64_t)na * N + n);
-                vb += __ldg(ap + (int64_t)nb * N + n);
-            }
-            if (ep.apply_gelu) {
-                va = gelu_erf(va);
-                vb = gelu_erf(vb);
-            }
-            yp[(int64_t)na * N + n] = va;
-            yp[(int64_t)nb * N + n] = vb;
-        }
-        __syncwarp();  // buf is rewritten by the next iteration
+        __syncthreads();  // the next plane's spectrum goes into the exchange lines' region
     }
 }
 
