@@ -42,10 +42,11 @@ HBM_FALLBACK_GBS = 6533.2  # measured copy bandwidth on this pool (MEASURED_PEAK
 # DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures summarised under
 # profiles/ (small-batch capture scaled to the full batch; traffic grows with the number of planes)
 TRAFFIC = {
-    # profiles/plane_kernels_c2_b8_full.md: batch-8 capture x 8 (reads + writes during the kernel)
-    ("c2", "plane_inv"): 8 * (8.697344e6 + 79.776e6),
-    ("c2", "plane_fwd"): 8 * (134.24e6 + 4.466176e6),
-    ("c2", "contraction"): None,
+    # profiles/spectral_block_c2_b8_full.md: batch-8 capture x 8 (reads + writes during the kernel; the
+    # plane kernels' traffic grows with the number of planes)
+    ("c2", "plane_inv"): 8 * (8.698368e6 + 80.557824e6),
+    ("c2", "plane_fwd"): 8 * (134.238976e6 + 4.504576e6),
+    ("c2", "contraction"): None,  # the weight stream does not scale with the batch
 }
 
 # name -> (description, batch, Ci, Co, grid, n_modes, factorization)
