@@ -186,6 +186,124 @@ def barrier(world: int):
         dist.barrier()
 
 
+def capture_graph(fn, stream):
+    """One call of `fn` captured into a CUDA graph on a side stream (plans and packed weights exist
+    from the warm-up, so capture allocates only workspace from the graph's pool)."""
+    try:
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side), torch.no_grad():
+            fn()  # one eager call on the capture stream
+            with torch.cuda.graph(g, stream=side):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        return g, "cuda_graph"
+    except Exception as exc:  # noqa: BLE001
+        print(f"graph capture failed, timing eager launches: {exc}", file=sys.stderr)
+        torch.cuda.synchronize()
+        return None, "eager"
+
+
+# full-model configs (BASELINE.json configs 0, 2, 3, 4): class, n_modes, hidden, in, out, grid, batch, kwargs
+MODELS = {
+    "c1": ("fno2d_darcy", "FNO", (16, 16), 32, 1, 1, (128, 128), 16, {}),
+    "c3": ("fno1d_burgers", "FNO", (16,), 64, 1, 1, (8192,), 256, {}),
+    "c4": ("tfno2d_ns", "TFNO", (64, 64), 64, 1, 1, (512, 512), 32,
+           dict(factorization="tucker", implementation="factorized", rank=0.1)),
+    "c5": ("fno3d", "FNO", (32, 32, 32), 32, 3, 3, (256, 256, 256), 8, {}),
+}
+
+
+def run_model(args, world, rank, local):
+    """FNO / TFNO forward (grid embedding, lifting, 4 FNO blocks, projection) at the config's size;
+    the spectral layers are also timed alone to give their share and their HBM roofline fraction."""
+    import neuraloperator_b200 as nb
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if args.config not in MODELS:
+        raise SystemExit(f"--model fno: no full-model config named {args.config} (have {sorted(MODELS)})")
+    desc, cls, modes, hidden, cin, cout, grid, batch, kw = MODELS[args.config]
+    if args.batch is not None:
+        batch = args.batch
+    if args.precision == "bf16":
+        kw = dict(kw, contraction_precision="bf16")
+    torch.manual_seed(0)
+    model = getattr(nb, cls)(n_modes=modes, in_channels=cin, out_channels=cout, hidden_channels=hidden,
+                             n_layers=4, **kw).to(dev).eval()
+    g = torch.Generator(device="cpu").manual_seed(0)
+    x = torch.randn((batch, cin, *grid), generator=g).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    steps, warm = args.steps, args.warmup
+    with torch.no_grad():
+        for _ in range(warm):
+            y = model(x)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            y = model(x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_eager = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        graph, launch = None, "eager"
+        if not args.no_graph and ms_eager < 5.0:
+            graph, launch = capture_graph(lambda: model(x), stream)
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            e0.record(stream)
+            for _ in range(steps):
+                if graph is not None:
+                    graph.replay()
+                else:
+                    y = model(x)
+            e1.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        del graph
+        # the spectral layers alone (same shapes as inside the blocks; the fused skip + GELU included)
+        conv = model.fno_blocks.convs[0]
+        h = torch.randn((batch, hidden, *grid), generator=g).to(dev)
+        skip = torch.randn((batch, hidden, *grid), generator=g).to(dev)
+        for _ in range(3):
+            conv(h, addend=skip, apply_gelu=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            conv(h, addend=skip, apply_gelu=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        spec_ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    if rank != 0:
+        return
+    hbm, peak_src = peaks()
+    p = math.prod(grid)
+    w = sum(t.numel() * t.element_size() for t in conv.weight.parameters())
+    spec_bytes = 3 * batch * hidden * p * 4 + w + hidden * 4  # x, skip, y + weights + bias
+    layers = model.n_layers
+    line = {
+        "metric": METRIC, "value": world * batch / (ms / 1e3), "unit": "samples/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if args.precision == "fp32" else "f32 (bf16 contraction)",
+        "data": "synthetic (seeded N(0,1) input, seeded random-init weights; no dataset)",
+        "config": {"workload": desc, "model": cls, "global_batch": batch * world, "per_gpu_batch": batch,
+                   "grid": list(grid), "hidden_channels": hidden, "n_modes": list(modes), "n_layers": layers,
+                   "in_channels": cin, "out_channels": cout, "parallelism": f"dp{world}" if world > 1 else "single",
+                   "launch": launch, "ms_per_step_eager": ms_eager, **{k: v for k, v in kw.items()}},
+        "spectral": {"ms_per_layer": spec_ms, "share": layers * spec_ms / ms,
+                     "roofline": {"bound": "hbm", "achieved": spec_bytes / (spec_ms / 1e3) / 1e9, "peak": hbm,
+                                  "unit": "GB/s", "frac": spec_bytes / (spec_ms / 1e3) / 1e9 / hbm,
+                                  "bytes_alg_per_layer": spec_bytes, "peak_source": peak_src,
+                                  "definition": "|x| + |skip| + |y| + |W| + |bias| per fused layer"}},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline(cfg, seconds=12.0):
     """Oracle (reference torch CPU path) on the host cores, bounded sample of the workload."""
     import oracle
@@ -292,6 +410,7 @@ def run_ours(args, cfg, world, rank, local):
     desc, batch, ci, co, grid, modes, fact = cfg
     conv, x = make_inputs(cfg, dev, seed=0)
     conv.engine = args.engine
+    conv.contraction_precision = args.precision
     stream = torch.cuda.current_stream(dev)
     steps, warm = args.steps, args.warmup
 
@@ -301,28 +420,46 @@ def run_ours(args, cfg, world, rank, local):
         torch.cuda.synchronize()
         geo = conv.geometry(list(grid))
         kind, _, ranks = conv.kernel_operands(geo)
-        desc_c = ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks, engine=args.engine)
+        desc_c = ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks, precision=args.precision,
+                               engine=args.engine)
         plan = ops.get_plan(desc_c, local)
 
-        # ---- device-resident timed region (per-kernel CUDA events on the launching stream) ----
+        # ---- per-kernel device times (CUDA events recorded by the library on the launching stream) ----
         from neuraloperator_b200 import _lib
         nk = plan.launches_per_forward
         marks = [_lib.LaunchEvents(nk) for _ in range(steps)]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier(world)
         torch.cuda.synchronize()
+        e0.record(stream)
+        for k in range(steps):
+            with marks[k]:
+                y = conv(x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_eager = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        per_kernel = [statistics.mean(m.durations_ms()[i] for m in marks) for i in range(nk)]
+
+        # ---- timed region: K forwards replayed from one captured CUDA graph (the same kernels with
+        # the host launch overhead removed); eager launches when capture is off or fails ----
+        graph, launch = None, "eager"
+        if not args.no_graph:
+            graph, launch = capture_graph(lambda: conv(x), stream)
+        barrier(world)
+        torch.cuda.synchronize()
         with ClockSampler(local) as clocks:
             e0.record(stream)
-            for k in range(steps):
-                with marks[k]:
+            for _ in range(steps):
+                if graph is not None:
+                    graph.replay()
+                else:
                     y = conv(x)
             e1.record(stream)
             torch.cuda.synchronize()
         barrier(world)
-        ms = e0.elapsed_time(e1) / steps
-        ms = max_over_ranks(ms, world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
         value = world * batch / (ms / 1e3)
-        per_kernel = [statistics.mean(m.durations_ms()[i] for m in marks) for i in range(nk)]
+        del graph
 
         e2e_how = None
         if args.no_e2e:
@@ -368,12 +505,14 @@ def run_ours(args, cfg, world, rank, local):
     dom = max(kernels, key=lambda k: k["ms"])
     line = {
         "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": steps, "warmup": warm,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.precision == "fp32" else "f32 (bf16 contraction)",
         "data": "synthetic (seeded N(0,1) input, seeded complex weights; no dataset)",
         "config": {"workload": desc, "global_batch": batch * world, "per_gpu_batch": batch, "grid": list(grid),
                    "channels": [ci, co], "n_modes": list(modes), "factorization": fact or "dense",
                    "parallelism": f"dp{world}" if world > 1 else "single", "engine": "fast" if plan.is_fast else
-                   "generic", "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB > 126 MB L2 (no flush needed)"},
+                   "generic", "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB > 126 MB L2 (no flush needed)",
+                   "launch": launch, "ms_per_step_eager": ms_eager},
         "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm, "unit": "GB/s", "frac": dom["frac"],
                      "traffic": TRAFFIC.get((args.config, dom["name"])), "kernel": dom["name"],
                      "bytes_alg_per_launch": dom["bytes_alg"], "ms_per_launch": dom["ms"],
@@ -405,6 +544,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of graph replay")
+    ap.add_argument("--model", choices=["layer", "fno"], default="layer",
+                    help="layer: one SpectralConv (the headline); fno: the whole FNO / TFNO forward")
+    ap.add_argument("--precision", choices=["fp32", "bf16"], default="fp32", help="contraction precision")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -418,7 +561,10 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        run_ours(args, cfg, world, rank, local)
+        if args.model == "fno":
+            run_model(args, world, rank, local)
+        else:
+            run_ours(args, cfg, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -223,6 +223,40 @@ int32_t nop_spectral_forward_static(const nop_spectral_desc* desc, const void* x
                                     int32_t n_weights, const float* bias, const float* addend,
                                     int32_t apply_gelu, void* y, void* stream);
 
+/* ---- fused per-pixel channel MLP (the FNO layers around the spectral block) -------------------
+ * One pass over HBM evaluates, at every spatial point of x [B, Cx, *spatial] (float32):
+ *     u = [x ; grid]                    grid: `grid_dims` coordinate channels lo + i (hi - lo) / N
+ *     h = act_hidden(W1 u + b1)         W1 [Ch, Cx + grid_dims] (Ch = 0: no first layer, h = u)
+ *     y = act_out(W2 h + b2 + g r + gb) W2 [Cy, Ch or Cx + grid_dims]; g, gb [Cy] gate r [B, Cy, *spatial]
+ *     z = W3 y                          W3 [Cz, Cy] (next_channels > 0)
+ * with act = exact GELU where set.  Weights as torch Conv1d weights ([out, in, 1], row-major).
+ * Replaces ChannelMLP.forward (neuralop/layers/channel_mlp.py:82-119), the soft-gating skip
+ * (neuralop/layers/skip_connections.py:53-94), the closing activation of
+ * FNOBlocks.forward_with_postactivation (neuralop/layers/fno_block.py:363-381), the next block's
+ * linear skip (skip_connections.py:96-127) and, for the lifting, GridEmbeddingND
+ * (neuralop/layers/embeddings.py:147-164).  Points per sample must be a multiple of 128 and every
+ * channel count at most 256; x, r, y, z 16-byte aligned. */
+typedef struct nop_pointwise_desc {
+    int32_t abi_version;                 /* NOP_ABI_VERSION                                          */
+    int32_t ndim;                        /* spatial dims, 1..NOP_MAX_DIMS                             */
+    int64_t batch;
+    int64_t spatial[NOP_MAX_DIMS];
+    int32_t in_channels;                 /* Cx                                                       */
+    int32_t grid_dims;                   /* 0 or ndim                                                */
+    int32_t hidden_channels;             /* Ch (0: single layer)                                     */
+    int32_t out_channels;                /* Cy                                                       */
+    int32_t next_channels;               /* Cz (0: no z)                                             */
+    int32_t act_hidden, act_out;         /* 1: exact GELU                                            */
+    int32_t gate, has_b1, has_b2, has_gate_bias;
+    float grid_lo[NOP_MAX_DIMS], grid_hi[NOP_MAX_DIMS];
+} nop_pointwise_desc;
+
+/* Shared memory one CTA of the fused kernel uses for this descriptor (NOP_E_UNSUPPORTED if too much). */
+int32_t nop_pointwise_smem_bytes(const nop_pointwise_desc* desc, size_t* bytes);
+int32_t nop_pointwise_forward(const nop_pointwise_desc* desc, const float* x, const float* w1, const float* b1,
+                              const float* w2, const float* b2, const float* r, const float* g,
+                              const float* gb, const float* w3, float* y, float* z, void* stream);
+
 /* ---- forward from host memory, copies overlapped with the kernels ---------------------------
  * The reference's SpectralConv.forward runs wherever its input lives; a serving caller that holds
  * inputs in host memory would copy the whole batch in, run, and copy the whole batch out, so the

@@ -1,7 +1,9 @@
 """FNO / TFNO: drop-ins for neuralop.models.FNO and TFNO (neuralop/models/fno.py:26-485).
 
 Same constructor arguments and forward: grid embedding -> lifting ChannelMLP -> n_layers x
-FNOBlocks -> projection ChannelMLP.  The spectral blocks run on libnop_b200's CUDA kernels.
+FNOBlocks -> projection ChannelMLP.  The spectral blocks run on libnop_b200's CUDA kernels; with
+the default layer shapes the grid embedding + lifting (which also emits the first block's linear
+skip) and the projection each run as one fused per-pixel kernel (``pointwise.channel_mlp``).
 Options the reference offers outside the FNO default path raise NotImplementedError here:
 ``domain_padding``, ``norm``, ``complex_data`` and ``fno_block_precision`` other than "full".
 """
@@ -10,9 +12,11 @@ from __future__ import annotations
 
 from typing import List, Tuple, Union
 
+import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import pointwise
 from .fno_block import FNOBlocks
 from .layers import ChannelMLP, GridEmbeddingND
 from .spectral_convolution import SpectralConv
@@ -98,8 +102,47 @@ class FNO(nn.Module):
                                      hidden_channels=self.projection_channels, n_layers=2, n_dim=self.n_dim,
                                      non_linearity=non_linearity)
 
+    def _mlp_ok(self, mlp, x, cin, cnext=0, grid=None):
+        """mlp (2 layers, GELU, no dropout) on cin data channels (+ grid channels) fits the fused kernel."""
+        ku = cin + (len(grid) if grid is not None else 0)
+        return (isinstance(mlp, ChannelMLP) and mlp.n_layers == 2 and mlp.dropout is None
+                and mlp.non_linearity is F.gelu and mlp.in_channels == ku
+                and pointwise.supported_dims(x.shape[0], x.shape[2:], cin, mlp.hidden_channels,
+                                             mlp.out_channels, cnext, grid))
+
+    def _fused_forward(self, x):
+        """Lifting (+ grid channels, + block 0's linear skip), fused blocks, projection; None when a
+        layer does not fit the fused kernels (the module path then runs)."""
+        pe = self.positional_embedding
+        if not (x.is_cuda and x.dtype == torch.float32) or (pe is not None and not isinstance(pe, GridEmbeddingND)):
+            return None
+        grid = [tuple(b) for b in pe.grid_boundaries] if pe is not None else None
+        blocks = self.fno_blocks
+        if not (blocks._fusable(0, x, None) and self.resolution_scaling_factor is None):
+            return None
+        cnext = blocks.fno_skips[0].conv.out_channels
+        if not (x.shape[1] == self.in_channels and self._mlp_ok(self.lifting, x, self.in_channels, cnext, grid)
+                and self._mlp_ok(self.projection, x, self.hidden_channels)):
+            return None
+        prof = get_active_profiler()
+        with maybe_profile(prof, "fno/positional_embedding_lifting_skip0", x.device):
+            fc1, fc2 = self.lifting.fcs
+            h, skip = pointwise.channel_mlp(x, fc1.weight, fc1.bias, fc2.weight, fc2.bias, grid=grid,
+                                            act_hidden=True, act_out=False, next_w=blocks.next_skip_weight(0))
+        blocks.set_pending_skip(h, 0, skip)
+        for i in range(self.n_layers):
+            h = blocks(h, i)
+        with maybe_profile(prof, "fno/projection", x.device):
+            fc1, fc2 = self.projection.fcs
+            y, _ = pointwise.channel_mlp(h, fc1.weight, fc1.bias, fc2.weight, fc2.bias, act_hidden=True,
+                                         act_out=False)
+        return y
+
     def forward(self, x, output_shape=None, **kwargs):
         if output_shape is None:
+            fused = self._fused_forward(x)
+            if fused is not None:
+                return fused
             output_shape = [None] * self.n_layers
         elif isinstance(output_shape, tuple):
             output_shape = [None] * (self.n_layers - 1) + [output_shape]

@@ -7,6 +7,11 @@ a ``SpectralConv`` of this package and no output resampling -- the skip add and 
 (a 1x1 conv) is computed first and handed to the kernel as an addend.  Every other
 configuration composes the same operations as the reference around the CUDA spectral block.
 Normalisation layers other than None are not provided (norm=None is the FNO default).
+
+With the default ChannelMLP (two layers, GELU, no dropout) and a soft-gating (or no) channel-MLP
+skip, the rest of the block -- ChannelMLP, soft-gating skip, closing GELU (:363-381) -- and the next
+block's linear skip run as one fused per-pixel kernel (``pointwise.channel_mlp``); the next block
+then takes that skip instead of recomputing it.
 """
 
 from __future__ import annotations
@@ -17,7 +22,8 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .layers import ChannelMLP, skip_connection
+from . import pointwise
+from .layers import ChannelMLP, SoftGating, skip_connection
 from .spectral_convolution import SpectralConv
 from .utils import get_active_profiler, maybe_profile, validate_scaling_factor
 
@@ -104,7 +110,57 @@ class FNOBlocks(nn.Module):
                 and self.stabilizer is None and self.non_linearity is F.gelu and output_shape is None
                 and conv.resolution_scaling_factor is None and x.is_cuda)
 
+    def _mlp_fusable(self, index, x) -> bool:
+        if not (self.use_channel_mlp and x.is_cuda and x.dtype == torch.float32):
+            return False
+        mlp = self.channel_mlp[index]
+        sg = self.channel_mlp_skips[index] if self.channel_mlp_skips is not None else None
+        if not (isinstance(mlp, ChannelMLP) and mlp.n_layers == 2 and mlp.dropout is None
+                and mlp.non_linearity is F.gelu and (sg is None or isinstance(sg, SoftGating))):
+            return False
+        nxt = self.fno_skips[index + 1].conv.out_channels if index + 1 < self.n_layers else 0
+        return pointwise.supported(x, self.out_channels, mlp.hidden_channels, mlp.out_channels, nxt)
+
+    def next_skip_weight(self, index):
+        """Weight [out, in, 1] of block `index`'s linear skip (None past the last block)."""
+        return self.fno_skips[index].conv.weight if index < self.n_layers else None
+
+    def set_pending_skip(self, x, index, skip):
+        """Hand block `index` the linear skip of its input x computed by a fused kernel upstream."""
+        self._pending_skip = (x, index, skip) if skip is not None else None
+
+    def fused_block(self, x, index, skip=None):
+        """Spectral block + skip add + GELU, then the fused ChannelMLP / soft-gating / GELU kernel, which
+        also returns the next block's linear skip.  Returns (y, next block's skip or None)."""
+        prof = get_active_profiler()
+        prefix = f"fno_blocks/{index}"
+        last = index >= self.n_layers - 1
+        conv = self.convs[index]
+        if skip is None:
+            with maybe_profile(prof, f"{prefix}/fno_skip", x.device):
+                skip, _ = pointwise.channel_mlp(x, None, None, self.fno_skips[index].conv.weight, None,
+                                                act_hidden=False, act_out=False)
+        with maybe_profile(prof, f"{prefix}/spectral_conv_skip_add_activation", x.device):
+            s = conv(x, addend=skip, apply_gelu=not last)
+        mlp = self.channel_mlp[index]
+        sg = self.channel_mlp_skips[index] if self.channel_mlp_skips is not None else None
+        with maybe_profile(prof, f"{prefix}/channel_mlp_skip_activation_next_skip", x.device):
+            y, z = pointwise.channel_mlp(
+                s, mlp.fcs[0].weight, mlp.fcs[0].bias, mlp.fcs[1].weight, mlp.fcs[1].bias, act_hidden=True,
+                act_out=not last, residual=x if sg is not None else None,
+                gate_w=sg.weight if sg is not None else None, gate_b=sg.bias if sg is not None else None,
+                next_w=self.next_skip_weight(index + 1))
+        return y, z
+
     def forward_with_postactivation(self, x, index=0, output_shape=None):
+        if self._fusable(index, x, output_shape) and self._mlp_fusable(index, x):
+            pending = getattr(self, "_pending_skip", None)
+            skip = pending[2] if pending is not None and pending[0] is x and pending[1] == index else None
+            self._pending_skip = None
+            y, z = self.fused_block(x, index, skip)
+            self.set_pending_skip(y, index + 1, z)
+            return y
+        self._pending_skip = None
         prof = get_active_profiler()
         prefix = f"fno_blocks/{index}"
         last = index >= self.n_layers - 1

@@ -99,3 +99,51 @@ def test_fast_engine_request_reports_unsupported_shape():
     rc = lib.nop_spectral_plan_create(ctypes.byref(d), ctypes.byref(h))
     assert rc == -2, _lib.last_error()
     assert "fused FFT engine" in _lib.last_error()
+
+
+def _pw_desc(**over):
+    from neuraloperator_b200.pointwise import NopPointwiseDesc
+    d = NopPointwiseDesc()
+    d.abi_version = _lib.ABI_VERSION
+    d.ndim, d.batch = 2, 2
+    d.spatial[0], d.spatial[1] = 16, 32
+    d.in_channels, d.hidden_channels, d.out_channels, d.next_channels = 8, 4, 8, 8
+    d.gate = 1
+    for k, v in over.items():
+        setattr(d, k, v)
+    return d
+
+
+def test_pointwise_desc_layout():
+    from neuraloperator_b200.pointwise import NopPointwiseDesc
+    # 2 int32, int64 batch, 4 int64 spatial, 11 int32, 8 float (+ padding to 8 bytes)
+    assert ctypes.sizeof(NopPointwiseDesc) == 8 + 8 + 32 + 11 * 4 + 8 * 4 + 4
+
+
+@pytest.mark.parametrize("over, code", [
+    (dict(), 0),
+    (dict(abi_version=7), -1),
+    (dict(ndim=0), -1),
+    (dict(grid_dims=1), -1),
+    (dict(in_channels=0), -1),
+    (dict(out_channels=300), -2),
+    (dict(hidden_channels=257), -2),
+    (dict(batch=-1), -1),
+])
+def test_pointwise_desc_validation_on_host(over, code):
+    from neuraloperator_b200 import pointwise
+    lib = _lib.library()
+    pointwise._declare(lib)
+    size = ctypes.c_size_t()
+    assert lib.nop_pointwise_smem_bytes(ctypes.byref(_pw_desc(**over)), ctypes.byref(size)) == code
+
+
+def test_pointwise_rejects_points_not_multiple_of_32():
+    from neuraloperator_b200 import pointwise
+    lib = _lib.library()
+    pointwise._declare(lib)
+    d = _pw_desc()
+    d.spatial[1] = 33
+    size = ctypes.c_size_t()
+    assert lib.nop_pointwise_smem_bytes(ctypes.byref(d), ctypes.byref(size)) == -2
+    assert b"multiple of 128" in lib.nop_last_error()
