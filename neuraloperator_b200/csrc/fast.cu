@@ -58,23 +58,30 @@ k_plane_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2*
     const int64_t plane = blockIdx.x;
     const int g = threadIdx.x / C::G;
     const int t = threadIdx.x % C::G;
-    for (int i = threadIdx.x; i < N; i += C::THREADS) tw[i] = twg[i];
-    __syncthreads();
-
     const float* xp = x + plane * (int64_t)N * N;
     float2* buf = X + g * C::LINE;
     // ---- rows: pair (2p, 2p+1) -> z = a + i b, keep bins k < Kx and their mirrors ----
+    // The next pair's loads are issued before the current pair is transformed (the first pair's
+    // before the twiddle table is staged).
+    float2 nxt[16];
+    auto load_pair = [&](int pr) {
+        const float* ra = xp + (int64_t)(2 * pr) * N + t;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) nxt[r] = make_float2(__ldg(ra + r * C::G), __ldg(ra + N + r * C::G));
+    };
+    if (g < N / 2) load_pair(g);
+    for (int i = threadIdx.x; i < N; i += C::THREADS) tw[i] = twg[i];
+    __syncthreads();
     for (int base = 0; base < N / 2; base += C::GROUPS) {
         const int pr = base + g;
         const bool active = pr < N / 2;
-        const float* ra = xp + (int64_t)(2 * pr) * N;
-        const float* rb = ra + N;
-        fft::line_fft<N, false>(
-            buf, tw, t, active,
-            [&](int i) { return active ? make_float2(__ldg(ra + i), __ldg(rb + i)) : make_float2(0.f, 0.f); },
-            [&](int k, float2 v) {
-                if (k < Kx || k > N - Kx) buf[pad(k)] = v;
-            });
+        float2 v[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) v[r] = active ? nxt[r] : make_float2(0.f, 0.f);
+        if (pr + C::GROUPS < N / 2) load_pair(pr + C::GROUPS);
+        fft::line_fft_regs<N, false>(v, buf, tw, t, active, [&](int k, float2 w) {
+            if (k < Kx || k > N - Kx) buf[pad(k)] = w;
+        });
         __syncwarp();
         if (active) {
             for (int k = t; k < Kx; k += C::G) {

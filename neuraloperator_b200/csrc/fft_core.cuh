@@ -160,15 +160,13 @@ __device__ __forceinline__ float2 table_tw(const float2* tw, int k) {
 // every load before it writes).  load(i) returns input element i; store(k, v) receives output k.
 // A group with no line to transform passes active = false: it still reaches every warp barrier
 // but writes nothing to `buf` (which may then point at another group's line).
-template <int N, bool INV, class Load, class Store>
-__device__ __forceinline__ void line_fft(float2* buf, const float2* tw, int t, bool active, Load&& load,
-                                         Store&& store) {
+// line_fft with the first pass's inputs already in registers: v[r] = element t + r G.
+template <int N, bool INV, class Store>
+__device__ __forceinline__ void line_fft_regs(float2 (&v)[16], float2* buf, const float2* tw, int t, bool active,
+                                              Store&& store) {
     using S = LineShape<N>;
     constexpr int G = S::G;
-    float2 v[16];
     // ---- pass 1: radix 16, NS = 1 ----
-#pragma unroll
-    for (int r = 0; r < 16; ++r) v[r] = load(t + r * G);
     dft16<INV>(v);
     if constexpr (S::N16 == 1 && S::RLAST == 1) {
 #pragma unroll
@@ -235,6 +233,16 @@ __device__ __forceinline__ void line_fft(float2* buf, const float2* tw, int t, b
             }
         }
     }
+}
+
+template <int N, bool INV, class Load, class Store>
+__device__ __forceinline__ void line_fft(float2* buf, const float2* tw, int t, bool active, Load&& load,
+                                         Store&& store) {
+    constexpr int G = LineShape<N>::G;
+    float2 v[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) v[r] = load(t + r * G);
+    line_fft_regs<N, INV>(v, buf, tw, t, active, store);
 }
 
 }  // namespace fft
