@@ -4,8 +4,8 @@
 //   * forward: the last radix-16 pass of every line computes only the outputs that are kept (and
 //     their Hermitian partners); the two packed real rows are separated with warp shuffles;
 //   * inverse: the first radix-16 pass reads only the non-zero (kept) inputs;
-//   * pass-2 twiddles: the forward kernel keeps its lane's 16 in registers; the inverse reads them
-//     from a padded per-lane table (two per 16-byte load);
+//   * pass-2 twiddles: the forward kernel keeps its lane's 16 in registers; the inverse keeps six
+//     and forms the rest as one product each (fewer registers next to its spectrum prefetch);
 //   * the forward kernel issues its first row loads before it builds the twiddle tables; an inverse
 //     CTA transforms `ppc` consecutive planes, with the kept spectrum of its next plane in flight
 //     while it finishes the current one (the first one's while the tables are built).
@@ -91,6 +91,20 @@ template <bool INV>
 __device__ __forceinline__ void pass2_twiddle_reg(float2* v, const float2* w) {
 #pragma unroll
     for (int r = 1; r < 16; ++r) v[r] = fft::cmul(v[r], INV ? w[r] : make_float2(w[r].x, -w[r].y));
+}
+
+// the same from six per-lane base twiddles W^(r t), r in {1, 2, 3, 4, 8, 12}: W^((4a + c) t) is one
+// product of two exactly-rounded table values (at most about one extra rounding)
+template <bool INV>
+__device__ __forceinline__ void pass2_twiddle_6(float2* v, const float2 (&b)[6]) {
+#pragma unroll
+    for (int r = 1; r < 16; ++r) {
+        const int a = r >> 2, c = r & 3;
+        const float2 wa = a == 1 ? b[3] : a == 2 ? b[4] : b[5];
+        const float2 wc = c == 1 ? b[0] : c == 2 ? b[1] : b[2];
+        const float2 w = a == 0 ? wc : c == 0 ? wa : fft::cmul(wa, wc);
+        v[r] = fft::cmul(v[r], INV ? w : make_float2(w.x, -w.y));
+    }
 }
 
 __device__ __forceinline__ void init_tables(float2* tw, float2* twp, const float2* twg) {
@@ -269,6 +283,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
     if (first < last) fetch(first);  // overlaps the table set-up
     init_tables(tw, twp, twg);
     const float2* twl = twp + t * TWP;
+    const float2 twb[6] = {twl[1], twl[2], twl[3], twl[4], twl[8], twl[12]};
     const int warp_first_group = (threadIdx.x & ~31) / G;
     float2* buf = X + g * LINE;
 #pragma unroll 1
@@ -297,7 +312,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
             __syncwarp();
 #pragma unroll
             for (int r = 0; r < 16; ++r) v[r] = col[t + 17 * r];
-            pass2_twiddle<true>(v, twl);
+            pass2_twiddle_6<true>(v, twb);
             fft::dft16<true>(v);
             __syncwarp();
             if (active) {
@@ -352,7 +367,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
             __syncwarp();
 #pragma unroll
             for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
-            pass2_twiddle<true>(v, twl);
+            pass2_twiddle_6<true>(v, twb);
             fft::dft16<true>(v);
 #pragma unroll
             for (int r = 0; r < 16; ++r) {
