@@ -16,6 +16,7 @@
 #include "nop_internal.cuh"
 #include "axis.cuh"
 #include "plane256.cuh"
+#include "plane512.cuh"
 #include "row1d.cuh"
 #include "mix_tc.cuh"
 
@@ -563,6 +564,43 @@ int32_t run_p256(const Plan& p, const void* x, const char* packed, const float* 
     return NOP_OK;
 }
 
+// 512 x 512 planes through the 256-point machinery (see plane512.cuh); same kept-mode rule as p256
+template <int KX, int MY>
+bool p512_applies(const nop_spectral_desc& d) {
+    nop_spectral_desc h = d;
+    if (d.n_in[0] != 512 || d.n_in[1] != 512) return false;
+    h.n_in[0] = h.n_in[1] = 256;  // the kept-mode / forced-real checks do not depend on the length
+    return p256_applies<KX, MY>(h);
+}
+
+template <int KX, int MY>
+int32_t run_p512(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
+                 int apply_gelu, void* y, char* ws, cudaStream_t s, int slot) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
+    constexpr size_t smem = p512::smem_bytes<KX, MY>();
+    const TwiddleTable* tt = p.table(512);
+    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
+    cudaError_t err;
+    if ((err = ensure_smem_attr(p512::k_fwd<KX, MY>, slot, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p512 fwd)");
+    if ((err = ensure_smem_attr(p512::k_inv<KX, MY>, slot + 1, p.device)) != cudaSuccess)
+        return cuda_fail(err, "cudaFuncSetAttribute(p512 inv)");
+    p512::k_fwd<KX, MY><<<(unsigned)Lin, p512::THREADS, smem, s>>>(static_cast<const float*>(x), Xh, tt->f_table,
+                                                                     (float)d.fwd_scale, Lin * 8);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p512 fwd launch");
+    launch_mark(s);
+    int32_t rc = mix_stage(p, Xh, packed, Yh, ws, s);
+    if (rc != NOP_OK) return rc;
+    p256::Epi ep{bias, addend, apply_gelu, (int)d.out_channels, 1};
+    p512::k_inv<KX, MY><<<(unsigned)Lout, p512::THREADS, smem, s>>>(Yh, static_cast<float*>(y), tt->f_table,
+                                                                      (float)d.inv_scale, Lout * 8, ep);
+    if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "p512 inv launch");
+    launch_mark(s);
+    return NOP_OK;
+}
+
 template <int N>
 int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
                      int apply_gelu, void* y, char* ws, cudaStream_t s) {
@@ -570,6 +608,10 @@ int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const flo
     if constexpr (N == 256) {
         if (p256_applies<33, 64>(d)) return run_p256<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 6);
         if (p256_applies<17, 32>(d)) return run_p256<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 8);
+    }
+    if constexpr (N == 512) {
+        if (p512_applies<33, 64>(d)) return run_p512<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 20);
+        if (p512_applies<17, 32>(d)) return run_p512<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 22);
     }
     const int Kx = (int)d.kept[1], My = (int)d.kept[0];
     const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
