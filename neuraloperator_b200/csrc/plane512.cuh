@@ -152,6 +152,16 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
             const int c = base + g;
             const bool active = c < KX;
             float2* col = T + (active ? c : 0) * TPITCH;
+            // odd phase: this lane's parked C_even values, loaded before the column transform
+            float2 ce[16];
+            if (e == 1 && active) {
+#pragma unroll
+                for (int r = 0; r < 16; ++r) {
+                    if (!((OUT_COL >> r) & 1)) continue;
+                    const int idx = ((t + 16 * r + MY / 2) & (NH - 1)) * KX + c;
+                    ce[r] = op[(idx >> 3) * blk_stride + (idx & 7)];
+                }
+            }
             float2 v[16];
 #pragma unroll
             for (int r = 0; r < 16; ++r) v[r] = col[t + 17 * r];
@@ -176,8 +186,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
                         stage[idx] = v[r];
                     } else {
                         // Y = C_even + W512^f C_odd, C_even parked in this plane's output slot
-                        const float2 ce = op[(idx >> 3) * blk_stride + (idx & 7)];
-                        stage[idx] = fft::cscale(fft::cadd(ce, fft::cmul(v[r], w512_at<false>(w512, m - MY / 2))),
+                        stage[idx] = fft::cscale(fft::cadd(ce[r], fft::cmul(v[r], w512_at<false>(w512, m - MY / 2))),
                                                  scale);
                     }
                 }
