@@ -304,6 +304,62 @@ def run_model(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_slab(args, cfg, world, rank, local):
+    """3D config with the first spatial axis split across the ranks (SlabSpectralConv: local plane
+    transforms, NCCL all-to-all of the kept plane modes, x transforms + contraction, all-to-all back,
+    local inverse planes).  Every rank holds Nx / world planes of the whole batch: the total work is
+    fixed as ranks are added (strong scaling)."""
+    import torch.distributed as dist
+    from neuraloperator_b200.distributed import SlabSpectralConv
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    desc, batch, ci, co, grid, modes, fact = cfg
+    if len(grid) != 3 or grid[0] % world or world < 2:
+        raise SystemExit("--parallel slab needs >= 2 ranks and a 3D config whose first axis divides by them")
+    conv, _ = make_inputs((desc, 1, ci, co, (1, 1, 1), modes, fact), "cpu", seed=0)  # seeded weights
+    conv = conv.to(dev)
+    nx = grid[0] // world
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)  # this rank's planes of a synthetic input
+    x = torch.randn((batch, ci, nx, *grid[1:]), generator=gen, device=dev)
+    slab = SlabSpectralConv(conv)
+    stream = torch.cuda.current_stream(dev)
+    steps, warm = args.steps, args.warmup
+    with torch.no_grad():
+        for _ in range(warm):
+            y = slab(x)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            e0.record(stream)
+            for _ in range(steps):
+                y = slab(x)
+            e1.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    if rank != 0:
+        return
+    hbm, peak_src = peaks()
+    b_alg = bytes_alg(cfg, conv)  # whole problem; per GPU it is / world
+    lay = slab.layout(x, rank=rank, world=world)
+    line = {
+        "metric": METRIC, "value": batch / (ms / 1e3), "unit": "samples/s", "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded N(0,1) input, seeded complex weights; no dataset)",
+        "config": {"workload": desc, "global_batch": batch, "grid": list(grid), "channels": [ci, co],
+                   "n_modes": list(modes), "parallelism": f"slab{world}", "x_planes_per_gpu": nx,
+                   "exchange_bytes_per_gpu": int(sum(lay.send1_split()) + sum(lay.send2_split()))},
+        "block_roofline": {"bound": "hbm", "achieved": b_alg / world / (ms / 1e3) / 1e9, "peak": hbm,
+                           "unit": "GB/s", "frac": b_alg / world / (ms / 1e3) / 1e9 / hbm,
+                           "definition": "(|x| + |y| + |W| + |bias|) / n_gpus per forward over the step time",
+                           "peak_source": peak_src},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline(cfg, seconds=12.0):
     """Oracle (reference torch CPU path) on the host cores, bounded sample of the workload."""
     import oracle
@@ -548,6 +604,8 @@ def main():
     ap.add_argument("--model", choices=["layer", "fno"], default="layer",
                     help="layer: one SpectralConv (the headline); fno: the whole FNO / TFNO forward")
     ap.add_argument("--precision", choices=["fp32", "bf16"], default="fp32", help="contraction precision")
+    ap.add_argument("--parallel", choices=["batch", "slab"], default="batch",
+                    help="batch: each rank its own slice of the batch (weak); slab: 3D x-axis split (strong)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -563,6 +621,8 @@ def main():
     try:
         if args.model == "fno":
             run_model(args, world, rank, local)
+        elif args.parallel == "slab":
+            run_slab(args, cfg, world, rank, local)
         else:
             run_ours(args, cfg, world, rank, local)
     finally:
