@@ -17,7 +17,7 @@
 // operands are rounded to bf16 and one kind::f16 MMA per K step replaces the three tf32 ones.
 //
 // Warp-specialised persistent CTAs (one per SM), connected by mbarriers:
-//   producer warps 4..11 : global X / W -> registers (next step prefetched) -> tf32 hi/lo or bf16 ->
+//   producer warps 4..11 : global X / W -> raw ring (cp.async, RS - 1 steps ahead) -> registers -> tf32 hi/lo or bf16 ->
 //                          shared-memory stage (ring of NS) in the canonical no-swizzle K-major layout
 //                          (8-row x 16-byte core matrices) -> arrive `full[s]`
 //   MMA warp 12 (lane 0) : wait `full[s]`, issue the step's MMAs for the four modes, commit to
@@ -60,12 +60,17 @@ struct Cfg {
     static constexpr int A_TILE = M * 32;               // bytes of one mode's A for one K step
     static constexpr int B_TILE = N * 32;
     static constexpr int STAGE = MODES * SPLITS * (A_TILE + B_TILE);
-    static constexpr int NS0 = (192 * 1024) / STAGE;
-    static constexpr int NS = NS0 > 6 ? 6 : NS0;         // stages in the ring
+    // raw ring: every producer thread's X / W values of one K step (cp.async, RS steps deep)
+    static constexpr int RAWF4 = BF16 ? 16 : 8;          // float4 per producer thread per step
+    static constexpr int RAW = PROD_THREADS * RAWF4 * 16;
+    static constexpr int RS = BF16 ? 2 : 3;
+    static constexpr int NS0 = (226 * 1024 - RS * RAW) / STAGE;
+    static constexpr int NS = NS0 > 6 ? 6 : NS0;         // operand stages in the ring
     static constexpr int ACC_COLS = MODES * N;          // tensor-memory columns of one tile
     static constexpr int NACC = ACC_COLS <= 256 ? 2 : 1;
     static constexpr int TMEM_COLS = 512;
-    static constexpr int BODY = NS * STAGE;
+    static constexpr int RAW_OFF = NS * STAGE;
+    static constexpr int BODY = NS * STAGE + RS * RAW;
     // after the stages: full[NS], empty[NS], acc_full[2], acc_empty[2], drain (8 bytes each), then the
     // tensor-memory address and the abort flag (4 bytes each)
     static constexpr int TAIL = (2 * NS + 5) * 8 + 8;
@@ -228,8 +233,17 @@ struct Step {
     float4 v[2 * KH];
 };
 
+__device__ __forceinline__ void cp_async16z(void* smem, const void* gmem, bool valid) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+// issue the copies of producer thread p's raw values for one K step into a raw-ring slot
+// (layout [value c][thread p] float4, so the threads' later reads are conflict-free); values out of
+// range are zero-filled
 template <int CO, bool BF16>
-__device__ __forceinline__ void load_step(Step<BF16>& st, const Problem& pr, const Tile& tl, int k0, int p) {
+__device__ __forceinline__ void issue_step(float4* slot, const Problem& pr, const Tile& tl, int k0, int p) {
     constexpr int KH = Step<BF16>::KH;
     if (p < 128) {
         const int b = p >> 1, kh = p & 1;
@@ -238,11 +252,9 @@ __device__ __forceinline__ void load_step(Step<BF16>& st, const Problem& pr, con
 #pragma unroll
         for (int c = 0; c < KH; ++c) {
             const bool ok = bok && k0 + kh * KH + c < pr.Ci;
-            if (ok) {
-                ldg32B(src + c * 8, st.v[2 * c], st.v[2 * c + 1]);
-            } else {
-                st.v[2 * c] = st.v[2 * c + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+            const float2* sc = ok ? src + c * 8 : pr.X;
+            cp_async16z(slot + (2 * c) * PROD_THREADS + p, sc, ok);
+            cp_async16z(slot + (2 * c + 1) * PROD_THREADS + p, ok ? sc + 2 : pr.X, ok);
         }
     } else if (p < 128 + 2 * CO) {
         const int u = p - 128;
@@ -252,9 +264,9 @@ __device__ __forceinline__ void load_step(Step<BF16>& st, const Problem& pr, con
         for (int c = 0; c < KH; ++c) {
             const int i = k0 + kh * KH + c;
             const bool ok = ook && i < pr.Ci;
-            const float4* s4 = tl.Wq + ((int64_t)i * 4 + 2 * tl.h) * pr.Co + tl.o0 + o;
-            st.v[2 * c] = ok ? __ldg(s4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            st.v[2 * c + 1] = ok ? __ldg(s4 + pr.Co) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4* s4 = ok ? tl.Wq + ((int64_t)i * 4 + 2 * tl.h) * pr.Co + tl.o0 + o : pr.Wp;
+            cp_async16z(slot + (2 * c) * PROD_THREADS + p, s4, ok);
+            cp_async16z(slot + (2 * c + 1) * PROD_THREADS + p, ok ? s4 + pr.Co : pr.Wp, ok);
         }
     }
 }
@@ -370,30 +382,40 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
     if (warp >= EPI_WARPS && warp < MMA_WARP) {
         // ------------------------------ producers ------------------------------
         const int p = tid - 32 * EPI_WARPS;
-        // tf32: the next step's loads are in flight while the current step is stored (two register
-        // sets; a third spills); bf16 units are twice as large, so they load and store one step at a time
-        constexpr bool PREFETCH = !BF16;
-        Step<BF16> cur, nxt;
-        int lk = 0, lkc = 0;              // tile and K step of the next load
+        // raw ring: the copies of the next RS - 1 steps are in flight (cp.async, no registers held)
+        // while this thread converts the current step; each thread reads back only what it copied
+        constexpr int RS = C::RS;
+        float4* raw = reinterpret_cast<float4*>(smem + C::RAW_OFF);
+        constexpr int SLOT_F4 = PROD_THREADS * C::RAWF4;
+        int lk = 0, lkc = 0;              // tile and K step of the next copy
         Tile ltile;
         if (my_tiles > 0) ltile = tile_k(0);
-        auto load_next = [&](Step<BF16>& dst) {
-            load_step<CO, BF16>(dst, pr, ltile, lkc * C::KS, p);
-            if (++lkc == nk) {
-                lkc = 0;
-                if (++lk < my_tiles) ltile = tile_k(lk);
+        int slot_in = 0, slot_out = 0;
+        auto issue_next = [&]() {
+            if (lk < my_tiles) {
+                issue_step<CO, BF16>(raw + slot_in * SLOT_F4, pr, ltile, lkc * C::KS, p);
+                if (++lkc == nk) {
+                    lkc = 0;
+                    if (++lk < my_tiles) ltile = tile_k(lk);
+                }
             }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+            if (++slot_in == RS) slot_in = 0;
         };
-        if (PREFETCH && my_tiles > 0) load_next(cur);
+#pragma unroll
+        for (int d = 0; d < RS - 1; ++d) issue_next();
+        Step<BF16> cur;
         int s = 0;
         uint32_t upar = 0;                // parity of the current use of stage s
         bool reuse = false;               // stage s held an earlier step
         for (int k = 0; k < my_tiles; ++k) {
             for (int kc = 0; kc < nk; ++kc) {
-                if (!PREFETCH)
-                    load_next(cur);
-                else if (lk < my_tiles)
-                    load_next(nxt);
+                issue_next();
+                asm volatile("cp.async.wait_group %0;\n" ::"n"(RS - 1) : "memory");
+                const float4* mine = raw + slot_out * SLOT_F4 + p;
+#pragma unroll
+                for (int c = 0; c < C::RAWF4; ++c) cur.v[c] = mine[c * PROD_THREADS];
+                if (++slot_out == RS) slot_out = 0;
                 if (reuse && !mbar_wait(&empty[s], upar ^ 1, abort_flag)) {
                     give_up();
                     k = my_tiles;
@@ -403,7 +425,6 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
-                if (PREFETCH) cur = nxt;
                 if (++s == NS) {
                     s = 0;
                     upar ^= 1;
@@ -411,6 +432,7 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
                 }
             }
         }
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     } else if (warp == MMA_WARP) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
