@@ -280,6 +280,43 @@ int32_t nop_spectral_forward_host(const nop_plan* plan, const void* x_host, int6
                                   int32_t apply_gelu, void* y_host, void* workspace, size_t workspace_bytes,
                                   int32_t n_streams, void* stream);
 
+/* ---- backward (training) ------------------------------------------------------------------
+ * Gradients of y = SpectralConv(x) for a real loss with g = dL/dy, equal to what torch autograd
+ * computes through the reference forward (neuralop/layers/spectral_convolution.py:417-570:
+ * rfftn, fftshift, slicing, the contraction einsum :21-103, ifftn, irfft, bias).
+ *   dL/dx    = the forward of the ADJOINT plan on g, with the conjugate-transposed weights
+ *              (dense: W'[o][i] = conj W[i][o]; Tucker / CP: in- and out-factors swapped, every
+ *              factor conjugated, the core's first two modes swapped) and no bias.  The adjoint
+ *              descriptor is the forward's with in/out channels, n_in/n_out, fwd_off/inv_off and
+ *              fwd_scale/inv_scale swapped; the doubling of interior last-axis bins in the c2r
+ *              adjoint cancels the halving in the r2c adjoint, so nothing else changes.
+ *   dL/dW, dL/dbias from nop_spectral_weight_grad, given the kept spectra of x (forward plan) and of
+ *              g (adjoint plan), both left by nop_spectral_forward_keep.
+ * Supported when n_out == n_in (no output resampling) and for every plan but slab plans. */
+
+/* Layout of the kept input-side spectrum a plan's forward computes: element (b, c, mode t) at complex
+ * index (t / 8) * strides[0] + b * strides[1] + c * strides[2] + t % 8; `bytes` = buffer size. Mode
+ * t runs over the kept modes of the weight's mode dims in row-major order. */
+int32_t nop_spectral_spectrum_layout(const nop_plan* plan, int64_t* strides, size_t* bytes);
+
+/* nop_spectral_forward (weights / n_weights; packed = NULL) or nop_spectral_forward_packed (packed /
+ * packed_bytes) that also leaves the kept input spectrum in x_spec (>= the layout's bytes, 256-byte
+ * aligned) for nop_spectral_weight_grad.  Same results in y. */
+int32_t nop_spectral_forward_keep(const nop_plan* plan, const void* x, const void* const* weights,
+                                  int32_t n_weights, const void* packed, size_t packed_bytes,
+                                  const float* bias, const float* addend, int32_t apply_gelu, void* y,
+                                  void* x_spec, size_t x_spec_bytes, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* Weight and bias gradients.  x_spec: kept spectrum of x from the forward plan; g_spec: kept
+ * spectrum of g from the adjoint plan (nop_spectral_forward_keep on each).  grad_w (or NULL):
+ * [Ci, Co, kept...] complex64 (separable: [C, kept...]), the gradient of the dense weight slice the
+ * forward used (for Tucker / CP weights, of the reconstructed weight; the factor gradients follow
+ * from it by the chain rule).  grad_bias (or NULL): [Co] float32.  Replaces the autograd of the
+ * contraction einsum (spectral_convolution.py:21-52) and of the bias add (:567-568). */
+int32_t nop_spectral_weight_grad(const nop_plan* plan, const void* x_spec, const nop_plan* adjoint_plan,
+                                 const void* g_spec, void* grad_w, float* grad_bias, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

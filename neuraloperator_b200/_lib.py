@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "nop_spectral_slab_info", "nop_spectral_slab_forward_planes", "nop_spectral_slab_modes",
     "nop_spectral_slab_inverse_planes", "nop_spectral_host_workspace_size", "nop_spectral_forward_host",
     "nop_device_status", "nop_pointwise_smem_bytes", "nop_pointwise_forward",
+    "nop_spectral_spectrum_layout", "nop_spectral_forward_keep", "nop_spectral_weight_grad",
 )
 
 MAX_SLAB_RANKS = 64
@@ -134,6 +135,17 @@ def _declare(lib):
     lib.nop_spectral_slab_inverse_planes.restype = ctypes.c_int32
     lib.nop_spectral_slab_inverse_planes.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                      ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+    lib.nop_spectral_spectrum_layout.restype = ctypes.c_int32
+    lib.nop_spectral_spectrum_layout.argtypes = [c_plan_p, ctypes.POINTER(ctypes.c_int64),
+                                                 ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_spectral_forward_keep.restype = ctypes.c_int32
+    lib.nop_spectral_forward_keep.argtypes = [
+        c_plan_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nop_spectral_weight_grad.restype = ctypes.c_int32
+    lib.nop_spectral_weight_grad.argtypes = [c_plan_p, ctypes.c_void_p, c_plan_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_void_p]
     lib.nop_device_status.restype = ctypes.c_int32
     lib.nop_device_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]
     lib.nop_spectral_host_workspace_size.restype = ctypes.c_int32
@@ -233,6 +245,12 @@ class Plan:
         size = ctypes.c_size_t()
         check(lib.nop_spectral_workspace_size(handle, ctypes.byref(size)))
         self.workspace_bytes = int(size.value)
+        self.spectrum_strides, self.spectrum_bytes = None, 0
+        if slab is None:
+            strides = (ctypes.c_int64 * 3)()
+            sb = ctypes.c_size_t()
+            check(lib.nop_spectral_spectrum_layout(handle, strides, ctypes.byref(sb)))
+            self.spectrum_strides, self.spectrum_bytes = tuple(strides), int(sb.value)
         self.is_fast = bool(lib.nop_spectral_plan_is_fast(handle))
         self.launches_per_forward = int(lib.nop_spectral_launches_per_forward(handle))
         check(lib.nop_spectral_packed_size(handle, ctypes.byref(size)))

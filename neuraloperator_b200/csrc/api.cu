@@ -320,9 +320,9 @@ int32_t nop_spectral_launches_per_forward(const nop_plan* plan) {
     return p.fast ? fast_launches(p) : generic_launches(p);
 }
 
-int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* const* weights, int32_t n_weights,
-                             const float* bias, const float* addend, int32_t apply_gelu, void* y, void* workspace,
-                             size_t workspace_bytes, void* stream) {
+static int32_t forward_impl(const nop_plan* plan, const void* x, const void* const* weights, int32_t n_weights,
+                            const float* bias, const float* addend, int32_t apply_gelu, void* y, void* workspace,
+                            size_t workspace_bytes, void* stream, float2* xs) {
     if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
     const Plan& p = *reinterpret_cast<const Plan*>(plan);
     const nop_spectral_desc& d = p.d;
@@ -357,8 +357,15 @@ int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* co
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     char* ws = static_cast<char*>(workspace);
     launch_mark_begin(s);
-    if (p.fast) return launch_mark_end(fast_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s));
-    return launch_mark_end(generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s));
+    if (p.fast) return launch_mark_end(fast_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s, xs));
+    return launch_mark_end(generic_forward(p, x, weights, bias, addend, apply_gelu, y, ws, s, xs));
+}
+
+int32_t nop_spectral_forward(const nop_plan* plan, const void* x, const void* const* weights, int32_t n_weights,
+                             const float* bias, const float* addend, int32_t apply_gelu, void* y, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    return forward_impl(plan, x, weights, n_weights, bias, addend, apply_gelu, y, workspace, workspace_bytes, stream,
+                        nullptr);
 }
 
 static int32_t check_workspace(const Plan& p, const void* workspace, size_t workspace_bytes) {
@@ -546,9 +553,9 @@ int32_t nop_spectral_pack_weights(const nop_plan* plan, const void* const* weigh
                      static_cast<cudaStream_t>(stream));
 }
 
-int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const void* packed, size_t packed_bytes,
-                                    const float* bias, const float* addend, int32_t apply_gelu, void* y,
-                                    void* workspace, size_t workspace_bytes, void* stream) {
+static int32_t forward_packed_impl(const nop_plan* plan, const void* x, const void* packed, size_t packed_bytes,
+                                   const float* bias, const float* addend, int32_t apply_gelu, void* y,
+                                   void* workspace, size_t workspace_bytes, void* stream, float2* xs) {
     if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
     const Plan& p = *reinterpret_cast<const Plan*>(plan);
     const nop_spectral_desc& d = p.d;
@@ -565,7 +572,60 @@ int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const v
     if ((rc = check_device(p)) != NOP_OK) return rc;
     launch_mark_begin(static_cast<cudaStream_t>(stream));
     return launch_mark_end(fast_forward_packed(p, x, static_cast<const char*>(packed), bias, addend, apply_gelu, y,
-                                               static_cast<char*>(workspace), static_cast<cudaStream_t>(stream)));
+                                               static_cast<char*>(workspace), static_cast<cudaStream_t>(stream), xs));
+}
+
+int32_t nop_spectral_forward_packed(const nop_plan* plan, const void* x, const void* packed, size_t packed_bytes,
+                                    const float* bias, const float* addend, int32_t apply_gelu, void* y,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    return forward_packed_impl(plan, x, packed, packed_bytes, bias, addend, apply_gelu, y, workspace, workspace_bytes,
+                               stream, nullptr);
+}
+
+/* ---- backward support ----------------------------------------------------------------------- */
+
+int32_t nop_spectral_spectrum_layout(const nop_plan* plan, int64_t* strides, size_t* bytes) {
+    if (!plan || !strides || !bytes) return fail(NOP_E_INVALID, "NULL argument");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    return spectrum_layout(p, &strides[0], &strides[1], &strides[2], bytes);
+}
+
+int32_t nop_spectral_forward_keep(const nop_plan* plan, const void* x, const void* const* weights, int32_t n_weights,
+                                  const void* packed, size_t packed_bytes, const float* bias, const float* addend,
+                                  int32_t apply_gelu, void* y, void* x_spec, size_t x_spec_bytes, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    if (!plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    int64_t st[3];
+    size_t need = 0;
+    int32_t rc = spectrum_layout(p, &st[0], &st[1], &st[2], &need);
+    if (rc != NOP_OK) return rc;
+    if (p.d.batch == 0) return NOP_OK;
+    if (!x_spec || x_spec_bytes < need)
+        return fail(NOP_E_WORKSPACE, "spectrum buffer missing or smaller than nop_spectral_spectrum_layout's size");
+    if ((uintptr_t)x_spec % kAlign) return fail(NOP_E_ALIGNMENT, "spectrum buffer must be 256-byte aligned");
+    float2* xs = static_cast<float2*>(x_spec);
+    if (packed)
+        return forward_packed_impl(plan, x, packed, packed_bytes, bias, addend, apply_gelu, y, workspace,
+                                   workspace_bytes, stream, xs);
+    return forward_impl(plan, x, weights, n_weights, bias, addend, apply_gelu, y, workspace, workspace_bytes, stream,
+                        xs);
+}
+
+int32_t nop_spectral_weight_grad(const nop_plan* plan, const void* x_spec, const nop_plan* adjoint_plan,
+                                 const void* g_spec, void* grad_w, float* grad_bias, void* stream) {
+    if (!plan || !adjoint_plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(plan);
+    const Plan& a = *reinterpret_cast<const Plan*>(adjoint_plan);
+    if (p.device != a.device) return fail(NOP_E_INVALID, "plans live on different devices");
+    if ((x_spec && (uintptr_t)x_spec % 8) || (g_spec && (uintptr_t)g_spec % 8) || (grad_w && (uintptr_t)grad_w % 8) ||
+        (grad_bias && (uintptr_t)grad_bias % 4))
+        return fail(NOP_E_ALIGNMENT, "spectra / gradients are not aligned to their element size");
+    int32_t rc = check_device(p);
+    if (rc != NOP_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    launch_mark_begin(s);
+    return launch_mark_end(weight_grad(p, x_spec, a, g_spec, grad_w, grad_bias, s));
 }
 
 /* ---- forward from host memory ------------------------------------------------------------- */

@@ -537,12 +537,12 @@ bool p256_applies(const nop_spectral_desc& d) {
 
 template <int KX, int MY>
 int32_t run_p256(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
-                 int apply_gelu, void* y, char* ws, cudaStream_t s, int slot) {
+                 int apply_gelu, void* y, char* ws, cudaStream_t s, int slot, float2* xs) {
     const nop_spectral_desc& d = p.d;
     const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
     constexpr size_t smem = p256::smem_bytes<KX, MY>();
     const TwiddleTable* tt = p.table(256);
-    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Xh = xs ? xs : reinterpret_cast<float2*>(ws + p.ws.buf_a);
     float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
     cudaError_t err;
     if ((err = ensure_smem_attr(p256::k_fwd<KX, MY>, slot, p.device)) != cudaSuccess)
@@ -575,12 +575,12 @@ bool p512_applies(const nop_spectral_desc& d) {
 
 template <int KX, int MY>
 int32_t run_p512(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
-                 int apply_gelu, void* y, char* ws, cudaStream_t s, int slot) {
+                 int apply_gelu, void* y, char* ws, cudaStream_t s, int slot, float2* xs) {
     const nop_spectral_desc& d = p.d;
     const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
     constexpr size_t smem = p512::smem_bytes<KX, MY>();
     const TwiddleTable* tt = p.table(512);
-    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Xh = xs ? xs : reinterpret_cast<float2*>(ws + p.ws.buf_a);
     float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
     cudaError_t err;
     if ((err = ensure_smem_attr(p512::k_fwd<KX, MY>, slot, p.device)) != cudaSuccess)
@@ -603,21 +603,21 @@ int32_t run_p512(const Plan& p, const void* x, const char* packed, const float* 
 
 template <int N>
 int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
-                     int apply_gelu, void* y, char* ws, cudaStream_t s) {
+                     int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs) {
     const nop_spectral_desc& d = p.d;
     if constexpr (N == 256) {
-        if (p256_applies<33, 64>(d)) return run_p256<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 6);
-        if (p256_applies<17, 32>(d)) return run_p256<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 8);
+        if (p256_applies<33, 64>(d)) return run_p256<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 6, xs);
+        if (p256_applies<17, 32>(d)) return run_p256<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 8, xs);
     }
     if constexpr (N == 512) {
-        if (p512_applies<33, 64>(d)) return run_p512<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 20);
-        if (p512_applies<17, 32>(d)) return run_p512<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 22);
+        if (p512_applies<33, 64>(d)) return run_p512<33, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 20, xs);
+        if (p512_applies<17, 32>(d)) return run_p512<17, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 22, xs);
     }
     const int Kx = (int)d.kept[1], My = (int)d.kept[0];
     const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
     const size_t smem = plane_smem_bytes<N>(Kx, My);
     const TwiddleTable* tt = p.table(N);
-    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Xh = xs ? xs : reinterpret_cast<float2*>(ws + p.ws.buf_a);
     float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
     cudaError_t err;
     constexpr int slot = fft::ilog2(N) - 7;  // 0, 1, 2 for N = 128, 256, 512
@@ -652,11 +652,11 @@ int32_t run_plane_2d(const Plan& p, const void* x, const char* packed, const flo
 // ---- 1D: long lines, few kept bins ----
 template <int N, int K>
 int32_t run_row1d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
-                  int apply_gelu, void* y, char* ws, cudaStream_t s) {
+                  int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs) {
     const nop_spectral_desc& d = p.d;
     const int64_t Lin = d.batch * d.in_channels, Lout = d.batch * d.out_channels;
     const TwiddleTable* tt = p.table(N);
-    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Xh = xs ? xs : reinterpret_cast<float2*>(ws + p.ws.buf_a);
     float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
     cudaError_t err;
     r1d::k_fwd<N, K><<<(unsigned)ceil_div(Lin, r1d::LINES), r1d::THREADS, 0, s>>>(
@@ -675,10 +675,10 @@ int32_t run_row1d(const Plan& p, const void* x, const char* packed, const float*
 
 template <int N>
 int32_t run_row1d_k(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
-                    int apply_gelu, void* y, char* ws, cudaStream_t s) {
+                    int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs) {
     switch (p.d.kept[0]) {
-        case 9: return run_row1d<N, 9>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
-        case 17: return run_row1d<N, 17>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        case 9: return run_row1d<N, 9>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
+        case 17: return run_row1d<N, 17>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
         default: return fail(NOP_E_UNSUPPORTED, "fused 1D engine: unsupported kept-bin count");
     }
 }
@@ -686,7 +686,7 @@ int32_t run_row1d_k(const Plan& p, const void* x, const char* packed, const floa
 // ---- 3D: (y, z) plane kernels, outer-axis transforms along x, contraction ----
 template <int KZ, int MY, int MX>
 int32_t run_vol3d(const Plan& p, const void* x, const char* packed, const float* bias, const float* addend,
-                  int apply_gelu, void* y, char* ws, cudaStream_t s, int slot) {
+                  int apply_gelu, void* y, char* ws, cudaStream_t s, int slot, float2* xs) {
     const nop_spectral_desc& d = p.d;
     const int64_t Nx = d.n_in[0];
     const int64_t BCi = d.batch * d.in_channels, BCo = d.batch * d.out_channels;
@@ -695,7 +695,7 @@ int32_t run_vol3d(const Plan& p, const void* x, const char* packed, const float*
     constexpr size_t smem = p256::smem_bytes<KZ, MY>();
     float2* Pa = reinterpret_cast<float2*>(ws + p.ws.pl_a);
     float2* Pb = reinterpret_cast<float2*>(ws + p.ws.pl_b);
-    float2* Xh = reinterpret_cast<float2*>(ws + p.ws.buf_a);
+    float2* Xh = xs ? xs : reinterpret_cast<float2*>(ws + p.ws.buf_a);
     float2* Yh = reinterpret_cast<float2*>(ws + p.ws.buf_b);
     const float2* tw256 = p.table(256)->f_table;
     cudaError_t err;
@@ -960,13 +960,13 @@ int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char*
 }
 
 int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
-                            const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
+                            const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs) {
     if (p.fast_kind == FastKind::Row1D) {
         switch (p.d.n_in[0]) {
-            case 2048: return run_row1d_k<2048>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
-            case 4096: return run_row1d_k<4096>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
-            case 8192: return run_row1d_k<8192>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
-            case 16384: return run_row1d_k<16384>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+            case 2048: return run_row1d_k<2048>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
+            case 4096: return run_row1d_k<4096>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
+            case 8192: return run_row1d_k<8192>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
+            case 16384: return run_row1d_k<16384>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
             default: return fail(NOP_E_UNSUPPORTED, "fused 1D engine: unsupported length");
         }
     }
@@ -975,13 +975,13 @@ int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, co
     if (p.fast_kind == FastKind::Vol3D) {
         int which = -1;
         vol3d_shape(p.d, &which);
-        if (which == 0) return run_vol3d<17, 32, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 10);
-        return run_vol3d<33, 64, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 12);
+        if (which == 0) return run_vol3d<17, 32, 32>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 10, xs);
+        return run_vol3d<33, 64, 64>(p, x, packed, bias, addend, apply_gelu, y, ws, s, 12, xs);
     }
     switch (p.d.n_in[0]) {
-        case 128: return run_plane_2d<128>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
-        case 256: return run_plane_2d<256>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
-        case 512: return run_plane_2d<512>(p, x, packed, bias, addend, apply_gelu, y, ws, s);
+        case 128: return run_plane_2d<128>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
+        case 256: return run_plane_2d<256>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
+        case 512: return run_plane_2d<512>(p, x, packed, bias, addend, apply_gelu, y, ws, s, xs);
         default: return fail(NOP_E_UNSUPPORTED, "fused engine: unsupported plane size");
     }
 }
@@ -1011,10 +1011,10 @@ int32_t fast_slab_planes_inv(const Plan& p, const void* recv2, const float* bias
 }
 
 int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
-                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
+                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs) {
     int32_t rc = fast_pack(p, weights, ws + p.ws.packed, ws, s);
     if (rc != NOP_OK) return rc;
-    return fast_forward_packed(p, x, ws + p.ws.packed, bias, addend, apply_gelu, y, ws, s);
+    return fast_forward_packed(p, x, ws + p.ws.packed, bias, addend, apply_gelu, y, ws, s, xs);
 }
 
 }  // namespace nop

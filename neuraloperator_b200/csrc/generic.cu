@@ -382,7 +382,7 @@ int64_t generic_buffer_elems(const nop_spectral_desc& d) {
 }
 
 int32_t generic_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
-                        const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s) {
+                        const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs) {
     const nop_spectral_desc& d = p.d;
     const int nd = d.ndim;
     const int64_t B = d.batch, Ci = d.in_channels, Co = d.out_channels;
@@ -419,6 +419,12 @@ int32_t generic_forward(const Plan& p, const void* x, const void* const* weights
                                                     R, (int)d.fwd_off[j], t->d_table, 1.0);
         if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "forward axis launch");
         cur ^= 1;
+    }
+
+    if (xs) {  // keep the kept input spectrum [B][Ci][Mt] for the caller (the buffers are reused below)
+        const size_t bytes = (size_t)B * Ci * p.modes_total * sizeof(float2);
+        if ((err = cudaMemcpyAsync(xs, bufs[cur], bytes, cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+            return cuda_fail(err, "spectrum copy");
     }
 
     // ---- contraction ----

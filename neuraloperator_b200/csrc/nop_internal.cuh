@@ -86,8 +86,10 @@ void contraction_layout(const Plan& p, size_t* off, WorkspaceLayout* ws);
 // generic direct-DFT engine (any sizes, any ndim): generic.cu
 // ------------------------------------------------------------------------------------------
 int64_t generic_buffer_elems(const nop_spectral_desc& d);
+// xs (nullable): also leave the kept input spectrum there (layout: spectrum_layout)
 int32_t generic_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
-                        const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+                        const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s,
+                        float2* xs = nullptr);
 
 int32_t generic_launches(const Plan& p);
 // Tucker core expanded along the spatial modes into the g / g_tmp workspace regions
@@ -106,15 +108,23 @@ int32_t fast_launches(const Plan& p);
 // status word of the tensor-core kernels on the current device (synchronous read, optional reset)
 int32_t fast_device_status(int* status, bool clear);
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s);
+// xs (nullable): the contraction reads the kept input spectrum from xs instead of the workspace,
+// so it is still there after the call
 int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
-                            const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+                            const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s,
+                            float2* xs = nullptr);
 int32_t fast_forward(const Plan& p, const void* x, const void* const* weights, const float* bias,
-                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s);
+                     const float* addend, int apply_gelu, void* y, char* ws, cudaStream_t s, float2* xs = nullptr);
 int32_t fast_slab_planes_fwd(const Plan& p, const float* x, void* send1, cudaStream_t s);
 int32_t fast_slab_modes(const Plan& p, const void* recv1, const char* packed, void* send2, char* ws,
                         cudaStream_t s);
 int32_t fast_slab_planes_inv(const Plan& p, const void* recv2, const float* bias, const float* addend,
                              int apply_gelu, float* y, cudaStream_t s);
+
+// backward: kept-spectrum layout of a plan's input side and the weight / bias gradients (grad.cu)
+int32_t spectrum_layout(const Plan& p, int64_t* q_stride, int64_t* b_stride, int64_t* c_stride, size_t* bytes);
+int32_t weight_grad(const Plan& p, const void* x_spec, const Plan& adjoint, const void* g_spec, void* grad_w,
+                    float* grad_bias, cudaStream_t s);
 
 // ------------------------------------------------------------------------------------------
 // small device helpers

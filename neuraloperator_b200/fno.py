@@ -20,7 +20,7 @@ from . import pointwise
 from .fno_block import FNOBlocks
 from .layers import ChannelMLP, GridEmbeddingND
 from .spectral_convolution import SpectralConv
-from .utils import get_active_profiler, maybe_profile
+from .utils import get_active_profiler, grad_needed, maybe_profile
 
 Number = Union[float, int]
 
@@ -115,6 +115,8 @@ class FNO(nn.Module):
         layer does not fit the fused kernels (the module path then runs)."""
         pe = self.positional_embedding
         if not (x.is_cuda and x.dtype == torch.float32) or (pe is not None and not isinstance(pe, GridEmbeddingND)):
+            return None
+        if grad_needed(x, self):
             return None
         grid = [tuple(b) for b in pe.grid_boundaries] if pe is not None else None
         blocks = self.fno_blocks

@@ -25,7 +25,7 @@ from torch import nn
 from . import pointwise
 from .layers import ChannelMLP, SoftGating, skip_connection
 from .spectral_convolution import SpectralConv
-from .utils import get_active_profiler, maybe_profile, validate_scaling_factor
+from .utils import get_active_profiler, grad_needed, maybe_profile, validate_scaling_factor
 
 Number = Union[int, float]
 
@@ -108,7 +108,7 @@ class FNOBlocks(nn.Module):
         conv = self.convs[index]
         return (isinstance(conv, SpectralConv) and self.fno_skip is not None and self.fno_skip.lower() == "linear"
                 and self.stabilizer is None and self.non_linearity is F.gelu and output_shape is None
-                and conv.resolution_scaling_factor is None and x.is_cuda)
+                and conv.resolution_scaling_factor is None and x.is_cuda and not grad_needed(x, self))
 
     def _mlp_fusable(self, index, x) -> bool:
         if not (self.use_channel_mlp and x.is_cuda and x.dtype == torch.float32):

@@ -132,3 +132,21 @@ def compute_geometry(in_sizes: Sequence[int], modes: Sequence[int], max_modes: S
     return Geometry(order=order, complex_data=complex_data, n_in=n_in, n_out=n_out, kept=kept,
                     weight_slices=tuple(w_slices), fwd_off=fwd_off, inv_off=inv_off,
                     fwd_scale=fwd_scale, inv_scale=inv_scale, zero_imag_bins=zero_imag)
+
+
+def adjoint_geometry(geo: Geometry) -> Geometry:
+    """Geometry of the adjoint of one forward call (the input gradient is its forward on dL/dy).
+
+    The forward is  y = inv_scale * c2r(pad(W . (fwd_scale * trunc(r2c(x)))));  its adjoint with respect
+    to the real inner product is the same chain with the grids, the bin maps (fwd_off <-> inv_off) and the
+    scales swapped and W replaced by its per-mode conjugate transpose: the c2r adjoint doubles interior
+    last-axis bins and the r2c adjoint halves them, which cancel.  Only defined here for n_out == n_in
+    (the Nyquist bin of one grid would otherwise be an interior bin of the other).
+    """
+    if list(geo.n_out) != list(geo.n_in):
+        raise NotImplementedError("backward of a SpectralConv that resamples its output "
+                                  f"({geo.n_in} -> {geo.n_out}) is not implemented")
+    return Geometry(order=geo.order, complex_data=geo.complex_data, n_in=list(geo.n_out), n_out=list(geo.n_in),
+                    kept=list(geo.kept), weight_slices=geo.weight_slices, fwd_off=list(geo.inv_off),
+                    inv_off=list(geo.fwd_off), fwd_scale=geo.inv_scale, inv_scale=geo.fwd_scale,
+                    zero_imag_bins=list(geo.zero_imag_bins))

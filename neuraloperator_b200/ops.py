@@ -101,12 +101,15 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
                      weight_kind: str = "dense", ranks: Sequence[int] = (), separable: bool = False,
                      bias: Optional[torch.Tensor] = None, addend: Optional[torch.Tensor] = None,
                      apply_gelu: bool = False, precision: str = "fp32", engine: str = "auto",
-                     out: Optional[torch.Tensor] = None, cache: Optional[dict] = None) -> torch.Tensor:
+                     out: Optional[torch.Tensor] = None, cache: Optional[dict] = None,
+                     keep_spectrum: bool = False):
     """Run one spectral-block forward on x's device and current stream.
 
     Fused-engine plans use packed weights (nop_spectral_pack_weights).  With ``cache`` (a dict
     owned by the calling module) the packed buffer is kept and reused while the weight tensors
     keep their storage and version counter; any in-place update or replacement repacks.
+    With ``keep_spectrum`` the kept input spectrum is kept too (nop_spectral_forward_keep) and
+    ``(y, Spectrum)`` is returned, for ``weight_grad``.
     """
     if not x.is_cuda:
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path); "
@@ -133,9 +136,20 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
     arr = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     lib = _lib.library()
+    spec = None
+    if keep_spectrum:
+        spec = torch.empty(max(plan.spectrum_bytes, 1), device=dev, dtype=torch.uint8)
     with torch.cuda.device(dev):
+        packed = None
         if plan.packed_bytes > 0:
             packed = _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream)
+        if spec is not None:
+            _lib.check(lib.nop_spectral_forward_keep(
+                plan.handle, _ptr(x), None if packed is not None else arr, 0 if packed is not None else len(ws),
+                _ptr(packed), plan.packed_bytes if packed is not None else 0, _ptr(b), _ptr(a),
+                int(bool(apply_gelu)), _ptr(y), _ptr(spec), plan.spectrum_bytes, _ptr(workspace),
+                plan.workspace_bytes, stream))
+        elif packed is not None:
             _lib.check(lib.nop_spectral_forward_packed(
                 plan.handle, _ptr(x), _ptr(packed), plan.packed_bytes, _ptr(b), _ptr(a), int(bool(apply_gelu)),
                 _ptr(y), _ptr(workspace), plan.workspace_bytes, stream))
@@ -143,7 +157,66 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
             _lib.check(lib.nop_spectral_forward(
                 plan.handle, _ptr(x), arr, len(ws), _ptr(b), _ptr(a), int(bool(apply_gelu)), _ptr(y),
                 _ptr(workspace), plan.workspace_bytes, stream))
+    if keep_spectrum:
+        return y, Spectrum(plan, spec)
     return y
+
+
+class Spectrum:
+    """Kept input spectrum left by a forward (``spectral_forward(..., keep_spectrum=True)``), with the
+    plan whose layout it follows (nop_spectral_spectrum_layout)."""
+
+    def __init__(self, plan, buf: torch.Tensor):
+        self.plan = plan
+        self.buf = buf
+
+
+def _conj_copy(t: torch.Tensor, dims=None) -> torch.Tensor:
+    """Contiguous conj(t) (with dims 0 and 1 swapped when ``dims`` is "T"), in one copy kernel."""
+    src = t.transpose(0, 1) if dims == "T" else t
+    out = torch.empty(src.shape, dtype=t.dtype, device=t.device)
+    out.copy_(src.conj())
+    return out
+
+
+def adjoint_operands(kind: str, weights: List[torch.Tensor], ranks: Sequence[int], separable: bool):
+    """Weight operands of the adjoint contraction W'[o, i, m] = conj(W[i, o, m]), in the same kind.
+
+    Dense: the conjugate transpose.  Tucker (core [r_in, r_out, r_1..], U_in, U_out, U_1..): core with its
+    first two modes swapped, in- and out-factors swapped, all conjugated.  CP (lambda, U_in, U_out, U_1..):
+    in- and out-factors swapped, all conjugated.  Separable weights are diagonal: conjugated only.
+    Returns (weights, ranks).
+    """
+    ws = [w.detach() for w in weights]
+    if separable:
+        return [_conj_copy(w) for w in ws], tuple(ranks)
+    if kind == "dense":
+        return [_conj_copy(ws[0], "T")], ()
+    if kind == "tucker":
+        core, u_in, u_out, *spatial = ws
+        r = list(ranks)
+        return ([_conj_copy(core, "T"), _conj_copy(u_out), _conj_copy(u_in)] + [_conj_copy(u) for u in spatial],
+                tuple([r[1], r[0]] + r[2:]))
+    if kind == "cp":
+        lam, u_in, u_out, *spatial = ws
+        return [_conj_copy(lam), _conj_copy(u_out), _conj_copy(u_in)] + [_conj_copy(u) for u in spatial], tuple(ranks)
+    raise ValueError(f"unknown weight kind {kind!r}")
+
+
+def weight_grad(fwd: Spectrum, adj: Spectrum, grad_w_shape: Optional[Sequence[int]], bias_channels: int = 0):
+    """dL/dW (dense-equivalent, ``grad_w_shape`` complex64, or None) and dL/dbias ([bias_channels] float32,
+    or None when 0) from the kept spectra of x (forward plan) and of dL/dy (adjoint plan)
+    (nop_spectral_weight_grad)."""
+    dev = fwd.buf.device
+    gw = None if grad_w_shape is None else torch.empty(tuple(grad_w_shape), device=dev, dtype=torch.complex64)
+    gb = torch.empty(bias_channels, device=dev, dtype=torch.float32) if bias_channels else None
+    if gw is None and gb is None:
+        return None, None
+    with torch.cuda.device(dev):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(_lib.library().nop_spectral_weight_grad(fwd.plan.handle, _ptr(fwd.buf), adj.plan.handle,
+                                                           _ptr(adj.buf), _ptr(gw), _ptr(gb), stream))
+    return gw, gb
 
 
 def default_chunk(batch: int, target_chunks: int = 8) -> int:

@@ -146,6 +146,10 @@ def channel_mlp(x: torch.Tensor, fc1_w: Optional[torch.Tensor], fc1_b: Optional[
     """
     if not x.is_cuda:
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path)")
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in
+                                       (x, fc1_w, fc1_b, fc2_w, fc2_b, residual, gate_w, gate_b, next_w)):
+        raise RuntimeError("the fused per-pixel kernel has no backward; call it under torch.no_grad() "
+                           "(the FNO modules use their torch layers whenever a gradient is needed)")
     x = x.contiguous()
     w1, b1, w2, b2 = _mat(fc1_w), _vec(fc1_b), _mat(fc2_w), _vec(fc2_b)
     g, gb, w3 = _vec(gate_w), _vec(gate_b), _mat(next_w)

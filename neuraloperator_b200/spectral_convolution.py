@@ -10,9 +10,15 @@ Two keyword arguments are added after the reference's:
 ``contraction_precision`` ("fp32" or "bf16": contraction operands rounded to bfloat16 with
 float32 accumulation) and ``engine`` ("auto", "fast", "generic").
 
+Backward (training) runs through the same kernels: the input gradient is the forward of the
+adjoint plan (grids, bin maps and scales swapped, conjugate-transposed weights) and the weight /
+bias gradients come from the kept spectra of x and dL/dy (nop_spectral_weight_grad); factorized
+weights get their factor gradients from the reconstructed weight's gradient by the chain rule.
+
 Differences that raise instead of silently diverging: ``fno_block_precision`` "half" /
 "mixed" (complex-half einsum, neuralop/layers/einsum_utils.py) raises NotImplementedError;
-calling ``backward`` through the block raises NotImplementedError (forward only).
+backward through an output-resampling call, or through the fused GELU epilogue, raises
+NotImplementedError.
 """
 
 from __future__ import annotations
@@ -24,7 +30,7 @@ from torch import nn
 
 from . import ops
 from .factorized import CPTensor, DenseTensor, FactorizedTensor, TTTensor, TuckerTensor
-from .geometry import Geometry, active_modes, compute_geometry, output_sizes
+from .geometry import Geometry, active_modes, adjoint_geometry, compute_geometry, output_sizes
 from .utils import validate_scaling_factor
 
 Number = Union[int, float]
@@ -42,17 +48,81 @@ class BaseSpectralConv(nn.Module):
         return x
 
 
+class _Call:
+    """One SpectralConv call: geometry, weight kind and options, with its forward and backward."""
+
+    def __init__(self, module, geo: Geometry, kind: str, ranks, apply_gelu: bool, train: bool):
+        self.module = module
+        self.geo = geo
+        self.kind = kind
+        self.ranks = tuple(ranks)
+        self.apply_gelu = apply_gelu
+        self.train = train
+
+    def forward(self, x, weights, bias, addend, keep_spectrum=False):
+        m = self.module
+        cache = m.__dict__.setdefault("_nop_pack_cache", {})
+        return ops.spectral_forward(x, self.geo, weights, out_channels=m.out_channels, weight_kind=self.kind,
+                                    ranks=self.ranks, separable=m.separable, bias=bias, addend=addend,
+                                    apply_gelu=self.apply_gelu, precision=m.contraction_precision, engine=m.engine,
+                                    cache=cache, keep_spectrum=keep_spectrum)
+
+    def backward(self, gy, weights, spec, need_x: bool, need_w: bool, need_b: bool):
+        """(dL/dx, [dL/d weight operand], dL/dbias [Co]) for dL/dy = gy; entries not needed are None."""
+        m = self.module
+        gy = gy.contiguous()
+        adj_ws, adj_ranks = ops.adjoint_operands(self.kind, weights, self.ranks, m.separable)
+        gx, gspec = ops.spectral_forward(gy, adjoint_geometry(self.geo), adj_ws, out_channels=m.in_channels,
+                                         weight_kind=self.kind, ranks=adj_ranks, separable=m.separable,
+                                         precision=m.contraction_precision, engine=m.engine, keep_spectrum=True)
+        lead = (m.in_channels,) if m.separable else (m.in_channels, m.out_channels)
+        gw, gb = ops.weight_grad(spec, gspec, lead + tuple(self.geo.kept) if need_w else None,
+                                 m.out_channels if need_b else 0)
+        gws = None
+        if need_w:
+            if self.kind == "dense":
+                gws = [gw.view(weights[0].shape)]
+            else:  # chain rule through the reconstruction of the factorized weight
+                with torch.enable_grad():
+                    leaves = [w.detach().requires_grad_() for w in weights]
+                    full = (_tucker_full(leaves[0], leaves[1:]) if self.kind == "tucker"
+                            else _cp_full(leaves[0], leaves[1:]))
+                    gws = list(torch.autograd.grad(full, leaves, gw))
+        return (gx if need_x else None), gws, gb
+
+
 class _SpectralFn(torch.autograd.Function):
-    """Forward through the CUDA kernels; backward is not implemented (raises)."""
+    """Forward and backward of one SpectralConv call through the CUDA kernels.
+
+    The forward keeps the kept input spectrum when a gradient will be needed; the backward runs the
+    adjoint forward on dL/dy and the weight / bias gradient kernel."""
 
     @staticmethod
-    def forward(ctx, x, bias, addend, runner, *weights):
-        return runner(x, list(weights), bias, addend)
+    def forward(ctx, x, bias, addend, call, *weights):
+        if not call.train:
+            return call.forward(x, list(weights), bias, addend)
+        if call.apply_gelu:
+            raise NotImplementedError("the fused GELU epilogue has no backward; call SpectralConv without "
+                                      "apply_gelu (FNOBlocks does so whenever a gradient is needed)")
+        y, spec = call.forward(x, list(weights), bias, addend, keep_spectrum=True)
+        ctx.call = call
+        ctx.spec = spec
+        ctx.bias_shape = None if bias is None else tuple(bias.shape)
+        ctx.save_for_backward(*weights)
+        return y
 
     @staticmethod
-    def backward(ctx, *grads):
-        raise NotImplementedError("backward of the neuraloperator_b200 spectral block is not implemented "
-                                  "(the CUDA kernels are forward-only)")
+    def backward(ctx, gy):
+        weights = list(ctx.saved_tensors)
+        need_x, need_b, need_a = ctx.needs_input_grad[:3]
+        need_w = any(ctx.needs_input_grad[4:])
+        need_b = bool(need_b and ctx.bias_shape is not None)
+        gx, gws, gb = ctx.call.backward(gy, weights, ctx.spec, need_x, need_w, need_b)
+        if gb is not None:
+            gb = gb.view(ctx.bias_shape)
+        ga = gy if need_a else None
+        gws = gws if gws is not None else [None] * len(weights)
+        return (gx, gb, ga, None, *gws)
 
 
 class SpectralConv(BaseSpectralConv):
@@ -167,12 +237,6 @@ class SpectralConv(BaseSpectralConv):
             return "dense", [w[idx]], ()
         raise ValueError(f"unexpected weight type {type(w).__name__}")
 
-    def _run(self, x, weights, bias, addend, *, geo, kind, ranks, apply_gelu):
-        cache = self.__dict__.setdefault("_nop_pack_cache", {})
-        return ops.spectral_forward(x, geo, weights, out_channels=self.out_channels, weight_kind=kind, ranks=ranks,
-                                    separable=self.separable, bias=bias, addend=addend, apply_gelu=apply_gelu,
-                                    precision=self.contraction_precision, engine=self.engine, cache=cache)
-
     def forward(self, x: torch.Tensor, output_shape: Optional[Tuple[int]] = None, *, addend=None,
                 apply_gelu: bool = False):
         """Spectral convolution of x (batch, channels, d1, ..., dN).
@@ -188,9 +252,13 @@ class SpectralConv(BaseSpectralConv):
         geo = self.geometry(list(x.shape[2:]), output_shape)
         kind, weights, ranks = self.kernel_operands(geo)
         bias = None if self.bias is None else self.bias
-        runner = lambda xx, ww, bb, aa: self._run(xx, ww, bb, aa, geo=geo, kind=kind, ranks=ranks,
-                                                   apply_gelu=apply_gelu)
-        return _SpectralFn.apply(x, bias, addend, runner, *weights)
+        train = torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (x, bias, addend, *weights))
+        if train and geo.n_out != geo.n_in:
+            raise NotImplementedError("backward of a SpectralConv that resamples its output is not implemented; "
+                                      "run it under torch.no_grad()")
+        call = _Call(self, geo, kind, ranks, apply_gelu, train)
+        return _SpectralFn.apply(x, bias, addend, call, *weights)
 
     @torch.no_grad()
     def forward_host(self, x: torch.Tensor, output_shape: Optional[Tuple[int]] = None, *, addend=None,

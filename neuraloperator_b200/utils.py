@@ -37,6 +37,15 @@ def validate_scaling_factor(scaling_factor, n_dim: int, n_layers: Optional[int] 
     return None
 
 
+def grad_needed(x: torch.Tensor, module: torch.nn.Module) -> bool:
+    """True when autograd will record this call: grad mode on and x or a parameter of ``module``
+    requires a gradient.  The fused per-pixel kernels and the fused GELU epilogue have no backward,
+    so the models take their composable path (torch layers + SpectralConv's autograd) then."""
+    if not torch.is_grad_enabled():
+        return False
+    return x.requires_grad or any(p.requires_grad for p in module.parameters())
+
+
 def count_model_params(model) -> int:
     """Parameter count with complex entries counted twice (neuralop/utils.py:19-28)."""
     return sum(p.numel() * 2 if p.is_complex() else p.numel() for p in model.parameters())

@@ -101,3 +101,30 @@ def spectral_conv_direct(x, w_dense, bias, *, n_in, n_out, kept, fwd_off, inv_of
     if bias is not None:
         y = y + bias.to(torch.float64)
     return y
+
+
+def mode_factors(kept, n_out, complex_data: bool) -> torch.Tensor:
+    """Per-mode factor d_t of the weight gradient, shape ``kept`` (float64).
+
+    torch's backward of the c2r inverse (irfft, neuralop/layers/spectral_convolution.py:547-559) is an
+    r2c transform of dL/dy with the interior one-sided bins doubled (they stand for two bins of the full
+    spectrum); bin 0 and, for even n_out, the Nyquist bin n_out/2 are not doubled.  Complex data: 1.
+    """
+    d = torch.ones(list(kept), dtype=torch.float64)
+    if complex_data:
+        return d
+    n = n_out[-1]
+    k = torch.arange(kept[-1])
+    last = torch.where((k == 0) | ((n % 2 == 0) & (k == n // 2)), 1.0, 2.0).to(torch.float64)
+    return d * last
+
+
+def weight_grad_direct(xs: torch.Tensor, gs: torch.Tensor, kept, n_out, complex_data: bool,
+                       separable: bool = False) -> torch.Tensor:
+    """dL/dW of the sliced dense weight from the kept spectra of x (forward geometry) and of dL/dy
+    (adjoint geometry: grids, bin maps and scales swapped), as torch autograd of the contraction einsum
+    (spectral_convolution.py:21-52) gives it: d_t * sum_b conj(xs[b, i, t]) * gs[b, o, t]."""
+    d = mode_factors(kept, n_out, complex_data)
+    if separable:
+        return torch.einsum("bi...,bi...->i...", xs.conj(), gs) * d
+    return torch.einsum("bi...,bo...->io...", xs.conj(), gs) * d

@@ -6,9 +6,10 @@ Run in the build container (it needs the reference checkout; see ``ref_loader``)
 
 Writes ``spectral_cases.pt`` (SpectralConv cases: dense, Tucker, CP, TT, separable,
 complex data, odd sizes, Nyquist kept, incremental modes, output_shape, fft_norm),
-``fno_cases.pt`` (FNOBlocks / FNO / TFNO end to end) and ``config_layers.pt`` (single
+``fno_cases.pt`` (FNOBlocks / FNO / TFNO end to end), ``config_layers.pt`` (single
 SpectralConv layers with the modes and grids of the five benchmark configurations, at
-reduced batch/channel counts).  Every tensor is generated from fixed seeds; the
+reduced batch/channel counts) and ``grad_cases.pt`` (gradients: torch autograd through the
+reference's forward for a seeded dL/dy, for SpectralConv layers and for small FNO / TFNO models).  Every tensor is generated from fixed seeds; the
 reference modules compute the outputs.  The files are committed so the tests need no
 reference checkout.
 """
@@ -248,12 +249,137 @@ def config_layers(mods):
     return cases
 
 
+def _grad_payload(w):
+    """Gradients of a stub weight container, in the structure of ``_weight_payload``."""
+    g = lambda p: None if p.grad is None else p.grad.detach().clone()
+    name = w.name.lower()
+    if name.endswith("dense"):
+        return g(w.tensor)
+    if name.endswith("tucker"):
+        return {"core": g(w.core), "factors": [g(f) for f in w.factors]}
+    if name.endswith("cp"):
+        return {"weights": g(w.weights), "factors": [g(f) for f in w.factors]}
+    return {"factors": [g(f) for f in w.factors]}
+
+
+def grad_cases(mods):
+    """Backward goldens: for y = module(x) and a seeded G = dL/dy (L = sum(y * G), real part for complex
+    data), the reference's autograd gives dL/dx and dL/d every parameter."""
+    SC = mods["spectral_convolution"].SpectralConv
+    layers = []
+
+    def add(name, ci, co, n_modes, size, batch=2, seed=100, set_modes=None, **kw):
+        gen = torch.Generator().manual_seed(seed)
+        conv = SC(ci, co, n_modes, **kw)
+        std = (2.0 / (ci + co)) ** 0.5
+        if kw.get("factorization") not in (None, "Dense", "dense"):
+            nf = sum(1 for _ in conv.weight.parameters())
+            _randomise_weight(conv.weight, gen, std ** (1.0 / max(nf - 1, 1)))
+        else:
+            _randomise_weight(conv.weight, gen, std)
+        if conv.bias is not None:
+            with torch.no_grad():
+                conv.bias.copy_(torch.randn(conv.bias.shape, generator=gen) * std)
+        if set_modes is not None:
+            conv.n_modes = set_modes
+        cplx = kw.get("complex_data", False)
+        x = _cn(gen, (batch, ci, *size), 1.0) if cplx else torch.randn((batch, ci, *size), generator=gen)
+        x.requires_grad_(True)
+        y = conv(x)
+        G = _cn(gen, y.shape, 1.0) if cplx else torch.randn(y.shape, generator=gen)
+        y.backward(G)
+        kind, payload = _weight_payload(conv.weight)
+        layers.append(dict(
+            name=name, in_channels=ci, out_channels=co, n_modes=list(n_modes),
+            active_modes=list(set_modes) if set_modes is not None else None, kwargs=dict(kw), forward_kwargs={},
+            weight_kind=kind, weight=payload, bias=None if conv.bias is None else conv.bias.detach().clone(),
+            x=x.detach().clone(), order=len(size), grad_y=G,
+            grad_x=x.grad.detach().clone(), grad_weight=_grad_payload(conv.weight),
+            grad_bias=None if conv.bias is None else conv.bias.grad.detach().clone()))
+
+    # generic-engine shapes
+    add("g_d1_even", 3, 4, (8,), (16,))
+    add("g_d1_odd", 3, 4, (5,), (9,))
+    add("g_d1_allbins", 2, 3, (16,), (16,))
+    add("g_d2_ref_modes", 3, 4, (10, 8), (12, 12))
+    add("g_d2_odd", 3, 4, (4, 5), (9, 9))
+    add("g_d2_nyquist", 2, 3, (8, 8), (8, 8))
+    add("g_d2_nohermitian", 3, 4, (4, 4), (8, 8), enforce_hermitian_symmetry=False)
+    add("g_d2_nobias", 3, 4, (6, 6), (12, 12), bias=False)
+    add("g_d3_odd", 3, 4, (4, 5, 7), (9, 9, 9))
+    add("g_d4", 2, 3, (4, 4, 4, 4), (6, 6, 6, 6))
+    add("g_d2_incremental", 3, 4, (8, 8), (12, 12), max_n_modes=(8, 8), set_modes=(4, 6))
+    add("g_d2_norm_backward", 3, 4, (6, 6), (12, 12), fft_norm="backward")
+    add("g_d2_norm_ortho", 3, 4, (6, 6), (12, 12), fft_norm="ortho")
+    add("g_c1", 3, 4, (6,), (12,), complex_data=True)
+    add("g_c2", 3, 4, (6, 4), (12, 10), complex_data=True)
+    add("g_d2_separable", 3, 3, (6, 6), (12, 12), separable=True)
+    add("g_tucker_d2", 3, 4, (10, 8), (12, 12), factorization="tucker", implementation="factorized", rank=0.4)
+    add("g_tucker_d2_recon", 3, 4, (10, 8), (12, 12), factorization="tucker", implementation="reconstructed",
+        rank=0.4)
+    add("g_tucker_sep_d1", 3, 3, (6,), (12,), separable=True, factorization="tucker",
+        implementation="factorized", rank=0.5)
+    add("g_cp_d2", 3, 4, (6, 6), (12, 12), factorization="cp", implementation="factorized", rank=0.5)
+    add("g_tt_d2", 3, 4, (6, 6), (12, 12), factorization="tt", implementation="factorized", rank=0.5)
+    # fused-engine shapes (plane kernels for 128 / 256, long 1D lines, Tucker core on 256); 512 x 512
+    # planes are checked on the GPU through the adjoint identity instead (fixture size)
+    add("g_fast_128", 2, 3, (16, 16), (128, 128), batch=1)
+    add("g_fast_256", 1, 2, (64, 64), (256, 256), batch=1)
+    add("g_fast_256_tucker", 1, 1, (64, 64), (256, 256), batch=1, factorization="tucker",
+        implementation="factorized", rank=0.1)
+    add("g_fast_1d", 2, 2, (16,), (8192,), batch=2)
+
+    FNO, TFNO = mods["fno"].FNO, mods["fno"].TFNO
+    models = []
+
+    def add_model(name, cls, size, batch, seed, **kw):
+        gen = torch.Generator().manual_seed(seed)
+        torch.manual_seed(seed)
+        model = cls(**kw)
+        _randomise_module(model, gen)
+        x = torch.randn((batch, kw["in_channels"], *size), generator=gen)
+        x.requires_grad_(True)
+        y = model(x)
+        G = torch.randn(y.shape, generator=gen)
+        y.backward(G)
+        fb = model.fno_blocks
+        blocks, gblocks, kind = [], [], None
+        for i in range(fb.n_layers):
+            kind, blk = _block_payload(fb, i)
+            blocks.append(blk)
+            gb = {"weight": _grad_payload(fb.convs[i].weight), "bias": fb.convs[i].bias.grad.detach().clone()}
+            sk = fb.fno_skips[i]
+            gb["fno_skip"] = (sk.conv.weight if hasattr(sk, "conv") else sk.weight).grad.detach().clone()
+            gb["mlp"] = [(fc.weight.grad.detach().clone(), fc.bias.grad.detach().clone())
+                         for fc in fb.channel_mlp[i].fcs]
+            gb["mlp_skip"] = fb.channel_mlp_skips[i].weight.grad.detach().clone()
+            gblocks.append(gb)
+        lin = lambda fcs: [(fc.weight.detach().clone(), fc.bias.detach().clone()) for fc in fcs]
+        glin = lambda fcs: [(fc.weight.grad.detach().clone(), fc.bias.grad.detach().clone()) for fc in fcs]
+        params = {"lifting": lin(model.lifting.fcs), "projection": lin(model.projection.fcs), "blocks": blocks}
+        grads = {"lifting": glin(model.lifting.fcs), "projection": glin(model.projection.fcs), "blocks": gblocks}
+        n_params = sum(1 for _ in model.parameters())
+        n_with_grad = sum(1 for p in model.parameters() if p.grad is not None)
+        models.append(dict(name=name, model=cls.__name__, kwargs=kw, weight_kind=kind, params=params,
+                           x=x.detach().clone(), y=y.detach().clone(), grad_y=G, grad_x=x.grad.detach().clone(),
+                           grads=grads, n_params=n_params, n_params_with_grad=n_with_grad))
+
+    add_model("fno2d_darcy_small", FNO, (32, 32), 2, 21, n_modes=(16, 16), in_channels=1, out_channels=1,
+              hidden_channels=8, n_layers=4)
+    add_model("tfno2d_small", TFNO, (32, 32), 2, 22, n_modes=(12, 12), in_channels=1, out_channels=1,
+              hidden_channels=8, n_layers=2)
+    add_model("fno1d_small", FNO, (64,), 2, 23, n_modes=(16,), in_channels=1, out_channels=1,
+              hidden_channels=8, n_layers=2)
+    return {"layers": layers, "models": models}
+
+
 def main():
     mods = ref_loader.install()
     torch.save(spectral_cases(mods), os.path.join(HERE, "spectral_cases.pt"))
     torch.save(fno_cases(mods), os.path.join(HERE, "fno_cases.pt"))
     torch.save(config_layers(mods), os.path.join(HERE, "config_layers.pt"))
-    for f in ("spectral_cases.pt", "fno_cases.pt", "config_layers.pt"):
+    torch.save(grad_cases(mods), os.path.join(HERE, "grad_cases.pt"))
+    for f in ("spectral_cases.pt", "fno_cases.pt", "config_layers.pt", "grad_cases.pt"):
         print(f, os.path.getsize(os.path.join(HERE, f)) // 1024, "KiB")
 
 

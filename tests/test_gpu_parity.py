@@ -142,11 +142,12 @@ def test_batch_zero_and_errors():
         conv(torch.randn(1, 2, 8, 8, device="cuda", dtype=torch.float64))
 
 
-def test_backward_raises():
+def test_backward_through_fused_gelu_raises():
+    """The fused GELU epilogue keeps no pre-activation, so a call that needs a gradient must not use it."""
     conv = nb.SpectralConv(2, 2, (4, 4)).cuda()
-    y = conv(torch.randn(1, 2, 8, 8, device="cuda", requires_grad=True))
+    x = torch.randn(1, 2, 8, 8, device="cuda", requires_grad=True)
     with pytest.raises(NotImplementedError):
-        y.sum().backward()
+        conv(x, apply_gelu=True)
 
 
 def test_nonzero_stream_and_repeat():
