@@ -588,6 +588,158 @@ def run_ours(args, cfg, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_train(args, cfg, world, rank, local):
+    """One SpectralConv training step at the config's size: the forward (keeping the kept input spectrum)
+    and the backward giving dL/dx, dL/dW and dL/dbias for a fixed dL/dy, through torch autograd and the
+    library's kernels (neuralop/training/trainer.py:629-700 runs forward + loss.backward() per batch).
+    Every rank runs its own batch (weak scaling).  The phases are also timed one by one (rank 0)."""
+    from neuraloperator_b200 import _lib, ops
+    from neuraloperator_b200.geometry import adjoint_geometry
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    desc, batch, ci, co, grid, modes, fact = cfg
+    conv, x = make_inputs(cfg, dev, seed=0)
+    conv.engine = args.engine
+    conv.contraction_precision = args.precision
+    x.requires_grad_(True)
+    params = list(conv.parameters())
+    gen = torch.Generator(device="cpu").manual_seed(1)
+    g = torch.randn((batch, co, *grid), generator=gen).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    steps, warm = args.steps, args.warmup
+
+    def step():
+        y = conv(x)
+        return torch.autograd.grad(y, [x] + params, g)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        grads = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_eager = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    del grads
+    # timed region: the whole step (forward, autograd backward, every kernel of both) replayed from one
+    # CUDA graph, which removes the Python / autograd host time between launches; eager if capture fails
+    graph, launch = None, "eager"
+    if not args.no_graph:
+        try:
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                step()
+                with torch.cuda.graph(graph, stream=side):
+                    grads = step()
+            stream.wait_stream(side)
+            torch.cuda.synchronize()
+            launch = "cuda_graph"
+        except Exception as exc:  # noqa: BLE001
+            print(f"graph capture failed, timing eager launches: {exc}", file=sys.stderr)
+            graph = None
+            torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    del graph
+    if rank != 0:
+        return
+
+    def timed(fn, n=max(3, min(steps, 20))):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            out = fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n, out
+
+    geo = conv.geometry(list(grid))
+    kind, ws, ranks = conv.kernel_operands(geo)
+    ws = [w.detach() for w in ws]
+    xd = x.detach()
+    ms_fwd, (_, spec) = timed(lambda: ops.spectral_forward(xd, geo, ws, out_channels=co, weight_kind=kind, ranks=ranks,
+                                                            precision=args.precision, engine=args.engine,
+                                                            keep_spectrum=True))
+    adj = adjoint_geometry(geo)
+    packed_adj = None
+    if kind == "dense":  # the backward packs the adjoint straight from W (conjugate transpose in the pack)
+        ms_ops, packed_adj = timed(lambda: ops.pack_adjoint_dense(adj, batch, ws[0], precision=args.precision,
+                                                                   engine=args.engine))
+        aw, ar = [], ()
+    else:
+        ms_ops, (aw, ar) = timed(lambda: ops.adjoint_operands(kind, ws, ranks, False))
+    ms_adj, (_, gspec) = timed(lambda: ops.spectral_forward(g, adj, aw, out_channels=ci, weight_kind=kind, ranks=ar,
+                                                             precision=args.precision, engine=args.engine,
+                                                             keep_spectrum=True, packed=packed_adj))
+    wshape = (ci, co) + tuple(geo.kept)
+    marks = _lib.LaunchEvents(3)
+    with marks:
+        ms_wg, (gw, _) = timed(lambda: ops.weight_grad(spec, gspec, wshape, co))
+    wg_kernel_ms = marks.durations_ms()[0]
+    ms_fac = 0.0
+    if kind == "tucker":
+        from neuraloperator_b200.spectral_convolution import _tucker_grads
+        ms_fac, _ = timed(lambda: _tucker_grads(ws[0], ws[1:], gw))
+
+    hbm, peak_src = peaks()
+    p = math.prod(grid)
+    w_bytes = sum(t.numel() * t.element_size() for t in conv.weight.parameters())
+    mt = math.prod(geo.kept)
+    # algorithmic bytes of a training step: x, y (forward), dL/dy, dL/dx (backward), W twice, dL/dW, bias
+    b_alg = 2 * batch * ci * p * 4 + 2 * batch * co * p * 4 + 2 * w_bytes + w_bytes + 2 * co * 4
+    wg_bytes = (batch * ci * mt + batch * co * mt + ci * co * mt) * 8
+    wg_flop = 8 * batch * ci * co * mt
+    plan_f = ops.get_plan(ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks, precision=args.precision,
+                                        engine=args.engine), local)
+    plan_a = ops.get_plan(ops.make_desc(adj, batch, co, ci, weight_kind=kind, ranks=ar, precision=args.precision,
+                                        engine=args.engine), local)
+    pack = (1 if kind == "dense" else 3 + len(geo.kept)) if plan_a.packed_bytes > 0 else 0
+    launches = plan_f.launches_per_forward + pack + plan_a.launches_per_forward + 2
+    gbs = b_alg / (ms / 1e3) / 1e9
+    line = {
+        "metric": "SpectralConv training step (forward + backward) samples/s", "value": world * batch / (ms / 1e3),
+        "unit": "samples/s", "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.precision == "fp32" else "f32 (bf16 contraction)",
+        "data": "synthetic (seeded N(0,1) input and dL/dy, seeded complex weights; no dataset)",
+        "config": {"workload": desc + "_train", "global_batch": batch * world, "per_gpu_batch": batch,
+                   "grid": list(grid), "channels": [ci, co], "n_modes": list(modes), "factorization": fact or "dense",
+                   "parallelism": f"dp{world}" if world > 1 else "single",
+                   "engine": "fast" if plan_f.is_fast else "generic", "launch": launch,
+                   "ms_per_step_eager": ms_eager,
+                   "l2": f"inputs {x.numel() * 4 / 1e9:.2f} GB > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "bytes_alg_per_step": b_alg, "peak_source": peak_src + " (copy bandwidth, burst)",
+                     "definition": "2|x| + 2|y| (x, y, dL/dy, dL/dx) + 2|W| + |dL/dW| + 2|bias| over the step time"},
+        "phases_ms": {"forward_keep_spectrum": ms_fwd, "adjoint_weights": ms_ops, "adjoint_forward": ms_adj,
+                      "weight_grad": ms_wg, "tucker_factor_grads": ms_fac},
+        "weight_grad_kernel": {"ms": wg_kernel_ms, "bytes_alg": wg_bytes,
+                               "gbs": wg_bytes / (wg_kernel_ms / 1e3) / 1e9, "tflops": wg_flop / (wg_kernel_ms / 1e3) / 1e12,
+                               "definition": "|Xh| + |Gh| + |dL/dW| bytes; 8 B Ci Co Mt flops (fp32 FMA)"},
+        "gpu_launches": launches * steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -606,6 +758,8 @@ def main():
     ap.add_argument("--precision", choices=["fp32", "bf16"], default="fp32", help="contraction precision")
     ap.add_argument("--parallel", choices=["batch", "slab"], default="batch",
                     help="batch: each rank its own slice of the batch (weak); slab: 3D x-axis split (strong)")
+    ap.add_argument("--pass", dest="pass_", choices=["forward", "train"], default="forward",
+                    help="forward: the headline forward; train: forward + backward of one layer")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -619,7 +773,9 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        if args.model == "fno":
+        if args.pass_ == "train":
+            run_train(args, cfg, world, rank, local)
+        elif args.model == "fno":
             run_model(args, world, rank, local)
         elif args.parallel == "slab":
             run_slab(args, cfg, world, rank, local)

@@ -309,13 +309,26 @@ int32_t nop_spectral_forward_keep(const nop_plan* plan, const void* x, const voi
                                   size_t workspace_bytes, void* stream);
 
 /* Weight and bias gradients.  x_spec: kept spectrum of x from the forward plan; g_spec: kept
- * spectrum of g from the adjoint plan (nop_spectral_forward_keep on each).  grad_w (or NULL):
+ * spectrum of g from the adjoint plan (nop_spectral_forward_keep on each).  workspace:
+ * nop_spectral_weight_grad_workspace_size bytes (256-byte aligned), or NULL when that is 0.  grad_w (or NULL):
  * [Ci, Co, kept...] complex64 (separable: [C, kept...]), the gradient of the dense weight slice the
  * forward used (for Tucker / CP weights, of the reconstructed weight; the factor gradients follow
  * from it by the chain rule).  grad_bias (or NULL): [Co] float32.  Replaces the autograd of the
  * contraction einsum (spectral_convolution.py:21-52) and of the bias add (:567-568). */
 int32_t nop_spectral_weight_grad(const nop_plan* plan, const void* x_spec, const nop_plan* adjoint_plan,
-                                 const void* g_spec, void* grad_w, float* grad_bias, void* stream);
+                                 const void* g_spec, void* grad_w, float* grad_bias, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Packed weights of an ADJOINT plan (dense, fused engine) straight from the forward's dense weight
+ * [Ci, Co, kept...] (the adjoint's Co, Ci): the conjugate transpose is taken while packing, so no
+ * transposed copy of the weight is made.  Same result as nop_spectral_pack_weights on conj(W)^T. */
+int32_t nop_spectral_pack_weights_adjoint(const nop_plan* adjoint_plan, const void* forward_weight, void* packed,
+                                          size_t packed_bytes, void* stream);
+
+/* Device workspace of nop_spectral_weight_grad for the forward plan (0: none needed).  Small mode
+ * counts with a large batch split the batch sum over more CTAs; the partial sums live here and are
+ * reduced in a fixed order, so results do not depend on scheduling. */
+int32_t nop_spectral_weight_grad_workspace_size(const nop_plan* plan, size_t* bytes);
 
 #ifdef __cplusplus
 }

@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "nop_spectral_slab_inverse_planes", "nop_spectral_host_workspace_size", "nop_spectral_forward_host",
     "nop_device_status", "nop_pointwise_smem_bytes", "nop_pointwise_forward",
     "nop_spectral_spectrum_layout", "nop_spectral_forward_keep", "nop_spectral_weight_grad",
+    "nop_spectral_weight_grad_workspace_size", "nop_spectral_pack_weights_adjoint",
 )
 
 MAX_SLAB_RANKS = 64
@@ -145,7 +146,12 @@ def _declare(lib):
         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.nop_spectral_weight_grad.restype = ctypes.c_int32
     lib.nop_spectral_weight_grad.argtypes = [c_plan_p, ctypes.c_void_p, c_plan_p, ctypes.c_void_p, ctypes.c_void_p,
-                                             ctypes.c_void_p, ctypes.c_void_p]
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.nop_spectral_pack_weights_adjoint.restype = ctypes.c_int32
+    lib.nop_spectral_pack_weights_adjoint.argtypes = [c_plan_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                                      ctypes.c_void_p]
+    lib.nop_spectral_weight_grad_workspace_size.restype = ctypes.c_int32
+    lib.nop_spectral_weight_grad_workspace_size.argtypes = [c_plan_p, ctypes.POINTER(ctypes.c_size_t)]
     lib.nop_device_status.restype = ctypes.c_int32
     lib.nop_device_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]
     lib.nop_spectral_host_workspace_size.restype = ctypes.c_int32

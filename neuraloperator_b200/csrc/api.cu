@@ -553,6 +553,23 @@ int32_t nop_spectral_pack_weights(const nop_plan* plan, const void* const* weigh
                      static_cast<cudaStream_t>(stream));
 }
 
+int32_t nop_spectral_pack_weights_adjoint(const nop_plan* adjoint_plan, const void* forward_weight, void* packed,
+                                          size_t packed_bytes, void* stream) {
+    if (!adjoint_plan) return fail(NOP_E_INVALID, "plan is NULL");
+    const Plan& p = *reinterpret_cast<const Plan*>(adjoint_plan);
+    if (p.packed_bytes == 0) return fail(NOP_E_UNSUPPORTED, "this plan takes its weights unpacked");
+    if (p.d.weight_kind != NOP_WEIGHT_DENSE || p.d.separable)
+        return fail(NOP_E_UNSUPPORTED, "adjoint packing needs a dense, non-separable weight");
+    if (!forward_weight) return fail(NOP_E_INVALID, "weight pointer is NULL");
+    if ((uintptr_t)forward_weight % 8) return fail(NOP_E_ALIGNMENT, "weights must be 8-byte aligned (complex64)");
+    if (!packed || packed_bytes < p.packed_bytes)
+        return fail(NOP_E_WORKSPACE, "packed-weight buffer missing or smaller than nop_spectral_packed_size");
+    if ((uintptr_t)packed % kAlign) return fail(NOP_E_ALIGNMENT, "packed-weight buffer must be 256-byte aligned");
+    int32_t rc = check_device(p);
+    if (rc != NOP_OK) return rc;
+    return fast_pack_adjoint(p, forward_weight, static_cast<char*>(packed), static_cast<cudaStream_t>(stream));
+}
+
 static int32_t forward_packed_impl(const nop_plan* plan, const void* x, const void* packed, size_t packed_bytes,
                                    const float* bias, const float* addend, int32_t apply_gelu, void* y,
                                    void* workspace, size_t workspace_bytes, void* stream, float2* xs) {
@@ -612,8 +629,15 @@ int32_t nop_spectral_forward_keep(const nop_plan* plan, const void* x, const voi
                         xs);
 }
 
+int32_t nop_spectral_weight_grad_workspace_size(const nop_plan* plan, size_t* bytes) {
+    if (!plan || !bytes) return fail(NOP_E_INVALID, "NULL argument");
+    *bytes = weight_grad_workspace(*reinterpret_cast<const Plan*>(plan));
+    return NOP_OK;
+}
+
 int32_t nop_spectral_weight_grad(const nop_plan* plan, const void* x_spec, const nop_plan* adjoint_plan,
-                                 const void* g_spec, void* grad_w, float* grad_bias, void* stream) {
+                                 const void* g_spec, void* grad_w, float* grad_bias, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
     if (!plan || !adjoint_plan) return fail(NOP_E_INVALID, "plan is NULL");
     const Plan& p = *reinterpret_cast<const Plan*>(plan);
     const Plan& a = *reinterpret_cast<const Plan*>(adjoint_plan);
@@ -625,7 +649,8 @@ int32_t nop_spectral_weight_grad(const nop_plan* plan, const void* x_spec, const
     if (rc != NOP_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     launch_mark_begin(s);
-    return launch_mark_end(weight_grad(p, x_spec, a, g_spec, grad_w, grad_bias, s));
+    if (workspace && (uintptr_t)workspace % kAlign) return fail(NOP_E_ALIGNMENT, "workspace must be 256-byte aligned");
+    return launch_mark_end(weight_grad(p, x_spec, a, g_spec, grad_w, grad_bias, workspace, workspace_bytes, s));
 }
 
 /* ---- forward from host memory ------------------------------------------------------------- */

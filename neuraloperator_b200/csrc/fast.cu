@@ -365,7 +365,7 @@ k_mix(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq, f
 // ------------------------------------------------------------------------------------------
 // per-mode weight, element (i, o, m) at W[i * s_i + o * s_o + m]  ->  [Q][I][4][O] float4
 __global__ void k_pack_modes(const float2* __restrict__ W, float4* __restrict__ Wp, int I, int O, int64_t Mt,
-                             int64_t Q, int64_t s_i, int64_t s_o) {
+                             int64_t Q, int64_t s_i, int64_t s_o, int conj = 0) {
     const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (idx >= Q * I * 4 * O) return;
     const int o = (int)(idx % O);
@@ -376,7 +376,7 @@ __global__ void k_pack_modes(const float2* __restrict__ W, float4* __restrict__ 
     const float2* src = W + i * s_i + o * s_o;
     const float2 a = m < Mt ? src[m] : make_float2(0.f, 0.f);
     const float2 b = m + 1 < Mt ? src[m + 1] : make_float2(0.f, 0.f);
-    Wp[idx] = make_float4(a.x, a.y, b.x, b.y);
+    Wp[idx] = conj ? make_float4(a.x, -a.y, b.x, -b.y) : make_float4(a.x, a.y, b.x, b.y);
 }
 
 // mode-independent weight, element (i, o) at U[i * s_i + o * s_o]  ->  [I][4][O] float4
@@ -922,6 +922,21 @@ int32_t fast_device_status(int* status, bool clear) {
 int32_t fast_launches(const Plan& p) {
     const int transforms = p.fast_kind == FastKind::Vol3D ? 4 : 2;
     return transforms + (p.d.weight_kind == NOP_WEIGHT_DENSE ? 1 : 3);
+}
+
+int32_t fast_pack_adjoint(const Plan& p, const void* W, char* packed, cudaStream_t s) {
+    // p is the adjoint plan (Ci' = Co, Co' = Ci); W the forward's dense weight [Co'][Ci'][Mt]:
+    // W'[i'][o'][m] = conj(W[o'][i'][m]) is element i' * Mt + o' * (Ci' * Mt) of W
+    const nop_spectral_desc& d = p.d;
+    if (d.weight_kind != NOP_WEIGHT_DENSE)
+        return fail(NOP_E_UNSUPPORTED, "adjoint packing from the forward weight needs dense weights");
+    const int64_t Q = mode_blocks(p), Mt = p.modes_total, Ci = d.in_channels, Co = d.out_channels;
+    const int64_t n = Q * Ci * 4 * Co;
+    k_pack_modes<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(W),
+                                                            reinterpret_cast<float4*>(packed + p.pk_w), (int)Ci,
+                                                            (int)Co, Mt, Q, Mt, Ci * Mt, 1);
+    cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? NOP_OK : cuda_fail(err, "adjoint pack launch");
 }
 
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s) {

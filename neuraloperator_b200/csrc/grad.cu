@@ -17,6 +17,7 @@
 // q * q_stride + b * b_stride + c * c_stride + l complex elements from the base.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "nop_internal.cuh"
@@ -60,13 +61,19 @@ __device__ __forceinline__ float mode_factor(int64_t t, int kl, int nyq, int dbl
     return (m == 0 || m == nyq) ? 1.f : 2.f;
 }
 
-// grid: (mode blocks Q, ceil(Ci / TI), ceil(Co / TO)); gw = [Ci][Co][Mt] complex64
+// grid: (mode blocks Q x batch splits S, ceil(Ci / TI), ceil(Co / TO)).  Split s sums batch rows
+// [s * bsplit, min(B, (s + 1) * bsplit)).  S == 1: gw = [Ci][Co][Mt] complex64 with the factor d_t;
+// S > 1: gw = partial sums [S][Ci][Co][Mt] without it (k_reduce_splits finishes).
 __global__ void __launch_bounds__(THREADS, 2)
-k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, int64_t Mt, int kl, int nyq, int dbl) {
+k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, int64_t Mt, int kl, int nyq, int dbl,
+              int64_t Q, int bsplit) {
     extern __shared__ __align__(16) float2 sm[];
     const int tid = threadIdx.x;
     const int l = tid & 7, ot = (tid >> 3) & 3, it = tid >> 5;
-    const int64_t q = blockIdx.x;
+    const int64_t q = blockIdx.x % Q;
+    const int split = (int)(blockIdx.x / Q);
+    const bool partial = gridDim.x > Q;
+    const int bbeg = split * bsplit, bend = min(B, bbeg + bsplit);
     const int i0 = blockIdx.y * TI, o0 = blockIdx.z * TO;
     const int64_t t_tid = 8 * q + l;
 
@@ -79,7 +86,7 @@ k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, in
             const int e = k * THREADS + tid;
             const int ll = e & 7, i = (e >> 3) % TI, b = e / (8 * TI);
             const int64_t t = 8 * q + ll;
-            const bool v = b0 + b < B && i0 + i < Ci && t < Mt;
+            const bool v = b0 + b < bend && i0 + i < Ci && t < Mt;
             cp_async8(xs + e, X.p + q * X.sq + (int64_t)(b0 + b) * X.sb + (int64_t)(i0 + i) * X.sc + ll, X.p, v);
         }
 #pragma unroll
@@ -87,7 +94,7 @@ k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, in
             const int e = k * THREADS + tid;
             const int ll = e & 7, o = (e >> 3) % TO, b = e / (8 * TO);
             const int64_t t = 8 * q + ll;
-            const bool v = b0 + b < B && o0 + o < Co && t < Mt;
+            const bool v = b0 + b < bend && o0 + o < Co && t < Mt;
             cp_async8(gs + b * (4 * GROW) + (o >> 3) * GROW + (o & 7) * 8 + ll,
                       G.p + q * G.sq + (int64_t)(b0 + b) * G.sb + (int64_t)(o0 + o) * G.sc + ll, G.p, v);
         }
@@ -100,11 +107,11 @@ k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, in
 #pragma unroll
         for (int s = 0; s < 8; ++s) acc[r][s] = make_float2(0.f, 0.f);
 
-    const int nchunks = (B + BK - 1) / BK;
-    load(0, 0);
+    const int nchunks = (bend - bbeg + BK - 1) / BK;
+    if (nchunks > 0) load(0, bbeg);
     for (int c = 0; c < nchunks; ++c) {
         if (c + 1 < nchunks) {
-            load((c + 1) & 1, (c + 1) * BK);
+            load((c + 1) & 1, bbeg + (c + 1) * BK);
             cp_wait<1>();
         } else {
             cp_wait<0>();
@@ -131,7 +138,8 @@ k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, in
     }
 
     if (t_tid >= Mt) return;
-    const float f = mode_factor(t_tid, kl, nyq, dbl);
+    const float f = partial ? 1.f : mode_factor(t_tid, kl, nyq, dbl);
+    float2* out = gw + (partial ? (int64_t)split * Ci * Co * Mt : 0);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const int i = i0 + it * 4 + r;
@@ -139,9 +147,24 @@ k_weight_grad(Spec X, Spec G, float2* __restrict__ gw, int B, int Ci, int Co, in
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             const int o = o0 + ot * 8 + s;
-            if (o < Co) gw[((int64_t)i * Co + o) * Mt + t_tid] = make_float2(f * acc[r][s].x, f * acc[r][s].y);
+            if (o < Co) out[((int64_t)i * Co + o) * Mt + t_tid] = make_float2(f * acc[r][s].x, f * acc[r][s].y);
         }
     }
+}
+
+// gw[e] = d_t * sum_s part[s][e] over the S batch splits, in split order (deterministic)
+__global__ void k_reduce_splits(const float2* __restrict__ part, float2* __restrict__ gw, int64_t n, int S,
+                                int64_t Mt, int kl, int nyq, int dbl) {
+    const int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    float2 a = part[e];
+    for (int s = 1; s < S; ++s) {
+        const float2 v = part[(int64_t)s * n + e];
+        a.x += v.x;
+        a.y += v.y;
+    }
+    const float f = mode_factor(e % Mt, kl, nyq, dbl);
+    gw[e] = make_float2(f * a.x, f * a.y);
 }
 
 // separable weights: gw = [C][Mt]; one thread per (c, t)
@@ -195,8 +218,29 @@ int32_t spectrum_layout(const Plan& p, int64_t* q_stride, int64_t* b_stride, int
     return NOP_OK;
 }
 
+// batch splits of the dense weight-gradient kernel: enough CTAs for about two waves of 2 CTAs per SM,
+// each split at least one pipeline stage of batch rows
+static void wg_splits(const Plan& p, int* S, int* bsplit) {
+    const nop_spectral_desc& d = p.d;
+    const int64_t base = ((p.modes_total + 7) / 8) * ceil_div(d.in_channels, wg::TI) * ceil_div(d.out_channels, wg::TO);
+    const int64_t chunks = ceil_div(d.batch, wg::BK);
+    const int64_t want = 4 * (int64_t)p.sm_count;
+    int64_t s = base >= want ? 1 : std::min<int64_t>(chunks, ceil_div(want, std::max<int64_t>(base, 1)));
+    s = std::max<int64_t>(1, std::min<int64_t>(s, 64));
+    const int64_t per = ceil_div(chunks, s) * wg::BK;  // batch rows per split, whole stages
+    *bsplit = (int)per;
+    *S = (int)ceil_div(d.batch, per);
+}
+
+size_t weight_grad_workspace(const Plan& p) {
+    if (p.d.separable || p.d.batch == 0) return 0;
+    int S, bs;
+    wg_splits(p, &S, &bs);
+    return S > 1 ? (size_t)S * p.d.in_channels * p.d.out_channels * p.modes_total * sizeof(float2) : 0;
+}
+
 int32_t weight_grad(const Plan& p, const void* x_spec, const Plan& a, const void* g_spec, void* grad_w,
-                    float* grad_bias, cudaStream_t s) {
+                    float* grad_bias, void* workspace, size_t workspace_bytes, cudaStream_t s) {
     const nop_spectral_desc& d = p.d;
     const nop_spectral_desc& e = a.d;
     if (e.ndim != d.ndim || e.batch != d.batch || e.in_channels != d.out_channels ||
@@ -235,11 +279,24 @@ int32_t weight_grad(const Plan& p, const void* x_spec, const Plan& a, const void
                     return cuda_fail(err, "cudaFuncSetAttribute(weight_grad)");
                 g_wg_attr.fetch_or(bit);
             }
-            const dim3 grid((unsigned)((Mt + 7) / 8), (unsigned)ceil_div(Ci, wg::TI), (unsigned)ceil_div(Co, wg::TO));
-            if (grid.x > 0x7fffffffu || grid.y > 65535u || grid.z > 65535u)
+            int S, bsplit;
+            wg_splits(p, &S, &bsplit);
+            const size_t need = weight_grad_workspace(p);
+            if (need > 0 && (!workspace || workspace_bytes < need))
+                return fail(NOP_E_WORKSPACE, "weight-gradient workspace missing or smaller than "
+                                             "nop_spectral_weight_grad_workspace_size");
+            const int64_t Q = (Mt + 7) / 8;
+            const dim3 grid((unsigned)(Q * S), (unsigned)ceil_div(Ci, wg::TI), (unsigned)ceil_div(Co, wg::TO));
+            if (Q * S > 0x7fffffff || grid.y > 65535u || grid.z > 65535u)
                 return fail(NOP_E_UNSUPPORTED, "weight gradient grid too large");
-            wg::k_weight_grad<<<grid, wg::THREADS, wg::SMEM, s>>>(X, G, static_cast<float2*>(grad_w), B, Ci, Co, Mt,
-                                                                  kl, nyq, dbl);
+            float2* dst = S > 1 ? static_cast<float2*>(workspace) : static_cast<float2*>(grad_w);
+            wg::k_weight_grad<<<grid, wg::THREADS, wg::SMEM, s>>>(X, G, dst, B, Ci, Co, Mt, kl, nyq, dbl, Q, bsplit);
+            if (S > 1 && (err = cudaGetLastError()) == cudaSuccess) {
+                launch_mark(s);
+                const int64_t n = (int64_t)Ci * Co * Mt;
+                wg::k_reduce_splits<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(dst, static_cast<float2*>(grad_w), n, S,
+                                                                              Mt, kl, nyq, dbl);
+            }
         }
         if ((err = cudaGetLastError()) != cudaSuccess) return cuda_fail(err, "weight gradient launch");
         launch_mark(s);

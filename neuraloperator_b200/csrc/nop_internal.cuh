@@ -108,6 +108,8 @@ int32_t fast_launches(const Plan& p);
 // status word of the tensor-core kernels on the current device (synchronous read, optional reset)
 int32_t fast_device_status(int* status, bool clear);
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s);
+// adjoint plan's packed weights straight from the forward's dense weight (conjugate transpose in the pack)
+int32_t fast_pack_adjoint(const Plan& p, const void* W, char* packed, cudaStream_t s);
 // xs (nullable): the contraction reads the kept input spectrum from xs instead of the workspace,
 // so it is still there after the call
 int32_t fast_forward_packed(const Plan& p, const void* x, const char* packed, const float* bias,
@@ -123,8 +125,9 @@ int32_t fast_slab_planes_inv(const Plan& p, const void* recv2, const float* bias
 
 // backward: kept-spectrum layout of a plan's input side and the weight / bias gradients (grad.cu)
 int32_t spectrum_layout(const Plan& p, int64_t* q_stride, int64_t* b_stride, int64_t* c_stride, size_t* bytes);
+size_t weight_grad_workspace(const Plan& p);
 int32_t weight_grad(const Plan& p, const void* x_spec, const Plan& adjoint, const void* g_spec, void* grad_w,
-                    float* grad_bias, cudaStream_t s);
+                    float* grad_bias, void* workspace, size_t workspace_bytes, cudaStream_t s);
 
 // ------------------------------------------------------------------------------------------
 // small device helpers

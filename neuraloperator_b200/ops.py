@@ -102,14 +102,15 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
                      bias: Optional[torch.Tensor] = None, addend: Optional[torch.Tensor] = None,
                      apply_gelu: bool = False, precision: str = "fp32", engine: str = "auto",
                      out: Optional[torch.Tensor] = None, cache: Optional[dict] = None,
-                     keep_spectrum: bool = False):
+                     keep_spectrum: bool = False, packed: Optional[torch.Tensor] = None):
     """Run one spectral-block forward on x's device and current stream.
 
     Fused-engine plans use packed weights (nop_spectral_pack_weights).  With ``cache`` (a dict
     owned by the calling module) the packed buffer is kept and reused while the weight tensors
     keep their storage and version counter; any in-place update or replacement repacks.
     With ``keep_spectrum`` the kept input spectrum is kept too (nop_spectral_forward_keep) and
-    ``(y, Spectrum)`` is returned, for ``weight_grad``.
+    ``(y, Spectrum)`` is returned, for ``weight_grad``.  ``packed``: weights already packed for this
+    call's plan (``weights`` is then unused).
     """
     if not x.is_cuda:
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path); "
@@ -140,8 +141,7 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
     if keep_spectrum:
         spec = torch.empty(max(plan.spectrum_bytes, 1), device=dev, dtype=torch.uint8)
     with torch.cuda.device(dev):
-        packed = None
-        if plan.packed_bytes > 0:
+        if packed is None and plan.packed_bytes > 0:
             packed = _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream)
         if spec is not None:
             _lib.check(lib.nop_spectral_forward_keep(
@@ -203,6 +203,25 @@ def adjoint_operands(kind: str, weights: List[torch.Tensor], ranks: Sequence[int
     raise ValueError(f"unknown weight kind {kind!r}")
 
 
+def pack_adjoint_dense(geo_adj: Geometry, batch: int, weight: torch.Tensor, *, precision: str = "fp32",
+                       engine: str = "auto") -> Optional[torch.Tensor]:
+    """Packed weights of the adjoint plan straight from the forward's dense weight [Ci, Co, kept...]
+    (nop_spectral_pack_weights_adjoint), or None when that plan takes its weights unpacked."""
+    ci, co = weight.shape[0], weight.shape[1]
+    dev = weight.device
+    desc = make_desc(geo_adj, batch, co, ci, weight_kind="dense", precision=precision, engine=engine)
+    plan = get_plan(desc, dev.index if dev.index is not None else torch.cuda.current_device())
+    if plan.packed_bytes == 0:
+        return None
+    w = weight.detach().to(torch.complex64).contiguous()
+    packed = torch.empty(plan.packed_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(_lib.library().nop_spectral_pack_weights_adjoint(plan.handle, _ptr(w), _ptr(packed),
+                                                                    plan.packed_bytes, stream))
+    return packed
+
+
 def weight_grad(fwd: Spectrum, adj: Spectrum, grad_w_shape: Optional[Sequence[int]], bias_channels: int = 0):
     """dL/dW (dense-equivalent, ``grad_w_shape`` complex64, or None) and dL/dbias ([bias_channels] float32,
     or None when 0) from the kept spectra of x (forward plan) and of dL/dy (adjoint plan)
@@ -212,10 +231,14 @@ def weight_grad(fwd: Spectrum, adj: Spectrum, grad_w_shape: Optional[Sequence[in
     gb = torch.empty(bias_channels, device=dev, dtype=torch.float32) if bias_channels else None
     if gw is None and gb is None:
         return None, None
+    lib = _lib.library()
+    size = ctypes.c_size_t()
+    _lib.check(lib.nop_spectral_weight_grad_workspace_size(fwd.plan.handle, ctypes.byref(size)))
+    ws = torch.empty(int(size.value), device=dev, dtype=torch.uint8) if size.value else None
     with torch.cuda.device(dev):
         stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        _lib.check(_lib.library().nop_spectral_weight_grad(fwd.plan.handle, _ptr(fwd.buf), adj.plan.handle,
-                                                           _ptr(adj.buf), _ptr(gw), _ptr(gb), stream))
+        _lib.check(lib.nop_spectral_weight_grad(fwd.plan.handle, _ptr(fwd.buf), adj.plan.handle, _ptr(adj.buf),
+                                                _ptr(gw), _ptr(gb), _ptr(ws), int(size.value), stream))
     return gw, gb
 
 
