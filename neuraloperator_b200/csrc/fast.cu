@@ -906,6 +906,8 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
     return off;
 }
 
+int* status_word(int device) { return device_status_ptr(device); }
+
 int32_t fast_device_status(int* status, bool clear) {
     int v = 0;
     cudaError_t err = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));

@@ -107,6 +107,8 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws);
 int32_t fast_launches(const Plan& p);
 // status word of the tensor-core kernels on the current device (synchronous read, optional reset)
 int32_t fast_device_status(int* status, bool clear);
+// device address of that status word on `device` (kernels write it when a bounded wait expires)
+int* status_word(int device);
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s);
 // adjoint plan's packed weights straight from the forward's dense weight (conjugate transpose in the pack)
 int32_t fast_pack_adjoint(const Plan& p, const void* W, char* packed, cudaStream_t s);

@@ -12,6 +12,7 @@
 // same sums as the reference's fp32 Conv1d / SoftGating / GELU ops).  The residual r is read from
 // global memory into registers right before the K loop of the layer that adds it.
 #include <cstdint>
+#include <cstdlib>
 #include <string>
 
 #include "nop_internal.cuh"
@@ -243,11 +244,22 @@ __global__ void __launch_bounds__(THREADS, 2) k_pointwise(Params p) {
 }  // namespace pw
 }  // namespace nop
 
+#include "pointwise_tc.cuh"
+
 using namespace nop;
 
 extern "C" int32_t nop_pointwise_smem_bytes(const nop_pointwise_desc* d, size_t* bytes);
 
 namespace {
+
+// NOP_POINTWISE=tc selects the tcgen05 kernel (pointwise_tc.cuh).  It is parity-tested but measured
+// slower than the CUDA-core kernel on B200 (C4 model 42.6 vs 40.1 ms, C5 358 vs 209 ms: one tile's
+// operands fill the CTA, so each SM runs one serialized GEMM -> epilogue chain at a time), so the
+// CUDA-core kernel is the default.
+bool pointwise_on_tensor_cores() {
+    const char* v = std::getenv("NOP_POINTWISE");
+    return v && std::string(v) == "tc";
+}
 
 int32_t build_params(const nop_pointwise_desc* d, pw::Params* p, size_t* smem, int* ns) {
     if (!d) return fail(NOP_E_INVALID, "descriptor is NULL");
@@ -366,6 +378,16 @@ int32_t nop_pointwise_forward(const nop_pointwise_desc* d, const float* x, const
     int dev = 0, sms = 148;
     NOP_CUDA_TRY(cudaGetDevice(&dev));
     NOP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    pwtc::Layout L;
+    if (pointwise_on_tensor_cores() && pwtc::plan_layout(p, &L)) {
+        int* status = status_word(dev);
+        if (!status) return fail(NOP_E_CUDA, "status word of the tensor-core kernels is not available");
+        NOP_CUDA_TRY(cudaFuncSetAttribute(pwtc::k_pointwise_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem));
+        const unsigned grid = (unsigned)(p.tiles < sms ? p.tiles : sms);
+        pwtc::k_pointwise_tc<<<grid, pwtc::THREADS, L.smem, static_cast<cudaStream_t>(stream)>>>(p, L, status);
+        NOP_CUDA_TRY(cudaGetLastError());
+        return NOP_OK;
+    }
     auto launch = [&](auto kernel) -> int32_t {
         NOP_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         int per_sm = 0;

@@ -72,8 +72,18 @@ CASES = [
 ]
 
 
+@pytest.fixture(params=["cuda_cores", "tensor_cores"])
+def engine(request, monkeypatch):
+    """Both per-pixel kernels: the CUDA-core one (default) and tcgen05 (NOP_POINTWISE=tc)."""
+    if request.param == "tensor_cores":
+        monkeypatch.setenv("NOP_POINTWISE", "tc")
+    else:
+        monkeypatch.delenv("NOP_POINTWISE", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
-def test_fused_channel_mlp_matches_reference(case):
+def test_fused_channel_mlp_matches_reference(case, engine):
     name, batch, spatial, cin, hidden, cout, cnext, grid, gate, gate_bias, act_out = case
     g = torch.Generator().manual_seed(3)
     ku = cin + (len(spatial) if grid is not None else 0)
@@ -100,6 +110,8 @@ def test_fused_channel_mlp_matches_reference(case):
     assert rel_l2(y.cpu(), y_ref) <= TOL
     if cnext:
         assert rel_l2(z.cpu(), z_ref) <= TOL
+    from neuraloperator_b200 import _lib
+    assert _lib.device_status() == 0
 
 
 def test_fused_fno_matches_module_path(monkeypatch):
