@@ -403,11 +403,19 @@ def fno_forward(x: torch.Tensor, params: dict, cfg: dict) -> torch.Tensor:
 
     ``params = {"lifting": [(W, b), ...], "projection": [(W, b), ...], "blocks": [blk, ...]}``;
     each ``blk`` holds ``weight``, ``bias``, ``fno_skip``, ``mlp`` and ``mlp_skip``.
+    With ``cfg["n_modes_per_layer"]`` (and optionally ``cfg["max_n_modes_per_layer"]``) block i uses its own
+    modes: ``FNOStaged.forward`` (neuralop/models/fno_staged.py:456-502), whose blocks repeat FNOBlocks'.
     """
     if cfg.get("positional_embedding", "grid") == "grid":
         x = grid_embedding(x)
     x = channel_mlp(x, params["lifting"])
     n_layers = len(params["blocks"])
+    per_layer = cfg.get("n_modes_per_layer")
     for i, blk in enumerate(params["blocks"]):
-        x = fno_block(x, blk, i, n_layers, cfg)
+        c = cfg
+        if per_layer is not None:
+            c = dict(cfg, n_modes=per_layer[i])
+            if cfg.get("max_n_modes_per_layer") is not None:
+                c["max_n_modes"] = cfg["max_n_modes_per_layer"][i]
+        x = fno_block(x, blk, i, n_layers, c)
     return channel_mlp(x, params["projection"])

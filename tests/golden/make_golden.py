@@ -9,7 +9,8 @@ complex data, odd sizes, Nyquist kept, incremental modes, output_shape, fft_norm
 ``fno_cases.pt`` (FNOBlocks / FNO / TFNO end to end), ``config_layers.pt`` (single
 SpectralConv layers with the modes and grids of the five benchmark configurations, at
 reduced batch/channel counts) and ``grad_cases.pt`` (gradients: torch autograd through the
-reference's forward for a seeded dL/dy, for SpectralConv layers and for small FNO / TFNO models).  Every tensor is generated from fixed seeds; the
+reference's forward for a seeded dL/dy, for SpectralConv layers and for small FNO / TFNO models)
+and ``staged_cases.pt`` (FNOStaged with per-layer modes: the reference's state_dict, input and output).  Every tensor is generated from fixed seeds; the
 reference modules compute the outputs.  The files are committed so the tests need no
 reference checkout.
 """
@@ -373,13 +374,40 @@ def grad_cases(mods):
     return {"layers": layers, "models": models}
 
 
+def staged_cases(mods):
+    """FNOStaged (neuralop/models/fno_staged.py): per-layer modes, the reference's state_dict and output."""
+    import importlib
+    FS = importlib.import_module("neuralop.models.fno_staged").FNOStaged
+    out = []
+
+    def add(name, size, batch, seed, **kw):
+        gen = torch.Generator().manual_seed(seed)
+        torch.manual_seed(seed)
+        model = FS(**kw)
+        _randomise_module(model, gen)
+        x = torch.randn((batch, kw["in_channels"], *size), generator=gen)
+        with torch.no_grad():
+            y = model(x)
+        sd = {k: v.detach().clone() for k, v in model.state_dict().items() if torch.is_tensor(v)}
+        out.append(dict(name=name, kwargs=kw, state_dict=sd, x=x, y=y.detach().clone()))
+
+    add("staged2d", (32, 32), 2, 31, n_modes_per_layer=[(12, 12), (8, 8), (6, 6)], in_channels=1,
+        out_channels=1, hidden_channels=8)
+    add("staged2d_max_modes", (24, 24), 2, 32, n_modes_per_layer=[(8, 8), (6, 6)],
+        max_n_modes_per_layer=[(10, 10), (8, 8)], in_channels=2, out_channels=1, hidden_channels=6)
+    add("staged1d_tucker", (64,), 2, 33, n_modes_per_layer=[(16,), (8,), (4,)], in_channels=1, out_channels=1,
+        hidden_channels=8, factorization="tucker", rank=0.5)
+    return out
+
+
 def main():
     mods = ref_loader.install()
     torch.save(spectral_cases(mods), os.path.join(HERE, "spectral_cases.pt"))
     torch.save(fno_cases(mods), os.path.join(HERE, "fno_cases.pt"))
     torch.save(config_layers(mods), os.path.join(HERE, "config_layers.pt"))
     torch.save(grad_cases(mods), os.path.join(HERE, "grad_cases.pt"))
-    for f in ("spectral_cases.pt", "fno_cases.pt", "config_layers.pt", "grad_cases.pt"):
+    torch.save(staged_cases(mods), os.path.join(HERE, "staged_cases.pt"))
+    for f in ("spectral_cases.pt", "fno_cases.pt", "config_layers.pt", "grad_cases.pt", "staged_cases.pt"):
         print(f, os.path.getsize(os.path.join(HERE, f)) // 1024, "KiB")
 
 
