@@ -34,6 +34,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "l2_hints.cuh"
 #include "nop_internal.cuh"
 
 namespace nop {
@@ -243,7 +244,8 @@ __device__ __forceinline__ void cp_async16z(void* smem, const void* gmem, bool v
 // (layout [value c][thread p] float4, so the threads' later reads are conflict-free); values out of
 // range are zero-filled
 template <int CO, bool BF16>
-__device__ __forceinline__ void issue_step(float4* slot, const Problem& pr, const Tile& tl, int k0, int p) {
+__device__ __forceinline__ void issue_step(float4* slot, const Problem& pr, const Tile& tl, int k0, int p,
+                                           uint64_t pol) {
     constexpr int KH = Step<BF16>::KH;
     if (p < 128) {
         const int b = p >> 1, kh = p & 1;
@@ -253,8 +255,8 @@ __device__ __forceinline__ void issue_step(float4* slot, const Problem& pr, cons
         for (int c = 0; c < KH; ++c) {
             const bool ok = bok && k0 + kh * KH + c < pr.Ci;
             const float2* sc = ok ? src + c * 8 : pr.X;
-            cp_async16z(slot + (2 * c) * PROD_THREADS + p, sc, ok);
-            cp_async16z(slot + (2 * c + 1) * PROD_THREADS + p, ok ? sc + 2 : pr.X, ok);
+            l2::cp_async16(slot + (2 * c) * PROD_THREADS + p, sc, ok, pol);
+            l2::cp_async16(slot + (2 * c + 1) * PROD_THREADS + p, ok ? sc + 2 : pr.X, ok, pol);
         }
     } else if (p < 128 + 2 * CO) {
         const int u = p - 128;
@@ -265,8 +267,8 @@ __device__ __forceinline__ void issue_step(float4* slot, const Problem& pr, cons
             const int i = k0 + kh * KH + c;
             const bool ok = ook && i < pr.Ci;
             const float4* s4 = ok ? tl.Wq + ((int64_t)i * 4 + 2 * tl.h) * pr.Co + tl.o0 + o : pr.Wp;
-            cp_async16z(slot + (2 * c) * PROD_THREADS + p, s4, ok);
-            cp_async16z(slot + (2 * c + 1) * PROD_THREADS + p, ok ? s4 + pr.Co : pr.Wp, ok);
+            l2::cp_async16(slot + (2 * c) * PROD_THREADS + p, s4, ok, pol);
+            l2::cp_async16(slot + (2 * c + 1) * PROD_THREADS + p, ok ? s4 + pr.Co : pr.Wp, ok, pol);
         }
     }
 }
@@ -382,6 +384,7 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
     if (warp >= EPI_WARPS && warp < MMA_WARP) {
         // ------------------------------ producers ------------------------------
         const int p = tid - 32 * EPI_WARPS;
+        const uint64_t pol_in = l2::evict_first();  // spectrum and weights are read once
         // raw ring: the copies of the next RS - 1 steps are in flight (cp.async, no registers held)
         // while this thread converts the current step; each thread reads back only what it copied
         constexpr int RS = C::RS;
@@ -393,7 +396,7 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
         int slot_in = 0, slot_out = 0;
         auto issue_next = [&]() {
             if (lk < my_tiles) {
-                issue_step<CO, BF16>(raw + slot_in * SLOT_F4, pr, ltile, lkc * C::KS, p);
+                issue_step<CO, BF16>(raw + slot_in * SLOT_F4, pr, ltile, lkc * C::KS, p, pol_in);
                 if (++lkc == nk) {
                     lkc = 0;
                     if (++lk < my_tiles) ltile = tile_k(lk);
@@ -493,6 +496,7 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
         const int qd = warp;                   // tensor-memory lane quadrant
         const bool im = lane >= 16;            // this lane holds the Xi row of its batch entry
         const int bl = qd * 16 + (lane & 15);  // batch entry within the tile
+        const uint64_t pol_out = l2::evict_last();  // the output spectrum is read back by the inverse
         for (int k = 0; k < my_tiles; ++k) {
             const int a = k % NACC;
             if (!mbar_wait(&acc_full[a], (uint32_t)((k / NACC) & 1), abort_flag)) {
@@ -541,9 +545,9 @@ k_mix_tc(const float2* __restrict__ X, const float4* __restrict__ Wp, int64_t wq
                     for (int c = 0; c < 4; ++c) {
                         const int o = tl.o0 + cb + (im ? 4 : 0) + c;
                         if (o >= Co) continue;
-                        stg32B(tl.Yq + ((int64_t)(tl.b0 + bl) * Co + o) * 8 + 4 * tl.h,
-                               make_float4(out[c][0], out[c][1], out[c][2], out[c][3]),
-                               make_float4(out[c][4], out[c][5], out[c][6], out[c][7]));
+                        l2::st8(tl.Yq + ((int64_t)(tl.b0 + bl) * Co + o) * 8 + 4 * tl.h,
+                                make_float4(out[c][0], out[c][1], out[c][2], out[c][3]),
+                                make_float4(out[c][4], out[c][5], out[c][6], out[c][7]), pol_out);
                     }
                 }
             }

@@ -13,6 +13,7 @@
 #pragma once
 
 #include "fft_masked.cuh"
+#include "l2_hints.cuh"
 #include "nop_internal.cuh"
 
 namespace nop {
@@ -140,11 +141,12 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
     // ---- rows: pairs (2p, 2p+1) as one complex line, kept bins to the column store ----
     // The next pair's 32 loads are issued before the current pair is transformed; the first pair's
     // loads are in flight while the twiddle tables are built.
+    const uint64_t pol_x = l2::evict_first();   // x is read once
     float2 nxt[16];
     {
         const float* ra = xp + (int64_t)(2 * g) * N + t;
 #pragma unroll
-        for (int r = 0; r < 16; ++r) nxt[r] = make_float2(__ldg(ra + 16 * r), __ldg(ra + N + 16 * r));
+        for (int r = 0; r < 16; ++r) nxt[r] = make_float2(l2::ld(ra + 16 * r, pol_x), l2::ld(ra + N + 16 * r, pol_x));
     }
     init_tables(tw, twp, twg);
     float2 twr[16];
@@ -159,7 +161,8 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
         if (base + GROUPS < N / 2) {
             const float* ra = xp + (int64_t)(2 * (pr + GROUPS)) * N + t;
 #pragma unroll
-            for (int r = 0; r < 16; ++r) nxt[r] = make_float2(__ldg(ra + 16 * r), __ldg(ra + N + 16 * r));
+            for (int r = 0; r < 16; ++r)
+                nxt[r] = make_float2(l2::ld(ra + 16 * r, pol_x), l2::ld(ra + N + 16 * r, pol_x));
         }
         fft::dft16<false>(v);
         __syncwarp();
@@ -224,11 +227,12 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
     constexpr int Mt = MY * KX;
     constexpr int Q = (Mt + 7) / 8;
     float2* op = out + plane * 8;
+    const uint64_t pol_s = l2::evict_last();  // the kept spectrum is read back by the next kernel
     for (int e = threadIdx.x; e < Q * 4; e += THREADS) {
         const int q = e >> 2, m = 8 * q + 2 * (e & 3);
         const float2 a = m < Mt ? stage[m] : make_float2(0.f, 0.f);
         const float2 b = m + 1 < Mt ? stage[m + 1] : make_float2(0.f, 0.f);
-        *reinterpret_cast<float4*>(op + q * blk_stride + 2 * (e & 3)) = make_float4(a.x, a.y, b.x, b.y);
+        l2::st4(op + q * blk_stride + 2 * (e & 3), make_float4(a.x, a.y, b.x, b.y), pol_s);
     }
 }
 
@@ -249,6 +253,8 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
       int64_t blk_stride, Epi ep, int64_t L, int ppc) {
     constexpr unsigned IN_COL = col_mask(MY);
     constexpr unsigned IN_ROW = row_in_mask(KX);
+    const uint64_t pol_s = l2::evict_first();  // the kept spectrum is read once
+    const uint64_t pol_y = l2::evict_first();  // y (and the skip addend) stream through
     constexpr int Mt = MY * KX;
     constexpr int Q = (Mt + 7) / 8;
     constexpr int NPF = (Q * 4 + THREADS - 1) / THREADS;  // 16-byte pieces of the spectrum per thread
@@ -268,7 +274,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
 #pragma unroll
         for (int k = 0; k < NPF; ++k) {
             const int e = threadIdx.x + k * THREADS;
-            if (e < Q * 4) pf[k] = __ldg(reinterpret_cast<const float4*>(ip + (e >> 2) * blk_stride + 2 * (e & 3)));
+            if (e < Q * 4) pf[k] = l2::ld4(ip + (e >> 2) * blk_stride + 2 * (e & 3), pol_s);
         }
     };
     auto put = [&]() {
@@ -375,15 +381,15 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
                 float va = v[r].x * scale + bias;
                 float vb = v[r].y * scale + bias;
                 if (ap) {
-                    va += __ldg(ap + (int64_t)na * N + n);
-                    vb += __ldg(ap + (int64_t)nb * N + n);
+                    va += l2::ld(ap + (int64_t)na * N + n, pol_y);
+                    vb += l2::ld(ap + (int64_t)nb * N + n, pol_y);
                 }
                 if (ep.apply_gelu) {
                     va = gelu_erf(va);
                     vb = gelu_erf(vb);
                 }
-                yp[(int64_t)na * N + n] = va;
-                yp[(int64_t)nb * N + n] = vb;
+                l2::st(yp + (int64_t)na * N + n, va, pol_y);
+                l2::st(yp + (int64_t)nb * N + n, vb, pol_y);
             }
             __syncwarp();  // buf is rewritten by the next iteration
         }

@@ -93,10 +93,11 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
 
     // row R as one complex line: nxt[r] = (x[R][2 m], x[R][2 m + 1]), m = t + 16 r
     float2 nxt[16];
+    const uint64_t pol_x = l2::evict_first();  // x is read once
     auto load_row = [&](int R) {
         const float2* rp = reinterpret_cast<const float2*>(xp + (int64_t)R * N) + t;
 #pragma unroll
-        for (int r = 0; r < 16; ++r) nxt[r] = __ldg(rp + 16 * r);
+        for (int r = 0; r < 16; ++r) nxt[r] = l2::ld2(rp + 16 * r, pol_x);
     };
     load_row(2 * g);  // in flight while the tables are built
     init_tables(tw, twp, w512, twg512);
@@ -198,7 +199,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
             const int q = ee >> 2, m = 8 * q + 2 * (ee & 3);
             const float2 a = m < Mt ? stage[m] : make_float2(0.f, 0.f);
             const float2 b = m + 1 < Mt ? stage[m + 1] : make_float2(0.f, 0.f);
-            *reinterpret_cast<float4*>(op + q * blk_stride + 2 * (ee & 3)) = make_float4(a.x, a.y, b.x, b.y);
+            l2::st4(op + q * blk_stride + 2 * (ee & 3), make_float4(a.x, a.y, b.x, b.y), l2::evict_last());
         }
         __syncthreads();
     }
@@ -229,6 +230,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
     float2* stage = X;
     float2* buf = X + g * LINE;
     const float2* ip = in + plane * 8;
+    const uint64_t pol_y = l2::evict_first();  // y (and the skip addend) stream through
     float4 pf[NPF];  // the kept spectrum; read again for the odd phase (the stage region is reused)
     auto fetch = [&]() {
 #pragma unroll
@@ -344,7 +346,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
                 float a0 = v[r].x * scale + bias;
                 float a1 = v[r].y * scale + bias;
                 if (ap) {
-                    const float2 s = __ldg(reinterpret_cast<const float2*>(ap + (int64_t)R * N) + m);
+                    const float2 s = l2::ld2(reinterpret_cast<const float2*>(ap + (int64_t)R * N) + m, pol_y);
                     a0 += s.x;
                     a1 += s.y;
                 }
@@ -352,7 +354,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
                     a0 = gelu_erf(a0);
                     a1 = gelu_erf(a1);
                 }
-                reinterpret_cast<float2*>(yp + (int64_t)R * N)[m] = make_float2(a0, a1);
+                l2::st2(reinterpret_cast<float2*>(yp + (int64_t)R * N) + m, make_float2(a0, a1), pol_y);
             }
             __syncwarp();  // buf is rewritten by the next row
         }

@@ -92,6 +92,10 @@ __device__ __forceinline__ void stage_tile(const Params& p, float* sm, int64_t t
 // out (M x TP) = W^T-stored weights (K x pitch) times in (K x TP).  Thread tile: channels m0..m0+3,
 // points p0..p0+3 (p fastest across a warp).  pre(m0, p0) runs before the K loop (to issue loads the
 // epilogue needs), epi(m0, p0, acc) after it.
+// The 16 products per K step run as 8 packed two-lane FMAs (__ffma2_rn, each lane rounded like fmaf):
+// channel pairs (w0, w1), (w2, w3) times point pairs (x0, x1), (x2, x3) accumulate the diagonal
+// entries (acc[2a][2b], acc[2a+1][2b+1]); times the swapped pairs (x1, x0), (x3, x2) the anti-diagonal
+// ones (acc[2a][2b+1], acc[2a+1][2b]), so no operand needs a broadcast.
 template <class Pre, class Epi>
 __device__ __forceinline__ void gemm(const float* __restrict__ WT, int pitch, int M, int K, const float* __restrict__ in,
                                      Pre pre, Epi epi) {
@@ -99,18 +103,36 @@ __device__ __forceinline__ void gemm(const float* __restrict__ WT, int pitch, in
     for (int tix = threadIdx.x; tix < ntiles; tix += THREADS) {
         const int m0 = (tix / PG) * 4, p0 = (tix % PG) * 4;
         pre(m0, p0);
-        float acc[4][4] = {};
+        float2 dg[2][2], ad[2][2];
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) dg[a][b] = ad[a][b] = make_float2(0.f, 0.f);
 #pragma unroll 4
         for (int k = 0; k < K; ++k) {
             const float4 w = *reinterpret_cast<const float4*>(WT + k * pitch + m0);
             const float4 v = *reinterpret_cast<const float4*>(in + k * TP + p0);
-            const float wv[4] = {w.x, w.y, w.z, w.w};
-            const float xv[4] = {v.x, v.y, v.z, v.w};
+            const float2 wp[2] = {make_float2(w.x, w.y), make_float2(w.z, w.w)};
+            const float2 xp[2] = {make_float2(v.x, v.y), make_float2(v.z, v.w)};
+            const float2 xs[2] = {make_float2(v.y, v.x), make_float2(v.w, v.z)};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int a = 0; a < 2; ++a)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], xv[j], acc[i][j]);
+                for (int b = 0; b < 2; ++b) {
+                    dg[a][b] = __ffma2_rn(wp[a], xp[b], dg[a][b]);
+                    ad[a][b] = __ffma2_rn(wp[a], xs[b], ad[a][b]);
+                }
         }
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                acc[2 * a][2 * b] = dg[a][b].x;
+                acc[2 * a + 1][2 * b + 1] = dg[a][b].y;
+                acc[2 * a][2 * b + 1] = ad[a][b].x;
+                acc[2 * a + 1][2 * b] = ad[a][b].y;
+            }
         epi(m0, p0, acc);
     }
 }

@@ -11,6 +11,7 @@
 #pragma once
 
 #include "fft_core.cuh"
+#include "l2_hints.cuh"
 #include "nop_internal.cuh"
 
 namespace nop {
@@ -35,6 +36,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
     const int64_t line = (int64_t)blockIdx.x * LINES + lr;
     const bool active = line < L;
     const float* xl = x + (active ? line : 0) * (int64_t)N;
+    const uint64_t pol_x = l2::evict_first();  // x is read once
     float2 acc[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) acc[k] = make_float2(0.f, 0.f);
@@ -44,7 +46,8 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
         float2 z[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-            z[j] = active ? make_float2(__ldg(xl + na + Q * j), __ldg(xl + nb + Q * j)) : make_float2(0.f, 0.f);
+            z[j] = active ? make_float2(l2::ld(xl + na + Q * j, pol_x), l2::ld(xl + nb + Q * j, pol_x))
+                          : make_float2(0.f, 0.f);
         fft::dft16<false>(z);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
@@ -85,7 +88,7 @@ k_fwd(const float* __restrict__ x, float2* __restrict__ out, const float2* __res
             }
             v = fft::cscale(v, scale);
         }
-        out[(k >> 3) * blk_stride + line * 8 + (k & 7)] = v;
+        l2::st2(out + (k >> 3) * blk_stride + line * 8 + (k & 7), v, l2::evict_last());
     }
 }
 
@@ -110,7 +113,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
     const int64_t line = (int64_t)blockIdx.x * LINES + lr;
     const bool active = line < L;
     if (active && lane64 < K) {
-        float2 v = in[(lane64 >> 3) * blk_stride + line * 8 + (lane64 & 7)];
+        float2 v = l2::ld2(in + (lane64 >> 3) * blk_stride + line * 8 + (lane64 & 7), l2::evict_first());
         if (lane64 == 0) v.y = 0.f;                      // bin 0 contributes its real part only
         zs[lr][lane64] = lane64 == 0 ? v : fft::cscale(v, 2.f);  // Hermitian weights 1, 2, 2, ...
     }
@@ -122,6 +125,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
     const float bias = ep.bias ? ep.bias[line % ep.C] : 0.f;
     float* yl = y + line * (int64_t)N;
     const float* al = ep.addend ? ep.addend + line * (int64_t)N : nullptr;
+    const uint64_t pol_y = l2::evict_first();  // y (and the skip addend) stream through
 #pragma unroll 1
     for (int s = 0; s < PER; ++s) {
         const int na = lane64 + TPR * s, nb = na + PAIRS;
@@ -155,15 +159,15 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
             float ra = u[j].x * scale + bias;
             float rb = u[j].y * scale + bias;
             if (al) {
-                ra += __ldg(al + na + Q * j);
-                rb += __ldg(al + nb + Q * j);
+                ra += l2::ld(al + na + Q * j, pol_y);
+                rb += l2::ld(al + nb + Q * j, pol_y);
             }
             if (ep.apply_gelu) {
                 ra = gelu_erf(ra);
                 rb = gelu_erf(rb);
             }
-            yl[na + Q * j] = ra;
-            yl[nb + Q * j] = rb;
+            l2::st(yl + na + Q * j, ra, pol_y);
+            l2::st(yl + nb + Q * j, rb, pol_y);
         }
     }
 }
