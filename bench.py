@@ -44,8 +44,8 @@ HBM_FALLBACK_GBS = 6533.2  # measured copy bandwidth on this pool (MEASURED_PEAK
 TRAFFIC = {
     # profiles/spectral_block_c2_b8_full.md: batch-8 capture x 8 (reads + writes during the kernel; the
     # plane kernels' traffic grows with the number of planes)
-    ("c2", "plane_inv"): 8 * (8.698368e6 + 80.557824e6),
-    ("c2", "plane_fwd"): 8 * (134.238976e6 + 4.504576e6),
+    ("c2", "plane_inv"): 8 * (8.701952e6 + 79.316992e6),
+    ("c2", "plane_fwd"): 8 * (134.246144e6 + 4.028928e6),
     ("c2", "contraction"): None,  # the weight stream does not scale with the batch
 }
 
