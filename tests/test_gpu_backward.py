@@ -201,3 +201,32 @@ def test_no_graph_without_grad():
     assert y.grad_fn is None
     conv.requires_grad_(False)
     assert conv(x).grad_fn is None
+
+
+@pytest.mark.parametrize("batch, ci, co, modes", [
+    (64, 64, 64, (64, 64)),   # the C2 layer's weight gradient (one input / output tile, aligned stores)
+    (40, 80, 48, (62, 61)),   # two input tiles, a partial output tile, batch not a multiple of 8,
+                              # Mt = 62 * 31 not a multiple of 4 (per-mode stores)
+])
+def test_tensor_core_weight_grad_matches_cuda_cores(batch, ci, co, modes, monkeypatch):
+    """dL/dW from the tcgen05 kernel equals the CUDA-core kernel's (NOP_CONTRACTION=simt) on shapes that
+    select it (batch >= 32, a tile per SM)."""
+    from neuraloperator_b200 import ops
+    torch.manual_seed(1)
+    x = torch.randn(batch, ci, 256, 256, device="cuda")
+    g = torch.randn(batch, co, 256, 256, device="cuda")
+    grads = {}
+    for mode in ("simt", "tc"):
+        if mode == "simt":
+            monkeypatch.setenv("NOP_CONTRACTION", "simt")
+        else:
+            monkeypatch.delenv("NOP_CONTRACTION", raising=False)
+        ops.clear_plans()
+        torch.manual_seed(2)
+        conv = nb.SpectralConv(ci, co, modes).cuda()
+        y = conv(x)
+        (gw,) = torch.autograd.grad(y, [conv.weight.tensor], g)
+        grads[mode] = gw
+    ops.clear_plans()
+    assert rel_l2(grads["tc"].cpu(), grads["simt"].cpu()) <= 1e-5
+    assert _lib.device_status() == 0
