@@ -661,12 +661,31 @@ def run_train(args, cfg, world, rank, local):
         return
 
     def timed(fn, n=max(3, min(steps, 20))):
-        fn()
+        """Device time of one phase, replayed from a CUDA graph like the step (eager launches would add
+        the Python host time between them); eager if capture fails."""
+        out = fn()
         torch.cuda.synchronize()
+        g_phase = None
+        if not args.no_graph:
+            try:
+                g_phase = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream()
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    with torch.cuda.graph(g_phase, stream=side):
+                        out = fn()
+                stream.wait_stream(side)
+                torch.cuda.synchronize()
+            except Exception:  # noqa: BLE001
+                g_phase = None
+                torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         for _ in range(n):
-            out = fn()
+            if g_phase is not None:
+                g_phase.replay()
+            else:
+                out = fn()
         b.record(stream)
         torch.cuda.synchronize()
         return a.elapsed_time(b) / n, out
@@ -690,9 +709,11 @@ def run_train(args, cfg, world, rank, local):
                                                              precision=args.precision, engine=args.engine,
                                                              keep_spectrum=True, packed=packed_adj))
     wshape = (ci, co) + tuple(geo.kept)
-    marks = _lib.LaunchEvents(3)
+    ms_wg, (gw, _) = timed(lambda: ops.weight_grad(spec, gspec, wshape, co))
+    marks = _lib.LaunchEvents(3)  # the weight-gradient kernel alone, one eager call
     with marks:
-        ms_wg, (gw, _) = timed(lambda: ops.weight_grad(spec, gspec, wshape, co))
+        ops.weight_grad(spec, gspec, wshape, co)
+    torch.cuda.synchronize()
     wg_kernel_ms = marks.durations_ms()[0]
     ms_fac = 0.0
     if kind == "tucker":
