@@ -10,7 +10,9 @@
 //   k_plane_inv  : column inverses of the kept modes, then row inverses (two real rows per complex
 //                  line) with the epilogue bias (+ skip) (+ GELU) fused into the final pass.
 // Other shapes fall back to the generic engine (plan-time decision).
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
 
 #include "fft_core.cuh"
 #include "nop_internal.cuh"
@@ -19,6 +21,7 @@
 #include "plane512.cuh"
 #include "row1d.cuh"
 #include "mix_tc.cuh"
+#include "mix_tma.cuh"
 
 namespace nop {
 namespace {
@@ -393,7 +396,7 @@ __global__ void k_pack_broadcast(const float2* __restrict__ U, float4* __restric
 constexpr size_t kSmemLimit = 227 * 1024;
 
 // per-device "dynamic shared memory limit raised" bits, one word per kernel instantiation
-std::atomic<uint64_t> g_attr_done[24];
+std::atomic<uint64_t> g_attr_done[32];
 
 template <class K>
 cudaError_t ensure_smem_attr(K kernel, int slot, int device, size_t bytes = kSmemLimit) {
@@ -453,6 +456,82 @@ cudaError_t launch_mix_tc(const Plan& p, const BlockMap& bm, const float2* X, co
     return cudaGetLastError();
 }
 
+// cuTensorMapEncodeTiled, looked up once through the runtime (no link against the driver library)
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_tiled() {
+    static const EncodeTiled fn = []() -> EncodeTiled {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<EncodeTiled>(f);
+    }();
+    return fn;
+}
+
+// The contraction with TMA operand loads (mix_tma.cuh).  Tensor maps, innermost dimension first:
+//   X  {16 floats (a mode block of one (q, b, i)), B, Ci, local blocks}, box {4, 64, KS, 1} (two modes)
+//      at {4 h, b0, k0, q}: strides Ci * 64 B, 64 B, B Ci 64 B (all multiples of 16 B; x = 4 h floats)
+//   W  {4 Co floats (float4 per output channel), 4 mode pairs, Ci, weight blocks}, box {4 CO, 1, KS, 1}
+//      at {4 o0, h, k0, qw}; without the block dimension when one matrix serves every block (wq = 0)
+//   Y  {16 floats, B, Co, local blocks} (stores), box {4, 16, 8, 1} (two modes of 16 rows of 8 channels,
+//      one epilogue warp's group; shared-memory image [channel][row][4 floats]) at {4 h, b0 + 16 w,
+//      o0 + 8 g, q}: strides Co * 64 B, 64 B, B Co 64 B
+template <int CO, bool BF16>
+cudaError_t launch_mix_tma(const Plan& p, const BlockMap& bm, const float2* X, const float4* W, int64_t wq,
+                           float2* Y, int Ci, int Co, int slot, cudaStream_t s) {
+    using C = tma_mix::Cfg<CO, BF16>;
+    const EncodeTiled enc = encode_tiled();
+    if (!enc) return cudaErrorNotSupported;
+    cudaError_t err = ensure_smem_attr(tma_mix::k_mix_tma<CO, BF16>, slot, p.device, C::SMEM);
+    if (err != cudaSuccess) return err;
+    int* status = device_status_ptr(p.device);
+    if (!status) return cudaErrorInvalidSymbol;
+    const int64_t B = p.d.batch;
+    const int64_t tiles = 4 * bm.local * ceil_div(B, tc::BT) * ceil_div(Co, CO);  // 4 mode pairs per block
+    if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;  // tile indices are 32-bit
+    CUtensorMap tmx, tmw;
+    const cuuint32_t ones[4] = {1, 1, 1, 1};
+    const cuuint64_t xd[4] = {16, (cuuint64_t)B, (cuuint64_t)Ci, (cuuint64_t)bm.local};
+    const cuuint64_t xs[3] = {(cuuint64_t)Ci * 64, 64, (cuuint64_t)(B * Ci * 64)};
+    const cuuint32_t xb[4] = {4, (cuuint32_t)tc::BT, (cuuint32_t)C::KS, 1};
+    if (enc(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float2*>(X), xd, xs, xb, ones,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    // weight blocks addressed: qw = (q / qpl) qtot + qbeg + q % qpl over the local blocks q
+    int64_t wblocks = 1;
+    if (wq != 0) {
+        const int64_t last = bm.local - 1;
+        int64_t mx = (last / bm.qpl) * bm.qtot + bm.qbeg + last % bm.qpl;
+        if (last >= bm.qpl) mx = std::max(mx, (last / bm.qpl - 1) * bm.qtot + bm.qbeg + bm.qpl - 1);
+        wblocks = mx + 1;
+    }
+    const cuuint64_t wd[4] = {(cuuint64_t)Co * 4, 4, (cuuint64_t)Ci, (cuuint64_t)wblocks};
+    const cuuint64_t wst[3] = {(cuuint64_t)Co * 16, (cuuint64_t)Co * 64, (cuuint64_t)(wq * 16)};
+    const cuuint32_t wb[4] = {(cuuint32_t)(4 * CO), 1, (cuuint32_t)C::KS, 1};
+    if (enc(&tmw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wq != 0 ? 4 : 3, const_cast<float4*>(W), wd, wst, wb, ones,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    CUtensorMap tmy;
+    const cuuint64_t yd[4] = {16, (cuuint64_t)B, (cuuint64_t)Co, (cuuint64_t)bm.local};
+    const cuuint64_t ys[3] = {(cuuint64_t)Co * 64, 64, (cuuint64_t)(B * Co * 64)};
+    const cuuint32_t yb[4] = {4, 16, 8, 1};
+    if (enc(&tmy, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Y, yd, ys, yb, ones, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)(tiles < p.sm_count ? tiles : p.sm_count);  // persistent, one CTA per SM
+    tma_mix::k_mix_tma<CO, BF16><<<grid, tma_mix::THREADS, C::SMEM, s>>>(
+        tmx, tmw, tmy, wq != 0 ? 4 : 3, (int)B, Ci, Co, (int)bm.local, bm.qpl, bm.qtot, bm.qbeg, status);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t wq, float2* Y, int Ci, int Co,
                        cudaStream_t s) {
     const BlockMap bm = block_map(p);
@@ -461,12 +540,22 @@ cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t 
     const bool bf16 = p.d.precision == NOP_PRECISION_BF16;
     if (p.mix_tc) {
         // 64-wide output tiles (N = 128) unless the channels fit a 32-wide tile
-        if (Co > 32)
-            err = bf16 ? launch_mix_tc<64, true>(p, bm, X, W, wq, Y, Ci, Co, 16, s)
-                       : launch_mix_tc<64, false>(p, bm, X, W, wq, Y, Ci, Co, 17, s);
-        else
-            err = bf16 ? launch_mix_tc<32, true>(p, bm, X, W, wq, Y, Ci, Co, 18, s)
-                       : launch_mix_tc<32, false>(p, bm, X, W, wq, Y, Ci, Co, 19, s);
+        // NOP_MIX_TMA=0: the per-thread-gather kernel (A/B timing and cross-check), read per launch
+        const char* sel = getenv("NOP_MIX_TMA");
+        if (sel && atoi(sel) == 0) {
+            if (Co > 32)
+                err = bf16 ? launch_mix_tc<64, true>(p, bm, X, W, wq, Y, Ci, Co, 16, s)
+                           : launch_mix_tc<64, false>(p, bm, X, W, wq, Y, Ci, Co, 17, s);
+            else
+                err = bf16 ? launch_mix_tc<32, true>(p, bm, X, W, wq, Y, Ci, Co, 18, s)
+                           : launch_mix_tc<32, false>(p, bm, X, W, wq, Y, Ci, Co, 19, s);
+        } else if (Co > 32) {
+            err = bf16 ? launch_mix_tma<64, true>(p, bm, X, W, wq, Y, Ci, Co, 24, s)
+                       : launch_mix_tma<64, false>(p, bm, X, W, wq, Y, Ci, Co, 25, s);
+        } else {
+            err = bf16 ? launch_mix_tma<32, true>(p, bm, X, W, wq, Y, Ci, Co, 26, s)
+                       : launch_mix_tma<32, false>(p, bm, X, W, wq, Y, Ci, Co, 27, s);
+        }
     } else {
         err = ensure_smem_attr(bf16 ? k_mix<true> : k_mix<false>, bf16 ? 14 : 15, p.device, kMixSmem);
         if (err != cudaSuccess) return err;

@@ -5,6 +5,9 @@ the bf16 contraction).  NOP_CONTRACTION=simt (read at plan creation) selects the
 which computes the same sums in plain fp32 FMAs; the two must agree to fp32 rounding
 (relative L2 <= 2e-6) on shapes that exercise every tile edge: batch not a multiple of 64, channel
 counts not multiples of 8 / 32 / 64, more than one output tile, factorized weights, 1D / 2D / 3D.
+The tensor-core kernel loads its operands and stores its results with tensor copies (TMA);
+NOP_MIX_TMA=0 (read per launch) selects its per-thread-gather twin, which must give bit-identical
+results (the same MMAs on the same operands in the same order).
 Every run must leave the device status word at 0 (no bounded wait expired).
 """
 
@@ -91,3 +94,34 @@ def test_tensor_core_contraction_against_oracle_fp32():
     ref = oracle.spectral_conv(x, conv.weight.tensor.detach().cpu(), conv.bias.detach().cpu(), (24, 24))
     assert rel_l2(y, ref) <= 1e-5
     assert _lib.device_status(clear=True) == 0
+
+
+def _forward_tma(conv, x, tma):
+    old = os.environ.get("NOP_MIX_TMA")
+    try:
+        if tma:
+            os.environ.pop("NOP_MIX_TMA", None)
+        else:
+            os.environ["NOP_MIX_TMA"] = "0"
+        with torch.no_grad():
+            y = conv(x)
+        torch.cuda.synchronize()
+        return y
+    finally:
+        if old is None:
+            os.environ.pop("NOP_MIX_TMA", None)
+        else:
+            os.environ["NOP_MIX_TMA"] = old
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"B{c[0]}_ci{c[1]}_co{c[2]}_{len(c[3])}d_{'_'.join(c[5])}" for c in CASES])
+def test_tma_contraction_bit_identical_to_gather_kernel(case):
+    batch, ci, co, grid, modes, kw = case
+    torch.manual_seed(0)
+    conv = nb.SpectralConv(ci, co, modes, **kw).cuda()
+    x = torch.randn((batch, ci, *grid), device="cuda")
+    _lib.device_status(clear=True)
+    y_tma = _forward_tma(conv, x, tma=True)
+    y_gather = _forward_tma(conv, x, tma=False)
+    assert _lib.device_status(clear=True) == 0
+    assert torch.equal(y_tma, y_gather)
