@@ -366,6 +366,7 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
                 }
             }
             fft::dft16_m<true, IN_ROW, 0xFFFFu>(v);
+            if (t == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // buf's last rows read
             __syncwarp();
 #pragma unroll
             for (int r = 0; r < 16; r += 2)
@@ -375,6 +376,10 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
             for (int r = 0; r < 16; ++r) v[r] = buf[t + 18 * r];
             pass2_twiddle_6<true>(v, twb);
             fft::dft16<true>(v);
+            // rows na, nb (contiguous in y) staged in the group's exchange line, written by one bulk copy;
+            // odd groups stage 64 bytes further in, off the banks of the even group of their warp
+            __syncwarp();  // every lane has read its exchange values
+            float* ob = reinterpret_cast<float*>(buf) + 16 * (g & 1);
 #pragma unroll
             for (int r = 0; r < 16; ++r) {
                 const int n = t + 16 * r;
@@ -388,13 +393,24 @@ k_inv(const float2* __restrict__ in, float* __restrict__ y, const float2* __rest
                     va = gelu_erf(va);
                     vb = gelu_erf(vb);
                 }
-                l2::st(yp + (int64_t)na * N + n, va, pol_y);
-                l2::st(yp + (int64_t)nb * N + n, vb, pol_y);
+                ob[n] = va;
+                ob[N + n] = vb;
             }
-            __syncwarp();  // buf is rewritten by the next iteration
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the bulk copy
+            __syncwarp();
+            if (t == 0) {
+                asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;" ::"l"(
+                                 yp + (int64_t)na * N),
+                             "r"((uint32_t)__cvta_generic_to_shared(ob)), "r"(2 * N * 4), "l"(pol_y)
+                             : "memory");
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
         }
-        __syncthreads();  // the next plane's spectrum goes into the exchange lines' region
+        // the next plane's spectrum goes into the exchange lines' region
+        if (t == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncthreads();
     }
+    if (t == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 }  // namespace p256
