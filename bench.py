@@ -46,7 +46,8 @@ TRAFFIC = {
     # plane kernels' traffic grows with the number of planes)
     ("c2", "plane_inv"): 8 * (8.701952e6 + 79.316992e6),
     ("c2", "plane_fwd"): 8 * (134.246144e6 + 4.028928e6),
-    ("c2", "contraction"): None,  # the weight stream does not scale with the batch
+    # profiles/contraction_tma_c2_full.md: full-size capture of the contraction (one launch)
+    ("c2", "contraction"): 138.643968e6 + 10.613504e6,
 }
 
 # name -> (description, batch, Ci, Co, grid, n_modes, factorization)
