@@ -24,6 +24,12 @@ bool mix_on_tensor_cores() {
     return !(v && strcmp(v, "simt") == 0);
 }
 
+// NOP_MIX_TMA=0: the tensor-core contraction with per-thread gathers on the float4 weight packing
+bool mix_with_tma() {
+    const char* v = getenv("NOP_MIX_TMA");
+    return !(v && strcmp(v, "0") == 0);
+}
+
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 bool mul_ok(int64_t a, int64_t b, int64_t* out) {
@@ -268,6 +274,7 @@ int32_t nop_spectral_plan_create(const nop_spectral_desc* desc, nop_plan** plan_
     p->fast = fast_ok && p->d.engine != NOP_ENGINE_GENERIC;
     p->fast_kind = p->fast ? kind : FastKind::None;
     p->mix_tc = mix_on_tensor_cores();
+    p->mix_tma = p->mix_tc && mix_with_tma();
 
     size_t off = 0;
     if (p->fast) {
@@ -412,6 +419,7 @@ int32_t nop_spectral_slab_plan_create(const nop_spectral_desc* desc, int32_t ran
     p->fast = true;
     p->fast_kind = FastKind::Vol3DSlab;
     p->mix_tc = mix_on_tensor_cores();
+    p->mix_tma = p->mix_tc && mix_with_tma();
     p->slab_rank = rank;
     p->slab_world = world;
     p->slab_nx = p->d.n_in[0] / world;

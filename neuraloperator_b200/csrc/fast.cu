@@ -473,17 +473,60 @@ EncodeTiled encode_tiled() {
     return fn;
 }
 
-// The contraction with TMA operand loads (mix_tma.cuh).  Tensor maps, innermost dimension first:
+// Geometry of the pre-split weight tiles of one contraction (I input, O output channels; Qw weight
+// blocks and H = 4 mode pairs each, or Qw = H = 1 for a matrix shared by every block): see
+// tma_mix::tc_tile.  Output tiles of 64 channels unless the channels fit 32.
+struct TcGeom {
+    int co, ot, nk;
+    bool bf16;
+    int64_t bytes;
+};
+
+TcGeom tc_geom(const Plan& p, int64_t I, int64_t O, int64_t Qw, int H) {
+    TcGeom g;
+    g.co = O > 32 ? 64 : 32;
+    g.bf16 = p.d.precision == NOP_PRECISION_BF16;
+    g.ot = (int)ceil_div(O, g.co);
+    g.nk = (int)ceil_div(I, g.bf16 ? 16 : 8);
+    g.bytes = Qw * H * g.ot * g.nk * tma_mix::TM * (g.bf16 ? 1 : 2) * (2 * g.co * 32);
+    return g;
+}
+
+// weight element (i, o, m) at W[i * s_i + o * s_o + m * s_m] (s_m = 0: shared by every block)
+cudaError_t pack_tc(const Plan& p, const float2* W, char* out, int64_t I, int64_t O, int64_t Qw, int H, int64_t s_i,
+                    int64_t s_o, int64_t s_m, int conj, cudaStream_t s) {
+    const TcGeom g = tc_geom(p, I, O, Qw, H);
+    const int64_t n = Qw * H * g.ot * g.nk * tma_mix::TM * 2 * g.co * 2;
+    const unsigned grid = (unsigned)ceil_div(n, 256);
+    const int64_t Mt = p.modes_total;
+    if (g.co == 64) {
+        if (g.bf16)
+            tma_mix::k_pack_tc<64, true><<<grid, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, Qw, H, g.ot, g.nk, s_i, s_o,
+                                                              s_m, conj);
+        else
+            tma_mix::k_pack_tc<64, false><<<grid, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, Qw, H, g.ot, g.nk, s_i,
+                                                               s_o, s_m, conj);
+    } else {
+        if (g.bf16)
+            tma_mix::k_pack_tc<32, true><<<grid, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, Qw, H, g.ot, g.nk, s_i, s_o,
+                                                              s_m, conj);
+        else
+            tma_mix::k_pack_tc<32, false><<<grid, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, Qw, H, g.ot, g.nk, s_i,
+                                                               s_o, s_m, conj);
+    }
+    return cudaGetLastError();
+}
+
+// The contraction with TMA operand loads and result stores (mix_tma.cuh) on weight tiles from
+// pack_tc.  Tensor maps, innermost dimension first:
 //   X  {16 floats (a mode block of one (q, b, i)), B, Ci, local blocks}, box {4, 64, KS, 1} (two modes)
 //      at {4 h, b0, k0, q}: strides Ci * 64 B, 64 B, B Ci 64 B (all multiples of 16 B; x = 4 h floats)
-//   W  {4 Co floats (float4 per output channel), 4 mode pairs, Ci, weight blocks}, box {4 CO, 1, KS, 1}
-//      at {4 o0, h, k0, qw}; without the block dimension when one matrix serves every block (wq = 0)
 //   Y  {16 floats, B, Co, local blocks} (stores), box {4, 16, 8, 1} (two modes of 16 rows of 8 channels,
 //      one epilogue warp's group; shared-memory image [channel][row][4 floats]) at {4 h, b0 + 16 w,
 //      o0 + 8 g, q}: strides Co * 64 B, 64 B, B Co 64 B
 template <int CO, bool BF16>
-cudaError_t launch_mix_tma(const Plan& p, const BlockMap& bm, const float2* X, const float4* W, int64_t wq,
-                           float2* Y, int Ci, int Co, int slot, cudaStream_t s) {
+cudaError_t launch_mix_tma_t(const Plan& p, const BlockMap& bm, const float2* X, const char* Wtc, int H, float2* Y,
+                             int Ci, int Co, int slot, cudaStream_t s) {
     using C = tma_mix::Cfg<CO, BF16>;
     const EncodeTiled enc = encode_tiled();
     if (!enc) return cudaErrorNotSupported;
@@ -494,7 +537,7 @@ cudaError_t launch_mix_tma(const Plan& p, const BlockMap& bm, const float2* X, c
     const int64_t B = p.d.batch;
     const int64_t tiles = 4 * bm.local * ceil_div(B, tc::BT) * ceil_div(Co, CO);  // 4 mode pairs per block
     if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;  // tile indices are 32-bit
-    CUtensorMap tmx, tmw;
+    CUtensorMap tmx, tmy;
     const cuuint32_t ones[4] = {1, 1, 1, 1};
     const cuuint64_t xd[4] = {16, (cuuint64_t)B, (cuuint64_t)Ci, (cuuint64_t)bm.local};
     const cuuint64_t xs[3] = {(cuuint64_t)Ci * 64, 64, (cuuint64_t)(B * Ci * 64)};
@@ -503,22 +546,6 @@ cudaError_t launch_mix_tma(const Plan& p, const BlockMap& bm, const float2* X, c
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
-    // weight blocks addressed: qw = (q / qpl) qtot + qbeg + q % qpl over the local blocks q
-    int64_t wblocks = 1;
-    if (wq != 0) {
-        const int64_t last = bm.local - 1;
-        int64_t mx = (last / bm.qpl) * bm.qtot + bm.qbeg + last % bm.qpl;
-        if (last >= bm.qpl) mx = std::max(mx, (last / bm.qpl - 1) * bm.qtot + bm.qbeg + bm.qpl - 1);
-        wblocks = mx + 1;
-    }
-    const cuuint64_t wd[4] = {(cuuint64_t)Co * 4, 4, (cuuint64_t)Ci, (cuuint64_t)wblocks};
-    const cuuint64_t wst[3] = {(cuuint64_t)Co * 16, (cuuint64_t)Co * 64, (cuuint64_t)(wq * 16)};
-    const cuuint32_t wb[4] = {(cuuint32_t)(4 * CO), 1, (cuuint32_t)C::KS, 1};
-    if (enc(&tmw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wq != 0 ? 4 : 3, const_cast<float4*>(W), wd, wst, wb, ones,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return cudaErrorInvalidValue;
-    CUtensorMap tmy;
     const cuuint64_t yd[4] = {16, (cuuint64_t)B, (cuuint64_t)Co, (cuuint64_t)bm.local};
     const cuuint64_t ys[3] = {(cuuint64_t)Co * 64, 64, (cuuint64_t)(B * Co * 64)};
     const cuuint32_t yb[4] = {4, 16, 8, 1};
@@ -528,8 +555,24 @@ cudaError_t launch_mix_tma(const Plan& p, const BlockMap& bm, const float2* X, c
         return cudaErrorInvalidValue;
     const unsigned grid = (unsigned)(tiles < p.sm_count ? tiles : p.sm_count);  // persistent, one CTA per SM
     tma_mix::k_mix_tma<CO, BF16><<<grid, tma_mix::THREADS, C::SMEM, s>>>(
-        tmx, tmw, tmy, wq != 0 ? 4 : 3, (int)B, Ci, Co, (int)bm.local, bm.qpl, bm.qtot, bm.qbeg, status);
+        tmx, Wtc, tmy, H, (int)B, Ci, Co, (int)bm.local, bm.qpl, bm.qtot, bm.qbeg, status);
     return cudaGetLastError();
+}
+
+cudaError_t launch_mix_tma(const Plan& p, const float2* X, const char* Wtc, int H, float2* Y, int Ci, int Co,
+                           cudaStream_t s) {
+    const BlockMap bm = block_map(p);
+    if (bm.local == 0) return cudaSuccess;
+    const bool bf16 = p.d.precision == NOP_PRECISION_BF16;
+    cudaError_t err;
+    if (Co > 32)
+        err = bf16 ? launch_mix_tma_t<64, true>(p, bm, X, Wtc, H, Y, Ci, Co, 24, s)
+                   : launch_mix_tma_t<64, false>(p, bm, X, Wtc, H, Y, Ci, Co, 25, s);
+    else
+        err = bf16 ? launch_mix_tma_t<32, true>(p, bm, X, Wtc, H, Y, Ci, Co, 26, s)
+                   : launch_mix_tma_t<32, false>(p, bm, X, Wtc, H, Y, Ci, Co, 27, s);
+    if (err == cudaSuccess) launch_mark(s);
+    return err;
 }
 
 cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t wq, float2* Y, int Ci, int Co,
@@ -540,22 +583,13 @@ cudaError_t launch_mix(const Plan& p, const float2* X, const float4* W, int64_t 
     const bool bf16 = p.d.precision == NOP_PRECISION_BF16;
     if (p.mix_tc) {
         // 64-wide output tiles (N = 128) unless the channels fit a 32-wide tile
-        // NOP_MIX_TMA=0: the per-thread-gather kernel (A/B timing and cross-check), read per launch
-        const char* sel = getenv("NOP_MIX_TMA");
-        if (sel && atoi(sel) == 0) {
-            if (Co > 32)
-                err = bf16 ? launch_mix_tc<64, true>(p, bm, X, W, wq, Y, Ci, Co, 16, s)
-                           : launch_mix_tc<64, false>(p, bm, X, W, wq, Y, Ci, Co, 17, s);
-            else
-                err = bf16 ? launch_mix_tc<32, true>(p, bm, X, W, wq, Y, Ci, Co, 18, s)
-                           : launch_mix_tc<32, false>(p, bm, X, W, wq, Y, Ci, Co, 19, s);
-        } else if (Co > 32) {
-            err = bf16 ? launch_mix_tma<64, true>(p, bm, X, W, wq, Y, Ci, Co, 24, s)
-                       : launch_mix_tma<64, false>(p, bm, X, W, wq, Y, Ci, Co, 25, s);
-        } else {
-            err = bf16 ? launch_mix_tma<32, true>(p, bm, X, W, wq, Y, Ci, Co, 26, s)
-                       : launch_mix_tma<32, false>(p, bm, X, W, wq, Y, Ci, Co, 27, s);
-        }
+        // 64-wide output tiles (N = 128) unless the channels fit a 32-wide tile
+        if (Co > 32)
+            err = bf16 ? launch_mix_tc<64, true>(p, bm, X, W, wq, Y, Ci, Co, 16, s)
+                       : launch_mix_tc<64, false>(p, bm, X, W, wq, Y, Ci, Co, 17, s);
+        else
+            err = bf16 ? launch_mix_tc<32, true>(p, bm, X, W, wq, Y, Ci, Co, 18, s)
+                       : launch_mix_tc<32, false>(p, bm, X, W, wq, Y, Ci, Co, 19, s);
     } else {
         err = ensure_smem_attr(bf16 ? k_mix<true> : k_mix<false>, bf16 ? 14 : 15, p.device, kMixSmem);
         if (err != cudaSuccess) return err;
@@ -577,6 +611,23 @@ int32_t mix_stage(const Plan& p, const float2* Xh, const char* packed, float2* Y
     const nop_spectral_desc& d = p.d;
     const int Ci = (int)d.in_channels, Co = (int)d.out_channels;
     cudaError_t err;
+    if (p.mix_tma) {
+        // weight tiles from pack_tc: per mode block (H = 4) or one matrix for every block (H = 1)
+        if (d.weight_kind == NOP_WEIGHT_DENSE) {
+            err = launch_mix_tma(p, Xh, packed + p.pk_w, 4, Yh, Ci, Co, s);
+            return err == cudaSuccess ? NOP_OK : cuda_fail(err, "mix launch");
+        }
+        const int rin = (int)d.ranks[0], rout = (int)d.ranks[1];
+        float2* xf = reinterpret_cast<float2*>(ws + p.ws.xf);
+        float2* z = reinterpret_cast<float2*>(ws + p.ws.z);
+        if ((err = launch_mix_tma(p, Xh, packed + p.pk_uin, 1, xf, Ci, rin, s)) != cudaSuccess)
+            return cuda_fail(err, "mix launch (input factor)");
+        if ((err = launch_mix_tma(p, xf, packed + p.pk_w, 4, z, rin, rout, s)) != cudaSuccess)
+            return cuda_fail(err, "mix launch (core)");
+        if ((err = launch_mix_tma(p, z, packed + p.pk_uout, 1, Yh, rout, Co, s)) != cudaSuccess)
+            return cuda_fail(err, "mix launch (output factor)");
+        return NOP_OK;
+    }
     if (d.weight_kind == NOP_WEIGHT_DENSE) {
         const float4* W = reinterpret_cast<const float4*>(packed + p.pk_w);
         err = launch_mix(p, Xh, W, (int64_t)Ci * 4 * Co, Yh, Ci, Co, s);
@@ -970,14 +1021,17 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
         pk += up256(bytes);
         return at;
     };
+    // packed weights: tiles for the TMA contraction (pack_tc) or [Q][I][4][O] float4 (k_pack_modes)
     if (d.weight_kind == NOP_WEIGHT_DENSE) {
-        p.pk_w = pk_take((size_t)Q * Ci * 4 * Co * sizeof(float4));
+        p.pk_w = pk_take(p.mix_tma ? (size_t)tc_geom(p, Ci, Co, Q, 4).bytes : (size_t)Q * Ci * 4 * Co * sizeof(float4));
         ws->xf = ws->z = ws->g = ws->g_tmp = 0;
     } else {
         const int64_t rin = d.ranks[0], rout = d.ranks[1];
-        p.pk_w = pk_take((size_t)Q * rin * 4 * rout * sizeof(float4));
-        p.pk_uin = pk_take((size_t)Ci * 4 * rin * sizeof(float4));
-        p.pk_uout = pk_take((size_t)rout * 4 * Co * sizeof(float4));
+        p.pk_w = pk_take(p.mix_tma ? (size_t)tc_geom(p, rin, rout, Q, 4).bytes
+                                   : (size_t)Q * rin * 4 * rout * sizeof(float4));
+        p.pk_uin = pk_take(p.mix_tma ? (size_t)tc_geom(p, Ci, rin, 1, 1).bytes : (size_t)Ci * 4 * rin * sizeof(float4));
+        p.pk_uout = pk_take(p.mix_tma ? (size_t)tc_geom(p, rout, Co, 1, 1).bytes
+                                      : (size_t)rout * 4 * Co * sizeof(float4));
         ws->xf = take((size_t)Q * 8 * B * rin * sizeof(float2));
         ws->z = take((size_t)Q * 8 * B * rout * sizeof(float2));
         int64_t g = 0;
@@ -1022,6 +1076,11 @@ int32_t fast_pack_adjoint(const Plan& p, const void* W, char* packed, cudaStream
     if (d.weight_kind != NOP_WEIGHT_DENSE)
         return fail(NOP_E_UNSUPPORTED, "adjoint packing from the forward weight needs dense weights");
     const int64_t Q = mode_blocks(p), Mt = p.modes_total, Ci = d.in_channels, Co = d.out_channels;
+    if (p.mix_tma) {
+        const cudaError_t e = pack_tc(p, static_cast<const float2*>(W), packed + p.pk_w, Ci, Co, Q, 4, Mt, Ci * Mt, 1,
+                                      1, s);
+        return e == cudaSuccess ? NOP_OK : cuda_fail(e, "adjoint pack launch");
+    }
     const int64_t n = Q * Ci * 4 * Co;
     k_pack_modes<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(W),
                                                             reinterpret_cast<float4*>(packed + p.pk_w), (int)Ci,
@@ -1034,6 +1093,26 @@ int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char*
     const nop_spectral_desc& d = p.d;
     const int64_t Q = mode_blocks(p), Mt = p.modes_total, Ci = d.in_channels, Co = d.out_channels;
     cudaError_t err;
+    if (p.mix_tma) {
+        if (d.weight_kind == NOP_WEIGHT_DENSE) {
+            err = pack_tc(p, static_cast<const float2*>(weights[0]), packed + p.pk_w, Ci, Co, Q, 4, Co * Mt, Mt, 1, 0, s);
+            return err == cudaSuccess ? NOP_OK : cuda_fail(err, "pack launch");
+        }
+        const int64_t rin = d.ranks[0], rout = d.ranks[1];
+        float2* G = expand_tucker_core(p, static_cast<const float2*>(weights[0]), weights, 3, rin * rout, ws, &err, s);
+        if (!G) return cuda_fail(err, "tucker core expansion");
+        if ((err = pack_tc(p, G, packed + p.pk_w, rin, rout, Q, 4, rout * Mt, Mt, 1, 0, s)) != cudaSuccess)
+            return cuda_fail(err, "pack launch (core)");
+        launch_mark(s);
+        // U_in [Ci][r_in]: xf[f] = sum_i x[i] U_in[i][f]
+        if ((err = pack_tc(p, static_cast<const float2*>(weights[1]), packed + p.pk_uin, Ci, rin, 1, 1, rin, 1, 0, 0,
+                           s)) != cudaSuccess)
+            return cuda_fail(err, "pack launch (input factor)");
+        launch_mark(s);
+        // U_out [Co][r_out]: y[o] = sum_g z[g] U_out[o][g]
+        err = pack_tc(p, static_cast<const float2*>(weights[2]), packed + p.pk_uout, rout, Co, 1, 1, 1, rout, 0, 0, s);
+        return err == cudaSuccess ? NOP_OK : cuda_fail(err, "pack launch (output factor)");
+    }
     if (d.weight_kind == NOP_WEIGHT_DENSE) {
         const int64_t n = Q * Ci * 4 * Co;
         k_pack_modes<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(static_cast<const float2*>(weights[0]),

@@ -9,17 +9,20 @@
 // alternate: the epilogue of one tile runs under the MMAs of the next.  Operands reach shared memory
 // by tensor copies:
 //
-//   TMA warp 13 (lane 0) : per K step two cp.async.bulk.tensor loads into a landing slot (ring of RS),
-//                          completing on `land_full[slot]` (transaction bytes):
-//                            X box {2 modes (4 floats), 64 batch rows, KS channels} of the
-//                              mode-blocked spectrum [Q][B][Ci][8 modes]  -> landing [i][b][4 floats]
-//                            W box {CO float4 (output channels), 1 mode pair, KS channels} of the
-//                              packed weights W_q[i][p][o]                -> landing [i][CO float4]
-//                          rows past B, channels past Ci / Co are zero-filled by the copy itself
-//   producer warps 4..11 : wait `land_full`, read their values (X: one batch row and a K half per thread,
-//                          consecutive threads on consecutive 16-byte rows; W: one output channel and a
-//                          K half), release the slot (`land_empty`), split into tf32 hi / lo (or round to
-//                          bf16) and store the canonical K-major stage (ring of NS) for the MMA warp
+//   TMA warp 13 (lane 0) : per K step
+//                            - one cp.async.bulk.tensor load of the X box {2 modes (4 floats), 64 batch
+//                              rows, KS channels} of the mode-blocked spectrum [Q][B][Ci][8 modes] into a
+//                              landing slot [i][b][4 floats] (ring of RS, `land_full[slot]`; rows past B
+//                              and channels past Ci zero-filled by the copy);
+//                            - once the MMAs have released stage s (`empty[s]`), one cp.async.bulk copy of
+//                              the step's weight tiles, packed ahead of time in the MMA's own layout (tf32
+//                              hi / lo or bf16, zero past Ci / Co; see k_pack_tc), straight into the B half
+//                              of stage s (transaction bytes on `full[s]`)
+//   producer warps 4..11 : wait `land_full`, read their X values (thread = one batch row, one K half, one
+//                          mode; consecutive threads read consecutive 8 bytes), release the slot
+//                          (`land_empty`), split into tf32 hi / lo (or round to bf16) and store the A half
+//                          of stage s in the canonical K-major layout (`full[s]`: 8 producer arrivals plus
+//                          the weight copy's bytes)
 //   MMA warp 12 (lane 0) : wait `full[s]`, issue the step's MMAs for the two modes, commit to `empty[s]`;
 //                          after a tile's last step commit to `acc_full[a]` (a = tile parity)
 //   epilogue warps 0..3  : wait `acc_full[a]`, tcgen05.ld their lane quadrant (the next column group's
@@ -30,7 +33,9 @@
 //                          producers need)
 //
 // Measured on B200 (C2 shapes, clock64 trace per role): with four-mode tiles the single accumulator
-// made every tile's epilogue (~12k cycles) stall the MMA and, through the full stages, the producers.
+// made every tile's epilogue (~12k cycles) stall the MMA and, through the full stages, the producers;
+// with the weights converted by the producers too, shared-memory traffic (~112 KB per K step) bounded
+// the producers, which the pre-split weight tiles cut to ~96 KB and half the producer work.
 // No multicast: every copy is a plain tiled load of this GPU's memory.  Every wait is bounded
 // (kWaitCycles); on expiry the kernel records the status word, the roles leave their loops, the
 // copies in flight and the issued MMAs are drained (bounded) and the tensor memory is freed.
@@ -62,8 +67,9 @@ struct Cfg {
     static constexpr int B_TILE = N * 32;
     static constexpr int STAGE = TM * SPLITS * (A_TILE + B_TILE);
     static constexpr int XBYTES = KS * BT * 16;         // [KS][64][4 floats]
-    static constexpr int WBYTES = KS * CO * 16;         // [KS][CO float4]
-    static constexpr int RAW = XBYTES + WBYTES;         // one landing slot
+    static constexpr int RAW = XBYTES;                  // one landing slot
+    static constexpr int A_BYTES = TM * SPLITS * A_TILE;  // the producers' half of a stage
+    static constexpr int W_STEP = TM * SPLITS * B_TILE;   // the weight copy's half (bytes per K step)
     static constexpr int RS = 4;
     // epilogue staging: per epilogue warp two 2 KB tiles [8 channels][16 rows][16 B]
     static constexpr int EPI_TILE = 2048;
@@ -92,12 +98,21 @@ struct Cfg {
                                       ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 };
 
-// one K step of a producer thread: per channel c of its K half, the two modes (re0, im0, re1, im1)
+// one K step of a producer thread: per channel c of its K half, its mode's (re, im)
 template <bool BF16>
 struct Step {
     static constexpr int KH = BF16 ? 8 : 4;
-    float4 v[KH];
+    float2 v[KH];
 };
+
+// Pre-split weight tiles (written by k_pack_tc, read by one bulk copy per K step).  Tile id
+//   T = (((qw * H + h) * ot + otile) * nk + k) * TM + jl
+// for weight block qw (0 for a matrix shared by every block, with H = 1 and h taken as 0), mode pair
+// h, output tile otile (CO channels), K step k and mode jl of the pair; per tile SPLITS B images of
+// 2 CO rows ([Wr | Wi] of the CO channels) x KS channels in the canonical K-major layout.
+__host__ __device__ __forceinline__ int64_t tc_tile(int64_t qw, int H, int h, int ot, int otile, int nk, int k, int jl) {
+    return (((qw * H + h) * ot + otile) * nk + k) * TM + jl;
+}
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
@@ -132,6 +147,15 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
         : "memory");
 }
 
+// contiguous global -> shared copy completing on an mbarrier (transaction bytes)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            tc::smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(tc::smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 // tile t: mode quarter h (fastest), output tile, local mode block q, batch tile -- the tiles that read
 // the same X rows run on neighbouring CTAs at the same time, so X comes from L2 after its first read
 struct TileIdx {
@@ -150,80 +174,103 @@ __device__ __forceinline__ TileIdx tile_idx(int t, int ot, int local, int qpl, i
     return r;
 }
 
-// producer thread p's values of one K step from a landing slot.  X threads p < 128: batch row
-// b = p % 64, K half p / 64 (consecutive threads read consecutive 16-byte rows); W threads: output
-// channel u % CO, K half u / CO (consecutive threads read consecutive float4).
+// producer thread p's values of one K step from a landing slot: mode jl = p % 2, batch row
+// b = (p / 2) % 64, K half p / 128 (consecutive threads read consecutive 8-byte pieces)
 template <int CO, bool BF16>
 __device__ __forceinline__ void read_landed(const char* slot, int p, Step<BF16>& st) {
-    using C = Cfg<CO, BF16>;
     constexpr int KH = Step<BF16>::KH;
-    if (p < 128) {
-        const int b = p & 63, kh = p >> 6;
-        const float4* x = reinterpret_cast<const float4*>(slot);
+    const int jl = p & 1, b = (p >> 1) & 63, kh = p >> 7;
+    const float2* x = reinterpret_cast<const float2*>(slot);
 #pragma unroll
-        for (int c = 0; c < KH; ++c) st.v[c] = x[(kh * KH + c) * BT + b];
-    } else if (p < 128 + 2 * CO) {
-        const int u = p - 128;
-        const int o = u % CO, kh = u / CO;
-        const float4* w = reinterpret_cast<const float4*>(slot + C::XBYTES);
-#pragma unroll
-        for (int c = 0; c < KH; ++c) st.v[c] = w[(kh * KH + c) * CO + o];
-    }
+    for (int c = 0; c < KH; ++c) st.v[c] = x[((kh * KH + c) * BT + b) * 2 + jl];
 }
 
-// the canonical K-major stage of one K step: 8-row x 16-byte core matrices (tc::tile_off), A rows
-// [Xr; Xi] in 16-row halves of every 32-row quadrant (tc::a_row), B rows [Wr | Wi]
+// the A half of a stage: the thread's mode jl, rows (Xr, Xi) of its batch entry, its K half, in the
+// canonical K-major layout (8-row x 16-byte core matrices, tc::tile_off; rows tc::a_row)
 template <int CO, bool BF16>
 __device__ __forceinline__ void store_landed(const Step<BF16>& st, char* stage, int p) {
     using C = Cfg<CO, BF16>;
     constexpr int KH = Step<BF16>::KH;
-    int rows[2], kh, tile_bytes;
-    char* base;
-    if (p < 128) {
-        rows[0] = tc::a_row(p & 63, 0);
-        rows[1] = tc::a_row(p & 63, 1);
-        kh = p >> 6;
-        base = stage;
-        tile_bytes = C::A_TILE;
-    } else if (p < 128 + 2 * CO) {
-        const int u = p - 128;
-        rows[0] = u % CO;       // columns of Wr
-        rows[1] = u % CO + CO;  // columns of Wi
-        kh = u / CO;
-        base = stage + TM * C::SPLITS * C::A_TILE;
-        tile_bytes = C::B_TILE;
-    } else {
-        return;
-    }
+    const int jl = p & 1, b = (p >> 1) & 63, kh = p >> 7;
 #pragma unroll
-    for (int jl = 0; jl < TM; ++jl) {
+    for (int e = 0; e < 2; ++e) {
+        const uint32_t off = tc::tile_off(tc::a_row(b, e), kh);
+        float x[KH];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const uint32_t off = tc::tile_off(rows[e], kh);
-            float x[KH];
+        for (int c = 0; c < KH; ++c) x[c] = e ? st.v[c].y : st.v[c].x;
+        if constexpr (BF16) {
+            uint4 w;
+            w.x = tc::pack_bf16(x[0], x[1]);
+            w.y = tc::pack_bf16(x[2], x[3]);
+            w.z = tc::pack_bf16(x[4], x[5]);
+            w.w = tc::pack_bf16(x[6], x[7]);
+            *reinterpret_cast<uint4*>(stage + jl * C::A_TILE + off) = w;
+        } else {
+            float hi[4], lo[4];
 #pragma unroll
-            for (int c = 0; c < KH; ++c) {
-                const float4 v = st.v[c];
-                x[c] = jl ? (e ? v.w : v.z) : (e ? v.y : v.x);
+            for (int c = 0; c < 4; ++c) {
+                hi[c] = tc::tf32_round(x[c]);
+                lo[c] = tc::tf32_round(x[c] - hi[c]);
             }
-            if constexpr (BF16) {
-                uint4 w;
-                w.x = tc::pack_bf16(x[0], x[1]);
-                w.y = tc::pack_bf16(x[2], x[3]);
-                w.z = tc::pack_bf16(x[4], x[5]);
-                w.w = tc::pack_bf16(x[6], x[7]);
-                *reinterpret_cast<uint4*>(base + jl * tile_bytes + off) = w;
-            } else {
-                float hi[4], lo[4];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    hi[c] = tc::tf32_round(x[c]);
-                    lo[c] = tc::tf32_round(x[c] - hi[c]);
-                }
-                *reinterpret_cast<float4*>(base + (jl * 2 + 0) * tile_bytes + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<float4*>(base + (jl * 2 + 1) * tile_bytes + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-            }
+            *reinterpret_cast<float4*>(stage + (jl * 2 + 0) * C::A_TILE + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<float4*>(stage + (jl * 2 + 1) * C::A_TILE + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
         }
+    }
+}
+
+// Weight packing for this kernel: element (i, o, m) of the weight at W[i * s_i + o * s_o + m * s_m]
+// (s_m = 0: one matrix for every block) into the tiles described at tc_tile, conjugated when `conj`.
+// One thread per 16-byte piece: B row r (r < CO: Re of channel otile * CO + r, else Im of channel
+// otile * CO + r - CO), K half kh; tf32 hi / lo pieces (the split of the producers, so the MMA
+// operands equal a per-launch split bit for bit) or 8 bf16.
+template <int CO, bool BF16>
+__global__ void k_pack_tc(const float2* __restrict__ W, char* __restrict__ out, int I, int O, int64_t Mt, int64_t Qw,
+                          int H, int ot, int nk, int64_t s_i, int64_t s_o, int64_t s_m, int conj) {
+    using C = Cfg<CO, BF16>;
+    constexpr int HALF = C::KS / 2;  // channels per 16-byte piece
+    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t tiles = Qw * H * ot * nk * TM;
+    if (idx >= tiles * 2 * CO * 2) return;
+    const int kh = (int)(idx & 1);
+    const int r = (int)((idx >> 1) % (2 * CO));
+    int64_t t = (idx >> 1) / (2 * CO);
+    const int jl = (int)(t % TM);
+    int64_t u = t / TM;
+    const int k = (int)(u % nk);
+    u /= nk;
+    const int otile = (int)(u % ot);
+    u /= ot;
+    const int h = (int)(u % H);
+    const int64_t qw = u / H;
+    const int o = otile * CO + (r < CO ? r : r - CO);
+    const int64_t m = 8 * qw + 2 * h + jl;
+    const bool ok = o < O && (s_m == 0 || m < Mt);
+    float v[HALF];
+#pragma unroll
+    for (int c = 0; c < HALF; ++c) {
+        const int i = k * C::KS + kh * HALF + c;
+        float2 w = make_float2(0.f, 0.f);
+        if (ok && i < I) w = W[i * s_i + o * s_o + (s_m ? m * s_m : 0)];
+        v[c] = r < CO ? w.x : (conj ? -w.y : w.y);
+    }
+    char* tile = out + t * C::SPLITS * C::B_TILE;
+    const uint32_t off = tc::tile_off(r, kh);
+    if constexpr (BF16) {
+        uint4 w;
+        w.x = tc::pack_bf16(v[0], v[1]);
+        w.y = tc::pack_bf16(v[2], v[3]);
+        w.z = tc::pack_bf16(v[4], v[5]);
+        w.w = tc::pack_bf16(v[6], v[7]);
+        *reinterpret_cast<uint4*>(tile + off) = w;
+    } else {
+        float hi[4], lo[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            hi[c] = tc::tf32_round(v[c]);
+            lo[c] = tc::tf32_round(v[c] - hi[c]);
+        }
+        *reinterpret_cast<float4*>(tile + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(tile + C::B_TILE + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -251,12 +298,12 @@ __device__ __forceinline__ void wait_regs(float (&v)[TM][8]) {
                  : "memory");
 }
 
-// Persistent: CTA c takes tiles c, c + gridDim.x, ...  `w_rank` 4: weights per mode block (map dims
-// {4 Co floats, 4, Ci, blocks}); 3: one weight matrix for every block (a Tucker factor).
+// Persistent: CTA c takes tiles c, c + gridDim.x, ...  Wtc: weight tiles from k_pack_tc; H = 4 for
+// weights per mode block, H = 1 for one matrix shared by every block (a Tucker factor).
 template <int CO, bool BF16>
 __global__ void __maxnreg__(128)
-k_mix_tma(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
-          const __grid_constant__ CUtensorMap tmy, int w_rank, int B, int Ci, int Co, int local, int qpl, int qtot,
+k_mix_tma(const __grid_constant__ CUtensorMap tmx, const char* __restrict__ Wtc,
+          const __grid_constant__ CUtensorMap tmy, int H, int B, int Ci, int Co, int local, int qpl, int qtot,
           int qbeg, int* __restrict__ status) {
     using C = Cfg<CO, BF16>;
     constexpr int NS = C::NS, NACC = C::NACC, RS = C::RS;
@@ -280,7 +327,7 @@ k_mix_tma(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUten
 
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
-            tc::mbar_init(&full[i], PROD_WARPS);  // one arrival per producer warp
+            tc::mbar_init(&full[i], PROD_WARPS + 1);  // one arrival per producer warp + the weight copy
             tc::mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < RS; ++i) {
@@ -316,31 +363,41 @@ k_mix_tma(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUten
         // ------------------------------ tensor copies ------------------------------
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmx)) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
             const uint64_t pol = l2::evict_first();  // spectrum and weights are read once
-            int issued = 0;
+            int issued = 0, issued_w = 0;
+            bool ok = true;
             TileIdx tl{};
-            for (int g = 0; g < steps; ++g) {
-                const int slot = g % RS, use = g / RS;
-                if (use > 0 && !tc::mbar_wait(&land_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) {
-                    give_up();
-                    break;
-                }
+            for (int g = 0; g < steps && ok; ++g) {
                 const int kc = g % nk;
                 if (kc == 0) tl = tile_k(g / nk);
+                // X box -> landing slot
+                const int slot = g % RS, use = g / RS;
+                if (use > 0 && !tc::mbar_wait(&land_empty[slot], (uint32_t)((use - 1) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 char* dst = smem + C::RAW_OFF + slot * C::RAW;
                 mbar_expect_tx(&land_full[slot], C::RAW);
                 tma_load_4d(dst, &tmx, 4 * tl.h, tl.b0, kc * C::KS, tl.q, &land_full[slot], pol);
-                if (w_rank == 4)
-                    tma_load_4d(dst + C::XBYTES, &tmw, 4 * tl.o0, tl.h, kc * C::KS, tl.qw, &land_full[slot], pol);
-                else
-                    tma_load_3d(dst + C::XBYTES, &tmw, 4 * tl.o0, tl.h, kc * C::KS, &land_full[slot], pol);
                 issued = g + 1;
+                // weight tiles -> the B half of stage s once the MMAs have released it
+                const int st = g % NS, suse = g / NS;
+                if (suse > 0 && !tc::mbar_wait(&empty[st], (uint32_t)((suse - 1) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int64_t tile = tc_tile(H == 1 ? 0 : tl.qw, H, H == 1 ? 0 : tl.h, ot, tl.o0 / CO, nk, kc, 0);
+                mbar_expect_tx(&full[st], C::W_STEP);
+                bulk_load(smem + st * C::STAGE + C::A_BYTES, Wtc + tile * C::SPLITS * C::B_TILE, C::W_STEP,
+                          &full[st], pol);
+                issued_w = g + 1;
             }
-            // the copies still in flight land before the CTA can exit (bounded; they depend on no
-            // other role)
+            if (!ok) give_up();
+            // the copies still in flight land before the CTA can exit (bounded)
             for (int g = issued - RS > 0 ? issued - RS : 0; g < issued; ++g)
                 if (!tc::mbar_wait(&land_full[g % RS], (uint32_t)((g / RS) & 1), nullptr)) give_up();
+            for (int g = issued_w - NS > 0 ? issued_w - NS : 0; g < issued_w; ++g)
+                if (!tc::mbar_wait(&full[g % NS], (uint32_t)((g / NS) & 1), nullptr)) give_up();
         }
     } else if (warp >= EPI_WARPS && warp < MMA_WARP) {
         // ------------------------------ producers ------------------------------
@@ -399,7 +456,7 @@ k_mix_tma(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUten
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t a0 = tc::smem_u32(smem + s * C::STAGE);
-                    const uint32_t bq = a0 + TM * C::SPLITS * C::A_TILE;
+                    const uint32_t bq = a0 + C::A_BYTES;
 #pragma unroll
                     for (int jl = 0; jl < TM; ++jl) {
                         const uint32_t d = dacc + jl * C::N;

@@ -60,6 +60,7 @@ struct Plan {
     WorkspaceLayout ws;
     size_t packed_bytes = 0;           // fused engine: packed-weight buffer size (0: no packing)
     bool mix_tc = true;                // fused engine: contraction on the tensor cores (tcgen05)
+    bool mix_tma = true;               // ... by the TMA kernel on pre-split weight tiles (packed layout)
     // 3D slab decomposition (FastKind::Vol3DSlab): this rank's x planes and everyone's mode blocks
     int slab_rank = 0, slab_world = 1;
     int64_t slab_nx = 0;                                   // x planes per rank

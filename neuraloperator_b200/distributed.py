@@ -125,7 +125,7 @@ class SlabSpectralConv:
     def _packed(self, plan, desc, weights, device):
         ws = [w.detach().to(device=device, dtype=torch.complex64).contiguous() for w in weights]
         cache = self.conv.__dict__.setdefault("_nop_pack_cache", {})
-        key = ("slab", bytes(desc), ops._weight_key(ws))
+        key = ("slab", bytes(desc), ops._weight_key(ws), plan.handle.value, plan.packed_bytes)
         entry = cache.get("slab_packed")
         if entry is not None and entry[0] == key:
             return entry[1]

@@ -84,8 +84,9 @@ def _weight_key(ws):
 
 def _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream):
     """Packed weight buffer of a fused plan: reused from ``cache`` while the weight tensors keep
-    their storage and version counter, else packed now (nop_spectral_pack_weights)."""
-    key = (bytes(desc), _weight_key(ws))
+    their storage and version counter and the plan is the same (the packed layout is the plan's
+    choice), else packed now (nop_spectral_pack_weights)."""
+    key = (bytes(desc), _weight_key(ws), plan.handle.value, plan.packed_bytes)
     entry = cache.get("packed") if cache is not None else None
     if entry is not None and entry[0] == key:
         return entry[1]

@@ -5,9 +5,10 @@ the bf16 contraction).  NOP_CONTRACTION=simt (read at plan creation) selects the
 which computes the same sums in plain fp32 FMAs; the two must agree to fp32 rounding
 (relative L2 <= 2e-6) on shapes that exercise every tile edge: batch not a multiple of 64, channel
 counts not multiples of 8 / 32 / 64, more than one output tile, factorized weights, 1D / 2D / 3D.
-The tensor-core kernel loads its operands and stores its results with tensor copies (TMA);
-NOP_MIX_TMA=0 (read per launch) selects its per-thread-gather twin, which must give bit-identical
-results (the same MMAs on the same operands in the same order).
+The tensor-core kernel loads its operands and stores its results with tensor copies (TMA), its
+weights pre-split into tf32 hi / lo tiles when they are packed; NOP_MIX_TMA=0 (read at plan creation)
+selects its per-thread-gather twin on the float4 packing, which must give bit-identical results (the
+same MMAs on the same operands in the same order).
 Every run must leave the device status word at 0 (no bounded wait expired).
 """
 
@@ -103,6 +104,8 @@ def _forward_tma(conv, x, tma):
             os.environ.pop("NOP_MIX_TMA", None)
         else:
             os.environ["NOP_MIX_TMA"] = "0"
+        ops.clear_plans()
+        conv.__dict__.pop("_nop_pack_cache", None)
         with torch.no_grad():
             y = conv(x)
         torch.cuda.synchronize()
@@ -112,6 +115,7 @@ def _forward_tma(conv, x, tma):
             os.environ.pop("NOP_MIX_TMA", None)
         else:
             os.environ["NOP_MIX_TMA"] = old
+        ops.clear_plans()
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"B{c[0]}_ci{c[1]}_co{c[2]}_{len(c[3])}d_{'_'.join(c[5])}" for c in CASES])
