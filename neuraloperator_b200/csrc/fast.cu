@@ -499,6 +499,25 @@ cudaError_t pack_tc(const Plan& p, const float2* W, char* out, int64_t I, int64_
     const int64_t n = Qw * H * g.ot * g.nk * tma_mix::TM * 2 * g.co * 2;
     const unsigned grid = (unsigned)ceil_div(n, 256);
     const int64_t Mt = p.modes_total;
+    if (H == 4 && s_m == 1) {  // per-block weights with contiguous modes: coalesced 64-byte reads
+        const unsigned blocks = (unsigned)(Qw * g.ot * g.nk);
+        if (g.co == 64) {
+            if (g.bf16)
+                tma_mix::k_pack_tc_block<64, true><<<blocks, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, g.ot, g.nk, s_i,
+                                                                          s_o, conj);
+            else
+                tma_mix::k_pack_tc_block<64, false><<<blocks, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, g.ot, g.nk,
+                                                                           s_i, s_o, conj);
+        } else {
+            if (g.bf16)
+                tma_mix::k_pack_tc_block<32, true><<<blocks, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, g.ot, g.nk, s_i,
+                                                                          s_o, conj);
+            else
+                tma_mix::k_pack_tc_block<32, false><<<blocks, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, g.ot, g.nk,
+                                                                           s_i, s_o, conj);
+        }
+        return cudaGetLastError();
+    }
     if (g.co == 64) {
         if (g.bf16)
             tma_mix::k_pack_tc<64, true><<<grid, 256, 0, s>>>(W, out, (int)I, (int)O, Mt, Qw, H, g.ot, g.nk, s_i, s_o,

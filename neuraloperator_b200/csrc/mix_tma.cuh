@@ -19,7 +19,7 @@
 //                              hi / lo or bf16, zero past Ci / Co; see k_pack_tc), straight into the B half
 //                              of stage s (transaction bytes on `full[s]`)
 //   producer warps 4..11 : wait `land_full`, read their X values (thread = one batch row, one K half, one
-//                          mode; consecutive threads read consecutive 8 bytes), release the slot
+//                          mode; a warp = one mode of 32 consecutive rows), release the slot
 //                          (`land_empty`), split into tf32 hi / lo (or round to bf16) and store the A half
 //                          of stage s in the canonical K-major layout (`full[s]`: 8 producer arrivals plus
 //                          the weight copy's bytes)
@@ -174,12 +174,14 @@ __device__ __forceinline__ TileIdx tile_idx(int t, int ot, int local, int qpl, i
     return r;
 }
 
-// producer thread p's values of one K step from a landing slot: mode jl = p % 2, batch row
-// b = (p / 2) % 64, K half p / 128 (consecutive threads read consecutive 8-byte pieces)
+// producer thread p's values of one K step from a landing slot: batch row b = p % 64, mode
+// jl = (p / 64) % 2, K half p / 128.  A warp holds one mode of 32 consecutive rows, so its stores
+// of the A half hit distinct bank groups (measured: lanes of both modes in one warp stored to tiles a
+// multiple of 128 bytes apart, 1.7 M extra shared-memory wavefronts on C2)
 template <int CO, bool BF16>
 __device__ __forceinline__ void read_landed(const char* slot, int p, Step<BF16>& st) {
     constexpr int KH = Step<BF16>::KH;
-    const int jl = p & 1, b = (p >> 1) & 63, kh = p >> 7;
+    const int b = p & 63, jl = (p >> 6) & 1, kh = p >> 7;
     const float2* x = reinterpret_cast<const float2*>(slot);
 #pragma unroll
     for (int c = 0; c < KH; ++c) st.v[c] = x[((kh * KH + c) * BT + b) * 2 + jl];
@@ -191,7 +193,7 @@ template <int CO, bool BF16>
 __device__ __forceinline__ void store_landed(const Step<BF16>& st, char* stage, int p) {
     using C = Cfg<CO, BF16>;
     constexpr int KH = Step<BF16>::KH;
-    const int jl = p & 1, b = (p >> 1) & 63, kh = p >> 7;
+    const int b = p & 63, jl = (p >> 6) & 1, kh = p >> 7;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
         const uint32_t off = tc::tile_off(tc::a_row(b, e), kh);
@@ -271,6 +273,70 @@ __global__ void k_pack_tc(const float2* __restrict__ W, char* __restrict__ out, 
         }
         *reinterpret_cast<float4*>(tile + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
         *reinterpret_cast<float4*>(tile + C::B_TILE + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// The same tiles for weights per mode block with contiguous modes (s_m = 1: dense weights, their
+// adjoint, the expanded Tucker core), one CTA per (weight block qw, output tile, K step): for every
+// (channel, output) pair of the step the block's 8 modes are one 64-byte run, read into shared
+// memory ([channel][mode][output], conflict-free both ways) a K half at a time, then written as the
+// 16-byte pieces of the 4 mode pairs x 2 modes (values identical to k_pack_tc's).
+template <int CO, bool BF16>
+__global__ void __launch_bounds__(256) k_pack_tc_block(const float2* __restrict__ W, char* __restrict__ out, int I,
+                                                       int O, int64_t Mt, int ot, int nk, int64_t s_i, int64_t s_o,
+                                                       int conj) {
+    using C = Cfg<CO, BF16>;
+    constexpr int HALF = C::KS / 2;  // channels per 16-byte piece
+    __shared__ float2 S[HALF][8][CO];
+    const int k = (int)(blockIdx.x % nk);
+    const int otile = (int)((blockIdx.x / nk) % ot);
+    const int64_t qw = blockIdx.x / ((int64_t)nk * ot);
+    for (int kh = 0; kh < 2; ++kh) {
+        for (int e = threadIdx.x; e < HALF * CO; e += blockDim.x) {
+            const int ol = e % CO, c = e / CO;
+            const int o = otile * CO + ol, i = k * C::KS + kh * HALF + c;
+            const bool ok = o < O && i < I;
+            const float2* src = W + (ok ? i * s_i + o * s_o + 8 * qw : 0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float2 w = make_float2(0.f, 0.f);
+                if (ok && 8 * qw + j < Mt) w = src[j];
+                S[c][j][ol] = conj ? make_float2(w.x, -w.y) : w;
+            }
+        }
+        __syncthreads();
+        for (int f = threadIdx.x; f < 4 * TM * 2 * CO; f += blockDim.x) {
+            const int r = f % (2 * CO);
+            const int jl = (f / (2 * CO)) % TM;
+            const int h = f / (2 * CO * TM);
+            const int ol = r < CO ? r : r - CO;
+            float v[HALF];
+#pragma unroll
+            for (int c = 0; c < HALF; ++c) {
+                const float2 w = S[c][2 * h + jl][ol];
+                v[c] = r < CO ? w.x : w.y;
+            }
+            char* tile = out + tc_tile(qw, 4, h, ot, otile, nk, k, jl) * C::SPLITS * C::B_TILE;
+            const uint32_t off = tc::tile_off(r, kh);
+            if constexpr (BF16) {
+                uint4 w;
+                w.x = tc::pack_bf16(v[0], v[1]);
+                w.y = tc::pack_bf16(v[2], v[3]);
+                w.z = tc::pack_bf16(v[4], v[5]);
+                w.w = tc::pack_bf16(v[6], v[7]);
+                *reinterpret_cast<uint4*>(tile + off) = w;
+            } else {
+                float hi[4], lo[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    hi[c] = tc::tf32_round(v[c]);
+                    lo[c] = tc::tf32_round(v[c] - hi[c]);
+                }
+                *reinterpret_cast<float4*>(tile + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(tile + C::B_TILE + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            }
+        }
+        __syncthreads();
     }
 }
 
