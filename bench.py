@@ -47,7 +47,7 @@ TRAFFIC = {
     ("c2", "plane_inv"): 8 * (8.701952e6 + 79.316992e6),
     ("c2", "plane_fwd"): 8 * (134.246144e6 + 4.028928e6),
     # profiles/contraction_tma_c2_full.md: full-size capture of the contraction (one launch)
-    ("c2", "contraction"): 138.643968e6 + 10.613504e6,
+    ("c2", "contraction"): 207.854080e6 + 10.398976e6,
 }
 
 # name -> (description, batch, Ci, Co, grid, n_modes, factorization)
