@@ -36,7 +36,7 @@
 // made every tile's epilogue (~12k cycles) stall the MMA and, through the full stages, the producers;
 // with the weights converted by the producers too, shared-memory traffic (~112 KB per K step) bounded
 // the producers, which the pre-split weight tiles cut to ~96 KB and half the producer work.
-// No multicast: every copy is a plain tiled load of this GPU's memory.  Every wait is bounded
+// Every copy is a plain (single-CTA) tiled copy of this GPU's own memory.  Every wait is bounded
 // (kWaitCycles); on expiry the kernel records the status word, the roles leave their loops, the
 // copies in flight and the issued MMAs are drained (bounded) and the tensor memory is freed.
 #pragma once
