@@ -214,8 +214,10 @@ int32_t nop_device_status(int32_t* status, int32_t clear);
  * workspace), runs the generic direct-DFT kernels and keeps their twiddle tables and intermediate
  * spectra in a 16 MiB scratch area compiled into the library (held by every GPU that loads the
  * library until the process exits).  Problems that need more scratch fail with NOP_E_WORKSPACE.
- * The first call on each device looks up that area's device address; make it before any stream
- * capture starts.  All calls on a device share the area and leave their contents in it (every
+ * The descriptor's engine field must be NOP_ENGINE_AUTO or NOP_ENGINE_GENERIC (NOP_ENGINE_FAST:
+ * NOP_E_UNSUPPORTED).  The first call in each CUDA context (per device; again after a
+ * cudaDeviceReset or in another driver-API context) looks up that area's device address; make it
+ * before any stream capture starts.  All calls on a device share the area and leave their contents in it (every
  * region is fully rewritten before it is read); calls that run concurrently on the GPU race on it,
  * so order them on one stream.  Arguments are those of nop_spectral_forward minus plan and
  * workspace; it never calls cudaMalloc or cudaFree. */

@@ -16,11 +16,16 @@
 //     kernels of a call before any kernel of that call reads it, so nothing needs clearing.
 //     Calls whose kernels overlap on the GPU (different streams without ordering between
 //     them, or different host threads) race on the scratch and produce garbage.
-//   * the first call on a device looks up the device address of the scratch with
-//     cudaGetSymbolAddress (host code cannot use the symbol itself: in host code its name
-//     stands for a host-side shadow, not device memory).  Make that first call before any
-//     stream capture begins.
+//   * the first call in a CUDA context (per device, with that device current) looks up the device
+//     address of the scratch with cudaGetSymbolAddress (host code cannot use the symbol itself: in
+//     host code its name stands for a host-side shadow, not device memory) and caches it under the
+//     context's unique id.  A new context on the device -- after cudaDeviceReset, or a driver-API
+//     context made current by the caller -- has another id, so its first call looks the address up
+//     again instead of reusing one that belonged to a destroyed context.  Make the first call in each
+//     context before any stream capture begins.
 #include <mutex>
+
+#include <cuda.h>
 
 #include "nop_internal.cuh"
 
@@ -33,21 +38,56 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
+struct ScratchAddr {
+    unsigned long long ctx_id = 0;  // id of the context the address belongs to (0: none yet)
+    char* addr = nullptr;
+};
+
 std::mutex g_addr_mutex;
-char* g_scratch_addr[kMaxDevices] = {};
+ScratchAddr g_scratch_addr[kMaxDevices];
 
 size_t round_up(size_t v) { return (v + kScratchAlign - 1) / kScratchAlign * kScratchAlign; }
 
-// Device address of g_static_scratch on device `dev` (current device), looked up once.
+// cuCtxGetCurrent / cuCtxGetId through the runtime's driver entry point (no link against libcuda)
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+using CtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+template <class F>
+F driver_fn(const char* name) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return reinterpret_cast<F>(f);
+}
+
+// Unique id of the current context of the calling thread (ids are never reused in a process).
+int32_t current_context_id(unsigned long long* id) {
+    static const CtxGetCurrent get_current = driver_fn<CtxGetCurrent>("cuCtxGetCurrent");
+    static const CtxGetId get_id = driver_fn<CtxGetId>("cuCtxGetId");
+    if (!get_current || !get_id) return fail(NOP_E_CUDA, "cuCtxGetCurrent / cuCtxGetId are not available");
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return fail(NOP_E_CUDA, "no current CUDA context");
+    if (get_id(ctx, id) != CUDA_SUCCESS) return fail(NOP_E_CUDA, "cuCtxGetId failed");
+    return NOP_OK;
+}
+
+// Device address of g_static_scratch on device `dev` (the current device) in the current context,
+// looked up once per context.
 int32_t scratch_address(int dev, char** out) {
+    unsigned long long ctx_id = 0;
+    int32_t rc = current_context_id(&ctx_id);
+    if (rc != NOP_OK) return rc;
     std::lock_guard<std::mutex> lock(g_addr_mutex);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr& e = g_scratch_addr[dev];
+    if (e.ctx_id != ctx_id || !e.addr) {
         void* p = nullptr;
         cudaError_t err = cudaGetSymbolAddress(&p, g_static_scratch);
         if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(static scratch)");
-        g_scratch_addr[dev] = static_cast<char*>(p);
+        e.addr = static_cast<char*>(p);
+        e.ctx_id = ctx_id;
     }
-    *out = g_scratch_addr[dev];
+    *out = e.addr;
     return NOP_OK;
 }
 
@@ -90,6 +130,9 @@ extern "C" int32_t nop_spectral_forward_static(const nop_spectral_desc* desc, co
         p.d.fwd_off[j] = p.d.inv_off[j] = 0;
     }
     const nop_spectral_desc& d = p.d;
+    if (d.engine == NOP_ENGINE_FAST)
+        return fail(NOP_E_UNSUPPORTED, "the allocation-free forward runs the generic engine only; "
+                                       "pass NOP_ENGINE_AUTO or NOP_ENGINE_GENERIC");
     if (n_weights != expected_weights(d))
         return fail(NOP_E_INVALID, "expected " + std::to_string(expected_weights(d)) + " weight pointers, got " +
                                        std::to_string(n_weights));

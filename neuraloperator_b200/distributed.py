@@ -125,7 +125,7 @@ class SlabSpectralConv:
     def _packed(self, plan, desc, weights, device):
         ws = [w.detach().to(device=device, dtype=torch.complex64).contiguous() for w in weights]
         cache = self.conv.__dict__.setdefault("_nop_pack_cache", {})
-        key = ("slab", bytes(desc), ops._weight_key(ws), plan.handle.value, plan.packed_bytes)
+        key = ("slab", bytes(desc), ops._weight_key(weights), plan.handle.value, plan.packed_bytes)
         entry = cache.get("slab_packed")
         if entry is not None and entry[0] == key:
             return entry[1]
@@ -136,7 +136,7 @@ class SlabSpectralConv:
         _lib.check(_lib.library().nop_spectral_pack_weights(plan.handle, arr, len(ws), ctypes.c_void_p(packed.data_ptr()),
                                                             plan.packed_bytes, ctypes.c_void_p(workspace.data_ptr()),
                                                             plan.workspace_bytes, stream))
-        cache["slab_packed"] = (key, packed)
+        cache["slab_packed"] = (key, packed, list(weights))  # referenced: addresses cannot be recycled
         return packed
 
     def stage_planes_fwd(self, x_slab: torch.Tensor, lay: SlabLayout) -> torch.Tensor:

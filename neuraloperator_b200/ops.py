@@ -78,15 +78,23 @@ def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
-def _weight_key(ws):
-    return tuple((w.data_ptr(), w._version, tuple(w.shape), tuple(w.stride())) for w in ws)
+def _weight_key(sources):
+    """Identity of the weight tensors as the caller passed them (before any dtype / device /
+    contiguity copy): storage address, version counter (shared with the base tensor for views, so an
+    in-place update of a sliced parameter is seen), shape and strides."""
+    return tuple((w.data_ptr(), w._version, w.dtype, tuple(w.shape), tuple(w.stride())) for w in sources)
 
 
-def _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream):
-    """Packed weight buffer of a fused plan: reused from ``cache`` while the weight tensors keep
-    their storage and version counter and the plan is the same (the packed layout is the plan's
-    choice), else packed now (nop_spectral_pack_weights)."""
-    key = (bytes(desc), _weight_key(ws), plan.handle.value, plan.packed_bytes)
+def _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream, sources=None):
+    """Packed weight buffer of a fused plan: reused from ``cache`` while the caller's weight tensors
+    (``sources``, default ``ws``) keep their storage and version counter and the plan is the same
+    (the packed layout is the plan's choice), else packed now (nop_spectral_pack_weights).
+
+    The cache entry holds references to the source tensors: while it exists their storage cannot be
+    freed and handed to a new tensor, so a weight rebuilt on every call (a reconstructed factorized
+    weight, a copy of a non-contiguous slice) never matches a stale entry by address and version."""
+    sources = list(ws if sources is None else sources)
+    key = (bytes(desc), _weight_key(sources), plan.handle.value, plan.packed_bytes)
     entry = cache.get("packed") if cache is not None else None
     if entry is not None and entry[0] == key:
         return entry[1]
@@ -94,7 +102,7 @@ def _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream):
     _lib.check(_lib.library().nop_spectral_pack_weights(plan.handle, arr, len(ws), _ptr(packed), plan.packed_bytes,
                                                         _ptr(workspace), plan.workspace_bytes, stream))
     if cache is not None:
-        cache["packed"] = (key, packed)
+        cache["packed"] = (key, packed, sources)
     return packed
 
 
@@ -143,7 +151,7 @@ def spectral_forward(x: torch.Tensor, geo: Geometry, weights: List[torch.Tensor]
         spec = torch.empty(max(plan.spectrum_bytes, 1), device=dev, dtype=torch.uint8)
     with torch.cuda.device(dev):
         if packed is None and plan.packed_bytes > 0:
-            packed = _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream)
+            packed = _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream, sources=weights)
         if spec is not None:
             _lib.check(lib.nop_spectral_forward_keep(
                 plan.handle, _ptr(x), None if packed is not None else arr, 0 if packed is not None else len(ws),
@@ -302,7 +310,7 @@ def spectral_forward_host(x: torch.Tensor, geo: Geometry, weights: List[torch.Te
         packed = None
         if plan.packed_bytes > 0:
             pack_ws = torch.empty(max(plan.workspace_bytes, 1), device=dev, dtype=torch.uint8)
-            packed = _packed_weights(plan, desc, ws, arr, dev, pack_ws, cache, stream)
+            packed = _packed_weights(plan, desc, ws, arr, dev, pack_ws, cache, stream, sources=weights)
         _lib.check(lib.nop_spectral_forward_host(
             plan.handle, _ptr(x), batch, None if packed is not None else arr, 0 if packed is not None else len(ws),
             _ptr(packed), plan.packed_bytes if packed is not None else 0, _ptr(b), _ptr(a), int(bool(apply_gelu)),

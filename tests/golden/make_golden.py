@@ -2,7 +2,7 @@
 
 Run in the build container (it needs the reference checkout; see ``ref_loader``):
 
-    python tests/golden/make_golden.py
+    NOP_REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 Writes ``spectral_cases.pt`` (SpectralConv cases: dense, Tucker, CP, TT, separable,
 complex data, odd sizes, Nyquist kept, incremental modes, output_shape, fft_norm),

@@ -29,7 +29,7 @@ import types
 import torch
 from torch import nn
 
-REF_ROOT = os.environ.get("NOP_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("NOP_REFERENCE_ROOT")  # the reference checkout (its parent of ``neuralop/``)
 
 
 def _tucker_rank(shape, rank):
@@ -211,6 +211,8 @@ _STUB_CLASSES = (_StubDense, _StubTucker, _StubCP, _StubTT)
 
 def install(ref_root: str = REF_ROOT):
     """Install the stand-ins and shell packages; return the reference modules."""
+    if not ref_root:
+        raise RuntimeError("set NOP_REFERENCE_ROOT to the reference checkout (the directory holding neuralop/)")
     if not os.path.isdir(os.path.join(ref_root, "neuralop")):
         raise FileNotFoundError(f"reference checkout not found under {ref_root}")
     tl = types.ModuleType("tensorly")

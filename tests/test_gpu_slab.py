@@ -124,14 +124,22 @@ def test_slab_emulated_tucker():
     assert rel_l2(y, ref) <= TOL_FP32
 
 
+def _free_port() -> int:
+    """A TCP port on 127.0.0.1 that nothing listens on right now (the rendezvous port)."""
+    import socket
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def test_slab_two_gpus_nccl(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     out = tmp_path / "slab.json"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29517", os.path.join(ROOT, "tests", "slab_nccl_worker.py"),
-           str(out)]
+           "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           os.path.join(ROOT, "tests", "slab_nccl_worker.py"), str(out)]
     subprocess.run(cmd, check=True, timeout=600, env=env, cwd=ROOT)
     res = json.loads(out.read_text())
     assert res["err"] <= TOL_FP32, res

@@ -1,10 +1,15 @@
-"""The allocation-free entry point agrees with the regular one.
+"""The allocation-free entry point agrees with the regular one and with the oracle.
 
 nop_spectral_forward_static serves callers that cannot allocate device memory (a host runtime
 that owns all device memory and passes only input/output buffers, or a loop that cannot risk the
 device-wide stall of a cudaMalloc).  It keeps its scratch in a fixed area inside the library, so
-two calls in a row reuse the same memory; both must match nop_spectral_forward.  This file is
-collected last so that a failure here never hides the other tests.
+every call reuses memory that the previous call left behind.  Each case runs twice in a row and is
+checked against nop_spectral_forward and against the oracle (the reference's forward restated on
+the CPU); the cases run from the largest scratch footprint to the smallest, so a region that a
+smaller problem failed to rewrite would still hold a larger problem's values.  Dense, Tucker and CP
+weights, complex data and 1D / 2D / 3D grids cover every scratch region (twiddle tables, spectra,
+factor intermediates).  This file is collected last so that a failure here never hides the other
+tests.
 """
 
 import ctypes
@@ -12,9 +17,10 @@ import ctypes
 import pytest
 import torch
 
+import neuraloperator_b200 as nb
+import oracle
 from conftest import rel_l2
 from neuraloperator_b200 import _lib, ops
-import neuraloperator_b200 as nb
 
 pytestmark = pytest.mark.gpu
 
@@ -31,39 +37,84 @@ def _static_fn():
     return fn
 
 
-def _case(seed, shape=(64, 64), modes=(16, 16), ci=4, co=4, batch=2):
+# name, grid, n_modes, channels (in, out), batch, factorization, complex data, fused skip + GELU;
+# ordered from the largest scratch footprint to the smallest
+CASES = [
+    ("dense2d_128", (128, 128), (32, 32), (8, 8), 2, None, False, True),
+    ("tucker3d_32", (32, 32, 32), (12, 12, 12), (6, 6), 2, "tucker", False, False),
+    ("dense2d_64", (64, 64), (16, 16), (4, 4), 2, None, False, True),
+    ("cp2d_48", (48, 40), (12, 10), (5, 3), 2, "cp", False, False),
+    ("complex2d_32", (32, 24), (10, 8), (3, 4), 1, None, True, False),
+    ("dense1d_256", (256,), (20,), (4, 6), 3, None, False, True),
+]
+
+
+def _conv(case, seed):
+    name, grid, modes, (ci, co), batch, fact, cplx, fused = case
     g = torch.Generator().manual_seed(seed)
-    conv = nb.SpectralConv(ci, co, modes)
+    kw = {}
+    if fact:
+        kw = dict(factorization=fact, implementation="factorized", rank=0.5)
+    conv = nb.SpectralConv(ci, co, modes, complex_data=cplx, **kw)
     with torch.no_grad():
-        conv.weight.tensor.copy_(torch.complex(torch.randn(conv.weight.shape, generator=g),
-                                               torch.randn(conv.weight.shape, generator=g)) * 0.3)
+        for p in conv.weight.parameters():
+            p.copy_(torch.complex(torch.randn(p.shape, generator=g), torch.randn(p.shape, generator=g)) * 0.3)
         conv.bias.copy_(torch.randn(conv.bias.shape, generator=g))
-    conv = conv.cuda()
-    x = torch.randn((batch, ci, *shape), generator=g).cuda()
-    skip = torch.randn((batch, co, *shape), generator=g).cuda()
+    if cplx:
+        x = torch.complex(torch.randn((batch, ci, *grid), generator=g), torch.randn((batch, ci, *grid), generator=g))
+    else:
+        x = torch.randn((batch, ci, *grid), generator=g)
+    skip = torch.randn((batch, co, *grid), generator=g) if fused else None
     return conv, x, skip
 
 
+def _oracle(conv, case, x, skip):
+    name, grid, modes, _, _, fact, cplx, fused = case
+    w = conv.weight
+    if fact == "tucker":
+        payload, kind = {"core": w.core.detach().cpu(), "factors": [f.detach().cpu() for f in w.factors]}, "tucker"
+    elif fact == "cp":
+        payload, kind = {"weights": w.weights.detach().cpu(), "factors": [f.detach().cpu() for f in w.factors]}, "cp"
+    else:
+        payload, kind = w.tensor.detach().cpu(), "dense"
+    y = oracle.spectral_conv(x, payload, conv.bias.detach().cpu(), modes, weight_kind=kind, complex_data=cplx)
+    if fused:
+        y = torch.nn.functional.gelu(y + skip)
+    return y
+
+
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
-def test_static_entry_matches_regular_entry_twice():
+def test_static_entry_matches_regular_entry_and_oracle():
     fn = _static_fn()
-    conv, x, skip = _case(0)
-    geo = conv.geometry(list(x.shape[2:]))
-    _, weights, _ = conv.kernel_operands(geo)
-    w = weights[0].detach().contiguous()
-    b = conv.bias.detach().reshape(-1).contiguous()
-    with torch.no_grad():
-        expect = ops.spectral_forward(x, geo, [w], out_channels=4, bias=b, addend=skip, apply_gelu=True)
-    desc = ops.make_desc(geo, x.shape[0], 4, 4)
     stream = torch.cuda.current_stream().cuda_stream
-    arr = (ctypes.c_void_p * 1)(w.data_ptr())
-    for _ in range(2):  # the second call runs on the scratch the first one left behind
-        y = torch.full_like(expect, float("nan"))
-        rc = fn(ctypes.byref(desc), ctypes.c_void_p(x.data_ptr()), arr, 1, ctypes.c_void_p(b.data_ptr()),
-                ctypes.c_void_p(skip.data_ptr()), 1, ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(stream))
-        assert rc == 0, _lib.last_error()
+    for seed, case in enumerate(CASES):
+        name, grid, modes, (ci, co), batch, fact, cplx, fused = case
+        conv, x_cpu, skip_cpu = _conv(case, seed)
+        with torch.no_grad():
+            expect_oracle = _oracle(conv, case, x_cpu, skip_cpu)
+        conv = conv.cuda()
+        x = x_cpu.cuda()
+        skip = skip_cpu.cuda() if fused else None
+        geo = conv.geometry(list(grid))
+        kind, weights, ranks = conv.kernel_operands(geo)
+        ws = [w.detach().to(torch.complex64).contiguous() for w in weights]
+        b = conv.bias.detach().reshape(-1).contiguous()
+        with torch.no_grad():
+            expect = ops.spectral_forward(x, geo, ws, out_channels=co, weight_kind=kind, ranks=ranks, bias=b,
+                                          addend=skip, apply_gelu=fused)
         torch.cuda.synchronize()
-        assert rel_l2(y, expect) <= TOL_FP32
+        assert rel_l2(expect, expect_oracle) <= TOL_FP32, name
+        desc = ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks)
+        arr = (ctypes.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+        for call in range(2):  # the second call runs on the scratch the first one left behind
+            y = torch.full_like(expect, float("nan"))
+            rc = fn(ctypes.byref(desc), ctypes.c_void_p(x.data_ptr()), arr, len(ws), ctypes.c_void_p(b.data_ptr()),
+                    None if skip is None else ctypes.c_void_p(skip.data_ptr()), int(fused),
+                    ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(stream))
+            assert rc == 0, (name, call, _lib.last_error())
+            torch.cuda.synchronize()
+            assert rel_l2(y, expect) <= TOL_FP32, (name, call)
+            assert rel_l2(y, expect_oracle) <= TOL_FP32, (name, call)
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
@@ -78,3 +129,17 @@ def test_static_entry_rejects_problems_beyond_its_scratch():
             ctypes.c_void_p(dummy.data_ptr()), None)
     assert rc == -4
     assert "static scratch" in _lib.last_error()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
+def test_static_entry_rejects_the_fast_engine():
+    fn = _static_fn()
+    conv = nb.SpectralConv(4, 4, (16, 16))
+    geo = conv.geometry([64, 64])
+    desc = ops.make_desc(geo, 1, 4, 4, engine="fast")
+    dummy = torch.empty(8, device="cuda")
+    arr = (ctypes.c_void_p * 1)(dummy.data_ptr())
+    rc = fn(ctypes.byref(desc), ctypes.c_void_p(dummy.data_ptr()), arr, 1, None, None, 0,
+            ctypes.c_void_p(dummy.data_ptr()), None)
+    assert rc == -2  # NOP_E_UNSUPPORTED
+    assert "generic engine" in _lib.last_error()
