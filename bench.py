@@ -1,22 +1,25 @@
-"""Benchmark of the FNO spectral block on B200 (driver contract: one JSON line on rank 0).
+"""Benchmark of the FNO forward on B200 (driver contract: one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c5]
 
-Default workload: one SpectralConv forward, batch 64 per GPU,
-Cin = Cout = 64, grid 256x256, n_modes (64, 64), fp32, synthetic N(0,1) input and seeded
-complex weights.  A step is one forward over the batch; under torchrun every rank runs its
-own batch (weak scaling, no collective on the data path) and the job value is
-sum(samples) / max-over-ranks(time).
+Default workload: the whole FNO forward (BASELINE.json's metric, "FNO fwd samples/s") on the largest
+configuration that fits one GPU, configs[4]: FNO 3D, 256^3 grid, batch 8, hidden 32, n_modes (32, 32, 32),
+3 input (+3 grid) and 3 output channels, fp32.  Input: three seeded periodic Gaussian random fields
+with covariance (-Lap + 16 I)^-2 (no dataset); weights: the reference initialisers, seed 0.
+A step is one forward over the batch.  N = 1: the batch on one GPU.  N > 1 (torchrun): the 256^3 grid
+is slab-decomposed along x across the ranks, with NCCL all-to-alls of the kept modes inside every
+spectral layer (strong scaling: the global batch stays 8); the job value is 8 / max-over-ranks(time).
 
-* value      : samples/s with x resident in HBM (CUDA events on the launching stream).
-* e2e        : the same through the public API with pinned host buffers, the H2D copy of x
-               and the D2H copy of y inside the timed region.
-* roofline   : the spectral block's algorithmic bytes |x|+|y|+|W|+|bias| per step over its
-               time, against the measured HBM copy bandwidth; traffic comes from an ncu
-               capture summarised under profiles/.
-* cpu_baseline: the oracle (the reference's torch CPU path restated in oracle/) on the
-               host cores over a bounded batch of the same workload.
---impl reference times that CPU path as the reference arm.
+* value        : samples/s with the input resident in HBM (CUDA events on the launching stream).
+* e2e          : the same through FNO.forward_host / SlabFNO.forward_host -- pinned host input in,
+                 pinned host output out, every copy inside the timed region.
+* roofline     : the forward's dominant kernel (most time per forward): its compulsory bytes per
+                 launch over its mean launch time from CUDA events recorded between the launches of
+                 one instrumented forward, against the measured HBM copy bandwidth; kernels[] lists all.
+* cpu_baseline : the oracle (the reference's torch CPU path restated in oracle/) on the host cores,
+                 one sample's forward.
+--impl reference times that CPU path as the reference arm.  --model layer runs the single-SpectralConv
+benchmarks (configs[1], the C2 microbench, by default) and their training step (--pass train).
 """
 
 from __future__ import annotations
@@ -207,51 +210,205 @@ def capture_graph(fn, stream):
         return None, "eager"
 
 
-# full-model configs (2, 3, 4): class, n_modes, hidden, in, out, grid, batch, kwargs
+# ---------------------------------------------------------------------------------------------------
+# Full FNO / TFNO forward (the headline: BASELINE.json's metric is FNO forward samples/s)
+# ---------------------------------------------------------------------------------------------------
+# name -> (workload, class, n_modes, hidden, in, out, grid, batch, kwargs, input field)
+# The input fields are seeded periodic Gaussian random fields with the covariances BASELINE.json gives
+# for each configuration (no dataset is available): (scale, tau^2, alpha) of s^2 (-Lap + tau^2 I)^-alpha,
+# plus the Darcy threshold to {3, 12}.
 MODELS = {
-    "c1": ("fno2d_darcy", "FNO", (16, 16), 32, 1, 1, (128, 128), 16, {}),
-    "c3": ("fno1d_burgers", "FNO", (16,), 64, 1, 1, (8192,), 256, {}),
+    "c1": ("fno2d_darcy", "FNO", (16, 16), 32, 1, 1, (128, 128), 16, {}, (1.0, 9.0, 2.0, "darcy")),
+    "c3": ("fno1d_burgers", "FNO", (16,), 64, 1, 1, (8192,), 256, {}, (625.0, 25.0, 2.0, None)),
     "c4": ("tfno2d_ns", "TFNO", (64, 64), 64, 1, 1, (512, 512), 32,
-           dict(factorization="tucker", implementation="factorized", rank=0.1)),
-    "c5": ("fno3d", "FNO", (32, 32, 32), 32, 3, 3, (256, 256, 256), 8, {}),
+           dict(factorization="tucker", implementation="factorized", rank=0.1), (7.0 ** 0.75, 49.0, 2.5, None)),
+    "c5": ("fno3d", "FNO", (32, 32, 32), 32, 3, 3, (256, 256, 256), 8, {}, (1.0, 16.0, 2.0, None)),
 }
 
 
-def run_model(args, world, rank, local):
-    """FNO / TFNO forward (grid embedding, lifting, 4 FNO blocks, projection) at the config's size;
-    the spectral layers are also timed alone to give their share and their HBM roofline fraction."""
+def grf(batch, channels, grid, field, seed, device):
+    """Seeded periodic Gaussian random field on [0, 1)^d with covariance s^2 (-Lap + tau^2 I)^-alpha:
+    complex white noise times the square root of the covariance's eigenvalues, inverse real FFT (an
+    input generator only; the timed path never calls it)."""
+    scale, tau2, alpha, kind = field
+    gen = torch.Generator(device=device).manual_seed(seed)
+    d = len(grid)
+    ks = [torch.fft.fftfreq(n, 1.0 / n, device=device) for n in grid[:-1]] + \
+         [torch.fft.rfftfreq(grid[-1], 1.0 / grid[-1], device=device)]
+    k2 = sum(k.reshape([-1 if i == j else 1 for i in range(d)]) ** 2 for j, k in enumerate(ks))
+    sqrt_eig = scale * (4 * math.pi ** 2 * k2 + tau2) ** (-alpha / 2)
+    shape = (batch, channels, *k2.shape)
+    noise = torch.complex(torch.randn(shape, generator=gen, device=device),
+                          torch.randn(shape, generator=gen, device=device)) / math.sqrt(2.0)
+    u = torch.fft.irfftn(noise * sqrt_eig, s=list(grid), dim=list(range(2, 2 + d)), norm="forward")
+    if kind == "darcy":
+        u = torch.where(u >= 0, torch.full_like(u, 12.0), torch.full_like(u, 3.0))
+    return u.to(torch.float32).contiguous()
+
+
+def build_model(cfg_name, device, precision="fp32"):
     import neuraloperator_b200 as nb
+    desc, cls, modes, hidden, cin, cout, grid, batch, kw, field = MODELS[cfg_name]
+    if precision == "bf16":
+        kw = dict(kw, contraction_precision="bf16")
+    torch.manual_seed(0)  # random-init weights of the architecture (reference initialisers)
+    model = getattr(nb, cls)(n_modes=modes, in_channels=cin, out_channels=cout, hidden_channels=hidden,
+                             n_layers=4, **kw)
+    return model.to(device).eval()
+
+
+def oracle_params(model):
+    """The model's parameters in the oracle's layout (CPU tensors): fno_forward(x, params, cfg)."""
+    lin = lambda fcs: [(fc.weight.detach().cpu(), fc.bias.detach().cpu()) for fc in fcs]  # noqa: E731
+    fb = model.fno_blocks
+    blocks = []
+    kind = "dense"
+    for i in range(fb.n_layers):
+        w = fb.convs[i].weight
+        if hasattr(w, "core"):
+            kind = "tucker"
+            wp = {"core": w.core.detach().cpu(), "factors": [f.detach().cpu() for f in w.factors]}
+        else:
+            wp = w.tensor.detach().cpu()
+        blocks.append({"weight": wp, "bias": fb.convs[i].bias.detach().cpu(),
+                       "fno_skip": fb.fno_skips[i].conv.weight.detach().cpu(), "mlp": lin(fb.channel_mlp[i].fcs),
+                       "mlp_skip": fb.channel_mlp_skips[i].weight.detach().cpu()})
+    params = {"lifting": lin(model.lifting.fcs), "projection": lin(model.projection.fcs), "blocks": blocks}
+    return params, {"n_modes": tuple(model.n_modes), "weight_kind": kind}
+
+
+def chain_bytes(kind, batch, p, hidden, cin, cout):
+    """Compulsory HBM bytes of one chain launch: its inputs and outputs, each touched once."""
+    act = batch * hidden * p * 4
+    return {"lifting": batch * cin * p * 4 + act, "block": 3 * act,
+            "last_block_projection": 2 * act + batch * cout * p * 4, "last_block": 3 * act,
+            "projection": act + batch * cout * p * 4}[kind]
+
+
+class _Marks:
+    """CUDA events recorded on the current stream between the launches of one instrumented forward."""
+
+    def __init__(self):
+        self.names, self.events = [], []
+        self.mark("start")
+
+    def mark(self, name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.names.append(name)
+        self.events.append(e)
+
+    def spans(self):
+        return [(self.names[i + 1], self.events[i].elapsed_time(self.events[i + 1]))
+                for i in range(len(self.events) - 1)]
+
+
+def instrumented_forward(model, x, spectral=None, grid_offset=None, grid_sizes=None):
+    """The fused forward of FNO.fused_forward launch by launch, with CUDA events between the launches
+    (and the library's per-kernel events inside each spectral layer).  Returns (y, [(kernel, ms)],
+    [(layer, spectral kernel ms list)])."""
+    from neuraloperator_b200 import _lib, pointwise
+    plan = model.fused_plan(x, grid_sizes)
+    if plan is None:
+        raise SystemExit("the model does not take the fused path at this size")
+    grid, fuse_proj = plan
+    marks = _Marks()
+    f1, f2 = model.lifting.fcs
+    h = pointwise.chain(x, f1.weight, f1.bias, f2.weight, f2.bias, grid=grid, grid_offset=grid_offset)
+    marks.mark("chain_lifting")
+    spec = []
+    blocks = model.fno_blocks
+    last = model.n_layers - 1
+    for i in range(model.n_layers):
+        conv = blocks.convs[i]
+        if spectral is None:
+            nk = None
+            geo = conv.geometry(list(h.shape[2:]))
+            from neuraloperator_b200 import ops
+            kind, _, ranks = conv.kernel_operands(geo)
+            pl = ops.get_plan(ops.make_desc(geo, h.shape[0], conv.in_channels, conv.out_channels, weight_kind=kind,
+                                            ranks=ranks, precision=conv.contraction_precision, engine=conv.engine),
+                              h.device.index)
+            nk = pl.launches_per_forward
+            ev = _lib.LaunchEvents(nk)
+            with ev:
+                s = conv(h)
+            spec.append(ev)
+        else:
+            s = spectral(i, conv, h)
+        marks.mark(f"spectral_{i}")
+        mlp, sg = blocks._mlp_parts(i)
+        kw = {}
+        proj = model.projection if (i == last and fuse_proj) else None
+        if proj is not None:
+            p1, p2 = proj.fcs
+            kw = dict(w3=p1.weight, b3=p1.bias, w4=p2.weight, b4=p2.bias)
+        h = pointwise.chain(h, mlp.fcs[0].weight, mlp.fcs[0].bias, mlp.fcs[1].weight, mlp.fcs[1].bias, s=s,
+                            w0=blocks.fno_skips[i].conv.weight, act_skip=i != last, act_out=i != last,
+                            gate_w=sg.weight if sg is not None else None, gate_b=sg.bias if sg is not None else None,
+                            **kw)
+        marks.mark(("chain_last_block_projection" if proj is not None else "chain_last_block") if i == last
+                   else "chain_block")
+    if not fuse_proj:
+        p1, p2 = model.projection.fcs
+        h = pointwise.chain(h, p1.weight, p1.bias, p2.weight, p2.bias)
+        marks.mark("chain_projection")
+    torch.cuda.synchronize()
+    return h, marks.spans(), [e.durations_ms() for e in spec]
+
+
+def run_model(args, world, rank, local):
+    """FNO / TFNO forward (grid embedding + lifting, 4 FNO blocks, projection) at the configuration's full
+    size.  N = 1: the whole batch on one GPU.  N > 1: the 3D configuration is slab-decomposed along x
+    (strong scaling: the global batch of 8 is fixed), the 1D / 2D ones shard the batch (weak scaling)."""
+    import neuraloperator_b200 as nb  # noqa: F401
+    from neuraloperator_b200 import _lib
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if args.config not in MODELS:
         raise SystemExit(f"--model fno: no full-model config named {args.config} (have {sorted(MODELS)})")
-    desc, cls, modes, hidden, cin, cout, grid, batch, kw = MODELS[args.config]
+    desc, cls, modes, hidden, cin, cout, grid, batch, kw, field = MODELS[args.config]
     if args.batch is not None:
         batch = args.batch
-    if args.precision == "bf16":
-        kw = dict(kw, contraction_precision="bf16")
-    torch.manual_seed(0)
-    model = getattr(nb, cls)(n_modes=modes, in_channels=cin, out_channels=cout, hidden_channels=hidden,
-                             n_layers=4, **kw).to(dev).eval()
-    g = torch.Generator(device="cpu").manual_seed(0)
-    x = torch.randn((batch, cin, *grid), generator=g).to(dev)
+    slab = world > 1 and len(grid) == 3
+    model = build_model(args.config, dev, args.precision)
+    gbatch = batch if slab else batch * world
+    nx = grid[0] // world if slab else grid[0]
+    if slab and grid[0] % world:
+        raise SystemExit(f"the slab decomposition needs {grid[0]} x planes to divide by {world} ranks")
+    # the synthetic input: every rank draws the same global field (slab) or its own samples (batch shards)
+    if slab:
+        x_full = grf(batch, cin, grid, field, seed=1, device=dev)
+        x = x_full[:, :, rank * nx:(rank + 1) * nx].contiguous()
+        del x_full
+    else:
+        x = grf(batch, cin, grid, field, seed=1 + rank, device=dev)
+    runner = None
+    if slab:
+        from neuraloperator_b200.distributed import SlabFNO
+        runner = SlabFNO(model)
+        fwd = lambda inp: runner(inp)  # noqa: E731
+    else:
+        fwd = lambda inp: model(inp)  # noqa: E731
     stream = torch.cuda.current_stream(dev)
     steps, warm = args.steps, args.warmup
     with torch.no_grad():
+        if not slab and model.fused_plan(x) is None:
+            raise SystemExit("the model does not take the fused path at this size")
         for _ in range(warm):
-            y = model(x)
+            y = fwd(x)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            y = model(x)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms_eager = max_over_ranks(e0.elapsed_time(e1) / steps, world)
         graph, launch = None, "eager"
-        if not args.no_graph and ms_eager < 5.0:
-            graph, launch = capture_graph(lambda: model(x), stream)
+        if not slab and not args.no_graph:
+            barrier(world)
+            e0.record(stream)
+            y = fwd(x)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if e0.elapsed_time(e1) < 5.0:  # launch-bound sizes: replay one captured forward
+                graph, launch = capture_graph(lambda: fwd(x), stream)
         barrier(world)
         torch.cuda.synchronize()
         with ClockSampler(local) as clocks:
@@ -260,48 +417,144 @@ def run_model(args, world, rank, local):
                 if graph is not None:
                     graph.replay()
                 else:
-                    y = model(x)
+                    y = fwd(x)
             e1.record(stream)
             torch.cuda.synchronize()
         barrier(world)
         ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
         del graph
-        # the spectral layers alone (same shapes as inside the blocks; the fused skip + GELU included)
-        conv = model.fno_blocks.convs[0]
-        h = torch.randn((batch, hidden, *grid), generator=g).to(dev)
-        skip = torch.randn((batch, hidden, *grid), generator=g).to(dev)
-        for _ in range(3):
-            conv(h, addend=skip, apply_gelu=True)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(steps):
-            conv(h, addend=skip, apply_gelu=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        spec_ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+        # ---- one instrumented forward: every launch timed with CUDA events on the launching stream ----
+        exch = None
+        if slab:
+            exch = runner.instrument(True)
+            barrier(world)
+            y_i, spans, spec_k = instrumented_forward(model, x, spectral=runner.spectral, grid_offset=runner.offset(x),
+                                                      grid_sizes=runner.grid_sizes(x))
+            exch_ms = [a.elapsed_time(b) for a, b in runner.instrument(False)]
+        else:
+            y_i, spans, spec_k = instrumented_forward(model, x)
+            exch_ms = []
+        same = bool(torch.equal(y_i, y))
+        del y_i
+
+        # ---- end to end through the public API: pinned host input, pinned host output ----
+        ms_e2e, e2e_how, h2d, d2h = float("nan"), None, 0, 0
+        if not args.no_e2e:
+            x_host = x.cpu().pin_memory()
+            y_host = torch.empty(tuple(y.shape), dtype=torch.float32).pin_memory()
+            chunk = 1
+            host_call = (lambda: runner.forward_host(x_host, out=y_host, chunk=chunk, synchronize=False)) if slab else \
+                (lambda: model.forward_host(x_host, out=y_host, chunk=chunk, n_streams=2, synchronize=False))
+            host_call()
+            torch.cuda.synchronize()
+            ok_e2e = bool(torch.equal(y_host, y.cpu()))
+            e2e_steps = max(1, min(steps, 5))
+            barrier(world)
+            torch.cuda.synchronize()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
+            for _ in range(e2e_steps):
+                host_call()
+            f1.record(stream)
+            torch.cuda.synchronize()
+            barrier(world)
+            ms_e2e = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+            h2d, d2h = x_host.numel() * 4, y_host.numel() * 4
+            e2e_how = (f"{'SlabFNO' if slab else cls}.forward_host: {batch // chunk} chunks of {chunk} sample(s) on 2 "
+                       f"streams, pinned host buffers; output equal to the device forward: {ok_e2e}")
+
+        # ---- slab: rank 0 checks its planes against a single-GPU forward of the whole input ----
+        check = None
+        if slab and args.slab_check:
+            barrier(world)
+            if rank == 0:
+                x_full = grf(batch, cin, grid, field, seed=1, device=dev)
+                y_full = model(x_full)
+                ref = y_full[:, :, :nx]
+                check = float((y - ref).double().norm() / ref.double().norm())
+                del x_full, y_full, ref
+            barrier(world)
     if rank != 0:
         return
     hbm, peak_src = peaks()
-    p = math.prod(grid)
-    w = sum(t.numel() * t.element_size() for t in conv.weight.parameters())
-    spec_bytes = 3 * batch * hidden * p * 4 + w + hidden * 4  # x, skip, y + weights + bias
-    layers = model.n_layers
+    p = math.prod(grid) // (world if slab else 1)
+    nk = len(spec_k[0]) if spec_k else 0
+    kernels = {}
+
+    def add(name, ms_, by):
+        k = kernels.setdefault(name, {"name": name, "launches": 0, "ms_total": 0.0, "bytes_alg_per_launch": by})
+        k["launches"] += 1
+        k["ms_total"] += ms_
+
+    first_conv = model.fno_blocks.convs[0]
+    for name, t in spans:
+        if name.startswith("chain_"):
+            kind = name[len("chain_"):]
+            add(name, t, chain_bytes(kind, batch, p, hidden, cin, cout))
+        elif not slab:
+            pass  # split below from the library's per-kernel events
+        else:
+            add("spectral_slab_layer", t, None)
+    if not slab:
+        cfg_l = (desc, batch, hidden, hidden, grid, modes, kw.get("factorization"))
+        names = kernel_names_for(first_conv, cfg_l)
+        for per in spec_k:
+            for n_, t in zip(names, per):
+                add(n_, t, kernel_bytes(n_, cfg_l, first_conv))
+    klist = []
+    for k in kernels.values():
+        k["ms"] = k["ms_total"] / k["launches"]
+        by = k["bytes_alg_per_launch"]
+        k["gbs"] = by / (k["ms"] / 1e3) / 1e9 if by else None
+        k["frac"] = k["gbs"] / hbm if by else None
+        k["share"] = k["ms_total"] / sum(v["ms_total"] for v in kernels.values())
+        klist.append(k)
+    dom = max((k for k in klist if k["bytes_alg_per_launch"]), key=lambda k: k["ms_total"])
+    total_alg = sum(k["bytes_alg_per_launch"] * k["launches"] for k in klist if k["bytes_alg_per_launch"])
+    launches = sum(k["launches"] for k in klist if not k["name"].startswith("spectral_slab"))
+    if slab:  # the slab layers' own kernels (their all-to-alls are NCCL's)
+        launches += sum(sl.launches(x) for sl in runner.slabs)
     line = {
-        "metric": METRIC, "value": world * batch / (ms / 1e3), "unit": "samples/s", "n_gpus": world,
-        "steps": steps, "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": gbatch / (ms / 1e3), "unit": "samples/s", "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if slab else "weak",
         "vs_baseline": None, "dtype": "f32" if args.precision == "fp32" else "f32 (bf16 contraction)",
-        "data": "synthetic (seeded N(0,1) input, seeded random-init weights; no dataset)",
-        "config": {"workload": desc, "model": cls, "global_batch": batch * world, "per_gpu_batch": batch,
-                   "grid": list(grid), "hidden_channels": hidden, "n_modes": list(modes), "n_layers": layers,
-                   "in_channels": cin, "out_channels": cout, "parallelism": f"dp{world}" if world > 1 else "single",
-                   "launch": launch, "ms_per_step_eager": ms_eager, **{k: v for k, v in kw.items()}},
-        "spectral": {"ms_per_layer": spec_ms, "share": layers * spec_ms / ms,
-                     "roofline": {"bound": "hbm", "achieved": spec_bytes / (spec_ms / 1e3) / 1e9, "peak": hbm,
-                                  "unit": "GB/s", "frac": spec_bytes / (spec_ms / 1e3) / 1e9 / hbm,
-                                  "bytes_alg_per_layer": spec_bytes, "peak_source": peak_src,
-                                  "definition": "|x| + |skip| + |y| + |W| + |bias| per fused layer"}},
+        "data": "synthetic: seeded periodic Gaussian random fields with the configuration's covariance; "
+                "seeded random-init weights (no dataset)",
+        "config": {"workload": f"{desc}_forward", "model": cls, "global_batch": gbatch,
+                   "per_gpu_batch": batch, "grid": list(grid), "hidden_channels": hidden, "n_modes": list(modes),
+                   "n_layers": model.n_layers, "in_channels": cin, "out_channels": cout,
+                   "parallelism": (f"slab{world}" if slab else f"dp{world}") if world > 1 else "single",
+                   "x_planes_per_gpu": nx if slab else None, "launch": launch,
+                   "l2": f"activations {batch * hidden * p * 4 / 1e9:.2f} GB > 126 MB L2 (no flush needed)",
+                   **{k: v for k, v in kw.items()}},
+        "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm, "unit": "GB/s", "frac": dom["frac"],
+                     "traffic": TRAFFIC.get((args.config, dom["name"])), "kernel": dom["name"],
+                     "bytes_alg_per_launch": dom["bytes_alg_per_launch"], "ms_per_launch": dom["ms"],
+                     "peak_source": peak_src + " (copy bandwidth, burst)"},
+        "model_roofline": {"bound": "hbm", "achieved": total_alg / (sum(k["ms_total"] for k in klist) / 1e3) / 1e9,
+                           "peak": hbm, "unit": "GB/s",
+                           "frac": total_alg / (sum(k["ms_total"] for k in klist) / 1e3) / 1e9 / hbm,
+                           "bytes_alg_per_forward": total_alg,
+                           "definition": "sum over the forward's launches of their compulsory bytes (inputs and "
+                                         "outputs once each) over the instrumented forward's time"},
+        "kernels": klist,
+        "instrumented_forward_matches_timed": same,
+        "e2e": ({"value": gbatch / (ms_e2e / 1e3), "unit": "samples/s", "h2d_bytes_per_step": h2d,
+                 "d2h_bytes_per_step": d2h, "path": e2e_how} if not args.no_e2e else None),
+        "gpu_launches": launches * steps,
         "clocks": clocks.summary(),
     }
+    if slab:
+        lay = runner.slabs[0].layout(x, rank=0, world=world)
+        counts = [lay.block_count(r) for r in range(world)]
+        line["slab"] = {"exchange_ms_per_layer": [exch_ms[2 * i:2 * i + 2] for i in range(len(exch_ms) // 2)],
+                        "exchange_bytes_per_gpu_per_layer": int(sum(lay.send1_split()) + sum(lay.send2_split())),
+                        "block_count_per_rank": counts,
+                        "block_imbalance": max(counts) / (sum(counts) / len(counts)),
+                        "rel_l2_rank0_vs_single_gpu": check}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_model(args.config, model)
     print(json.dumps(line), flush=True)
 
 
@@ -389,14 +642,11 @@ def cpu_baseline(cfg, seconds=12.0):
             "sample": f"{sample_b} of {batch} samples per forward, {n} forwards, torch {torch.__version__} CPU"}
 
 
-def run_reference(args, cfg, world, rank):
-    if rank != 0:
-        return
+def run_reference_layer(args, cfg, threads):
+    """Reference arm of the single-layer workload: the oracle's SpectralConv forward on a sub-batch."""
     steps, warm = args.steps, args.warmup
     import oracle
     desc, batch, ci, co, grid, modes, fact = cfg
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
     sample_b = max(1, min(batch, 4 if math.prod(grid) <= 512 * 512 else 1))
     conv, x = make_inputs((desc, sample_b, ci, co, grid, modes, fact), "cpu", seed=1)
     if fact:
@@ -423,6 +673,109 @@ def run_reference(args, cfg, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def _oracle_stages(model, cfg, x):
+    """The oracle's FNO forward (oracle.fno_forward: fno.py:342-408) cut into four stages of similar cost:
+    [grid embedding + lifting + block 0], [block 1], [block 2], [block 3 + projection].  Returns a list of
+    callables h -> h."""
+    import oracle
+    params, ocfg = oracle_params(model)
+    n = len(params["blocks"])
+
+    def stage(first, last):
+        def run(h):
+            if first == 0:
+                h = oracle.grid_embedding(h)
+                h = oracle.channel_mlp(h, params["lifting"])
+            for i in range(first, last):
+                h = oracle.fno_block(h, params["blocks"][i], i, n, ocfg)
+            if last == n:
+                h = oracle.channel_mlp(h, params["projection"])
+            return h
+        return run
+
+    bounds = [(0, 1), (1, 2), (2, 3), (3, n)] if n == 4 else [(0, n)]
+    return [stage(a, b) for a, b in bounds]
+
+
+def cpu_baseline_model(cfg_name, model, seconds=None):
+    """The oracle (the reference's FNO forward restated on the CPU with torch) on every host core, on one
+    sample of the configuration (1 sample is the bounded sample; its time is per sample)."""
+    desc, cls, modes, hidden, cin, cout, grid, batch, kw, field = MODELS[cfg_name]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x = grf(1, cin, grid, field, seed=1, device="cpu")
+    stages = _oracle_stages(model, None, x)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        h = x
+        for st in stages:
+            h = st(h)
+        dt = time.perf_counter() - t0
+    return {"value": 1.0 / dt, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"1 of {batch} samples, one full forward ({dt:.1f} s), torch {torch.__version__} CPU, "
+                      f"{threads} threads"}
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the reference's own CPU path for the forward (the oracle restates it; the
+    reference package cannot be imported here -- tensorly / tensorly-torch / opt-einsum are absent) on all
+    host threads, on rank 0 only.  FNO: each step runs one of the forward's four stages on one sample
+    (lifting + block 0, block 1, block 2, block 3 + projection, in turn) so a step stays a few seconds;
+    samples/s = 1 / (sum over the stages of their mean step time).  Layer: each step is one SpectralConv
+    forward on a bounded sub-batch."""
+    if rank != 0:
+        return
+    steps, warm = args.steps, args.warmup
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    if args.model == "layer":
+        run_reference_layer(args, CONFIGS[args.config] if args.batch is None else
+                            (CONFIGS[args.config][0], args.batch) + tuple(CONFIGS[args.config][2:]), threads)
+        return
+    desc, cls, modes, hidden, cin, cout, grid, batch, kw, field = MODELS[args.config]
+    model = build_model(args.config, "cpu", args.precision)
+    x = grf(1, cin, grid, field, seed=1, device="cpu")
+    stages = _oracle_stages(model, None, x)
+    ns = len(stages)
+    inputs = [x] + [None] * (ns - 1)
+    times = [[] for _ in range(ns)]
+    budget_s = args.reference_seconds
+    t_start = time.perf_counter()
+    done = 0
+    with torch.no_grad():
+        # warm-up steps run the stages in order, which also produces every stage's input
+        for k in range(max(warm, ns)):
+            j = k % ns
+            h = stages[j](inputs[j])
+            if j + 1 < ns and inputs[j + 1] is None:
+                inputs[j + 1] = h
+        for k in range(steps):
+            j = k % ns
+            t0 = time.perf_counter()
+            stages[j](inputs[j])
+            times[j].append(time.perf_counter() - t0)
+            done += 1
+            if time.perf_counter() - t_start > budget_s and all(times):
+                break
+    per_sample = sum(statistics.mean(t) for t in times if t) * ns / sum(1 for t in times if t)
+    value = 1.0 / per_sample
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
+            "steps": done, "warmup": max(warm, ns), "ms_per_step": per_sample / ns * 1e3, "higher_is_better": True,
+            "scaling": "strong" if (args.gpus > 1 and len(grid) == 3) else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (the same seeded random field and seeded random-init weights)",
+            "config": {"workload": f"{desc}_forward", "model": cls, "global_batch": batch, "sample_batch": 1,
+                       "grid": list(grid), "hidden_channels": hidden, "n_modes": list(modes), "parallelism": "cpu",
+                       "stage_ms": [statistics.mean(t) * 1e3 if t else None for t in times],
+                       "steps_requested": steps, **{k: v for k, v in kw.items()}},
+            "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
+                             "sample": f"1 of {batch} samples; each step one quarter of the forward (lifting + "
+                                       f"block 0, block 1, block 2, block 3 + projection in turn); {done} timed "
+                                       f"steps within a {budget_s:.0f} s budget (oracle = reference torch CPU "
+                                       f"path, torch {torch.__version__})"},
+            "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def kernel_names(plan, cfg):
     """Names of the kernels one forward launches, in launch order (fused engine layouts)."""
     fact = cfg[6]
@@ -435,6 +788,18 @@ def kernel_names(plan, cfg):
     if nd == 1:
         return ["row_fwd"] + mix + ["row_inv"]
     return ["plane_fwd"] + mix + ["plane_inv"]
+
+
+def kernel_names_for(conv, cfg):
+    """kernel_names for the plan a SpectralConv uses on the layer configuration ``cfg``."""
+    from neuraloperator_b200 import ops
+    desc, batch, ci, co, grid, modes, fact = cfg
+    geo = conv.geometry(list(grid))
+    kind, _, ranks = conv.kernel_operands(geo)
+    plan = ops.get_plan(ops.make_desc(geo, batch, ci, co, weight_kind=kind, ranks=ranks,
+                                      precision=conv.contraction_precision, engine=conv.engine),
+                        torch.cuda.current_device())
+    return kernel_names(plan, cfg)
 
 
 def kernel_bytes(name, cfg, conv):
@@ -765,40 +1130,49 @@ def run_train(args, cfg, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--model", choices=["fno", "layer"], default="fno",
+                    help="fno: the whole FNO / TFNO forward (the headline); layer: one SpectralConv")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default=None,
+                    help="default c5 (FNO 3D, the largest single-GPU configuration) for --model fno, c2 for layer")
     ap.add_argument("--engine", choices=["auto", "fast", "generic"], default="auto")
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--reference-seconds", type=float, default=240.0,
+                    help="time budget of the reference arm's timed steps (the FNO stages take seconds each)")
+    ap.add_argument("--no-slab-check", dest="slab_check", action="store_false",
+                    help="skip rank 0's comparison of its slab with a single-GPU forward")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of graph replay")
-    ap.add_argument("--model", choices=["layer", "fno"], default="layer",
-                    help="layer: one SpectralConv (the headline); fno: the whole FNO / TFNO forward")
     ap.add_argument("--precision", choices=["fp32", "bf16"], default="fp32", help="contraction precision")
     ap.add_argument("--parallel", choices=["batch", "slab"], default="batch",
-                    help="batch: each rank its own slice of the batch (weak); slab: 3D x-axis split (strong)")
+                    help="--model layer only: batch (each rank its own batch, weak) or slab (3D x split, strong)")
     ap.add_argument("--pass", dest="pass_", choices=["forward", "train"], default="forward",
-                    help="forward: the headline forward; train: forward + backward of one layer")
+                    help="--model layer only: forward, or train (forward + backward of one layer)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
-    if args.batch is not None:
-        cfg = (cfg[0], args.batch) + tuple(cfg[2:])
+    if args.config is None:
+        args.config = "c5" if args.model == "fno" else "c2"
+    if args.model == "fno" and args.config == "c2":
+        raise SystemExit("c2 is the single-SpectralConv microbench: use --model layer")
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
-        run_reference(args, cfg, world, rank)
+        run_reference(args, world, rank)
         return
+    cfg = CONFIGS[args.config]
+    if args.batch is not None:
+        cfg = (cfg[0], args.batch) + tuple(cfg[2:])
     world, rank, local = dist_setup()
     try:
-        if args.pass_ == "train":
-            run_train(args, cfg, world, rank, local)
-        elif args.model == "fno":
+        if args.model == "fno":
             run_model(args, world, rank, local)
+        elif args.pass_ == "train":
+            run_train(args, cfg, world, rank, local)
         elif args.parallel == "slab":
             run_slab(args, cfg, world, rank, local)
         else:

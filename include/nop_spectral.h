@@ -225,39 +225,65 @@ int32_t nop_spectral_forward_static(const nop_spectral_desc* desc, const void* x
                                     int32_t n_weights, const float* bias, const float* addend,
                                     int32_t apply_gelu, void* y, void* stream);
 
-/* ---- fused per-pixel channel MLP (the FNO layers around the spectral block) -------------------
- * One pass over HBM evaluates, at every spatial point of x [B, Cx, *spatial] (float32):
- *     u = [x ; grid]                    grid: `grid_dims` coordinate channels lo + i (hi - lo) / N
- *     h = act_hidden(W1 u + b1)         W1 [Ch, Cx + grid_dims] (Ch = 0: no first layer, h = u)
- *     y = act_out(W2 h + b2 + g r + gb) W2 [Cy, Ch or Cx + grid_dims]; g, gb [Cy] gate r [B, Cy, *spatial]
- *     z = W3 y                          W3 [Cz, Cy] (next_channels > 0)
- * with act = exact GELU where set.  Weights as torch Conv1d weights ([out, in, 1], row-major).
- * Replaces ChannelMLP.forward (neuralop/layers/channel_mlp.py:82-119), the soft-gating skip
- * (neuralop/layers/skip_connections.py:53-94), the closing activation of
- * FNOBlocks.forward_with_postactivation (neuralop/layers/fno_block.py:363-381), the next block's
- * linear skip (skip_connections.py:96-127) and, for the lifting, GridEmbeddingND
- * (neuralop/layers/embeddings.py:147-164).  Points per sample must be a multiple of 128 and every
- * channel count at most 256; x, r, y, z 16-byte aligned. */
-typedef struct nop_pointwise_desc {
+/* ---- per-pixel layer chain on the tensor cores (the FNO layers around each spectral block) ----
+ * One pass over HBM evaluates, at every spatial point of x [B, Cx, *spatial] (float32, contiguous):
+ *     u = skip_channels ? act_skip(W0 x + s) : [x ; grid]   s [B, skip_channels, *spatial]: the block's
+ *                                                          spectral output (bias included)
+ *     h = GELU(W1 u + b1)
+ *     y = act_out(W2 h + b2 + g * x + gb)                   g, gb [out_channels]: soft-gating of x (gate)
+ *     p = GELU(W3 y + b3),  out = W4 p + b4                 when proj_hidden > 0
+ * and writes y [B, out_channels, *spatial] (proj_hidden == 0) or out [B, proj_out, *spatial] to `y`.
+ * GELU is the exact (erf) one.  Grid channels (lifting, skip_channels == 0 only): axis j's coordinate
+ * grid_lo[j] + (i_j + grid_offset[j]) * grid_step[j] for index i_j of this call's points (grid_offset:
+ * the first index of a slab of a larger grid).  Weights are torch Conv1d weights [out, in(, 1)]
+ * row-major; b1, b2, gb, b3, b4 may be NULL (zero).  Every GEMM runs on tcgen05 (tf32, three-pass
+ * split: float32 accuracy).
+ * Replaces, in one kernel: FNOBlocks.forward_with_postactivation after the spectral convolution
+ * (neuralop/layers/fno_block.py:339-381: the linear skip (skip_connections.py:96-127) added to the
+ * SpectralConv output, GELU, ChannelMLP (neuralop/layers/channel_mlp.py:82-119), the soft-gating skip
+ * (skip_connections.py:53-94), GELU), the lifting ChannelMLP with GridEmbeddingND
+ * (neuralop/models/fno.py:387-396, neuralop/layers/embeddings.py:147-164) and the projection
+ * ChannelMLP (fno.py:404-406), fused into the last block when proj_hidden > 0.
+ * Limits: channel counts <= 256, points per sample a multiple of 4, x and s 16-byte aligned. */
+typedef struct nop_chain_desc {
     int32_t abi_version;                 /* NOP_ABI_VERSION                                          */
     int32_t ndim;                        /* spatial dims, 1..NOP_MAX_DIMS                             */
     int64_t batch;
-    int64_t spatial[NOP_MAX_DIMS];
-    int32_t in_channels;                 /* Cx                                                       */
-    int32_t grid_dims;                   /* 0 or ndim                                                */
-    int32_t hidden_channels;             /* Ch (0: single layer)                                     */
-    int32_t out_channels;                /* Cy                                                       */
-    int32_t next_channels;               /* Cz (0: no z)                                             */
-    int32_t act_hidden, act_out;         /* 1: exact GELU                                            */
-    int32_t gate, has_b1, has_b2, has_gate_bias;
-    float grid_lo[NOP_MAX_DIMS], grid_hi[NOP_MAX_DIMS];
-} nop_pointwise_desc;
+    int64_t spatial[NOP_MAX_DIMS];       /* sizes of this call's x                                   */
+    int32_t x_channels;                  /* Cx                                                       */
+    int32_t grid_dims;                   /* 0 or ndim (only with skip_channels == 0)                 */
+    float grid_lo[NOP_MAX_DIMS], grid_step[NOP_MAX_DIMS];
+    int64_t grid_offset[NOP_MAX_DIMS];
+    int32_t skip_channels;               /* rows of W0 = channels of s (0: no skip stage)            */
+    int32_t act_skip;                    /* 1: GELU after the skip add                               */
+    int32_t hidden_channels;             /* rows of W1 (> 0)                                         */
+    int32_t out_channels;                /* rows of W2                                               */
+    int32_t act_out;                     /* 1: GELU on y                                             */
+    int32_t gate;                        /* 1: add g * x (+ gb); needs x_channels == out_channels    */
+    int32_t proj_hidden;                 /* rows of W3 (0: no projection)                            */
+    int32_t proj_out;                    /* rows of W4                                               */
+} nop_chain_desc;
 
-/* Shared memory one CTA of the fused kernel uses for this descriptor (NOP_E_UNSUPPORTED if too much). */
-int32_t nop_pointwise_smem_bytes(const nop_pointwise_desc* desc, size_t* bytes);
-int32_t nop_pointwise_forward(const nop_pointwise_desc* desc, const float* x, const float* w1, const float* b1,
-                              const float* w2, const float* b2, const float* r, const float* g,
-                              const float* gb, const float* w3, float* y, float* z, void* stream);
+typedef struct nop_chain_operands {
+    const float* x;
+    const float* s;
+    const float* w0;
+    const float* w1;
+    const float* b1;
+    const float* w2;
+    const float* b2;
+    const float* g;
+    const float* gb;
+    const float* w3;
+    const float* b3;
+    const float* w4;
+    const float* b4;
+    float* y;
+} nop_chain_operands;
+
+/* NOP_OK when the kernel takes this descriptor; *groups (nullable) = tiles in flight per CTA. */
+int32_t nop_chain_query(const nop_chain_desc* desc, int32_t* groups);
+int32_t nop_chain_forward(const nop_chain_desc* desc, const nop_chain_operands* operands, void* stream);
 
 /* ---- forward from host memory, copies overlapped with the kernels ---------------------------
  * The reference's SpectralConv.forward runs wherever its input lives; a serving caller that holds

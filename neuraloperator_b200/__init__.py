@@ -11,4 +11,4 @@ from .fno_block import FNOBlocks  # noqa: F401
 from .fno_staged import FNOStaged  # noqa: F401
 from .layers import ChannelMLP, GridEmbeddingND, SoftGating, skip_connection  # noqa: F401
 from .spectral_convolution import BaseSpectralConv, SpectralConv  # noqa: F401
-from .utils import TimingProfiler, count_model_params, profiling  # noqa: F401
+from .utils import count_model_params  # noqa: F401

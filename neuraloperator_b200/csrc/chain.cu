@@ -1,0 +1,778 @@
+// Per-pixel layer chain of the FNO on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// At every spatial point of x [B, Cx, P] (P = points per sample; s [B, Cs, P] when the skip stage is on):
+//
+//   u = Cs ? act_skip(W0 x + s) : [x ; grid]        the block's linear skip added to the spectral output
+//   h = GELU(W1 u + b1)                              ChannelMLP, first layer
+//   y = act_out(W2 h + b2 + g * x + gb)              second layer + soft-gating skip of x (gate)
+//   p = GELU(W3 y + b3),  out = W4 p + b4            the projection ChannelMLP (when proj_hidden > 0)
+//
+// One FNO block after its spectral convolution is a single pass over HBM: read x and s, write y.  The
+// last block also evaluates the projection, and the lifting is the chain without the skip stage.
+//
+// Each layer is a GEMM per tile of 128 points:  D[p][n] = sum_k A[p][k] W[n][k]  (M = 128 points,
+// N = output channels padded to 16, K = input channels).  The A operand (activations, one row per
+// point) lives in TENSOR MEMORY, written by the thread that owns the point with tcgen05.st (lane p =
+// point p, column k = channel k): every epilogue writes the next layer's operand in place, so no
+// activation ever passes through shared memory in the MMA's layout.  W (K-major hi / lo images in the
+// canonical no-swizzle layout) sits in shared memory for the whole kernel.  fp32 accuracy from tf32
+// MMAs by the three-pass split: each operand value v = hi + lo (hi = tf32(v), lo = tf32(v - hi)) and
+// D = A_hi W_hi + A_hi W_lo + A_lo W_hi in fp32 (the dropped lo * lo term is below 2^-22 relative).
+//
+// Work split: a CTA (one per SM, persistent) holds up to four independent groups of 128 threads; group
+// g walks its own tiles and issues its own MMAs (one elected thread), so the epilogue arithmetic of one
+// group runs while the MMAs and loads of the others are in flight.  Per tile a group:
+//   1. waits for its x tile (TMA box {128 points, Cx channels} -> stash [c][p]) and writes A = x
+//      (+ grid coordinates) and, for the gate, the raw x into tensor memory; the stash is free: the
+//      next tile's x load is issued;
+//   2. skip stage: MMA, wait; u = act(acc + s) -> A (the s stash is free: the next tile's s load);
+//   3. fc1 / fc2: MMA(s), wait; h = GELU(acc + b1) -> A; MMA, wait.  A wide hidden layer runs in chunks
+//      of NC channels: chunk c's fc2 MMA and chunk c + 1's fc1 MMA are issued together;
+//   4. y = act(acc + b2 + g x + gb): stored (coalesced: a warp writes 32 consecutive points of a
+//      channel), or written as A of the projection, which repeats step 3 and stores its output.
+// Tensor memory per group: the raw-x region (gate), the chunk regions, A (hi | lo) and the accumulator;
+// the host planner picks the group count and chunk widths that fit 512 columns and 227 KB of shared
+// memory.  Every wait is bounded: on expiry the kernel records NOP_DEVICE_MMA_TIMEOUT in the status
+// word, every group leaves its loop at the next group barrier, issued MMAs and loads are drained
+// (bounded) and the tensor memory is freed.
+#include <cuda.h>
+
+#include <cstring>
+#include <string>
+
+#include "l2_hints.cuh"
+#include "mix_tc.cuh"
+
+namespace nop {
+namespace chain {
+
+constexpr int TP = 128;          // points per tile (MMA M)
+constexpr int GT = 128;          // threads per group: one per point / tensor-memory lane
+constexpr int MAX_GROUPS = 4;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_LIMIT = 227 * 1024;
+
+__host__ __device__ inline int up8(int v) { return (v + 7) & ~7; }
+__host__ __device__ inline int up16(int v) { return (v + 15) & ~15; }
+__host__ __device__ inline int up1k(int v) { return (v + 1023) & ~1023; }
+
+struct Params {
+    int64_t P, tiles, tps;          // points per sample, tiles, tiles per sample
+    int Cx, Cs, nd, Ch, Cy, Cp, Co; // real channel counts (Co: rows of W4)
+    int act0, act2, gate;
+    int64_t sp[NOP_MAX_DIMS];       // spatial sizes of this call (row-major point index)
+    int64_t goff[NOP_MAX_DIMS];     // index offset of the first point per axis (slabs)
+    float glo[NOP_MAX_DIMS], gstep[NOP_MAX_DIMS];
+    const float *w0, *w1, *b1, *w2, *b2, *g, *gb, *w3, *b3, *w4, *b4;
+    float* y;
+};
+
+struct Layout {
+    int Kx;                          // A columns written from x (+ grid channels)
+    int RX;                          // raw-x columns (gate) or 0
+    int N0, K1, N1, N2, N3, N4;      // padded GEMM sizes (0: stage absent)
+    int NC1, NC3;                    // chunk widths (== N1 / N3 when the layer runs whole)
+    int KA;                          // columns of each half (hi, lo) of the A region
+    int cX, cC1, cH1, cC3, cH3, cA, cD, cols;  // tensor-memory columns relative to the group's base
+    int groups;
+    int o_w0, o_w1, o_w2, o_w3, o_w4;          // weight images (hi, then lo), shared-memory bytes
+    int o_vec;                                 // b1 [N1], b2 + gb [N2], g [N2], b3 [N3], b4 [N4]
+    int o_stash, stash_bytes;                  // per group: x stash (Cx rows), then s stash (Cs rows)
+    int o_bar;
+    int smem;
+};
+
+__host__ __device__ inline uint32_t idesc_tf32(int N) {
+    // D f32, A and B tf32, both K-major, N >> 3, M >> 4
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TP >> 4) << 24);
+}
+
+// byte offset of element (row n, column k) of an N-row K-major operand image (core matrices of 8 rows x
+// 16 bytes; K halves of a 32-byte K step 128 B apart, 8-row groups 256 B apart, K steps N * 32 B apart)
+__host__ __device__ inline uint32_t kmaj_off(int n, int k, int N) {
+    return (k >> 3) * (N * 32) + (n >> 3) * 256 + ((k >> 2) & 1) * 128 + (n & 7) * 16 + (k & 3) * 4;
+}
+
+// ------------------------------------------------------------------------------------------------
+// device helpers
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(GT) : "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// wait for this thread's tensor-memory loads; the registers are operands so no use moves above it
+__device__ __forceinline__ void tmem_wait_ld(float (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
+                   "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]),
+                   "+f"(v[15])
+                 :
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
+// hi / lo split of 16 values written to two column groups (the A operand's halves)
+__device__ __forceinline__ void st_split16(uint32_t t_hi, uint32_t t_lo, const float (&v)[16]) {
+    uint32_t h[16], l[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float hv = tc::tf32_round(v[j]);
+        h[j] = __float_as_uint(hv);
+        l[j] = __float_as_uint(tc::tf32_round(v[j] - hv));
+    }
+    tmem_st16(t_hi, h);
+    tmem_st16(t_lo, l);
+}
+
+// D (tensor memory) += A (tensor memory) * B (shared-memory descriptor), tf32
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        :
+        : "r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
+// One layer (or one chunk of one) as three-pass tf32 MMAs: A columns a .. a + K (hi) and a + lo_off ..
+// (lo) of the group's tensor memory; W rows row0 .. row0 + N of an Nfull-row image whose K steps start
+// at ks0; D columns d .. d + N.  `acc` = 0 clears D first.
+__device__ __forceinline__ void layer_mma(uint32_t tb, int a, int lo_off, int K, uint32_t w_hi, uint32_t w_lo,
+                                          int Nfull, int row0, int ks0, int d, int N, bool acc) {
+    const uint32_t idesc = idesc_tf32(N);
+    for (int ks = 0; ks < K / 8; ++ks) {
+        const uint32_t boff = (uint32_t)((ks0 + ks) * Nfull * 32 + (row0 >> 3) * 256);
+        const uint64_t bh = tc::smem_desc(w_hi + boff), bl = tc::smem_desc(w_lo + boff);
+        const uint32_t ta = tb + (uint32_t)(a + 8 * ks);
+        const uint32_t td = tb + (uint32_t)d;
+        mma_ts(td, ta, bh, idesc, (acc || ks > 0) ? 1u : 0u);
+        mma_ts(td, ta, bl, idesc, 1u);
+        mma_ts(td, ta + (uint32_t)lo_off, bh, idesc, 1u);
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+                                            uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(tc::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(tc::smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// K-major hi / lo images of W [rows x cols] (row-major, out x in) padded with zeros to N x K
+__device__ void load_weight(char* sm, int off, const float* w, int rows, int cols, int N, int K) {
+    if (N == 0) return;
+    float* hi = reinterpret_cast<float*>(sm + off);
+    float* lo = reinterpret_cast<float*>(sm + off + 4 * N * K);
+    for (int e = threadIdx.x; e < N * K; e += blockDim.x) {
+        const int n = e / K, k = e % K;
+        const float v = (n < rows && k < cols) ? __ldg(w + (int64_t)n * cols + k) : 0.f;
+        const float h = tc::tf32_round(v);
+        const uint32_t o = kmaj_off(n, k, N) / 4;
+        hi[o] = h;
+        lo[o] = tc::tf32_round(v - h);
+    }
+}
+
+__device__ __forceinline__ float vec_or0(const float* v, int i, int n) { return (v && i < n) ? __ldg(v + i) : 0.f; }
+
+// ------------------------------------------------------------------------------------------------
+// the kernel
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(MAX_GROUPS * GT, 1)
+k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tms, Params p, Layout L,
+        int* __restrict__ status) {
+    extern __shared__ __align__(1024) char sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int grp = warp >> 2;                 // group
+    const int quad = warp & 3;                 // tensor-memory lane quadrant of this warp
+    const int pt = quad * 32 + lane;           // this thread's point in the tile (= its lane)
+    const bool leader = (tid & (GT - 1)) == 0;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.o_bar);
+    uint64_t* mbar = bars + 3 * grp;           // MMA completion of this group
+    uint64_t* xfull = mbar + 1;                // x stash landed
+    uint64_t* sfull = mbar + 2;                // s stash landed
+    uint64_t* drain = bars + 3 * L.groups;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* gflag = abort_flag + 1 + grp;  // this group gives up (read after a group barrier)
+
+    if (tid == 0) {
+        for (int i = 0; i < 3 * L.groups; ++i) tc::mbar_init(&bars[i], 1);
+        tc::mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *abort_flag = 0;
+        for (int i = 0; i < MAX_GROUPS; ++i) abort_flag[1 + i] = 0;
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // weights and vectors, once per CTA
+    const int K1r = p.Cs ? p.Cs : p.Cx + p.nd;
+    load_weight(sm, L.o_w0, p.w0, p.Cs, p.Cx, L.N0, L.Kx);
+    load_weight(sm, L.o_w1, p.w1, p.Ch, K1r, L.N1, L.K1);
+    load_weight(sm, L.o_w2, p.w2, p.Cy, p.Ch, L.N2, L.N1);
+    load_weight(sm, L.o_w3, p.w3, p.Cp, p.Cy, L.N3, L.N2);
+    load_weight(sm, L.o_w4, p.w4, p.Co, p.Cp, L.N4, L.N3);
+    float* vb1 = reinterpret_cast<float*>(sm + L.o_vec);
+    float* vb2 = vb1 + L.N1;
+    float* vg = vb2 + L.N2;
+    float* vb3 = vg + L.N2;
+    float* vb4 = vb3 + L.N3;
+    for (int c = tid; c < L.N1; c += blockDim.x) vb1[c] = vec_or0(p.b1, c, p.Ch);
+    for (int c = tid; c < L.N2; c += blockDim.x) {
+        vb2[c] = vec_or0(p.b2, c, p.Cy) + (p.gate ? vec_or0(p.gb, c, p.Cy) : 0.f);
+        vg[c] = p.gate ? vec_or0(p.g, c, p.Cy) : 0.f;
+    }
+    for (int c = tid; c < L.N3; c += blockDim.x) vb3[c] = vec_or0(p.b3, c, p.Cp);
+    for (int c = tid; c < L.N4; c += blockDim.x) vb4[c] = vec_or0(p.b4, c, p.Co);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // weight images -> tensor-core reads
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+
+    const uint32_t tb = *tmem_slot + (uint32_t)(grp * L.cols);   // this group's columns, lane 0
+    const uint32_t tl = tb + ((uint32_t)(quad * 32) << 16);      // this warp's lane quadrant
+    const uint32_t s_w0 = tc::smem_u32(sm + L.o_w0), s_w1 = tc::smem_u32(sm + L.o_w1);
+    const uint32_t s_w2 = tc::smem_u32(sm + L.o_w2), s_w3 = tc::smem_u32(sm + L.o_w3);
+    const uint32_t s_w4 = tc::smem_u32(sm + L.o_w4);
+    const uint32_t lo0 = 4u * L.N0 * L.Kx, lo1 = 4u * L.N1 * L.K1, lo2 = 4u * L.N2 * L.N1;
+    const uint32_t lo3 = 4u * L.N3 * L.N2, lo4 = 4u * L.N4 * L.N3;
+    const float* xst = reinterpret_cast<const float*>(sm + L.o_stash + grp * L.stash_bytes);
+    const float* sst = xst + up1k(p.Cx * TP * 4) / 4;  // 1 KB aligned (tensor-copy destination)
+    const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 > 0 && L.NC3 < L.N3;
+    const int nch1 = L.N1 / L.NC1, nch3 = L.N3 ? L.N3 / L.NC3 : 0;
+    const uint32_t xbytes = (uint32_t)p.Cx * TP * 4, sbytes = (uint32_t)p.Cs * TP * 4;
+    const uint64_t pol = l2::evict_first();
+    const int bar_id = 1 + grp;
+
+    auto give_up = [&]() {
+        *gflag = 1;
+        *abort_flag = 1;
+        atomicExch(status, tc::kStatusMmaTimeout);
+    };
+    // bounded wait of every thread; a thread whose wait expires flags the group (seen after the next
+    // group barrier, where all threads of the group leave together)
+    auto wait_bar = [&](uint64_t* b, uint32_t ph) {
+        if (!tc::mbar_wait(b, ph, abort_flag)) give_up();
+    };
+    const int64_t stride = (int64_t)gridDim.x * L.groups;
+    int64_t t = (int64_t)blockIdx.x * L.groups + grp;
+    auto issue_x = [&](int64_t tt) {
+        const int64_t b = tt / p.tps;
+        expect_tx(xfull, xbytes);
+        tma_load_2d(const_cast<float*>(xst), &tmx, (int)((tt % p.tps) * TP), (int)(b * p.Cx), xfull, pol);
+    };
+    auto issue_s = [&](int64_t tt) {
+        const int64_t b = tt / p.tps;
+        expect_tx(sfull, sbytes);
+        tma_load_2d(const_cast<float*>(sst), &tms, (int)((tt % p.tps) * TP), (int)(b * p.Cs), sfull, pol);
+    };
+    int x_pending = 0, s_pending = 0;  // loads issued and not yet waited for (leader's count)
+    if (leader && t < p.tiles) {
+        issue_x(t);
+        ++x_pending;
+        if (p.Cs) {
+            issue_s(t);
+            ++s_pending;
+        }
+    }
+    uint32_t mph = 0, xph = 0, sph = 0;
+    bool stop = false;
+    // group barrier; false when the group has given up (every thread of the group sees the same flag)
+    auto barrier_ok = [&]() -> bool {
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        group_bar(bar_id);
+        if (*gflag) {
+            stop = true;
+            return false;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        return true;
+    };
+    auto commit_wait = [&]() {
+        if (leader) tc::mma_commit(mbar);
+        wait_bar(mbar, mph);
+        mph ^= 1;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    };
+
+    for (; t < p.tiles && !stop; t += stride) {
+        const int64_t b = t / p.tps;
+        const int64_t pnt = (t % p.tps) * TP + pt;
+        const bool valid = pnt < p.P;
+        const int64_t nt = t + stride;
+
+        // ---- 1. x tile -> A (hi | lo) [+ grid coordinates], raw x for the gate ----
+        wait_bar(xfull, xph);
+        xph ^= 1;
+        if (leader) --x_pending;
+        float crd[NOP_MAX_DIMS] = {0.f, 0.f, 0.f, 0.f};
+        if (p.nd) {
+            int64_t idx = pnt;
+#pragma unroll
+            for (int a = NOP_MAX_DIMS - 1; a >= 0; --a) {
+                if (a < p.nd) {
+                    const int64_t ia = idx % p.sp[a];
+                    idx /= p.sp[a];
+                    crd[a] = p.glo[a] + (float)(ia + p.goff[a]) * p.gstep[a];
+                }
+            }
+        }
+        const int kw = L.Kx > L.RX ? L.Kx : L.RX;
+        for (int c0 = 0; c0 < kw; c0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = c0 + j;
+                float val = 0.f;
+                if (c < p.Cx) {
+                    val = xst[c * TP + pt];
+                } else {
+                    const int a = c - p.Cx;
+                    if (a < p.nd) val = a == 0 ? crd[0] : a == 1 ? crd[1] : a == 2 ? crd[2] : crd[3];
+                }
+                v[j] = val;
+            }
+            if (c0 < L.Kx) {
+                uint32_t h[8], l[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float hv = tc::tf32_round(v[j]);
+                    h[j] = __float_as_uint(hv);
+                    l[j] = __float_as_uint(tc::tf32_round(v[j] - hv));
+                }
+                tmem_st8(tl + L.cA + c0, h);
+                tmem_st8(tl + L.cA + L.KA + c0, l);
+            }
+            if (c0 < L.RX) {
+                uint32_t r[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) r[j] = __float_as_uint(v[j]);
+                tmem_st8(tl + L.cX + c0, r);
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // stash reads before the next TMA write
+        if (!barrier_ok()) break;
+        if (leader) {
+            if (nt < p.tiles) {
+                issue_x(nt);
+                ++x_pending;
+            }
+            if (L.N0)
+                layer_mma(tb, L.cA, L.KA, L.Kx, s_w0, s_w0 + lo0, L.N0, 0, 0, L.cD, L.N0, false);
+            else
+                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false);
+        }
+        commit_wait();
+
+        // ---- 2. skip stage: u = act(W0 x + s) -> A ----
+        if (L.N0) {
+            wait_bar(sfull, sph);
+            sph ^= 1;
+            if (leader) --s_pending;
+            for (int c0 = 0; c0 < L.N0; c0 += 16) {
+                float v[16];
+                tmem_ld16(tl + L.cD + c0, v);
+                tmem_wait_ld(v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int c = c0 + j;
+                    float u = v[j];
+                    if (c < p.Cs) u += sst[c * TP + pt];
+                    v[j] = p.act0 ? gelu_erf(u) : u;
+                }
+                st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (!barrier_ok()) break;
+            if (leader) {
+                if (nt < p.tiles) {
+                    issue_s(nt);
+                    ++s_pending;
+                }
+                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false);
+            }
+            commit_wait();
+        }
+
+        // ---- 3. fc1 (chunks) -> GELU -> fc2 ----
+        bool broke = false;
+        for (int c = 0; c < nch1; ++c) {
+            const int src = ch1 ? L.cC1 : L.cD;
+            const int dst = ch1 ? L.cH1 : L.cA;
+            const int dlo = ch1 ? L.NC1 : L.KA;
+            for (int c0 = 0; c0 < L.NC1; c0 += 16) {
+                float v[16];
+                tmem_ld16(tl + src + c0, v);
+                tmem_wait_ld(v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j] + vb1[c * L.NC1 + c0 + j]);
+                st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
+            }
+            if (!barrier_ok()) {
+                broke = true;
+                break;
+            }
+            if (leader) {
+                layer_mma(tb, dst, dlo, L.NC1, s_w2, s_w2 + lo2, L.N2, 0, c * L.NC1 / 8, L.cD, L.N2, c > 0);
+                if (c + 1 < nch1)
+                    layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, (c + 1) * L.NC1, 0, L.cC1, L.NC1, false);
+            }
+            commit_wait();
+        }
+        if (broke) break;
+
+        // ---- 4. y = act(fc2 + b2 + g x + gb): store, or A of the projection ----
+        const int64_t ybase = b * (L.N3 ? p.Co : p.Cy) * p.P + pnt;
+        for (int c0 = 0; c0 < L.N2; c0 += 16) {
+            float v[16], xr[16];
+            tmem_ld16(tl + L.cD + c0, v);
+            if (p.gate) tmem_ld16(tl + L.cX + c0, xr);
+            tmem_wait_ld(v);
+            if (p.gate) tmem_wait_ld(xr);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int c = c0 + j;
+                float o = v[j] + vb2[c];
+                if (p.gate) o = fmaf(vg[c], xr[j], o);
+                v[j] = p.act2 ? gelu_erf(o) : o;
+            }
+            if (L.N3) {
+                st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
+            } else if (valid) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < p.Cy) __stcs(p.y + ybase + (int64_t)(c0 + j) * p.P, v[j]);
+            }
+        }
+        if (!L.N3) continue;
+
+        // ---- 5. projection: p = GELU(W3 y + b3) (chunks), out = W4 p + b4 ----
+        if (!barrier_ok()) break;
+        if (leader) layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, 0, 0, ch3 ? L.cC3 : L.cD, L.NC3, false);
+        commit_wait();
+        for (int c = 0; c < nch3; ++c) {
+            const int src = ch3 ? L.cC3 : L.cD;
+            const int dst = ch3 ? L.cH3 : L.cA;
+            const int dlo = ch3 ? L.NC3 : L.KA;
+            for (int c0 = 0; c0 < L.NC3; c0 += 16) {
+                float v[16];
+                tmem_ld16(tl + src + c0, v);
+                tmem_wait_ld(v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j] + vb3[c * L.NC3 + c0 + j]);
+                st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
+            }
+            if (!barrier_ok()) {
+                broke = true;
+                break;
+            }
+            if (leader) {
+                layer_mma(tb, dst, dlo, L.NC3, s_w4, s_w4 + lo4, L.N4, 0, c * L.NC3 / 8, L.cD, L.N4, c > 0);
+                if (c + 1 < nch3)
+                    layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, (c + 1) * L.NC3, 0, L.cC3, L.NC3, false);
+            }
+            commit_wait();
+        }
+        if (broke) break;
+        for (int c0 = 0; c0 < L.N4; c0 += 16) {
+            float v[16];
+            tmem_ld16(tl + L.cD + c0, v);
+            tmem_wait_ld(v);
+            if (valid) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < p.Co) __stcs(p.y + ybase + (int64_t)(c0 + j) * p.P, v[j] + vb4[c0 + j]);
+            }
+        }
+    }
+
+    // drain: loads still in flight land, and after an expired wait the issued MMAs finish, before the
+    // shared and tensor memory are released (all bounded)
+    if (leader) {
+        for (; x_pending > 0; --x_pending, xph ^= 1)
+            if (!tc::mbar_wait(xfull, xph, nullptr)) atomicExch(status, tc::kStatusMmaTimeout);
+        for (; s_pending > 0; --s_pending, sph ^= 1)
+            if (!tc::mbar_wait(sfull, sph, nullptr)) atomicExch(status, tc::kStatusMmaTimeout);
+    }
+    if (leader && *gflag) {  // a wait expired: let the issued MMAs finish before the memory is freed
+        tc::mma_commit(mbar);
+        tc::mbar_wait(mbar, mph, nullptr);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot), "r"(TMEM_COLS) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------------
+// host planner
+// ------------------------------------------------------------------------------------------------
+struct Sizes {
+    int Cx, Cs, nd, Ch, Cy, Cp, Co, gate;
+};
+
+bool layout_for(const Sizes& z, int groups, int nc1, int nc3, Layout* out) {
+    Layout L{};
+    L.groups = groups;
+    L.Kx = up8(z.Cx + (z.Cs ? 0 : z.nd));
+    L.RX = z.gate ? up16(z.Cx) : 0;
+    L.N0 = z.Cs ? up16(z.Cs) : 0;
+    L.K1 = z.Cs ? L.N0 : L.Kx;
+    L.N1 = up16(z.Ch);
+    L.N2 = up16(z.Cy);
+    L.N3 = z.Cp ? up16(z.Cp) : 0;
+    L.N4 = z.Cp ? up16(z.Co) : 0;
+    L.NC1 = nc1;
+    L.NC3 = L.N3 ? nc3 : 0;
+    const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 && L.NC3 < L.N3;
+    int ka = L.Kx;
+    auto mx = [](int& a, int b) { a = b > a ? b : a; };
+    mx(ka, L.N0);
+    if (!ch1) mx(ka, L.N1);
+    if (L.N3) mx(ka, L.N2);
+    if (L.N3 && !ch3) mx(ka, L.N3);
+    L.KA = up8(ka);
+    int nd = L.N0;
+    mx(nd, L.N2);
+    mx(nd, L.N4);
+    if (!ch1) mx(nd, L.N1);
+    if (L.N3 && !ch3) mx(nd, L.N3);
+    // temporary region: raw x (live until the gate) next to fc1's chunk regions; the projection's chunk
+    // regions reuse it once the gate is done
+    const int t1 = L.RX + (ch1 ? 3 * L.NC1 : 0);
+    const int t3 = ch3 ? 3 * L.NC3 : 0;
+    const int tw = up16(t1 > t3 ? t1 : t3);
+    L.cX = 0;
+    L.cC1 = L.RX;
+    L.cH1 = L.RX + L.NC1;
+    L.cC3 = 0;
+    L.cH3 = L.NC3;
+    L.cA = tw;
+    L.cD = L.cA + 2 * L.KA;
+    L.cols = up16(L.cD + nd);
+    if (L.cols * groups > TMEM_COLS) return false;
+    int off = 0;
+    auto take = [&](int bytes) {
+        const int at = off;
+        off += up1k(bytes);
+        return at;
+    };
+    L.o_w0 = take(8 * L.N0 * L.Kx);
+    L.o_w1 = take(8 * L.N1 * L.K1);
+    L.o_w2 = take(8 * L.N2 * L.N1);
+    L.o_w3 = take(8 * L.N3 * L.N2);
+    L.o_w4 = take(8 * L.N4 * L.N3);
+    L.o_vec = take(4 * (L.N1 + 2 * L.N2 + L.N3 + L.N4));
+    L.stash_bytes = up1k(z.Cx * TP * 4) + up1k(z.Cs * TP * 4);
+    L.o_stash = off;
+    off += groups * L.stash_bytes;
+    L.o_bar = off;
+    off += 8 * (3 * groups + 1) + 8 + 4 * (1 + MAX_GROUPS);
+    L.smem = off;
+    if (L.smem > SMEM_LIMIT) return false;
+    // more than half an SM's shared memory: one CTA per SM, so a second CTA never waits in
+    // tcgen05.alloc for the first one's tensor memory
+    if (L.smem < 120 * 1024) L.smem = 120 * 1024;
+    *out = L;
+    return true;
+}
+
+// the layout with the most groups, then the widest chunks (fewest MMA round trips)
+bool plan_layout(const Sizes& z, Layout* out) {
+    const int N1 = up16(z.Ch), N3 = z.Cp ? up16(z.Cp) : 16;
+    int opts1[4], n1 = 0, opts3[4], n3 = 0;
+    for (int c : {N1, 64, 32, 16})
+        if (c == N1 || (c < N1 && N1 % c == 0)) opts1[n1++] = c;
+    for (int c : {N3, 64, 32, 16})
+        if (c == N3 || (c < N3 && N3 % c == 0)) opts3[n3++] = c;
+    for (int groups = MAX_GROUPS; groups >= 1; --groups)
+        for (int i = 0; i < n1; ++i)
+            for (int j = 0; j < (z.Cp ? n3 : 1); ++j)
+                if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, out)) return true;
+    return false;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// rows [B * C] of P floats, box {128 points, C channels}
+bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t P, int C) {
+    const EncodeTiled enc = reinterpret_cast<EncodeTiled>(tensor_map_encoder());
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)P, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)P * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)TP, (cuuint32_t)C};
+    const cuuint32_t ones[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int32_t check_desc(const nop_chain_desc* d, Sizes* z, int64_t* P) {
+    if (!d) return fail(NOP_E_INVALID, "descriptor is NULL");
+    if (d->abi_version != NOP_ABI_VERSION) return fail(NOP_E_INVALID, "ABI version mismatch");
+    if (d->ndim < 1 || d->ndim > NOP_MAX_DIMS) return fail(NOP_E_INVALID, "ndim must be in 1..4");
+    if (d->batch < 0) return fail(NOP_E_INVALID, "batch must be >= 0");
+    if (d->grid_dims != 0 && d->grid_dims != d->ndim) return fail(NOP_E_INVALID, "grid_dims must be 0 or ndim");
+    if (d->x_channels < 1 || d->hidden_channels < 1 || d->out_channels < 1)
+        return fail(NOP_E_INVALID, "x_channels, hidden_channels and out_channels must be positive");
+    if (d->skip_channels < 0 || d->proj_hidden < 0 || (d->proj_hidden > 0 && d->proj_out < 1))
+        return fail(NOP_E_INVALID, "skip_channels / proj_hidden must be >= 0 and proj_out >= 1 with a projection");
+    if (d->skip_channels && d->grid_dims)
+        return fail(NOP_E_INVALID, "grid channels are appended only without the skip stage");
+    if (d->gate && d->x_channels != d->out_channels)
+        return fail(NOP_E_INVALID, "the soft-gating skip needs x_channels == out_channels");
+    const int mx = 256;
+    if (d->x_channels + d->grid_dims > mx || d->skip_channels > mx || d->hidden_channels > mx ||
+        d->out_channels > mx || d->proj_hidden > mx || d->proj_out > mx)
+        return fail(NOP_E_UNSUPPORTED, "channel counts above 256 are not supported");
+    int64_t n = 1;
+    for (int j = 0; j < d->ndim; ++j) {
+        if (d->spatial[j] < 1) return fail(NOP_E_INVALID, "spatial sizes must be >= 1");
+        n *= d->spatial[j];
+    }
+    if (n % 4) return fail(NOP_E_UNSUPPORTED, "points per sample must be a multiple of 4 (16-byte rows)");
+    if (n > 0x7fffff80LL) return fail(NOP_E_UNSUPPORTED, "more than 2^31 points per sample");
+    if (d->batch * (d->x_channels > d->skip_channels ? d->x_channels : d->skip_channels) > 0x7fffffffLL)
+        return fail(NOP_E_UNSUPPORTED, "batch x channels exceeds 2^31 rows");
+    *P = n;
+    z->Cx = d->x_channels;
+    z->Cs = d->skip_channels;
+    z->nd = d->grid_dims;
+    z->Ch = d->hidden_channels;
+    z->Cy = d->out_channels;
+    z->Cp = d->proj_hidden;
+    z->Co = d->proj_hidden ? d->proj_out : 0;
+    z->gate = d->gate ? 1 : 0;
+    return NOP_OK;
+}
+
+}  // namespace chain
+}  // namespace nop
+
+using namespace nop;
+
+extern "C" {
+
+int32_t nop_chain_query(const nop_chain_desc* d, int32_t* groups) {
+    chain::Sizes z;
+    int64_t P = 0;
+    int32_t rc = chain::check_desc(d, &z, &P);
+    if (rc != NOP_OK) return rc;
+    chain::Layout L;
+    if (!chain::plan_layout(z, &L))
+        return fail(NOP_E_UNSUPPORTED, "weights and tiles exceed the tensor or shared memory of a CTA");
+    if (groups) *groups = L.groups;
+    return NOP_OK;
+}
+
+int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, void* stream) {
+    chain::Sizes z;
+    int64_t P = 0;
+    int32_t rc = chain::check_desc(d, &z, &P);
+    if (rc != NOP_OK) return rc;
+    if (!o) return fail(NOP_E_INVALID, "operands are NULL");
+    chain::Layout L;
+    if (!chain::plan_layout(z, &L))
+        return fail(NOP_E_UNSUPPORTED, "weights and tiles exceed the tensor or shared memory of a CTA");
+    if (d->batch == 0) return NOP_OK;
+    if (!o->x || !o->w1 || !o->w2 || !o->y) return fail(NOP_E_INVALID, "x, w1, w2 and y must be non-NULL");
+    if (z.Cs && (!o->s || !o->w0)) return fail(NOP_E_INVALID, "s and w0 are needed with skip_channels > 0");
+    if (z.gate && !o->g) return fail(NOP_E_INVALID, "g is needed when gate is set");
+    if (z.Cp && (!o->w3 || !o->w4)) return fail(NOP_E_INVALID, "w3 and w4 are needed with proj_hidden > 0");
+    if ((uintptr_t)o->x % 16 || (o->s && (uintptr_t)o->s % 16))
+        return fail(NOP_E_ALIGNMENT, "x and s must be 16-byte aligned (tensor copies)");
+    if ((uintptr_t)o->y % 4) return fail(NOP_E_ALIGNMENT, "y must be 4-byte aligned");
+    chain::Params p{};
+    p.P = P;
+    p.tps = ceil_div(P, chain::TP);
+    p.tiles = d->batch * p.tps;
+    p.Cx = z.Cx;
+    p.Cs = z.Cs;
+    p.nd = z.nd;
+    p.Ch = z.Ch;
+    p.Cy = z.Cy;
+    p.Cp = z.Cp;
+    p.Co = z.Co;
+    p.act0 = d->act_skip ? 1 : 0;
+    p.act2 = d->act_out ? 1 : 0;
+    p.gate = z.gate;
+    for (int j = 0; j < NOP_MAX_DIMS; ++j) {
+        p.sp[j] = j < d->ndim ? d->spatial[j] : 1;
+        p.goff[j] = j < d->ndim ? d->grid_offset[j] : 0;
+        p.glo[j] = d->grid_lo[j];
+        p.gstep[j] = d->grid_step[j];
+    }
+    p.w0 = o->w0;
+    p.w1 = o->w1;
+    p.b1 = o->b1;
+    p.w2 = o->w2;
+    p.b2 = o->b2;
+    p.g = o->g;
+    p.gb = o->gb;
+    p.w3 = o->w3;
+    p.b3 = o->b3;
+    p.w4 = o->w4;
+    p.b4 = o->b4;
+    p.y = o->y;
+    CUtensorMap tmx, tms;
+    if (!chain::make_map(&tmx, o->x, d->batch * z.Cx, P, z.Cx))
+        return fail(NOP_E_CUDA, "cuTensorMapEncodeTiled(x) failed");
+    if (z.Cs) {
+        if (!chain::make_map(&tms, o->s, d->batch * z.Cs, P, z.Cs))
+            return fail(NOP_E_CUDA, "cuTensorMapEncodeTiled(s) failed");
+    } else {
+        tms = tmx;  // unused
+    }
+    int dev = 0, sms = 148;
+    NOP_CUDA_TRY(cudaGetDevice(&dev));
+    NOP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    int* status = status_word(dev);
+    if (!status) return fail(NOP_E_CUDA, "status word of the tensor-core kernels is not available");
+    NOP_CUDA_TRY(cudaFuncSetAttribute(chain::k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem));
+    const int64_t ctas = ceil_div(p.tiles, L.groups);
+    const unsigned grid = (unsigned)(ctas < sms ? ctas : sms);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    chain::k_chain<<<grid, L.groups * chain::GT, L.smem, s>>>(tmx, tms, p, L, status);
+    NOP_CUDA_TRY(cudaGetLastError());
+    return NOP_OK;
+}
+
+}  // extern "C"

@@ -1070,6 +1070,8 @@ size_t fast_workspace_bytes(Plan& p, WorkspaceLayout* ws) {
 
 int* status_word(int device) { return device_status_ptr(device); }
 
+void* tensor_map_encoder() { return reinterpret_cast<void*>(encode_tiled()); }
+
 int32_t fast_device_status(int* status, bool clear) {
     int v = 0;
     cudaError_t err = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));

@@ -110,6 +110,8 @@ int32_t fast_launches(const Plan& p);
 int32_t fast_device_status(int* status, bool clear);
 // device address of that status word on `device` (kernels write it when a bounded wait expires)
 int* status_word(int device);
+// cuTensorMapEncodeTiled looked up through the runtime (nullptr when the driver lacks it)
+void* tensor_map_encoder();
 int32_t fast_pack(const Plan& p, const void* const* weights, char* packed, char* ws, cudaStream_t s);
 // adjoint plan's packed weights straight from the forward's dense weight (conjugate transpose in the pack)
 int32_t fast_pack_adjoint(const Plan& p, const void* W, char* packed, cudaStream_t s);

@@ -96,6 +96,7 @@ class SlabSpectralConv:
         self.conv = conv
         self.group = group
         self._plans = {}
+        self.exchange_events = None  # a list: (start, end) CUDA event pairs around each all-to-all
 
     def layout(self, x_slab: torch.Tensor, rank: Optional[int] = None, world: Optional[int] = None) -> SlabLayout:
         """Split of this rank (or of ``rank`` of ``world`` when given, without a process group)."""
@@ -174,15 +175,115 @@ class SlabSpectralConv:
         return y
 
     # -- one forward ------------------------------------------------------------------------------------
+    def _exchange(self, recv, send, out_splits, in_splits):
+        ev = self.exchange_events
+        if ev is not None:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        dist.all_to_all_single(recv, send, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                               group=self.group)
+        if ev is not None:
+            b.record()
+            ev.append((a, b))
+
     def __call__(self, x_slab: torch.Tensor, addend: Optional[torch.Tensor] = None, apply_gelu: bool = False):
         x_slab = x_slab.contiguous()
         lay = self.layout(x_slab)
         send1 = self.stage_planes_fwd(x_slab, lay)
         recv1 = torch.empty(sum(lay.recv1_split()), dtype=send1.dtype, device=send1.device)
-        dist.all_to_all_single(recv1, send1, output_split_sizes=lay.recv1_split(),
-                               input_split_sizes=lay.send1_split(), group=self.group)
+        self._exchange(recv1, send1, lay.recv1_split(), lay.send1_split())
         send2 = self.stage_modes(recv1, x_slab, lay)
         recv2 = torch.empty(sum(lay.recv2_split()), dtype=send2.dtype, device=send2.device)
-        dist.all_to_all_single(recv2, send2, output_split_sizes=lay.recv2_split(),
-                               input_split_sizes=lay.send2_split(), group=self.group)
+        self._exchange(recv2, send2, lay.recv2_split(), lay.send2_split())
         return self.stage_planes_inv(recv2, x_slab, lay, addend=addend, apply_gelu=apply_gelu)
+
+    def launches(self, x_slab: torch.Tensor) -> int:
+        """Kernel launches of this library per call (the two all-to-alls are NCCL's)."""
+        plan, _, _ = self._plan(x_slab, self.layout(x_slab))
+        return plan.launches_per_forward
+
+
+class SlabFNO:
+    """Forward of a 3D ``FNO`` / ``TFNO`` whose input is split along the first spatial axis.
+
+    ``SlabFNO(model, group)(x_slab)`` with ``x_slab`` = this rank's planes [B, Cin, Nx / world, Ny, Nz]
+    returns this rank's planes of the model output.  Weights are replicated.  The lifting, the per-pixel
+    part of every block and the projection are pointwise in space, so they run on the local planes (the
+    grid channels placed at the slab's global x offset); every spectral layer is a ``SlabSpectralConv``
+    (two NCCL all-to-alls of the kept modes).  The model must take the fused path
+    (``FNO.fused_plan``); other layer shapes raise NotImplementedError.
+    """
+
+    def __init__(self, model, group=None):
+        self.model = model
+        self.group = group
+        self.slabs = [SlabSpectralConv(conv, group) for conv in model.fno_blocks.convs]
+
+    def _rank_world(self):
+        return dist.get_rank(self.group), dist.get_world_size(self.group)
+
+    def grid_sizes(self, x_slab: torch.Tensor):
+        _, world = self._rank_world()
+        return (x_slab.shape[2] * world, *x_slab.shape[3:])
+
+    def offset(self, x_slab: torch.Tensor):
+        rank, _ = self._rank_world()
+        return (rank * x_slab.shape[2],) + (0,) * (x_slab.ndim - 3)
+
+    def spectral(self, index, conv, h):
+        return self.slabs[index](h)
+
+    def instrument(self, on: bool):
+        """Start (on=True) or stop recording CUDA events around every all-to-all; stopping returns the
+        (start, end) pairs in call order (two per layer)."""
+        if on:
+            for s in self.slabs:
+                s.exchange_events = []
+            return None
+        pairs = []
+        for s in self.slabs:
+            pairs += s.exchange_events or []
+            s.exchange_events = None
+        return pairs
+
+    def __call__(self, x_slab: torch.Tensor) -> torch.Tensor:
+        if x_slab.ndim != 5:
+            raise ValueError("SlabFNO takes 3D inputs [B, C, Nx / world, Ny, Nz]")
+        y = self.model.fused_forward(x_slab, spectral=self.spectral, grid_offset=self.offset(x_slab),
+                                     grid_sizes=self.grid_sizes(x_slab))
+        if y is None:
+            raise NotImplementedError("the slab-decomposed FNO needs the fused layer shapes (FNO.fused_plan)")
+        return y
+
+    @torch.no_grad()
+    def forward_host(self, x_slab: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: int = 1,
+                     n_streams: int = 2, synchronize: bool = True) -> torch.Tensor:
+        """``__call__`` on this rank's planes held in HOST memory, cut into chunks of ``chunk`` samples whose
+        copies in and out overlap the other chunks' kernels (every rank must make the same calls: the chunks'
+        all-to-alls pair up in order)."""
+        if x_slab.is_cuda:
+            raise ValueError("forward_host takes a host tensor")
+        dev = next(self.model.parameters()).device
+        batch = x_slab.shape[0]
+        if chunk < 1 or batch % chunk:
+            raise ValueError(f"chunk {chunk} does not divide the batch {batch}")
+        y_shape = (batch, self.model.out_channels, *x_slab.shape[2:])
+        y = out if out is not None else torch.empty(y_shape, dtype=torch.float32, pin_memory=True)
+        if y.is_cuda or tuple(y.shape) != y_shape or not y.is_contiguous():
+            raise ValueError(f"out must be a contiguous host tensor of shape {y_shape}")
+        cur = torch.cuda.current_stream(dev)
+        if getattr(self, "_streams", None) is None or len(self._streams) != n_streams:
+            self._streams = [torch.cuda.Stream(dev) for _ in range(n_streams)]
+        for st in self._streams:
+            st.wait_stream(cur)
+        for k in range(batch // chunk):
+            st = self._streams[k % n_streams]
+            with torch.cuda.stream(st):
+                xd = x_slab[k * chunk:(k + 1) * chunk].to(dev, non_blocking=True)
+                yd = self(xd)
+                y[k * chunk:(k + 1) * chunk].copy_(yd, non_blocking=True)
+        for st in self._streams:
+            cur.wait_stream(st)
+        if synchronize:
+            cur.synchronize()
+        return y

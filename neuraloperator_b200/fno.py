@@ -2,25 +2,26 @@
 
 Same constructor arguments and forward: grid embedding -> lifting ChannelMLP -> n_layers x
 FNOBlocks -> projection ChannelMLP.  The spectral blocks run on libnop_b200's CUDA kernels; with
-the default layer shapes the grid embedding + lifting (which also emits the first block's linear
-skip) and the projection each run as one fused per-pixel kernel (``pointwise.channel_mlp``).
+the default layer shapes the grid embedding + lifting is one per-pixel tensor-core kernel
+(``pointwise.chain``), every block is its spectral convolution plus one such kernel, and the
+projection is fused into the last block's kernel.
 Options the reference offers outside the FNO default path raise NotImplementedError here:
 ``domain_padding``, ``norm``, ``complex_data`` and ``fno_block_precision`` other than "full".
 """
 
 from __future__ import annotations
 
-from typing import List, Tuple, Union
+from typing import List, Optional, Tuple, Union
 
 import torch
 import torch.nn.functional as F
 from torch import nn
 
-from . import pointwise
+from . import ops, pointwise
 from .fno_block import FNOBlocks
 from .layers import ChannelMLP, GridEmbeddingND
 from .spectral_convolution import SpectralConv
-from .utils import get_active_profiler, grad_needed, maybe_profile
+from .utils import grad_needed
 
 Number = Union[float, int]
 
@@ -102,63 +103,119 @@ class FNO(nn.Module):
                                      hidden_channels=self.projection_channels, n_layers=2, n_dim=self.n_dim,
                                      non_linearity=non_linearity)
 
-    def _mlp_ok(self, mlp, x, cin, cnext=0, grid=None):
-        """mlp (2 layers, GELU, no dropout) on cin data channels (+ grid channels) fits the fused kernel."""
-        ku = cin + (len(grid) if grid is not None else 0)
+    @staticmethod
+    def _mlp_ok(mlp) -> bool:
+        """A two-layer GELU ChannelMLP without dropout (the chain kernel's form)."""
         return (isinstance(mlp, ChannelMLP) and mlp.n_layers == 2 and mlp.dropout is None
-                and mlp.non_linearity is F.gelu and mlp.in_channels == ku
-                and pointwise.supported_dims(x.shape[0], x.shape[2:], cin, mlp.hidden_channels,
-                                             mlp.out_channels, cnext, grid))
+                and mlp.non_linearity is F.gelu)
 
-    def _fused_forward(self, x):
-        """Lifting (+ grid channels, + block 0's linear skip), fused blocks, projection; None when a
-        layer does not fit the fused kernels (the module path then runs)."""
+    def fused_plan(self, x, grid_sizes=None):
+        """(grid, fuse_projection) when the fused forward takes x, else None.  ``grid_sizes``: the full
+        grid's sizes when x is a slab of it (the coordinate step follows the full grid)."""
         pe = self.positional_embedding
-        if not (x.is_cuda and x.dtype == torch.float32) or (pe is not None and not isinstance(pe, GridEmbeddingND)):
+        if not (x.is_cuda and x.dtype == torch.float32 and x.ndim == 2 + self.n_dim) or grad_needed(x, self):
             return None
-        if grad_needed(x, self):
+        if (pe is not None and not isinstance(pe, GridEmbeddingND)) or self.resolution_scaling_factor is not None:
             return None
-        grid = [tuple(b) for b in pe.grid_boundaries] if pe is not None else None
+        if x.shape[1] != self.in_channels or not (self._mlp_ok(self.lifting) and self._mlp_ok(self.projection)):
+            return None
         blocks = self.fno_blocks
-        if not (blocks._fusable(0, x, None) and self.resolution_scaling_factor is None):
+        batch, spatial = x.shape[0], tuple(x.shape[2:])
+        grid = pointwise.grid_params(pe.grid_boundaries, grid_sizes or spatial) if pe is not None else None
+        f1, f2 = self.lifting.fcs
+        if self.lifting.in_channels != self.in_channels + (self.n_dim if pe is not None else 0):
             return None
-        cnext = blocks.fno_skips[0].conv.out_channels
-        if not (x.shape[1] == self.in_channels and self._mlp_ok(self.lifting, x, self.in_channels, cnext, grid)
-                and self._mlp_ok(self.projection, x, self.hidden_channels)):
+        if not pointwise.supported(batch, spatial, self.in_channels, f1.out_channels, f2.out_channels, grid=grid):
             return None
-        prof = get_active_profiler()
-        with maybe_profile(prof, "fno/positional_embedding_lifting_skip0", x.device):
-            fc1, fc2 = self.lifting.fcs
-            h, skip = pointwise.channel_mlp(x, fc1.weight, fc1.bias, fc2.weight, fc2.bias, grid=grid,
-                                            act_hidden=True, act_out=False, next_w=blocks.next_skip_weight(0))
-        blocks.set_pending_skip(h, 0, skip)
         for i in range(self.n_layers):
-            h = blocks(h, i)
-        with maybe_profile(prof, "fno/projection", x.device):
-            fc1, fc2 = self.projection.fcs
-            y, _ = pointwise.channel_mlp(h, fc1.weight, fc1.bias, fc2.weight, fc2.bias, act_hidden=True,
-                                         act_out=False)
-        return y
+            if not (blocks._fusable(i, x, None) and blocks.chain_supported(i, batch, spatial)):
+                return None
+        # the projection rides in the last block's kernel unless its weights would leave one tile in flight
+        fuse_proj = blocks.chain_supported(self.n_layers - 1, batch, spatial, proj=self.projection, min_groups=2)
+        if not fuse_proj:
+            p1, p2 = self.projection.fcs
+            if not pointwise.supported(batch, spatial, self.hidden_channels, p1.out_channels, p2.out_channels):
+                return None
+        return grid, fuse_proj
+
+    def fused_forward(self, x, spectral=None, grid_offset=None, grid_sizes=None):
+        """Grid embedding + lifting (one chain kernel), every block as spectral convolution + one chain
+        kernel, the projection fused into the last block's chain (or one more chain call); None when a
+        layer does not fit the fused kernels (the module path then runs).  ``spectral(index, conv, h)``
+        replaces the blocks' spectral calls and ``grid_offset`` / ``grid_sizes`` place x in a larger grid
+        (the slab-decomposed forward)."""
+        plan = self.fused_plan(x, grid_sizes)
+        if plan is None:
+            return None
+        grid, fuse_proj = plan
+        f1, f2 = self.lifting.fcs
+        h = pointwise.chain(x, f1.weight, f1.bias, f2.weight, f2.bias, grid=grid, grid_offset=grid_offset)
+        last = self.n_layers - 1
+        for i in range(self.n_layers):
+            h = self.fno_blocks.fused_block(h, i, spectral=spectral,
+                                            proj=self.projection if (i == last and fuse_proj) else None)
+        if not fuse_proj:
+            p1, p2 = self.projection.fcs
+            h = pointwise.chain(h, p1.weight, p1.bias, p2.weight, p2.bias)
+        return h
 
     def forward(self, x, output_shape=None, **kwargs):
         if output_shape is None:
-            fused = self._fused_forward(x)
+            fused = self.fused_forward(x)
             if fused is not None:
                 return fused
             output_shape = [None] * self.n_layers
         elif isinstance(output_shape, tuple):
             output_shape = [None] * (self.n_layers - 1) + [output_shape]
-        prof = get_active_profiler()
         if self.positional_embedding is not None:
-            with maybe_profile(prof, "fno/positional_embedding", x.device):
-                x = self.positional_embedding(x)
-        with maybe_profile(prof, "fno/lifting", x.device):
-            x = self.lifting(x)
+            x = self.positional_embedding(x)
+        x = self.lifting(x)
         for i in range(self.n_layers):
             x = self.fno_blocks(x, i, output_shape=output_shape[i])
-        with maybe_profile(prof, "fno/projection", x.device):
-            x = self.projection(x)
+        x = self.projection(x)
         return x
+
+    @torch.no_grad()
+    def forward_host(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: Optional[int] = None,
+                     n_streams: int = 2, synchronize: bool = True) -> torch.Tensor:
+        """``forward`` of a batch held in HOST memory: the batch is cut into chunks of ``chunk`` samples
+        and each chunk's host-to-device copy, forward and device-to-host copy run on one of ``n_streams``
+        streams, so the PCIe transfers of one chunk overlap the kernels of another.  ``x`` and ``out``
+        are CPU tensors (page-locked for the overlap; the returned tensor is page-locked when ``out`` is
+        None); the parameters stay on their CUDA device.  With ``synchronize=False`` the call returns once
+        the work is queued on the device's current stream.  Inference only."""
+        if x.is_cuda:
+            raise ValueError("forward_host takes a host tensor; call the module on device tensors")
+        dev = next(self.parameters()).device
+        if dev.type != "cuda":
+            raise RuntimeError("neuraloperator_b200 models run on CUDA devices only (there is no CPU path)")
+        batch = x.shape[0]
+        chunk = ops.default_chunk(batch) if chunk is None else int(chunk)
+        if chunk < 1 or batch % chunk:
+            raise ValueError(f"chunk {chunk} does not divide the batch {batch}")
+        y_shape = (batch, self.out_channels, *x.shape[2:])
+        y = out if out is not None else torch.empty(y_shape, dtype=torch.float32, pin_memory=True)
+        if y.is_cuda or tuple(y.shape) != y_shape or not y.is_contiguous():
+            raise ValueError(f"out must be a contiguous host tensor of shape {y_shape}")
+        cur = torch.cuda.current_stream(dev)
+        streams = self.__dict__.setdefault("_nop_host_streams", {})
+        key = (dev.index, int(n_streams))
+        if key not in streams:
+            streams[key] = [torch.cuda.Stream(dev) for _ in range(int(n_streams))]
+        side = streams[key]
+        for st in side:
+            st.wait_stream(cur)
+        for k in range(batch // chunk):
+            st = side[k % len(side)]
+            with torch.cuda.stream(st):
+                xd = x[k * chunk:(k + 1) * chunk].to(dev, non_blocking=True)
+                yd = self(xd)
+                y[k * chunk:(k + 1) * chunk].copy_(yd, non_blocking=True)
+        for st in side:
+            cur.wait_stream(st)
+        if synchronize:
+            cur.synchronize()
+        return y
 
     @property
     def n_modes(self):

@@ -1,17 +1,14 @@
 """FNOBlocks: drop-in for neuralop.layers.fno_block.FNOBlocks (neuralop/layers/fno_block.py:18-481).
 
-Same constructor, parameters and forward semantics.  When the block has the FNO default
-shape -- ``fno_skip="linear"``, real data, no norm, no stabilizer, GELU, post-activation,
-a ``SpectralConv`` of this package and no output resampling -- the skip add and the GELU
-(:356-361) run inside the spectral block's inverse-transform epilogue: the skip GEMM
-(a 1x1 conv) is computed first and handed to the kernel as an addend.  Every other
-configuration composes the same operations as the reference around the CUDA spectral block.
+Same constructor, parameters and forward semantics.  When a block has the FNO default shape --
+``fno_skip="linear"``, real data, no norm, no stabilizer, GELU, post-activation, a ``SpectralConv`` of
+this package, no output resampling, and the default ChannelMLP (two layers, GELU, no dropout) with a
+soft-gating (or no) channel-MLP skip -- it runs as two launch sequences: the spectral convolution
+(its own kernels, bias included), then ONE per-pixel tensor-core kernel (``pointwise.chain``) that adds
+the linear skip W_skip x to the spectral output, applies GELU, the ChannelMLP, the soft-gating skip of x
+and the closing GELU (:339-381).  x is read twice from HBM and the block output written once.  Every
+other configuration composes the same operations as the reference around the CUDA spectral block.
 Normalisation layers other than None are not provided (norm=None is the FNO default).
-
-With the default ChannelMLP (two layers, GELU, no dropout) and a soft-gating (or no) channel-MLP
-skip, the rest of the block -- ChannelMLP, soft-gating skip, closing GELU (:363-381) -- and the next
-block's linear skip run as one fused per-pixel kernel (``pointwise.channel_mlp``); the next block
-then takes that skip instead of recomputing it.
 """
 
 from __future__ import annotations
@@ -25,7 +22,7 @@ from torch import nn
 from . import pointwise
 from .layers import ChannelMLP, SoftGating, skip_connection
 from .spectral_convolution import SpectralConv
-from .utils import get_active_profiler, grad_needed, maybe_profile, validate_scaling_factor
+from .utils import grad_needed, validate_scaling_factor
 
 Number = Union[int, float]
 
@@ -86,8 +83,6 @@ class FNOBlocks(nn.Module):
                         fno_block_precision=fno_block_precision, decomposition_kwargs=decomposition_kwargs,
                         complex_data=complex_data, **extra)
             for i in range(n_layers)])
-        for i, conv in enumerate(self.convs):
-            setattr(conv, "profile_prefix", f"fno_blocks/{i}/spectral_conv")
         self.fno_skips = (nn.ModuleList([skip_connection(self.in_channels, self.out_channels, skip_type=fno_skip,
                                                          n_dim=self.n_dim) for _ in range(n_layers)])
                           if fno_skip is not None else None)
@@ -105,94 +100,85 @@ class FNOBlocks(nn.Module):
         return self.forward_with_postactivation(x, index, output_shape)
 
     def _fusable(self, index, x, output_shape) -> bool:
+        """The spectral convolution of block `index` runs bare (no resampling) and its linear skip, GELU
+        and the rest of the block can be composed around it."""
         conv = self.convs[index]
-        return (isinstance(conv, SpectralConv) and self.fno_skip is not None and self.fno_skip.lower() == "linear"
+        return (isinstance(conv, SpectralConv) and self.fno_skips is not None and self.fno_skip.lower() == "linear"
                 and self.stabilizer is None and self.non_linearity is F.gelu and output_shape is None
                 and conv.resolution_scaling_factor is None and x.is_cuda and not grad_needed(x, self))
 
-    def _mlp_fusable(self, index, x) -> bool:
-        if not (self.use_channel_mlp and x.is_cuda and x.dtype == torch.float32):
-            return False
+    def _mlp_parts(self, index):
+        """(ChannelMLP, soft-gating skip or None) of block `index` when they fit the chain kernel's form."""
+        if not self.use_channel_mlp:
+            return None
         mlp = self.channel_mlp[index]
         sg = self.channel_mlp_skips[index] if self.channel_mlp_skips is not None else None
         if not (isinstance(mlp, ChannelMLP) and mlp.n_layers == 2 and mlp.dropout is None
                 and mlp.non_linearity is F.gelu and (sg is None or isinstance(sg, SoftGating))):
+            return None
+        return mlp, sg
+
+    def chain_supported(self, index, batch, spatial, proj=None, min_groups=1) -> bool:
+        """Block `index` after its spectral convolution (and, with `proj`, the FNO projection ChannelMLP)
+        fits one chain kernel call for an input of `batch` samples on a grid of `spatial` points, with at
+        least `min_groups` tiles in flight per SM."""
+        parts = self._mlp_parts(index)
+        if parts is None:
             return False
-        nxt = self.fno_skips[index + 1].conv.out_channels if index + 1 < self.n_layers else 0
-        return pointwise.supported(x, self.out_channels, mlp.hidden_channels, mlp.out_channels, nxt)
-
-    def next_skip_weight(self, index):
-        """Weight [out, in, 1] of block `index`'s linear skip (None past the last block)."""
-        return self.fno_skips[index].conv.weight if index < self.n_layers else None
-
-    def set_pending_skip(self, x, index, skip):
-        """Hand block `index` the linear skip of its input x computed by a fused kernel upstream."""
-        self._pending_skip = (x, index, skip) if skip is not None else None
-
-    def fused_block(self, x, index, skip=None):
-        """Spectral block + skip add + GELU, then the fused ChannelMLP / soft-gating / GELU kernel, which
-        also returns the next block's linear skip.  Returns (y, next block's skip or None)."""
-        prof = get_active_profiler()
-        prefix = f"fno_blocks/{index}"
+        mlp, sg = parts
         last = index >= self.n_layers - 1
+        kw = {}
+        if proj is not None:
+            kw = dict(proj_hidden=proj.fcs[0].out_channels, proj_out=proj.fcs[1].out_channels)
+        return pointwise.supported(batch, tuple(spatial), self.in_channels, mlp.hidden_channels, self.out_channels,
+                                   skip=self.out_channels, act_skip=not last, act_out=not last, gate=sg is not None,
+                                   min_groups=min_groups, **kw)
+
+    def fused_block(self, x, index, spectral=None, proj=None):
+        """Spectral convolution, then ONE chain kernel for the rest of the block: the linear skip added to
+        the spectral output, GELU, ChannelMLP, soft-gating skip, GELU (fno_block.py:339-381) -- and, with
+        `proj` (a ChannelMLP), the FNO's projection on the block output.  ``spectral(index, conv, x)``
+        replaces the spectral call (the slab-decomposed path passes its own)."""
         conv = self.convs[index]
-        if skip is None:
-            with maybe_profile(prof, f"{prefix}/fno_skip", x.device):
-                skip, _ = pointwise.channel_mlp(x, None, None, self.fno_skips[index].conv.weight, None,
-                                                act_hidden=False, act_out=False)
-        with maybe_profile(prof, f"{prefix}/spectral_conv_skip_add_activation", x.device):
-            s = conv(x, addend=skip, apply_gelu=not last)
-        mlp = self.channel_mlp[index]
-        sg = self.channel_mlp_skips[index] if self.channel_mlp_skips is not None else None
-        with maybe_profile(prof, f"{prefix}/channel_mlp_skip_activation_next_skip", x.device):
-            y, z = pointwise.channel_mlp(
-                s, mlp.fcs[0].weight, mlp.fcs[0].bias, mlp.fcs[1].weight, mlp.fcs[1].bias, act_hidden=True,
-                act_out=not last, residual=x if sg is not None else None,
-                gate_w=sg.weight if sg is not None else None, gate_b=sg.bias if sg is not None else None,
-                next_w=self.next_skip_weight(index + 1))
-        return y, z
+        s = conv(x) if spectral is None else spectral(index, conv, x)
+        mlp, sg = self._mlp_parts(index)
+        last = index >= self.n_layers - 1
+        kw = {}
+        if proj is not None:
+            (f1, f2) = proj.fcs
+            kw = dict(w3=f1.weight, b3=f1.bias, w4=f2.weight, b4=f2.bias)
+        return pointwise.chain(x, mlp.fcs[0].weight, mlp.fcs[0].bias, mlp.fcs[1].weight, mlp.fcs[1].bias, s=s,
+                               w0=self.fno_skips[index].conv.weight, act_skip=not last, act_out=not last,
+                               gate_w=sg.weight if sg is not None else None,
+                               gate_b=sg.bias if sg is not None else None, **kw)
 
     def forward_with_postactivation(self, x, index=0, output_shape=None):
-        if self._fusable(index, x, output_shape) and self._mlp_fusable(index, x):
-            pending = getattr(self, "_pending_skip", None)
-            skip = pending[2] if pending is not None and pending[0] is x and pending[1] == index else None
-            self._pending_skip = None
-            y, z = self.fused_block(x, index, skip)
-            self.set_pending_skip(y, index + 1, z)
-            return y
-        self._pending_skip = None
-        prof = get_active_profiler()
-        prefix = f"fno_blocks/{index}"
+        if (self._fusable(index, x, output_shape) and x.dtype == torch.float32
+                and self.chain_supported(index, x.shape[0], x.shape[2:])):
+            return self.fused_block(x, index)
         last = index >= self.n_layers - 1
         if self.use_channel_mlp and self.channel_mlp_skips is not None:
-            with maybe_profile(prof, f"{prefix}/channel_mlp_skip", x.device):
-                x_skip_mlp = self.channel_mlp_skips[index](x)
-                x_skip_mlp = self.convs[index].transform(x_skip_mlp, output_shape=output_shape)
+            x_skip_mlp = self.channel_mlp_skips[index](x)
+            x_skip_mlp = self.convs[index].transform(x_skip_mlp, output_shape=output_shape)
         if self._fusable(index, x, output_shape):
-            with maybe_profile(prof, f"{prefix}/fno_skip", x.device):
-                x_skip = self.fno_skips[index](x)
-            with maybe_profile(prof, f"{prefix}/spectral_conv_skip_add_activation", x.device):
-                x = self.convs[index](x, addend=x_skip, apply_gelu=not last)
+            x_skip = self.fno_skips[index](x)
+            x = self.convs[index](x, addend=x_skip, apply_gelu=not last)
         else:
             if self.fno_skips is not None:
-                with maybe_profile(prof, f"{prefix}/fno_skip", x.device):
-                    x_skip = self.fno_skips[index](x)
-                    x_skip = self.convs[index].transform(x_skip, output_shape=output_shape)
+                x_skip = self.fno_skips[index](x)
+                x_skip = self.convs[index].transform(x_skip, output_shape=output_shape)
             if self.stabilizer == "tanh":
                 x = torch.tanh(x)
-            with maybe_profile(prof, f"{prefix}/spectral_conv", x.device):
-                x_fno = self.convs[index](x, output_shape=output_shape)
+            x_fno = self.convs[index](x, output_shape=output_shape)
             x = x_fno + x_skip if self.fno_skips is not None else x_fno
             if not last:
                 x = self.non_linearity(x)
         if self.use_channel_mlp:
-            with maybe_profile(prof, f"{prefix}/channel_mlp", x.device):
-                x = self.channel_mlp[index](x)
-                if self.channel_mlp_skips is not None:
-                    x = x + x_skip_mlp
+            x = self.channel_mlp[index](x)
+            if self.channel_mlp_skips is not None:
+                x = x + x_skip_mlp
         if not last:
-            with maybe_profile(prof, f"{prefix}/activation_1", x.device):
-                x = self.non_linearity(x)
+            x = self.non_linearity(x)
         return x
 
     def forward_with_preactivation(self, x, index=0, output_shape=None):

@@ -87,8 +87,6 @@ class FNOStaged(FNO):
                         factorization=factorization, fno_block_precision=fno_block_precision,
                         decomposition_kwargs=decomposition_kwargs, complex_data=complex_data, **extra)
             for i in range(len(modes))])
-        for i, conv in enumerate(blocks.convs):
-            setattr(conv, "profile_prefix", f"fno_blocks/{i}/spectral_conv")
 
     @property
     def n_modes(self):

@@ -1,22 +1,23 @@
-"""Fused per-pixel channel MLP (nop_pointwise_forward): the FNO layers around the spectral block.
+"""Per-pixel layer chain on the tensor cores (nop_chain_forward): the FNO layers around each spectral block.
 
-``channel_mlp(x, fc1, fc2, ...)`` evaluates, in one pass over HBM,
+``chain(x, ...)`` evaluates, in one pass over HBM, at every spatial point
 
-    u = [x ; grid]                       (grid coordinates generated in the kernel, optional)
-    y = act_out(fc2(act_hidden(fc1(u))) + g * r + gb)
-    z = w3 y                             (optional)
+    u = act_skip(W0 x + s)      if s is given (s = the block's spectral output), else u = [x ; grid]
+    h = GELU(W1 u + b1)
+    y = act_out(W2 h + b2 + g * x + gb)
+    out = W4 GELU(W3 y + b3) + b4      (when the projection weights are given)
 
-with the reference modules' own parameters: ChannelMLP (neuralop/layers/channel_mlp.py:82-119),
-SoftGating (neuralop/layers/skip_connections.py:53-94), the linear skip
-(skip_connections.py:96-127) and GridEmbeddingND (neuralop/layers/embeddings.py:147-164).
-``supported`` tells the caller whether the kernel takes a problem; callers keep the module path
-otherwise.
+with the reference modules' own parameters: the linear skip (neuralop/layers/skip_connections.py:96-127),
+ChannelMLP (neuralop/layers/channel_mlp.py:82-119), SoftGating (skip_connections.py:53-94),
+GridEmbeddingND (neuralop/layers/embeddings.py:147-164), and the FNO's lifting / projection ChannelMLPs
+(neuralop/models/fno.py:387-406).  ``supported`` tells the caller whether the kernel takes a problem;
+callers keep the module path otherwise.
 """
 
 from __future__ import annotations
 
 import ctypes
-from typing import Optional, Sequence, Tuple
+from typing import Optional, Sequence
 
 import torch
 
@@ -25,37 +26,42 @@ from . import _lib
 MAX_DIMS = 4
 
 
-class NopPointwiseDesc(ctypes.Structure):
+class NopChainDesc(ctypes.Structure):
     _fields_ = [
         ("abi_version", ctypes.c_int32),
         ("ndim", ctypes.c_int32),
         ("batch", ctypes.c_int64),
         ("spatial", ctypes.c_int64 * MAX_DIMS),
-        ("in_channels", ctypes.c_int32),
+        ("x_channels", ctypes.c_int32),
         ("grid_dims", ctypes.c_int32),
+        ("grid_lo", ctypes.c_float * MAX_DIMS),
+        ("grid_step", ctypes.c_float * MAX_DIMS),
+        ("grid_offset", ctypes.c_int64 * MAX_DIMS),
+        ("skip_channels", ctypes.c_int32),
+        ("act_skip", ctypes.c_int32),
         ("hidden_channels", ctypes.c_int32),
         ("out_channels", ctypes.c_int32),
-        ("next_channels", ctypes.c_int32),
-        ("act_hidden", ctypes.c_int32),
         ("act_out", ctypes.c_int32),
         ("gate", ctypes.c_int32),
-        ("has_b1", ctypes.c_int32),
-        ("has_b2", ctypes.c_int32),
-        ("has_gate_bias", ctypes.c_int32),
-        ("grid_lo", ctypes.c_float * MAX_DIMS),
-        ("grid_hi", ctypes.c_float * MAX_DIMS),
+        ("proj_hidden", ctypes.c_int32),
+        ("proj_out", ctypes.c_int32),
     ]
 
 
+class NopChainOperands(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in
+                ("x", "s", "w0", "w1", "b1", "w2", "b2", "g", "gb", "w3", "b3", "w4", "b4", "y")]
+
+
 def _declare(lib):
-    if getattr(lib, "_pw_declared", False):
+    if getattr(lib, "_chain_declared", False):
         return
-    lib.nop_pointwise_smem_bytes.restype = ctypes.c_int32
-    lib.nop_pointwise_smem_bytes.argtypes = [ctypes.POINTER(NopPointwiseDesc), ctypes.POINTER(ctypes.c_size_t)]
-    lib.nop_pointwise_forward.restype = ctypes.c_int32
-    lib.nop_pointwise_forward.argtypes = [ctypes.POINTER(NopPointwiseDesc)] + [ctypes.c_void_p] * 11 + \
-        [ctypes.c_void_p]
-    lib._pw_declared = True
+    lib.nop_chain_query.restype = ctypes.c_int32
+    lib.nop_chain_query.argtypes = [ctypes.POINTER(NopChainDesc), ctypes.POINTER(ctypes.c_int32)]
+    lib.nop_chain_forward.restype = ctypes.c_int32
+    lib.nop_chain_forward.argtypes = [ctypes.POINTER(NopChainDesc), ctypes.POINTER(NopChainOperands),
+                                      ctypes.c_void_p]
+    lib._chain_declared = True
 
 
 def _mat(w: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -72,104 +78,105 @@ def _vec(v: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     return None if v is None else v.detach().reshape(-1).to(torch.float32).contiguous()
 
 
-def _ptr(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+def grid_params(boundaries: Sequence[Sequence[float]], sizes: Sequence[int]):
+    """(lo, step) per axis of GridEmbeddingND's coordinates on a grid of ``sizes`` points
+    (torch.linspace(lo, hi, n + 1)[:-1], neuralop/layers/embeddings.py:351-383)."""
+    return [(float(lo), (float(hi) - float(lo)) / float(n)) for (lo, hi), n in zip(boundaries, sizes)]
 
 
-def _desc(x, cin, hidden, cout, cnext, grid, act_hidden, act_out, gate, has_b1, has_b2, has_gb):
-    d = NopPointwiseDesc()
-    d.abi_version = _lib.ABI_VERSION
-    d.ndim = x.ndim - 2
-    d.batch = x.shape[0]
-    for j, n in enumerate(x.shape[2:]):
-        d.spatial[j] = n
-    d.in_channels = cin
-    d.grid_dims = 0 if grid is None else d.ndim
-    if grid is not None:
-        for j, (lo, hi) in enumerate(grid):
-            d.grid_lo[j] = float(lo)
-            d.grid_hi[j] = float(hi)
-    d.hidden_channels = hidden
-    d.out_channels = cout
-    d.next_channels = cnext
-    d.act_hidden = int(bool(act_hidden))
-    d.act_out = int(bool(act_out))
-    d.gate = int(bool(gate))
-    d.has_b1 = int(bool(has_b1))
-    d.has_b2 = int(bool(has_b2))
-    d.has_gate_bias = int(bool(has_gb))
-    return d
-
-
-def supported_dims(batch: int, spatial: Sequence[int], cin: int, hidden: int, cout: int, cnext: int = 0,
-                   grid=None) -> bool:
-    """Whether the fused kernel takes a problem of these sizes (points per sample a multiple of 128,
-    every channel count <= 256, the weights fitting one CTA's shared memory)."""
-    if not 1 <= len(spatial) <= MAX_DIMS:
-        return False
-    pts = 1
-    for n in spatial:
-        pts *= int(n)
-    if pts % 128:
-        return False
-    lib = _lib.library()
-    _declare(lib)
-    d = NopPointwiseDesc()
+def make_desc(batch: int, spatial: Sequence[int], cx: int, hidden: int, cout: int, *, skip: int = 0,
+              act_skip: bool = False, act_out: bool = False, gate: bool = False, grid=None, grid_offset=None,
+              proj_hidden: int = 0, proj_out: int = 0) -> NopChainDesc:
+    """Descriptor of one chain call.  ``grid``: per-axis (lo, step) of the coordinate channels (see
+    grid_params) or None; ``grid_offset``: the index of this call's first point per axis."""
+    d = NopChainDesc()
     d.abi_version = _lib.ABI_VERSION
     d.ndim = len(spatial)
     d.batch = int(batch)
     for j, n in enumerate(spatial):
         d.spatial[j] = int(n)
-    d.in_channels, d.hidden_channels, d.out_channels, d.next_channels = cin, hidden, cout, cnext
-    d.grid_dims = 0 if grid is None else d.ndim
-    d.gate = 1  # counts the residual tile, the larger footprint
-    size = ctypes.c_size_t()
-    return lib.nop_pointwise_smem_bytes(ctypes.byref(d), ctypes.byref(size)) == _lib.NOP_OK
+    d.x_channels = int(cx)
+    d.grid_dims = 0 if grid is None else len(spatial)
+    if grid is not None:
+        for j, (lo, step) in enumerate(grid):
+            d.grid_lo[j] = lo
+            d.grid_step[j] = step
+            d.grid_offset[j] = int(grid_offset[j]) if grid_offset is not None else 0
+    d.skip_channels = int(skip)
+    d.act_skip = int(bool(act_skip))
+    d.hidden_channels = int(hidden)
+    d.out_channels = int(cout)
+    d.act_out = int(bool(act_out))
+    d.gate = int(bool(gate))
+    d.proj_hidden = int(proj_hidden)
+    d.proj_out = int(proj_out)
+    return d
 
 
-def supported(x: torch.Tensor, cin: int, hidden: int, cout: int, cnext: int = 0, grid=None) -> bool:
-    """supported_dims for the CUDA fp32 tensor x (with cin channels)."""
-    if not (x.is_cuda and x.dtype == torch.float32 and 3 <= x.ndim <= 2 + MAX_DIMS and x.shape[1] == cin):
+def query(desc: NopChainDesc) -> int:
+    """Tiles in flight per CTA for this descriptor, or 0 when the kernel does not take it."""
+    lib = _lib.library()
+    _declare(lib)
+    groups = ctypes.c_int32(0)
+    return int(groups.value) if lib.nop_chain_query(ctypes.byref(desc), ctypes.byref(groups)) == _lib.NOP_OK else 0
+
+
+def supported(batch: int, spatial: Sequence[int], cx: int, hidden: int, cout: int, min_groups: int = 1,
+              **kw) -> bool:
+    """Whether the kernel takes a chain of these sizes (channel counts <= 256, the weights and
+    in-flight tiles fitting one CTA's tensor and shared memory, points per sample a multiple of 4) with
+    at least ``min_groups`` tiles in flight per SM."""
+    if not 1 <= len(spatial) <= MAX_DIMS:
         return False
-    return supported_dims(x.shape[0], x.shape[2:], cin, hidden, cout, cnext, grid)
+    return query(make_desc(batch, spatial, cx, hidden, cout, **kw)) >= min_groups
 
 
-def channel_mlp(x: torch.Tensor, fc1_w: Optional[torch.Tensor], fc1_b: Optional[torch.Tensor],
-                fc2_w: torch.Tensor, fc2_b: Optional[torch.Tensor], *, grid: Optional[Sequence] = None,
-                act_hidden: bool = True, act_out: bool = False, residual: Optional[torch.Tensor] = None,
-                gate_w: Optional[torch.Tensor] = None, gate_b: Optional[torch.Tensor] = None,
-                next_w: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """(y, z) of the fused kernel on x's device and current stream (see the module docstring).
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
 
-    ``fc1_w = None`` makes it a single layer y = act_out(fc2(u) + ...).  ``grid``: per-axis
-    (lo, hi) boundaries of the coordinate channels appended to x, or None.
-    """
+
+def chain(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: torch.Tensor,
+          b2: Optional[torch.Tensor], *, s: Optional[torch.Tensor] = None, w0: Optional[torch.Tensor] = None,
+          act_skip: bool = False, act_out: bool = False, gate_w: Optional[torch.Tensor] = None,
+          gate_b: Optional[torch.Tensor] = None, grid=None, grid_offset=None, w3: Optional[torch.Tensor] = None,
+          b3: Optional[torch.Tensor] = None, w4: Optional[torch.Tensor] = None, b4: Optional[torch.Tensor] = None,
+          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One chain call on x's device and current stream (see the module docstring); returns y (or the
+    projection's output when w3 / w4 are given).  ``gate_w`` switches on the soft-gating skip of x."""
     if not x.is_cuda:
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path)")
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in
-                                       (x, fc1_w, fc1_b, fc2_w, fc2_b, residual, gate_w, gate_b, next_w)):
-        raise RuntimeError("the fused per-pixel kernel has no backward; call it under torch.no_grad() "
+                                       (x, s, w0, w1, b1, w2, b2, gate_w, gate_b, w3, b3, w4, b4)):
+        raise RuntimeError("the per-pixel chain kernel has no backward; call it under torch.no_grad() "
                            "(the FNO modules use their torch layers whenever a gradient is needed)")
+    if x.dtype != torch.float32:
+        raise TypeError(f"expected float32 input, got {x.dtype}")
     x = x.contiguous()
-    w1, b1, w2, b2 = _mat(fc1_w), _vec(fc1_b), _mat(fc2_w), _vec(fc2_b)
-    g, gb, w3 = _vec(gate_w), _vec(gate_b), _mat(next_w)
-    cin = x.shape[1]
-    hidden = 0 if w1 is None else w1.shape[0]
-    cout = w2.shape[0]
-    cnext = 0 if w3 is None else w3.shape[0]
-    gate = residual is not None
-    r = residual.contiguous() if gate else None
-    if gate and g is None:
-        raise ValueError("a residual needs gate weights")
-    d = _desc(x, cin, hidden, cout, cnext, grid, act_hidden, act_out, gate, b1 is not None, b2 is not None,
-              gb is not None)
     spatial = tuple(x.shape[2:])
-    y = torch.empty((x.shape[0], cout, *spatial), device=x.device, dtype=torch.float32)
-    z = torch.empty((x.shape[0], cnext, *spatial), device=x.device, dtype=torch.float32) if cnext else None
+    m0, m1, m2, m3, m4 = _mat(w0), _mat(w1), _mat(w2), _mat(w3), _mat(w4)
+    v1, v2, v3, v4 = _vec(b1), _vec(b2), _vec(b3), _vec(b4)
+    g, gb = _vec(gate_w), _vec(gate_b)
+    if s is not None:
+        s = s.contiguous()
+        if m0 is None or tuple(s.shape) != (x.shape[0], m0.shape[0], *spatial):
+            raise ValueError("s must be [batch, rows of w0, *spatial] and w0 must be given")
+    proj = m3 is not None
+    cout = m4.shape[0] if proj else m2.shape[0]
+    d = make_desc(x.shape[0], spatial, x.shape[1], m1.shape[0], m2.shape[0], skip=0 if s is None else m0.shape[0],
+                  act_skip=act_skip, act_out=act_out, gate=g is not None, grid=grid, grid_offset=grid_offset,
+                  proj_hidden=m3.shape[0] if proj else 0, proj_out=cout if proj else 0)
+    y_shape = (x.shape[0], cout, *spatial)
+    if out is None:
+        out = torch.empty(y_shape, device=x.device, dtype=torch.float32)
+    elif tuple(out.shape) != y_shape or not out.is_contiguous() or out.dtype != torch.float32:
+        raise ValueError(f"out must be a contiguous float32 tensor of shape {y_shape}")
+    ops = NopChainOperands()
+    for name, t in (("x", x), ("s", s), ("w0", m0), ("w1", m1), ("b1", v1), ("w2", m2), ("b2", v2), ("g", g),
+                    ("gb", gb), ("w3", m3), ("b3", v3), ("w4", m4), ("b4", v4), ("y", out)):
+        setattr(ops, name, None if t is None else t.data_ptr())
     lib = _lib.library()
     _declare(lib)
     stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
     with torch.cuda.device(x.device):
-        _lib.check(lib.nop_pointwise_forward(ctypes.byref(d), _ptr(x), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
-                                             _ptr(r), _ptr(g), _ptr(gb), _ptr(w3), _ptr(y), _ptr(z), stream))
-    return y, z
+        _lib.check(lib.nop_chain_forward(ctypes.byref(d), ctypes.byref(ops), stream))
+    return out

@@ -76,13 +76,3 @@ def test_golden_spectral_weights_load(case):
     kind, ws, ranks = conv.kernel_operands(geo)
     assert kind in ("dense", "tucker", "cp")
     assert tuple(geo.n_out) == tuple(case["y"].shape[2:])
-
-
-def test_profiler_sections():
-    prof = nb.TimingProfiler()
-    with nb.profiling(prof):
-        from neuraloperator_b200.utils import get_active_profiler, maybe_profile
-        with maybe_profile(get_active_profiler(), "fno/lifting"):
-            pass
-    assert "fno/lifting" in prof.stats
-    assert "fno/lifting" in prof.summary()

@@ -101,49 +101,62 @@ def test_fast_engine_request_reports_unsupported_shape():
     assert "fused FFT engine" in _lib.last_error()
 
 
-def _pw_desc(**over):
-    from neuraloperator_b200.pointwise import NopPointwiseDesc
-    d = NopPointwiseDesc()
-    d.abi_version = _lib.ABI_VERSION
-    d.ndim, d.batch = 2, 2
-    d.spatial[0], d.spatial[1] = 16, 32
-    d.in_channels, d.hidden_channels, d.out_channels, d.next_channels = 8, 4, 8, 8
-    d.gate = 1
+def _chain_desc(**over):
+    from neuraloperator_b200 import pointwise
+    d = pointwise.make_desc(2, (16, 32), 32, 16, 32, skip=32, act_skip=True, act_out=True, gate=True)
     for k, v in over.items():
         setattr(d, k, v)
     return d
 
 
-def test_pointwise_desc_layout():
-    from neuraloperator_b200.pointwise import NopPointwiseDesc
-    # 2 int32, int64 batch, 4 int64 spatial, 11 int32, 8 float (+ padding to 8 bytes)
-    assert ctypes.sizeof(NopPointwiseDesc) == 8 + 8 + 32 + 11 * 4 + 8 * 4 + 4
+def test_chain_desc_layout():
+    from neuraloperator_b200.pointwise import NopChainDesc, NopChainOperands
+    # 2 int32, int64 batch, 4 int64 spatial, 2 int32, 8 float, 4 int64 offsets, 8 int32
+    assert ctypes.sizeof(NopChainDesc) == 8 + 8 + 32 + 8 + 32 + 32 + 32
+    assert ctypes.sizeof(NopChainOperands) == 14 * 8
 
 
 @pytest.mark.parametrize("over, code", [
     (dict(), 0),
     (dict(abi_version=7), -1),
     (dict(ndim=0), -1),
-    (dict(grid_dims=1), -1),
-    (dict(in_channels=0), -1),
-    (dict(out_channels=300), -2),
+    (dict(grid_dims=2), -1),          # grid channels only without the skip stage
+    (dict(x_channels=0), -1),
+    (dict(hidden_channels=0), -1),
+    (dict(out_channels=300, gate=0), -2),
     (dict(hidden_channels=257), -2),
     (dict(batch=-1), -1),
+    (dict(out_channels=16), -1),      # the gate needs x_channels == out_channels
+    (dict(proj_hidden=64, proj_out=0), -1),
 ])
-def test_pointwise_desc_validation_on_host(over, code):
+def test_chain_desc_validation_on_host(over, code):
     from neuraloperator_b200 import pointwise
     lib = _lib.library()
     pointwise._declare(lib)
-    size = ctypes.c_size_t()
-    assert lib.nop_pointwise_smem_bytes(ctypes.byref(_pw_desc(**over)), ctypes.byref(size)) == code
+    groups = ctypes.c_int32()
+    assert lib.nop_chain_query(ctypes.byref(_chain_desc(**over)), ctypes.byref(groups)) == code, _lib.last_error()
 
 
-def test_pointwise_rejects_points_not_multiple_of_32():
+def test_chain_rejects_points_not_multiple_of_4():
     from neuraloperator_b200 import pointwise
     lib = _lib.library()
     pointwise._declare(lib)
-    d = _pw_desc()
-    d.spatial[1] = 33
-    size = ctypes.c_size_t()
-    assert lib.nop_pointwise_smem_bytes(ctypes.byref(d), ctypes.byref(size)) == -2
-    assert b"multiple of 128" in lib.nop_last_error()
+    d = _chain_desc()
+    d.spatial[0], d.spatial[1] = 15, 33
+    assert lib.nop_chain_query(ctypes.byref(d), None) == -2
+    assert b"multiple of 4" in lib.nop_last_error()
+
+
+@pytest.mark.parametrize("name, kw, groups", [
+    ("block_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True), 4),
+    ("block_h64", dict(cx=64, hidden=32, cout=64, skip=64, gate=True), 2),
+    ("lifting_3d_h32", dict(cx=3, hidden=64, cout=32, grid=[(0.0, 1 / 256)] * 3), 4),
+    ("lifting_2d_h64", dict(cx=1, hidden=128, cout=64, grid=[(0.0, 1 / 512)] * 2), 4),
+    ("last_block_proj_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True, proj_hidden=64, proj_out=3), 3),
+])
+def test_chain_planner_tiles_in_flight(name, kw, groups):
+    """The planner fits the FNO shapes with several tiles in flight per SM (tensor memory 512 columns,
+    227 KB of shared memory)."""
+    from neuraloperator_b200 import pointwise
+    nd = 3 if "3d" in name else 2
+    assert pointwise.query(pointwise.make_desc(2, (64,) * nd, **kw)) == groups
