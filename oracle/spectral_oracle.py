@@ -66,39 +66,49 @@ def contract_tucker(x: torch.Tensor, core: torch.Tensor, factors: Sequence[torch
                     separable: bool = False) -> torch.Tensor:
     """``_contract_tucker`` (spectral_convolution.py:76-103).
 
-    Non-separable 2D example: ``abcd,fghi,bf,eg,ch,di->aecd``.
+    Non-separable 2D example: ``abcd,fghi,bf,eg,ch,di->aecd``.  The reference evaluates the equation with
+    opt_einsum choosing the pairwise order; torch.einsum without opt_einsum (not installed here) would
+    contract left to right and form the outer product of x and the core (hundreds of GB at the TFNO
+    configuration's size).  The same sum is therefore taken in an explicit order -- the core expanded
+    over the spatial factors, then the input factor, the expanded core per mode, the output factor --
+    which changes only the rounding, as opt_einsum's choice does.
     """
     order = x.ndim
     xs = _SYMBOLS[:order]
-    o = _SYMBOLS[order]
+    a, b, modes = xs[0], xs[1], xs[2:]
+    o, ri, ro = _SYMBOLS[order:order + 3]
+    lead = 1 if separable else 2
+    g = core
+    for j, u in enumerate(factors[lead:]):  # the core over each spatial factor: r_j -> m_j
+        g = torch.tensordot(u, g.movedim(lead + j, 0), dims=([1], [0])).movedim(0, lead + j)
     if separable:
-        cs = _SYMBOLS[order + 1: 2 * order]
-        fs = [a + r for a, r in zip(xs[1:], cs)]
-        out = xs
-    else:
-        cs = _SYMBOLS[order + 1: 2 * order + 1]
-        fs = [xs[1] + cs[0], o + cs[1]] + [a + r for a, r in zip(xs[2:], cs[2:])]
-        out = xs[0] + o + xs[2:]
-    eq = f"{xs},{cs},{','.join(fs)}->{out}"
-    return torch.einsum(eq, x, core, *factors)
+        return x * torch.einsum(f"{ri}{modes},{b}{ri}->{b}{modes}", g, factors[0])
+    t = torch.einsum(f"{xs},{b}{ri}->{a}{ri}{modes}", x, factors[0])
+    t = torch.einsum(f"{a}{ri}{modes},{ri}{ro}{modes}->{a}{ro}{modes}", t, g)
+    return torch.einsum(f"{a}{ro}{modes},{o}{ro}->{a}{o}{modes}", t, factors[1])
 
 
 def contract_cp(x: torch.Tensor, weights: torch.Tensor, factors: Sequence[torch.Tensor],
                 separable: bool = False) -> torch.Tensor:
-    """``_contract_cp`` (spectral_convolution.py:55-73). 2D: ``abcd,e,be,fe,ce,de->afcd``."""
+    """``_contract_cp`` (spectral_convolution.py:55-73). 2D: ``abcd,e,be,fe,ce,de->afcd``.
+
+    Evaluated in an explicit pairwise order (input factor, the rank-wise weights and spatial factors,
+    output factor) for the reason given at contract_tucker; only the rounding differs."""
     order = x.ndim
     xs = _SYMBOLS[:order]
-    r = _SYMBOLS[order]
-    o = _SYMBOLS[order + 1]
-    out = list(xs)
+    a, b, modes = xs[0], xs[1], xs[2:]
+    o, r = _SYMBOLS[order:order + 2]
+    lead = 1 if separable else 2
+    # w[r, modes] = weights[r] prod_j U_j[m_j, r]
+    w = weights.reshape(-1, *([1] * len(modes)))
+    for j, u in enumerate(factors[lead:]):
+        shape = [1] * (1 + len(modes))
+        shape[0], shape[1 + j] = u.shape[1], u.shape[0]
+        w = w * u.transpose(0, 1).reshape(shape)
     if separable:
-        fs = [xs[1] + r]
-    else:
-        out[1] = o
-        fs = [xs[1] + r, o + r]
-    fs += [a + r for a in xs[2:]]
-    eq = f"{xs},{r},{','.join(fs)}->{''.join(out)}"
-    return torch.einsum(eq, x, weights, *factors)
+        return x * torch.einsum(f"{r}{modes},{b}{r}->{b}{modes}", w, factors[0])
+    t = torch.einsum(f"{xs},{b}{r}->{a}{r}{modes}", x, factors[0]) * w.unsqueeze(0)
+    return torch.einsum(f"{a}{r}{modes},{o}{r}->{a}{o}{modes}", t, factors[1])
 
 
 def contract_tt(x: torch.Tensor, factors: Sequence[torch.Tensor], separable: bool = False) -> torch.Tensor:

@@ -77,3 +77,27 @@ def case_scaling(case):
         return None
     order = case["order"]
     return [r] * order if isinstance(r, (int, float)) else list(r)
+
+
+def oracle_weight(conv):
+    """(payload, kind) of a SpectralConv's weight in the oracle's format (CPU tensors)."""
+    w = conv.weight
+    if hasattr(w, "core"):
+        return {"core": w.core.detach().cpu(), "factors": [f.detach().cpu() for f in w.factors]}, "tucker"
+    if hasattr(w, "weights"):
+        return {"weights": w.weights.detach().cpu(), "factors": [f.detach().cpu() for f in w.factors]}, "cp"
+    return w.tensor.detach().cpu(), "dense"
+
+
+def oracle_model(model):
+    """(params, cfg) of an FNO / TFNO in the oracle's format: oracle.fno_forward(x, params, cfg)."""
+    lin = lambda fcs: [(fc.weight.detach().cpu(), fc.bias.detach().cpu()) for fc in fcs]  # noqa: E731
+    fb = model.fno_blocks
+    blocks, kind = [], "dense"
+    for i in range(fb.n_layers):
+        wp, kind = oracle_weight(fb.convs[i])
+        blocks.append({"weight": wp, "bias": fb.convs[i].bias.detach().cpu(),
+                       "fno_skip": fb.fno_skips[i].conv.weight.detach().cpu(), "mlp": lin(fb.channel_mlp[i].fcs),
+                       "mlp_skip": fb.channel_mlp_skips[i].weight.detach().cpu()})
+    params = {"lifting": lin(model.lifting.fcs), "projection": lin(model.projection.fcs), "blocks": blocks}
+    return params, {"n_modes": tuple(model.n_modes), "weight_kind": kind}

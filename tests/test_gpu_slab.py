@@ -143,3 +143,4 @@ def test_slab_two_gpus_nccl(tmp_path):
     subprocess.run(cmd, check=True, timeout=600, env=env, cwd=ROOT)
     res = json.loads(out.read_text())
     assert res["err"] <= TOL_FP32, res
+    assert res["err_fno"] <= TOL_FP32, res
