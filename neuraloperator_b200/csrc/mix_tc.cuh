@@ -118,7 +118,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // bounded wait for the completion of the phase with parity `parity`; gives up early when `abort`
-// (if given) is set
+// (if given) is set.  Each try_wait may suspend the thread until the phase completes, for at most
+// kSuspendNs, so a waiting thread costs a few instructions per wake-up rather than a spin loop, and
+// the time limit and the abort flag are still checked at least every kSuspendNs.
+constexpr uint32_t kSuspendNs = 20000;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     const uint32_t addr = smem_u32(bar);
     const long long t0 = clock64();
@@ -126,10 +129,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(done)
-            : "r"(addr), "r"(parity)
+            : "r"(addr), "r"(parity), "r"(kSuspendNs)
             : "memory");
         if (done) return true;
         if ((abort && *abort) || clock64() - t0 > kWaitCycles) return false;
