@@ -443,7 +443,9 @@ def run_model(args, world, rank, local):
         if not args.no_e2e:
             x_host = x.cpu().pin_memory()
             y_host = torch.empty(tuple(y.shape), dtype=torch.float32).pin_memory()
-            chunk = 1
+            # chunks of at least one sample and at most a quarter of the batch: a 256^3 sample (2 GB of
+            # activations per layer) fills the GPU alone, small 2D samples are grouped
+            chunk = max(1, batch // 4)
             host_call = (lambda: runner.forward_host(x_host, out=y_host, chunk=chunk, synchronize=False)) if slab else \
                 (lambda: model.forward_host(x_host, out=y_host, chunk=chunk, n_streams=2, synchronize=False))
             host_call()

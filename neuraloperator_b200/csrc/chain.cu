@@ -37,6 +37,7 @@
 // (bounded) and the tensor memory is freed.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -72,10 +73,13 @@ struct Layout {
     int RX;                          // raw-x columns (gate) or 0
     int N0, K1, N1, N2, N3, N4;      // padded GEMM sizes (0: stage absent)
     int NC1, NC3;                    // chunk widths (== N1 / N3 when the layer runs whole)
+    int tail;                        // 1: the final layer (<= 4 outputs) runs on CUDA cores in the last epilogue
+    int Kt;                          // its input width (N1 without, N3 with the projection)
     int KA;                          // columns of each half (hi, lo) of the A region
     int cX, cC1, cH1, cC3, cH3, cA, cD, cols;  // tensor-memory columns relative to the group's base
     int groups;
     int o_w0, o_w1, o_w2, o_w3, o_w4;          // weight images (hi, then lo), shared-memory bytes
+    int o_wt;                                  // the CUDA-core final layer's weights, fp32 [4][Kt] (zero padded)
     int o_vec;                                 // b1 [N1], b2 + gb [N2], g [N2], b3 [N3], b4 [N4]
     int o_stash, stash_bytes;                  // per group: x stash (Cx rows), then s stash (Cs rows)
     int o_bar;
@@ -96,6 +100,12 @@ __host__ __device__ inline uint32_t kmaj_off(int n, int k, int N) {
 // ------------------------------------------------------------------------------------------------
 // device helpers
 // ------------------------------------------------------------------------------------------------
+// v rounded to tf32 (10 mantissa bits), to nearest with ties away from zero like cvt.rna.tf32.f32, on
+// the integer pipe: add half a tf32 ulp to the bit pattern and clear the 13 dropped bits (a carry into
+// the exponent is the correct rounding up; inputs are finite)
+__device__ __forceinline__ float tf32_rna(float v) {
+    return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
+}
 __device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(GT) : "memory"); }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -135,16 +145,36 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                  : "memory");
 }
 
+// The CUDA-core final layer: acc[j] += sum_i wt[j][k0 + i] v[i] for the 4 (zero-padded) outputs, as
+// pairs of partial sums (even / odd i) with packed FMAs; wt is fp32 [4][Kt] in shared memory (broadcast
+// reads, 16-byte aligned: Kt and k0 are multiples of 16)
+__device__ __forceinline__ void tail_acc16(float2 (&acc)[4], const float* __restrict__ wt, int Kt, int k0,
+                                           const float (&v)[16]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float* w = wt + j * Kt + k0;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(w + i);
+            acc[j] = __ffma2_rn(make_float2(q.x, q.y), make_float2(v[i], v[i + 1]), acc[j]);
+            acc[j] = __ffma2_rn(make_float2(q.z, q.w), make_float2(v[i + 2], v[i + 3]), acc[j]);
+        }
+    }
+}
+
 // hi / lo split of 16 values written to two column groups (the A operand's halves).  lo = v - hi is
 // exact in fp32; the tensor core reads its top 19 bits (tf32), so lo is not rounded first: the dropped
 // low bits are below 2^-21 of v, the order of the lo * lo term the split omits anyway.
 __device__ __forceinline__ void st_split16(uint32_t t_hi, uint32_t t_lo, const float (&v)[16]) {
     uint32_t h[16], l[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const float hv = tc::tf32_round(v[j]);
-        h[j] = __float_as_uint(hv);
-        l[j] = __float_as_uint(v[j] - hv);
+    for (int j = 0; j < 16; j += 2) {
+        const float2 hv = make_float2(tf32_rna(v[j]), tf32_rna(v[j + 1]));
+        const float2 lv = __ffma2_rn(hv, make_float2(-1.0f, -1.0f), make_float2(v[j], v[j + 1]));  // exact
+        h[j] = __float_as_uint(hv.x);
+        h[j + 1] = __float_as_uint(hv.y);
+        l[j] = __float_as_uint(lv.x);
+        l[j + 1] = __float_as_uint(lv.y);
     }
     tmem_st16(t_hi, h);
     tmem_st16(t_lo, l);
@@ -161,20 +191,40 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
         : "memory");
 }
 
+// D (tensor memory) += A (tensor memory) * B, always accumulating (no predicate to evaluate)
+__device__ __forceinline__ void mma_ts_acc(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+    asm volatile("tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%4, %5, %6, %7}, 1;" ::"r"(d), "r"(a),
+                 "l"(b), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0)
+                 : "memory");
+}
+
 // One layer (or one chunk of one) as three-pass tf32 MMAs: A columns a .. a + K (hi) and a + lo_off ..
 // (lo) of the group's tensor memory; W rows row0 .. row0 + N of an Nfull-row image whose K steps start
-// at ks0; D columns d .. d + N.  `acc` = 0 clears D first.
+// at ks0; D columns d .. d + N.  `acc` = 0 clears D first.  Each MMA costs the issuing thread about 55
+// cycles whatever N (measured on B200 for N <= 64), so the loop keeps everything else out of the way:
+// both weight descriptors are built once and stepped through the K steps by adding to their address
+// field (shared-memory byte address / 16 in the low 14 bits; the images stay below 256 KB, so the add
+// never carries out of the field).
 __device__ __forceinline__ void layer_mma(uint32_t tb, int a, int lo_off, int K, uint32_t w_hi, uint32_t w_lo,
                                           int Nfull, int row0, int ks0, int d, int N, bool acc) {
     const uint32_t idesc = idesc_tf32(N);
-    for (int ks = 0; ks < K / 8; ++ks) {
-        const uint32_t boff = (uint32_t)((ks0 + ks) * Nfull * 32 + (row0 >> 3) * 256);
-        const uint64_t bh = tc::smem_desc(w_hi + boff), bl = tc::smem_desc(w_lo + boff);
-        const uint32_t ta = tb + (uint32_t)(a + 8 * ks);
-        const uint32_t td = tb + (uint32_t)d;
-        mma_ts(td, ta, bh, idesc, (acc || ks > 0) ? 1u : 0u);
-        mma_ts(td, ta, bl, idesc, 1u);
-        mma_ts(td, ta + (uint32_t)lo_off, bh, idesc, 1u);
+    const uint32_t boff = (uint32_t)(ks0 * Nfull * 32 + (row0 >> 3) * 256);
+    uint64_t bh = tc::smem_desc(w_hi + boff), bl = tc::smem_desc(w_lo + boff);
+    const uint64_t step = (uint64_t)((Nfull * 32) >> 4);
+    const uint32_t td = tb + (uint32_t)d;
+    uint32_t ta = tb + (uint32_t)a;
+    const int nk = K / 8;
+    if (acc) mma_ts_acc(td, ta, bh, idesc);
+    else mma_ts(td, ta, bh, idesc, 0u);
+    mma_ts_acc(td, ta, bl, idesc);
+    mma_ts_acc(td, ta + (uint32_t)lo_off, bh, idesc);
+    for (int ks = 1; ks < nk; ++ks) {
+        bh += step;
+        bl += step;
+        ta += 8;
+        mma_ts_acc(td, ta, bh, idesc);
+        mma_ts_acc(td, ta, bl, idesc);
+        mma_ts_acc(td, ta + (uint32_t)lo_off, bh, idesc);
     }
 }
 
@@ -209,6 +259,7 @@ __device__ void load_weight(char* sm, int off, const float* w, int rows, int col
 
 __device__ __forceinline__ float vec_or0(const float* v, int i, int n) { return (v && i < n) ? __ldg(v + i) : 0.f; }
 
+
 // Exact-form GELU, 0.5 v (1 + erf(v / sqrt 2)), with erf from the rational approximation of
 // Abramowitz & Stegun, Handbook of Mathematical Functions (1964), eq. 7.1.26 (after Hastings):
 //     erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),  t = 1 / (1 + p x),  x >= 0,
@@ -219,7 +270,7 @@ __device__ __forceinline__ float vec_or0(const float* v, int i, int n) { return 
 // over [-8, 8]); relative L2 against the exact GELU on N(0, 1) inputs is 9e-8.
 __device__ __forceinline__ float gelu_fast(float v) {
     const float x = v * 0.70710678118654752440f;
-    const float ax = fabsf(x);
+    const float ax = __uint_as_float(__float_as_uint(x) & 0x7fffffffu);
     float t;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
     float poly = fmaf(t, 1.061405429f, -1.453152027f);
@@ -229,15 +280,70 @@ __device__ __forceinline__ float gelu_fast(float v) {
     poly *= t;
     float e;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-(ax * ax) * 1.4426950408889634f));
-    const float erf_x = copysignf(fmaf(-poly, e, 1.0f), x);
+    const float erf_x = __uint_as_float(__float_as_uint(fmaf(-poly, e, 1.0f)) | (__float_as_uint(x) & 0x80000000u));
     const float h = 0.5f * v;
     return fmaf(h, erf_x, h);
+}
+
+// gelu_fast of two values with packed fp32x2 arithmetic (the same operations and roundings per lane:
+// the polynomial is evaluated with negated coefficients, which negates every intermediate exactly)
+__device__ __forceinline__ float2 gelu_fast2(float2 v) {
+    const float2 x = __fmul2_rn(v, make_float2(0.70710678118654752440f, 0.70710678118654752440f));
+    const float2 ax = make_float2(__uint_as_float(__float_as_uint(x.x) & 0x7fffffffu),
+                                  __uint_as_float(__float_as_uint(x.y) & 0x7fffffffu));
+    const float2 d = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), ax, make_float2(1.0f, 1.0f));
+    float2 t;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.y) : "f"(d.y));
+    float2 q = __ffma2_rn(t, make_float2(-1.061405429f, -1.061405429f), make_float2(1.453152027f, 1.453152027f));
+    q = __ffma2_rn(t, q, make_float2(-1.421413741f, -1.421413741f));
+    q = __ffma2_rn(t, q, make_float2(0.284496736f, 0.284496736f));
+    q = __ffma2_rn(t, q, make_float2(-0.254829592f, -0.254829592f));
+    q = __fmul2_rn(q, t);  // -poly
+    const float2 arg = __fmul2_rn(__fmul2_rn(ax, ax), make_float2(-1.4426950408889634f, -1.4426950408889634f));
+    float2 e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
+    float2 r = __ffma2_rn(q, e, make_float2(1.0f, 1.0f));
+    // sign of x onto r (r = 1 - poly e >= 0)
+    r.x = __uint_as_float(__float_as_uint(r.x) | (__float_as_uint(x.x) & 0x80000000u));
+    r.y = __uint_as_float(__float_as_uint(r.y) | (__float_as_uint(x.y) & 0x80000000u));
+    const float2 h = __fmul2_rn(v, make_float2(0.5f, 0.5f));
+    return __ffma2_rn(h, r, h);
+}
+
+// GELU of 16 values in place (pairs)
+__device__ __forceinline__ void gelu16(float (&v)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+        const float2 g = gelu_fast2(make_float2(v[j], v[j + 1]));
+        v[j] = g.x;
+        v[j + 1] = g.y;
+    }
+}
+
+// v[j] += a[j] for 16 values (pairs)
+__device__ __forceinline__ void add16(float (&v)[16], const float* __restrict__ a) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(a + j);
+        const float2 s0 = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(q.x, q.y));
+        const float2 s1 = __fadd2_rn(make_float2(v[j + 2], v[j + 3]), make_float2(q.z, q.w));
+        v[j] = s0.x;
+        v[j + 1] = s0.y;
+        v[j + 2] = s1.x;
+        v[j + 3] = s1.y;
+    }
 }
 
 // ------------------------------------------------------------------------------------------------
 // the kernel
 // ------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(MAX_GROUPS * GT, 1)
+// Instantiated per group count G so each launch gets the registers its thread count allows (4 groups:
+// 128 per thread; 3: 168; 2 and 1: 255), which sets how many independent GELU chains the compiler keeps
+// in flight per thread.
+template <int G>
+__global__ void __launch_bounds__(G * GT, 1)
 k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tms, Params p, Layout L,
         int* __restrict__ status) {
     extern __shared__ __align__(1024) char sm[];
@@ -272,9 +378,18 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const int K1r = p.Cs ? p.Cs : p.Cx + p.nd;
     load_weight(sm, L.o_w0, p.w0, p.Cs, p.Cx, L.N0, L.Kx);
     load_weight(sm, L.o_w1, p.w1, p.Ch, K1r, L.N1, L.K1);
-    load_weight(sm, L.o_w2, p.w2, p.Cy, p.Ch, L.N2, L.N1);
+    if (!(L.tail && !p.Cp)) load_weight(sm, L.o_w2, p.w2, p.Cy, p.Ch, L.N2, L.N1);
     load_weight(sm, L.o_w3, p.w3, p.Cp, p.Cy, L.N3, L.N2);
-    load_weight(sm, L.o_w4, p.w4, p.Co, p.Cp, L.N4, L.N3);
+    if (!L.tail) load_weight(sm, L.o_w4, p.w4, p.Co, p.Cp, L.N4, L.N3);
+    if (L.tail) {  // fp32 [4][Kt], rows past the outputs and columns past the hidden width zero
+        float* wt = reinterpret_cast<float*>(sm + L.o_wt);
+        const float* src = p.Cp ? p.w4 : p.w2;
+        const int rows = p.Cp ? p.Co : p.Cy, cols = p.Cp ? p.Cp : p.Ch;
+        for (int e = threadIdx.x; e < 4 * L.Kt; e += blockDim.x) {
+            const int r = e / L.Kt, k = e % L.Kt;
+            wt[e] = (r < rows && k < cols) ? __ldg(src + (int64_t)r * cols + k) : 0.f;
+        }
+    }
     float* vb1 = reinterpret_cast<float*>(sm + L.o_vec);
     float* vb2 = vb1 + L.N1;
     float* vg = vb2 + L.N2;
@@ -287,6 +402,16 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     }
     for (int c = tid; c < L.N3; c += blockDim.x) vb3[c] = vec_or0(p.b3, c, p.Cp);
     for (int c = tid; c < L.N4; c += blockDim.x) vb4[c] = vec_or0(p.b4, c, p.Co);
+    {  // zero the stash padding rows of every group (the tensor copies fill only the first Cx / Cs rows)
+        const int xr = L.Kx > L.RX ? L.Kx : L.RX;
+        const int xpad = (xr - p.Cx) * TP, spad = (L.N0 - p.Cs) * TP;
+        for (int g = 0; g < L.groups; ++g) {
+            float* xs = reinterpret_cast<float*>(sm + L.o_stash + g * L.stash_bytes);
+            float* ss = xs + up1k(xr * TP * 4) / 4;
+            for (int e = tid; e < xpad; e += blockDim.x) xs[p.Cx * TP + e] = 0.f;
+            for (int e = tid; e < spad; e += blockDim.x) ss[p.Cs * TP + e] = 0.f;
+        }
+    }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // weight images -> tensor-core reads
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -300,7 +425,8 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const uint32_t lo0 = 4u * L.N0 * L.Kx, lo1 = 4u * L.N1 * L.K1, lo2 = 4u * L.N2 * L.N1;
     const uint32_t lo3 = 4u * L.N3 * L.N2, lo4 = 4u * L.N4 * L.N3;
     const float* xst = reinterpret_cast<const float*>(sm + L.o_stash + grp * L.stash_bytes);
-    const float* sst = xst + up1k(p.Cx * TP * 4) / 4;  // 1 KB aligned (tensor-copy destination)
+    const int xrows = L.Kx > L.RX ? L.Kx : L.RX;       // stash rows read in stage 1 (>= Cx)
+    const float* sst = xst + up1k(xrows * TP * 4) / 4;  // 1 KB aligned (tensor-copy destination)
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 > 0 && L.NC3 < L.N3;
     const int nch1 = L.N1 / L.NC1, nch3 = L.N3 ? L.N3 / L.NC3 : 0;
     const uint32_t xbytes = (uint32_t)p.Cx * TP * 4, sbytes = (uint32_t)p.Cs * TP * 4;
@@ -393,26 +519,23 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 }
             }
         }
-        const int kw = L.Kx > L.RX ? L.Kx : L.RX;
-        for (int c0 = 0; c0 < kw; c0 += 8) {
+        for (int c0 = 0; c0 < xrows; c0 += 8) {
             float v[8];
+            const float* xc = xst + c0 * TP + pt;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = c0 + j;
-                float val = 0.f;
-                if (c < p.Cx) {
-                    val = xst[c * TP + pt];
-                } else {
-                    const int a = c - p.Cx;
-                    if (a < p.nd) val = a == 0 ? crd[0] : a == 1 ? crd[1] : a == 2 ? crd[2] : crd[3];
+            for (int j = 0; j < 8; ++j) v[j] = xc[j * TP];  // rows past Cx read the zeroed padding
+            if (p.nd) {  // grid channels Cx .. Cx + nd - 1 (lifting only)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int a = c0 + j - p.Cx;
+                    if (a >= 0 && a < p.nd) v[j] = a == 0 ? crd[0] : a == 1 ? crd[1] : a == 2 ? crd[2] : crd[3];
                 }
-                v[j] = val;
             }
             if (c0 < L.Kx) {
                 uint32_t h[8], l[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const float hv = tc::tf32_round(v[j]);
+                    const float hv = tf32_rna(v[j]);
                     h[j] = __float_as_uint(hv);
                     l[j] = __float_as_uint(v[j] - hv);
                 }
@@ -447,12 +570,15 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 tmem_ld16(tl + L.cD + c0, v);
                 tmem_wait_ld(v);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int c = c0 + j;
-                    float u = v[j];
-                    if (c < p.Cs) u += sst[c * TP + pt];
-                    v[j] = p.act0 ? gelu_fast(u) : u;
+                for (int j = 0; j < 16; j += 2) {
+                    const int c = c0 + j;  // channels past Cs (padding) add 0
+                    const float s0 = sst[c * TP + pt];  // rows past Cs read the zeroed padding
+                    const float s1 = sst[(c + 1) * TP + pt];
+                    const float2 u = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(s0, s1));
+                    v[j] = u.x;
+                    v[j + 1] = u.y;
                 }
+                if (p.act0) gelu16(v);
                 st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -467,6 +593,31 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             commit_wait(false);
         }
 
+        // ---- 3'. fc1 -> GELU -> fc2 with fc2 (<= 4 outputs) on CUDA cores: one epilogue, no round trip ----
+        float* const yb = p.y + ((int64_t)b * (L.N3 ? p.Co : p.Cy) * p.P + pnt);  // channel c at yb + c P
+        const float* wt = reinterpret_cast<const float*>(sm + L.o_wt);
+        if (L.tail && !L.N3) {
+            float2 acc[4] = {};
+            for (int c0 = 0; c0 < L.N1; c0 += 16) {
+                float v[16];
+                tmem_ld16(tl + L.cD + c0, v);
+                tmem_wait_ld(v);
+                add16(v, vb1 + c0);
+                gelu16(v);
+                tail_acc16(acc, wt, L.Kt, c0, v);
+            }
+            if (valid) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (j < p.Cy) {
+                        const float o = acc[j].x + acc[j].y + vb2[j];
+                        __stcs(yb + (int64_t)j * p.P, p.act2 ? gelu_fast(o) : o);
+                    }
+                }
+            }
+            continue;
+        }
+
         // ---- 3. fc1 (chunks) -> GELU -> fc2 ----
         bool broke = false;
         for (int c = 0; c < nch1; ++c) {
@@ -477,8 +628,8 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 float v[16];
                 tmem_ld16(tl + src + c0, v);
                 tmem_wait_ld(v);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = gelu_fast(v[j] + vb1[c * L.NC1 + c0 + j]);
+                add16(v, vb1 + c * L.NC1 + c0);
+                gelu16(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
             }
             if (!barrier_ok()) {
@@ -495,26 +646,40 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         if (broke) break;
 
         // ---- 4. y = act(fc2 + b2 + g x + gb): store, or A of the projection ----
-        const int64_t ybase = (int64_t)b * (L.N3 ? p.Co : p.Cy) * p.P + pnt;
         for (int c0 = 0; c0 < L.N2; c0 += 16) {
             float v[16], xr[16];
             tmem_ld16(tl + L.cD + c0, v);
             if (p.gate) tmem_ld16(tl + L.cX + c0, xr);
             tmem_wait_ld(v);
             if (p.gate) tmem_wait_ld(xr);
+            add16(v, vb2 + c0);
+            if (p.gate) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int c = c0 + j;
-                float o = v[j] + vb2[c];
-                if (p.gate) o = fmaf(vg[c], xr[j], o);
-                v[j] = p.act2 ? gelu_fast(o) : o;
+                for (int j = 0; j < 16; j += 4) {
+                    const float4 gq = *reinterpret_cast<const float4*>(vg + c0 + j);
+                    const float2 o0 = __ffma2_rn(make_float2(gq.x, gq.y), make_float2(xr[j], xr[j + 1]),
+                                                 make_float2(v[j], v[j + 1]));
+                    const float2 o1 = __ffma2_rn(make_float2(gq.z, gq.w), make_float2(xr[j + 2], xr[j + 3]),
+                                                 make_float2(v[j + 2], v[j + 3]));
+                    v[j] = o0.x;
+                    v[j + 1] = o0.y;
+                    v[j + 2] = o1.x;
+                    v[j + 3] = o1.y;
+                }
             }
+            if (p.act2) gelu16(v);
             if (L.N3) {
                 st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
             } else if (valid) {
+                float* yc = yb + (int64_t)c0 * p.P;
+                if (c0 + 16 <= p.Cy) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (c0 + j < p.Cy) __stcs(p.y + ybase + (int64_t)(c0 + j) * p.P, v[j]);
+                    for (int j = 0; j < 16; ++j) __stcs(yc + (int64_t)j * p.P, v[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (c0 + j < p.Cy) __stcs(yc + (int64_t)j * p.P, v[j]);
+                }
             }
         }
         if (!L.N3) continue;
@@ -523,6 +688,23 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         if (!barrier_ok()) break;
         if (leader) layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, 0, 0, ch3 ? L.cC3 : L.cD, L.NC3, false);
         commit_wait(false);
+        if (L.tail) {  // out = W4 GELU(W3 y + b3) + b4 with W4 (<= 4 outputs) on CUDA cores
+            float2 acc[4] = {};
+            for (int c0 = 0; c0 < L.N3; c0 += 16) {
+                float v[16];
+                tmem_ld16(tl + L.cD + c0, v);
+                tmem_wait_ld(v);
+                add16(v, vb3 + c0);
+                gelu16(v);
+                tail_acc16(acc, wt, L.Kt, c0, v);
+            }
+            if (valid) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < p.Co) __stcs(yb + (int64_t)j * p.P, acc[j].x + acc[j].y + vb4[j]);
+            }
+            continue;
+        }
         for (int c = 0; c < nch3; ++c) {
             const int src = ch3 ? L.cC3 : L.cD;
             const int dst = ch3 ? L.cH3 : L.cA;
@@ -531,8 +713,8 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 float v[16];
                 tmem_ld16(tl + src + c0, v);
                 tmem_wait_ld(v);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = gelu_fast(v[j] + vb3[c * L.NC3 + c0 + j]);
+                add16(v, vb3 + c * L.NC3 + c0);
+                gelu16(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
             }
             if (!barrier_ok()) {
@@ -554,7 +736,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             if (valid) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    if (c0 + j < p.Co) __stcs(p.y + ybase + (int64_t)(c0 + j) * p.P, v[j] + vb4[c0 + j]);
+                    if (c0 + j < p.Co) __stcs(yb + (int64_t)(c0 + j) * p.P, v[j] + vb4[c0 + j]);
             }
         }
     }
@@ -594,19 +776,28 @@ bool layout_for(const Sizes& z, int groups, int nc1, int nc3, Layout* out) {
     L.N2 = up16(z.Cy);
     L.N3 = z.Cp ? up16(z.Cp) : 0;
     L.N4 = z.Cp ? up16(z.Co) : 0;
+    // the final layer runs on CUDA cores when it has at most 4 outputs (the FNO projection to 1 or 3
+    // channels): its hidden input is then consumed in the epilogue that produces it, so it needs no MMA
+    // round trip and the layer before it runs unchunked
+    L.tail = (z.Cp ? z.Co <= 4 : (z.Cy <= 4 && !z.gate)) ? 1 : 0;
+    if (L.tail) {
+        if (z.Cp) nc3 = L.N3;
+        else nc1 = L.N1;
+    }
+    L.Kt = L.tail ? (z.Cp ? L.N3 : L.N1) : 0;
     L.NC1 = nc1;
     L.NC3 = L.N3 ? nc3 : 0;
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 && L.NC3 < L.N3;
     int ka = L.Kx;
     auto mx = [](int& a, int b) { a = b > a ? b : a; };
     mx(ka, L.N0);
-    if (!ch1) mx(ka, L.N1);
+    if (!ch1 && !(L.tail && !z.Cp)) mx(ka, L.N1);  // h written as A (not when fc2 runs on CUDA cores)
     if (L.N3) mx(ka, L.N2);
-    if (L.N3 && !ch3) mx(ka, L.N3);
+    if (L.N3 && !ch3 && !L.tail) mx(ka, L.N3);
     L.KA = up8(ka);
     int nd = L.N0;
-    mx(nd, L.N2);
-    mx(nd, L.N4);
+    if (!(L.tail && !z.Cp)) mx(nd, L.N2);
+    if (!L.tail) mx(nd, L.N4);
     if (!ch1) mx(nd, L.N1);
     if (L.N3 && !ch3) mx(nd, L.N3);
     // temporary region: raw x (live until the gate) next to fc1's chunk regions; the projection's chunk
@@ -631,11 +822,14 @@ bool layout_for(const Sizes& z, int groups, int nc1, int nc3, Layout* out) {
     };
     L.o_w0 = take(8 * L.N0 * L.Kx);
     L.o_w1 = take(8 * L.N1 * L.K1);
-    L.o_w2 = take(8 * L.N2 * L.N1);
+    L.o_w2 = take((L.tail && !z.Cp) ? 0 : 8 * L.N2 * L.N1);
     L.o_w3 = take(8 * L.N3 * L.N2);
-    L.o_w4 = take(8 * L.N4 * L.N3);
+    L.o_w4 = take(L.tail ? 0 : 8 * L.N4 * L.N3);
+    L.o_wt = take(L.tail ? 16 * L.Kt : 0);
     L.o_vec = take(4 * (L.N1 + 2 * L.N2 + L.N3 + L.N4));
-    L.stash_bytes = up1k(z.Cx * TP * 4) + up1k(z.Cs * TP * 4);
+    // per group: x stash padded to the rows stage 1 reads, s stash padded to N0 rows; the copies fill the
+    // first Cx / Cs rows, the padding rows are zeroed once so the reads need no per-channel guard
+    L.stash_bytes = up1k((L.Kx > L.RX ? L.Kx : L.RX) * TP * 4) + up1k(L.N0 * TP * 4);
     L.o_stash = off;
     off += groups * L.stash_bytes;
     L.o_bar = off;
@@ -649,15 +843,22 @@ bool layout_for(const Sizes& z, int groups, int nc1, int nc3, Layout* out) {
     return true;
 }
 
-// the layout with the most groups, then the widest chunks (fewest MMA round trips)
+// the layout with the most groups, then the widest chunks (fewest MMA round trips).  NOP_CHAIN_MAX_GROUPS
+// (1..4, read at every call) caps the group count, for A/B timing of fewer tiles in flight with wider
+// chunks against more tiles in flight with narrower ones.
 bool plan_layout(const Sizes& z, Layout* out) {
+    int max_groups = MAX_GROUPS;
+    if (const char* e = std::getenv("NOP_CHAIN_MAX_GROUPS")) {
+        const int v = std::atoi(e);
+        if (v >= 1 && v <= MAX_GROUPS) max_groups = v;
+    }
     const int N1 = up16(z.Ch), N3 = z.Cp ? up16(z.Cp) : 16;
     int opts1[4], n1 = 0, opts3[4], n3 = 0;
     for (int c : {N1, 64, 32, 16})
         if (c == N1 || (c < N1 && N1 % c == 0)) opts1[n1++] = c;
     for (int c : {N3, 64, 32, 16})
         if (c == N3 || (c < N3 && N3 % c == 0)) opts3[n3++] = c;
-    for (int groups = MAX_GROUPS; groups >= 1; --groups)
+    for (int groups = max_groups; groups >= 1; --groups)
         for (int i = 0; i < n1; ++i)
             for (int j = 0; j < (z.Cp ? n3 : 1); ++j)
                 if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, out)) return true;
@@ -804,12 +1005,22 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
     NOP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     int* status = status_word(dev);
     if (!status) return fail(NOP_E_CUDA, "status word of the tensor-core kernels is not available");
-    NOP_CUDA_TRY(cudaFuncSetAttribute(chain::k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem));
     const int64_t ctas = ceil_div(p.tiles, L.groups);
     const unsigned grid = (unsigned)(ctas < sms ? ctas : sms);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    chain::k_chain<<<grid, L.groups * chain::GT, L.smem, s>>>(tmx, tms, p, L, status);
-    NOP_CUDA_TRY(cudaGetLastError());
+    auto launch = [&](auto kernel) -> int32_t {
+        NOP_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem));
+        kernel<<<grid, L.groups * chain::GT, L.smem, s>>>(tmx, tms, p, L, status);
+        NOP_CUDA_TRY(cudaGetLastError());
+        return NOP_OK;
+    };
+    switch (L.groups) {
+        case 4: rc = launch(chain::k_chain<4>); break;
+        case 3: rc = launch(chain::k_chain<3>); break;
+        case 2: rc = launch(chain::k_chain<2>); break;
+        default: rc = launch(chain::k_chain<1>); break;
+    }
+    if (rc != NOP_OK) return rc;
     return NOP_OK;
 }
 
