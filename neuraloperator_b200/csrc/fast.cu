@@ -1086,7 +1086,9 @@ int32_t fast_device_status(int* status, bool clear) {
 }
 
 int32_t fast_launches(const Plan& p) {
-    const int transforms = p.fast_kind == FastKind::Vol3D ? 4 : 2;
+    // 3D (whole or slab): plane transforms and outer-axis transforms in both directions
+    const bool vol = p.fast_kind == FastKind::Vol3D || p.fast_kind == FastKind::Vol3DSlab;
+    const int transforms = vol ? 4 : 2;
     return transforms + (p.d.weight_kind == NOP_WEIGHT_DENSE ? 1 : 3);
 }
 
