@@ -49,7 +49,7 @@ namespace chain {
 
 constexpr int TP = 128;          // points per tile (MMA M)
 constexpr int GT = 128;          // threads per group: one per point / tensor-memory lane
-constexpr int MAX_GROUPS = 4;
+constexpr int MAX_GROUPS = 5;
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_LIMIT = 227 * 1024;
 
@@ -65,12 +65,14 @@ struct Params {
     int64_t goff[NOP_MAX_DIMS];     // index offset of the first point per axis (slabs)
     float glo[NOP_MAX_DIMS], gstep[NOP_MAX_DIMS];
     const float *w0, *w1, *b1, *w2, *b2, *g, *gb, *w3, *b3, *w4, *b4;
+    const float* x;  // the block input, re-read for the gate when it is not kept in tensor memory
     float* y;
 };
 
 struct Layout {
     int Kx;                          // A columns written from x (+ grid channels)
     int RX;                          // raw-x columns (gate) or 0
+    int gx;                          // 1: the gate re-reads x from L2 instead of keeping it in tensor memory
     int N0, K1, N1, N2, N3, N4;      // padded GEMM sizes (0: stage absent)
     int NC1, NC3;                    // chunk widths (== N1 / N3 when the layer runs whole)
     int tail;                        // 1: the final layer (<= 4 outputs) runs on CUDA cores in the last epilogue
@@ -431,6 +433,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const int nch1 = L.N1 / L.NC1, nch3 = L.N3 ? L.N3 / L.NC3 : 0;
     const uint32_t xbytes = (uint32_t)p.Cx * TP * 4, sbytes = (uint32_t)p.Cs * TP * 4;
     const uint64_t pol = l2::evict_first();
+    const uint64_t pol_x = L.gx ? l2::evict_normal() : pol;  // x must survive in L2 until the gate reads it
     const int bar_id = 1 + grp;
 
     auto give_up = [&]() {
@@ -449,7 +452,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     auto issue_x = [&](int64_t tt) {
         const uint32_t b = (uint32_t)tt / tps;
         expect_tx(xfull, xbytes);
-        tma_load_2d(const_cast<float*>(xst), &tmx, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * p.Cx), xfull, pol);
+        tma_load_2d(const_cast<float*>(xst), &tmx, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * p.Cx), xfull, pol_x);
     };
     auto issue_s = [&](int64_t tt) {
         const uint32_t b = (uint32_t)tt / tps;
@@ -648,10 +651,15 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         // ---- 4. y = act(fc2 + b2 + g x + gb): store, or A of the projection ----
         for (int c0 = 0; c0 < L.N2; c0 += 16) {
             float v[16], xr[16];
+            if (L.gx) {  // x from L2 (coalesced: a warp reads 32 consecutive points of a channel)
+                const float* xg = p.x + ((int64_t)b * p.Cx + c0) * p.P + pnt;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) xr[j] = (valid && c0 + j < p.Cx) ? l2::ld(xg + (int64_t)j * p.P, pol) : 0.f;
+            }
             tmem_ld16(tl + L.cD + c0, v);
-            if (p.gate) tmem_ld16(tl + L.cX + c0, xr);
+            if (p.gate && !L.gx) tmem_ld16(tl + L.cX + c0, xr);
             tmem_wait_ld(v);
-            if (p.gate) tmem_wait_ld(xr);
+            if (p.gate && !L.gx) tmem_wait_ld(xr);
             add16(v, vb2 + c0);
             if (p.gate) {
 #pragma unroll
@@ -765,11 +773,12 @@ struct Sizes {
     int Cx, Cs, nd, Ch, Cy, Cp, Co, gate;
 };
 
-bool layout_for(const Sizes& z, int groups, int nc1, int nc3, Layout* out) {
+bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, Layout* out) {
     Layout L{};
     L.groups = groups;
     L.Kx = up8(z.Cx + (z.Cs ? 0 : z.nd));
-    L.RX = z.gate ? up16(z.Cx) : 0;
+    L.gx = (z.gate && gate_global) ? 1 : 0;
+    L.RX = (z.gate && !gate_global) ? up16(z.Cx) : 0;
     L.N0 = z.Cs ? up16(z.Cs) : 0;
     L.K1 = z.Cs ? L.N0 : L.Kx;
     L.N1 = up16(z.Ch);
@@ -858,10 +867,13 @@ bool plan_layout(const Sizes& z, Layout* out) {
         if (c == N1 || (c < N1 && N1 % c == 0)) opts1[n1++] = c;
     for (int c : {N3, 64, 32, 16})
         if (c == N3 || (c < N3 && N3 % c == 0)) opts3[n3++] = c;
+    // the gate's x stays in tensor memory unless dropping it buys another group (it is then re-read
+    // from L2, where the tile's copy left it)
     for (int groups = max_groups; groups >= 1; --groups)
-        for (int i = 0; i < n1; ++i)
-            for (int j = 0; j < (z.Cp ? n3 : 1); ++j)
-                if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, out)) return true;
+        for (int gg = 0; gg < (z.gate ? 2 : 1); ++gg)
+            for (int i = 0; i < n1; ++i)
+                for (int j = 0; j < (z.Cp ? n3 : 1); ++j)
+                    if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, gg == 1, out)) return true;
     return false;
 }
 
@@ -991,6 +1003,7 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
     p.w4 = o->w4;
     p.b4 = o->b4;
     p.y = o->y;
+    p.x = o->x;
     CUtensorMap tmx, tms;
     if (!chain::make_map(&tmx, o->x, d->batch * z.Cx, P, z.Cx))
         return fail(NOP_E_CUDA, "cuTensorMapEncodeTiled(x) failed");
@@ -1015,6 +1028,7 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
         return NOP_OK;
     };
     switch (L.groups) {
+        case 5: rc = launch(chain::k_chain<5>); break;
         case 4: rc = launch(chain::k_chain<4>); break;
         case 3: rc = launch(chain::k_chain<3>); break;
         case 2: rc = launch(chain::k_chain<2>); break;

@@ -148,11 +148,11 @@ def test_chain_rejects_points_not_multiple_of_4():
 
 
 @pytest.mark.parametrize("name, kw, groups", [
-    ("block_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True), 4),
+    ("block_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True), 5),
     ("block_h64", dict(cx=64, hidden=32, cout=64, skip=64, gate=True), 2),
-    ("lifting_3d_h32", dict(cx=3, hidden=64, cout=32, grid=[(0.0, 1 / 256)] * 3), 4),
+    ("lifting_3d_h32", dict(cx=3, hidden=64, cout=32, grid=[(0.0, 1 / 256)] * 3), 5),
     ("lifting_2d_h64", dict(cx=1, hidden=128, cout=64, grid=[(0.0, 1 / 512)] * 2), 4),
-    ("last_block_proj_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True, proj_hidden=64, proj_out=3), 3),
+    ("last_block_proj_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True, proj_hidden=64, proj_out=3), 4),
 ])
 def test_chain_planner_tiles_in_flight(name, kw, groups):
     """The planner fits the FNO shapes with several tiles in flight per SM (tensor memory 512 columns,
