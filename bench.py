@@ -424,7 +424,10 @@ def run_model(args, world, rank, local):
         ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
         del graph
 
-        # ---- one instrumented forward: every launch timed with CUDA events on the launching stream ----
+        # ---- one instrumented forward: every launch timed with CUDA events on the launching stream (after
+        # one eager forward, so the caching allocator holds every buffer again once the graph is gone) ----
+        y = fwd(x)
+        torch.cuda.synchronize()
         exch = None
         if slab:
             exch = runner.instrument(True)
