@@ -1105,6 +1105,10 @@ def run_train(args, cfg, world, rank, local):
                                         engine=args.engine), local)
     pack = (1 if kind == "dense" else 3 + len(geo.kept)) if plan_a.packed_bytes > 0 else 0
     launches = plan_f.launches_per_forward + pack + plan_a.launches_per_forward + 2
+    if kind == "tucker":  # nop_tucker_grads: one mode product per projected mode, conj(core), gram + sum per factor
+        nm = len(ws) - 1
+        nl, nr = nm // 2, nm - nm // 2
+        launches += (nr + 2 * nl + nl * (nl - 1) + nr * (nr - 1)) + 1 + 2 * nm
     gbs = b_alg / (ms / 1e3) / 1e9
     line = {
         "metric": "SpectralConv training step (forward + backward) samples/s", "value": world * batch / (ms / 1e3),

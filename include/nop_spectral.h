@@ -358,6 +358,19 @@ int32_t nop_spectral_pack_weights_adjoint(const nop_plan* adjoint_plan, const vo
  * reduced in a fixed order, so results do not depend on scheduling. */
 int32_t nop_spectral_weight_grad_workspace_size(const nop_plan* plan, size_t* bytes);
 
+/* Gradients of a Tucker-factorized weight W = core x_0 U_0 x_1 U_1 ... x_{n-1} U_{n-1} (n = ndim + 2
+ * modes; U_0 = U_in [Ci, r_in], U_1 = U_out [Co, r_out], U_{k+2} = [kept_k, r_k]; core [r_0, ..., r_{n-1}];
+ * all complex64, row-major) from grad_w = dL/dW ([Ci, Co, kept...], from nop_spectral_weight_grad):
+ *   grad_core = grad_w x_0 conj(U_0) ... x_{n-1} conj(U_{n-1}),
+ *   grad_factors[k] = sum over every mode but k of (grad_w x_j conj(U_j) for j != k) * conj(core),
+ * torch's convention for complex leaves.  Replaces autograd through the reconstruction einsum of
+ * _contract_tucker (spectral_convolution.py:76-103).  dims / ranks: the n mode sizes and ranks.  workspace:
+ * nop_tucker_grads_workspace_size bytes, 256-byte aligned.  fp32 arithmetic, deterministic order. */
+int32_t nop_tucker_grads_workspace_size(int32_t n, const int64_t* dims, const int64_t* ranks, size_t* bytes);
+int32_t nop_tucker_grads(int32_t n, const int64_t* dims, const int64_t* ranks, const void* core,
+                         const void* const* factors, const void* grad_w, void* grad_core, void* const* grad_factors,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

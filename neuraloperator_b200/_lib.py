@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "nop_device_status", "nop_chain_query", "nop_chain_forward",
     "nop_spectral_spectrum_layout", "nop_spectral_forward_keep", "nop_spectral_weight_grad",
     "nop_spectral_weight_grad_workspace_size", "nop_spectral_pack_weights_adjoint",
+    "nop_tucker_grads_workspace_size", "nop_tucker_grads",
 )
 
 MAX_SLAB_RANKS = 64
@@ -152,6 +153,14 @@ def _declare(lib):
                                                       ctypes.c_void_p]
     lib.nop_spectral_weight_grad_workspace_size.restype = ctypes.c_int32
     lib.nop_spectral_weight_grad_workspace_size.argtypes = [c_plan_p, ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_tucker_grads_workspace_size.restype = ctypes.c_int32
+    lib.nop_tucker_grads_workspace_size.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int64),
+                                                    ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_tucker_grads.restype = ctypes.c_int32
+    lib.nop_tucker_grads.argtypes = [
+        ctypes.c_int32, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+        ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.nop_device_status.restype = ctypes.c_int32
     lib.nop_device_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]
     lib.nop_spectral_host_workspace_size.restype = ctypes.c_int32

@@ -251,6 +251,36 @@ def weight_grad(fwd: Spectrum, adj: Spectrum, grad_w_shape: Optional[Sequence[in
     return gw, gb
 
 
+def tucker_grads(core: torch.Tensor, factors: List[torch.Tensor], gw: torch.Tensor) -> List[torch.Tensor]:
+    """[dL/dcore, dL/dU_0, ..., dL/dU_{n-1}] of the Tucker weight W = core x_0 U_0 ... x_{n-1} U_{n-1} given
+    dL/dW = ``gw`` (complex64 CUDA tensors; nop_tucker_grads): the values autograd through the
+    reconstruction einsum (neuralop/layers/spectral_convolution.py:76-103) gives."""
+    if not gw.is_cuda:
+        raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path)")
+    n = len(factors)
+    dev = gw.device
+    c64 = lambda t: t.detach().to(device=dev, dtype=torch.complex64).contiguous()  # noqa: E731
+    core, facs, gw = c64(core), [c64(u) for u in factors], c64(gw)
+    dims = (ctypes.c_int64 * n)(*[u.shape[0] for u in facs])
+    ranks = (ctypes.c_int64 * n)(*[u.shape[1] for u in facs])
+    if tuple(gw.shape) != tuple(dims) or tuple(core.shape) != tuple(ranks):
+        raise ValueError(f"grad_w {tuple(gw.shape)} / core {tuple(core.shape)} do not match the factors' "
+                         f"sizes {tuple(dims)} / ranks {tuple(ranks)}")
+    g_core = torch.empty_like(core)
+    g_fac = [torch.empty_like(u) for u in facs]
+    lib = _lib.library()
+    size = ctypes.c_size_t()
+    _lib.check(lib.nop_tucker_grads_workspace_size(n, dims, ranks, ctypes.byref(size)))
+    ws = torch.empty(int(size.value), device=dev, dtype=torch.uint8)
+    fptr = (ctypes.c_void_p * n)(*[u.data_ptr() for u in facs])
+    gptr = (ctypes.c_void_p * n)(*[g.data_ptr() for g in g_fac])
+    with torch.cuda.device(dev):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(lib.nop_tucker_grads(n, dims, ranks, _ptr(core), fptr, _ptr(gw), _ptr(g_core), gptr, _ptr(ws),
+                                        int(size.value), stream))
+    return [g_core] + g_fac
+
+
 def default_chunk(batch: int, target_chunks: int = 8) -> int:
     """Largest divisor of ``batch`` that cuts it into at least ``target_chunks`` chunks (or 1)."""
     limit = max(1, batch // target_chunks)

@@ -23,7 +23,6 @@ NotImplementedError.
 
 from __future__ import annotations
 
-import math
 from typing import List, Optional, Tuple, Union
 
 import torch
@@ -303,56 +302,9 @@ def _cp_full(lam, factors):
     return torch.einsum(eq, lam, *factors)
 
 
-def _mode_dot(t, u, k):
-    """t x_k u^T: mode k (size n) of t contracted with the first index of u [n, r]; the result's mode k has
-    size r.  Computed as a (batched) GEMM on views of t, so the large operand is not permuted."""
-    shp = t.shape
-    pre, n, post = math.prod(shp[:k]), shp[k], math.prod(shp[k + 1:])
-    if post == 1:
-        out = t.reshape(pre, n) @ u
-    else:
-        out = torch.matmul(u.transpose(0, 1), t.reshape(pre, n, post))
-    return out.reshape(*shp[:k], u.shape[1], *shp[k + 1:])
-
-
-def _mode_gram(t, c, k):
-    """sum over every mode but k of t[..., x, ...] * c[..., a, ...] -> [x, a] (t and c agree off mode k)."""
-    shp = t.shape
-    pre, post = math.prod(shp[:k]), math.prod(shp[k + 1:])
-    tv, cv = t.reshape(pre, shp[k], post), c.reshape(pre, c.shape[k], post)
-    if post == 1:
-        return tv[..., 0].transpose(0, 1) @ cv[..., 0]
-    if pre == 1:
-        return tv[0] @ cv[0].transpose(0, 1)
-    return torch.matmul(tv, cv.transpose(1, 2)).sum(0)
-
-
 def _tucker_grads(core, factors, gw):
-    """Gradients of (core, U_0..U_{n-1}) for W = core x_0 U_0 ... x_{n-1} U_{n-1} given dL/dW = gw.
-
-    torch's convention for complex leaves (dL/dRe + i dL/dIm) makes these the adjoint products
-        dL/dcore = gw x_0 conj(U_0) ... x_{n-1} conj(U_{n-1})
-        dL/dU_k  = sum over modes j != k of T_k * conj(core),   T_k = gw x_j conj(U_j) for every j != k,
-    the values autograd of the reconstruction gives.  The projections of the two halves of the modes
-    are shared, so the full-size gw is read by two chains of GEMMs instead of one per factor.
-    """
-    n = len(factors)
-    fh = [u.conj().resolve_conj() for u in factors]
-
-    def proj(t, modes):
-        # the first and last modes are plain GEMMs on views; middle modes are batched and cost torch a copy
-        # of the operand, so they run last, on the already reduced tensor
-        for k in sorted(modes, key=lambda j: (0 < j < n - 1, factors[j].shape[1] - factors[j].shape[0])):
-            t = _mode_dot(t, fh[k], k)
-        return t
-
-    left, right = list(range(n // 2)), list(range(n // 2, n))
-    a_right = proj(gw, right)   # modes in `right` at rank size
-    a_left = proj(gw, left)
-    g_core = proj(a_right, left)
-    cc = core.conj().resolve_conj()
-    g_fac = []
-    for k in range(n):
-        t = proj(a_right, [j for j in left if j != k]) if k in left else proj(a_left, [j for j in right if j != k])
-        g_fac.append(_mode_gram(t, cc, k))
-    return [g_core] + g_fac
+    """Gradients of (core, U_0..U_{n-1}) for W = core x_0 U_0 ... x_{n-1} U_{n-1} given dL/dW = gw, on the
+    library's kernels (nop_tucker_grads): dL/dcore = gw x_0 conj(U_0) ... x_{n-1} conj(U_{n-1}) and
+    dL/dU_k = sum over modes j != k of (gw x_j conj(U_j) for j != k) * conj(core), the values autograd
+    of the reconstruction (spectral_convolution.py:76-103) gives."""
+    return ops.tucker_grads(core, factors, gw)

@@ -92,16 +92,49 @@ def test_backward_recipe_matches_reference(case):
         assert rel_l2(gb.to(torch.float32), case["grad_bias"].reshape(-1)) <= TOL
 
 
-@pytest.mark.parametrize("shape, ranks", [((16, 16, 12, 9), (6, 5, 4, 3)), ((5, 6, 7), (2, 3, 4)), ((4, 9), (3, 5))])
+def _mode_dot(t, u, k):
+    """t x_k conj(u): mode k (size n) of t against u [n, r] (k_mode_dot of csrc/tucker_grad.cu)."""
+    return torch.tensordot(t, u.conj(), dims=([k], [0])).movedim(-1, k)
+
+
+def _mode_gram(t, c, k):
+    """sum over every mode but k of t[.., x, ..] * c[.., a, ..] -> [x, a] (k_mode_gram)."""
+    other = [j for j in range(t.ndim) if j != k]
+    return torch.tensordot(t, c, dims=(other, other))
+
+
+def tucker_grads_recipe(core, factors, gw):
+    """float64 restatement of nop_tucker_grads' orchestration: gw projected on the right half of the
+    modes (A_right) and on the left half (A_left), each half largest reduction first; the core gradient
+    is A_right projected on the left half, factor k's gram takes the other modes of k's half projected
+    from A_right (k left) or A_left (k right) against conj(core)."""
+    n = len(factors)
+
+    def proj(t, modes):
+        for k in sorted(modes, key=lambda j: -(factors[j].shape[0] - factors[j].shape[1])):
+            t = _mode_dot(t, factors[k], k)
+        return t
+
+    left, right = list(range(n // 2)), list(range(n // 2, n))
+    a_right, a_left = proj(gw, right), proj(gw, left)
+    g_fac = []
+    for k in range(n):
+        t = proj(a_right, [j for j in left if j != k]) if k in left else proj(a_left, [j for j in right if j != k])
+        g_fac.append(_mode_gram(t, core.conj(), k))
+    return [proj(a_right, left)] + g_fac
+
+
+@pytest.mark.parametrize("shape, ranks", [((16, 16, 12, 9), (6, 5, 4, 3)), ((5, 6, 7), (2, 3, 4)), ((4, 9), (3, 5)),
+                                          ((6, 5, 4, 3, 7), (2, 2, 3, 3, 4))])
 def test_tucker_grads_equal_autograd_of_reconstruction(shape, ranks):
-    """The direct Tucker factor gradients (shared half-mode projections) equal torch autograd through
-    the reconstructed weight, the route the reference's TFNO backward takes."""
-    from neuraloperator_b200.spectral_convolution import _tucker_grads
+    """The Tucker factor-gradient recipe of the CUDA kernels (shared half-mode projections, then one
+    gram per factor) equals torch autograd through the reconstructed weight, the route the reference's
+    TFNO backward takes."""
     g = torch.Generator().manual_seed(len(shape))
     c = lambda *s: torch.complex(torch.randn(s, generator=g, dtype=torch.float64),
                                  torch.randn(s, generator=g, dtype=torch.float64))
     core, facs, gw = c(*ranks), [c(n, r) for n, r in zip(shape, ranks)], c(*shape)
     leaves = [core.clone().requires_grad_()] + [f.clone().requires_grad_() for f in facs]
     ref = torch.autograd.grad(_tucker_full(leaves[0], leaves[1:]), leaves, gw)
-    for a, b in zip(_tucker_grads(core, facs, gw), ref):
+    for a, b in zip(tucker_grads_recipe(core, facs, gw), ref):
         assert rel_l2(a, b) <= 1e-12

@@ -160,3 +160,20 @@ def test_chain_planner_tiles_in_flight(name, kw, groups):
     from neuraloperator_b200 import pointwise
     nd = 3 if "3d" in name else 2
     assert pointwise.query(pointwise.make_desc(2, (64,) * nd, **kw)) == groups
+
+
+def test_tucker_grads_host_checks():
+    """Workspace sizing and argument checks of nop_tucker_grads run on the host (no device call)."""
+    lib = _lib.library()
+    dims = (ctypes.c_int64 * 4)(64, 64, 64, 33)
+    ranks = (ctypes.c_int64 * 4)(7, 7, 7, 4)
+    size = ctypes.c_size_t()
+    assert lib.nop_tucker_grads_workspace_size(4, dims, ranks, ctypes.byref(size)) == 0, _lib.last_error()
+    # four buffers of the largest intermediate (gw projected on one mode: 64 x 64 x 64 x 4... at most gw)
+    assert 0 < size.value <= 4 * 64 * 64 * 64 * 33 * 8 + (1 << 20)
+    assert lib.nop_tucker_grads_workspace_size(1, dims, ranks, ctypes.byref(size)) == -1
+    bad = (ctypes.c_int64 * 4)(64, 0, 64, 33)
+    assert lib.nop_tucker_grads_workspace_size(4, bad, ranks, ctypes.byref(size)) == -1
+    ptrs = (ctypes.c_void_p * 4)()
+    rc = lib.nop_tucker_grads(4, dims, ranks, None, ptrs, None, None, ptrs, None, 0, None)
+    assert rc == -1 and "NULL" in _lib.last_error()
