@@ -13,10 +13,10 @@
 // core gradient is A_right projected on the left half, and factor k's T_k is A_right (k in the left
 // half) or A_left (k in the right half) projected on the remaining modes of its half.  Two kernels:
 //   k_mode_dot   out[p][r][q] = sum_n t[p][n][q] conj(u[n][r])        (one mode at rank size)
-//   k_mode_gram  g[x][a]     = sum_{p,q} t[p][x][q] c[p][a][q]         (c = conj(core), two stages: the
-//                                                                     reduction order is fixed)
-// Every product runs in fp32 with fp32 accumulation on CUDA cores (the tensors are small: the C4
-// gradient is 69 MB, the projections a few MB).
+//   k_mode_gram  g[x][a]     = sum_{p,q} t[p][x][q] c[p][a][q]         (c = conj(core))
+// Every product runs in fp32 with fp32 accumulation on CUDA cores, every sum in a fixed order (the
+// results do not depend on scheduling).  The tensors are small -- the C4 gradient is 69 MB, the
+// projections a few MB -- so the two passes over gw bound the time.
 #include <cuda_runtime.h>
 
 #include <string>
@@ -26,46 +26,67 @@
 namespace nop {
 namespace tg {
 
-constexpr int RB = 16;           // ranks per pass of k_mode_dot
 constexpr int THREADS = 256;
-constexpr int GA = 16;           // columns a per block of k_mode_gram
+constexpr int MD_THREADS = 256;  // k_mode_dot block
+constexpr int NCH = 128;    // rows of conj(u) staged per pass of k_mode_dot
+constexpr int MAX_RB = 16;  // ranks per pass of k_mode_dot
+constexpr int GX = 64;      // k_gram_part output tile: GX rows x by 16 JA columns a
+constexpr int LC = 32;      // summation indices staged per step of k_gram_part
 constexpr int MAX_MODES = NOP_MAX_DIMS + 2;
 
-__device__ __forceinline__ float2 cfma(float2 a, float2 b, float2 acc) {  // acc + a b
-    acc.x = fmaf(a.x, b.x, fmaf(-a.y, b.y, acc.x));
-    acc.y = fmaf(a.x, b.y, fmaf(a.y, b.x, acc.y));
-    return acc;
+// acc + a b for complex a, b with b given as (b.re, b.im, -b.im, b.re): two packed FMAs
+__device__ __forceinline__ float2 cmac(float2 a, float4 b, float2 acc) {
+    acc = __ffma2_rn(make_float2(a.x, a.x), make_float2(b.x, b.y), acc);
+    return __ffma2_rn(make_float2(a.y, a.y), make_float2(b.z, b.w), acc);
 }
 
-// out[p][r][q] = sum_n t[p][n][q] conj(u[n][r]); thread = (p, q), ranks r0 .. r0 + RB (grid.y); conj(u) is
-// staged in shared memory NC rows at a time
-constexpr int NC = 256;
-__global__ void __launch_bounds__(THREADS, 2) k_mode_dot(const float2* __restrict__ t, const float2* __restrict__ u,
-                                                      float2* __restrict__ out, int64_t P, int N, int64_t Q, int R) {
-    __shared__ float2 us[NC * RB];
-    const int r0 = blockIdx.y * RB;
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const bool live = idx < P * Q;
-    const int64_t p = live ? idx / Q : 0, q = live ? idx - p * Q : 0;
+__device__ __forceinline__ float4 cexpand(float2 b) { return make_float4(b.x, b.y, -b.y, b.x); }
+
+// out[p][r][q] = sum_n t[p][n][q] conj(u[n][r]).  Thread = one (p, q) column over the whole n sum, RB ranks
+// per block, so loads and stores run along q and every output has one owner (fixed summation order).
+// Block b takes rank pass b % passes of column tile b / passes: the passes over one tile run side by
+// side and read t from L2 after the first.  conj(u) is staged in shared memory NCH rows at a time in the
+// expanded form cmac takes; four rows of t are loaded ahead.
+template <int RB>
+__global__ void __launch_bounds__(MD_THREADS) k_mode_dot(const float2* __restrict__ t, const float2* __restrict__ u,
+                                                      float2* __restrict__ out, int64_t P, int N, int64_t Q, int R,
+                                                      int passes) {
+    __shared__ float4 us[NCH * RB];
+    const int r0 = (int)(blockIdx.x % passes) * RB;
+    const int64_t PQ = P * Q;
+    const int64_t c = (int64_t)(blockIdx.x / passes) * MD_THREADS + threadIdx.x;
+    const bool live = c < PQ;
+    const int64_t p = live ? c / Q : 0, q = live ? c - p * Q : 0;
+    const float2* tp = t + p * N * Q + q;
     float2 acc[RB];
 #pragma unroll
     for (int j = 0; j < RB; ++j) acc[j] = make_float2(0.f, 0.f);
-    const float2* tp = t + p * N * Q + q;
-    for (int n0 = 0; n0 < N; n0 += NC) {
-        const int nc = N - n0 < NC ? N - n0 : NC;
+    for (int n0 = 0; n0 < N; n0 += NCH) {
+        const int nc = N - n0 < NCH ? N - n0 : NCH;
         __syncthreads();
-        for (int e = threadIdx.x; e < nc * RB; e += blockDim.x) {
+        for (int e = threadIdx.x; e < nc * RB; e += MD_THREADS) {
             const int n = e / RB, j = e % RB;
             const float2 v = r0 + j < R ? u[(int64_t)(n0 + n) * R + r0 + j] : make_float2(0.f, 0.f);
-            us[e] = make_float2(v.x, -v.y);
+            us[e] = cexpand(make_float2(v.x, -v.y));
         }
         __syncthreads();
-        if (live)
-            for (int n = 0; n < nc; ++n) {
-                const float2 tv = tp[(int64_t)(n0 + n) * Q];
+        if (!live) continue;
+        const float2* tc = tp + (int64_t)n0 * Q;
+        int n = 0;
+        for (; n + 4 <= nc; n += 4) {
+            float2 v[4];
 #pragma unroll
-                for (int j = 0; j < RB; ++j) acc[j] = cfma(tv, us[n * RB + j], acc[j]);
-            }
+            for (int i = 0; i < 4; ++i) v[i] = tc[(int64_t)(n + i) * Q];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < RB; ++j) acc[j] = cmac(v[i], us[(n + i) * RB + j], acc[j]);
+        }
+        for (; n < nc; ++n) {
+            const float2 x = tc[(int64_t)n * Q];
+#pragma unroll
+            for (int j = 0; j < RB; ++j) acc[j] = cmac(x, us[n * RB + j], acc[j]);
+        }
     }
     if (!live) return;
     float2* op = out + (p * R + r0) * Q + q;
@@ -74,51 +95,90 @@ __global__ void __launch_bounds__(THREADS, 2) k_mode_dot(const float2* __restric
         if (r0 + j < R) op[(int64_t)j * Q] = acc[j];
 }
 
-// stage 1 of g[x][a] = sum_{p,q} t[p][x][q] c[p][a][q]: block (split s, x, column group) sums the index
-// range [s * chunk, (s + 1) * chunk) of the flattened (p, q) space; part[s][x][a] holds the sums
-__global__ void __launch_bounds__(THREADS) k_mode_gram(const float2* __restrict__ t, const float2* __restrict__ c,
+// one tile of g[x][a] = sum_l t[p][x][q] c[p][a][q], l = (p, q) flattened, over the index range of split
+// blockIdx.x ([s * lper, (s + 1) * lper)); rows x0 .. x0 + GX (blockIdx.y), columns a0 .. a0 + 16 JA
+// (blockIdx.z).  Thread (tx, ta) owns x = x0 + tx + 16 i (i < 4), a = a0 + ta + 16 j (j < JA); the partial
+// sums go to part[x][a][s] and k_gram_sum adds the splits in order.  The element offsets of each staged
+// l are computed once per step (one division per l).
+template <int JA>
+__global__ void __launch_bounds__(THREADS) k_gram_part(const float2* __restrict__ t, const float2* __restrict__ c,
                                                        float2* __restrict__ part, int64_t P, int X, int A, int64_t Q,
-                                                       int64_t chunk) {
-    __shared__ float2 red[THREADS][GA + 1];
-    const int s = blockIdx.x, x = blockIdx.y, a0 = blockIdx.z * GA;
-    const int64_t PQ = P * Q, lo = (int64_t)s * chunk, hi = lo + chunk < PQ ? lo + chunk : PQ;
-    float2 acc[GA];
+                                                       int64_t lper, int S) {
+    constexpr int AT = 16 * JA;
+    __shared__ float2 ts[LC][GX + 1];  // padded: the staging stores along l hit distinct banks
+    __shared__ float2 cs[LC][AT + 1];
+    __shared__ int64_t off_t[LC], off_c[LC];
+    const int tx = threadIdx.x & 15, ta = threadIdx.x >> 4;
+    const int x0 = blockIdx.y * GX, a0 = blockIdx.z * AT;
+    const int64_t L = P * Q, lb = (int64_t)blockIdx.x * lper;
+    const int64_t le = lb + lper < L ? lb + lper : L;
+    const bool lfast = Q >= 8;  // load order: along l when q runs contiguous, else along x / a
+    float2 acc[4][JA];
 #pragma unroll
-    for (int j = 0; j < GA; ++j) acc[j] = make_float2(0.f, 0.f);
-    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        const int64_t p = i / Q, q = i - p * Q;
-        const float2 tv = t[(p * X + x) * Q + q];
-        const float2* cp = c + (p * A + a0) * Q + q;
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < GA; ++j)
-            if (a0 + j < A) acc[j] = cfma(tv, cp[(int64_t)j * Q], acc[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < GA; ++j) red[threadIdx.x][j] = acc[j];
-    __syncthreads();
-    for (int w = THREADS / 2; w > 0; w >>= 1) {  // fixed-order tree
-        if (threadIdx.x < w)
-#pragma unroll
-            for (int j = 0; j < GA; ++j) {
-                red[threadIdx.x][j].x += red[threadIdx.x + w][j].x;
-                red[threadIdx.x][j].y += red[threadIdx.x + w][j].y;
-            }
+        for (int j = 0; j < JA; ++j) acc[i][j] = make_float2(0.f, 0.f);
+    for (int64_t l0 = lb; l0 < le; l0 += LC) {
         __syncthreads();
+        if (threadIdx.x < LC) {
+            const int64_t l = l0 + threadIdx.x;
+            const int64_t pp = l / Q, qq = l - pp * Q;
+            off_t[threadIdx.x] = l < le ? pp * X * Q + qq : -1;
+            off_c[threadIdx.x] = l < le ? pp * A * Q + qq : -1;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < LC * GX; e += THREADS) {
+            const int li = lfast ? e % LC : e / GX, xi = lfast ? e / LC : e % GX;
+            const int64_t o = off_t[li];
+            ts[li][xi] = o >= 0 && x0 + xi < X ? t[o + (int64_t)(x0 + xi) * Q] : make_float2(0.f, 0.f);
+        }
+        for (int e = threadIdx.x; e < LC * AT; e += THREADS) {
+            const int li = lfast ? e % LC : e / AT, ai = lfast ? e / LC : e % AT;
+            const int64_t o = off_c[li];
+            cs[li][ai] = o >= 0 && a0 + ai < A ? c[o + (int64_t)(a0 + ai) * Q] : make_float2(0.f, 0.f);
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int li = 0; li < LC; ++li) {
+            float2 tv[4];
+            float4 cv[JA];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tv[i] = ts[li][tx + 16 * i];
+#pragma unroll
+            for (int j = 0; j < JA; ++j) cv[j] = cexpand(cs[li][ta + 16 * j]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < JA; ++j) acc[i][j] = cmac(tv[i], cv[j], acc[i][j]);
+        }
     }
-    if (threadIdx.x < GA && a0 + threadIdx.x < A) part[((int64_t)s * X + x) * A + a0 + threadIdx.x] = red[0][threadIdx.x];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < JA; ++j) {
+            const int x = x0 + tx + 16 * i, a = a0 + ta + 16 * j;
+            if (x < X && a < A) part[((int64_t)x * A + a) * S + blockIdx.x] = acc[i][j];
+        }
 }
 
-// stage 2: g[x][a] = sum over splits in order
-__global__ void k_gram_sum(const float2* __restrict__ part, float2* __restrict__ g, int S, int XA) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+// g[i] = sum over the S splits of part[i][s]: one warp per output, lane k adding splits k, k + 32, ...
+// in order, then a fixed butterfly across the lanes
+__global__ void k_gram_sum(const float2* __restrict__ part, float2* __restrict__ g, int S, int64_t XA) {
+    const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
     if (i >= XA) return;
     float2 acc = make_float2(0.f, 0.f);
-    for (int s = 0; s < S; ++s) {
-        const float2 v = part[(int64_t)s * XA + i];
+    for (int s = lane; s < S; s += 32) {
+        const float2 v = part[i * S + s];
         acc.x += v.x;
         acc.y += v.y;
     }
-    g[i] = acc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+    }
+    if (lane == 0) g[i] = acc;
 }
 
 // dims of a tensor: mode sizes; every mode k is either full (d_k) or projected (r_k)
@@ -131,8 +191,6 @@ struct Shape {
         return v;
     }
 };
-
-constexpr int kGramSplits = 64;
 
 struct Plan {
     int n;
@@ -169,9 +227,21 @@ int32_t project(const Plan& pl, const float2* const* U, const float2* src, Shape
         const int N = (int)sh->s[k], R = (int)pl.r[k];
         float2* out = i == m - 1 ? dst : ((i & 1) ? b1 : b0);
         if (P * R * Q > *peak) *peak = P * R * Q;
+        if (ceil_div(P * Q, MD_THREADS) * ceil_div(R, 4) > INT32_MAX)
+            return fail(NOP_E_UNSUPPORTED, "the weight is too large for the mode-product grid");
         if (run) {
-            const dim3 grid((unsigned)ceil_div(P * Q, THREADS), (unsigned)ceil_div(R, RB));
-            k_mode_dot<<<grid, THREADS, 0, s>>>(cur, U[k], out, P, N, Q, R);
+            const int64_t passes = ceil_div(R, MAX_RB), per = ceil_div(R, passes);
+            const int rb = per <= 4 ? 4 : per <= 8 ? 8 : per <= 12 ? 12 : MAX_RB;
+            const int np = (int)ceil_div(R, rb);
+            const unsigned grid = (unsigned)(ceil_div(P * Q, MD_THREADS) * np);
+            if (rb == 4)
+                k_mode_dot<4><<<grid, MD_THREADS, 0, s>>>(cur, U[k], out, P, N, Q, R, np);
+            else if (rb == 8)
+                k_mode_dot<8><<<grid, MD_THREADS, 0, s>>>(cur, U[k], out, P, N, Q, R, np);
+            else if (rb == 12)
+                k_mode_dot<12><<<grid, MD_THREADS, 0, s>>>(cur, U[k], out, P, N, Q, R, np);
+            else
+                k_mode_dot<MAX_RB><<<grid, MD_THREADS, 0, s>>>(cur, U[k], out, P, N, Q, R, np);
             cudaError_t e = cudaGetLastError();
             if (e != cudaSuccess) return cuda_fail(e, "tucker mode product launch");
         }
@@ -181,16 +251,40 @@ int32_t project(const Plan& pl, const float2* const* U, const float2* src, Shape
     return NOP_OK;
 }
 
+int gram_ja(int A) { return A <= 32 ? 2 : A <= 48 ? 3 : 4; }
+
+// splits of a gram's summation range: about two blocks per SM over all output tiles, LC-aligned ranges
+void gram_split(int X, int A, int64_t L, int* S, int64_t* lper) {
+    const int64_t tiles = ceil_div(X, GX) * ceil_div(A, 16 * gram_ja(A));
+    int64_t splits = ceil_div(296, tiles), most = ceil_div(L, LC);
+    splits = splits < most ? splits : most;
+    splits = splits < 1 ? 1 : splits;
+    *lper = ceil_div(ceil_div(L, splits), LC) * LC;
+    *S = (int)ceil_div(L, *lper);
+}
+
+// factor k's gradient g[x][a] from T_k (shape sh, mode k full) and conj(core); part: the split sums
+// (*part_peak: their element count, for workspace sizing)
 int32_t gram(const float2* t, const Shape& sh, const float2* cc, int k, int A, float2* part, float2* g,
-             cudaStream_t s) {
+             int64_t* part_peak, cudaStream_t s, bool run) {
     int64_t P = 1, Q = 1;
     for (int j = 0; j < k; ++j) P *= sh.s[j];
     for (int j = k + 1; j < sh.n; ++j) Q *= sh.s[j];
     const int X = (int)sh.s[k];
-    const int64_t chunk = ceil_div(P * Q, kGramSplits);
-    const dim3 grid(kGramSplits, X, (unsigned)ceil_div(A, GA));
-    k_mode_gram<<<grid, THREADS, 0, s>>>(t, cc, part, P, X, A, Q, chunk);
-    k_gram_sum<<<(unsigned)ceil_div((int64_t)X * A, 256), 256, 0, s>>>(part, g, kGramSplits, X * A);
+    int S;
+    int64_t lper;
+    gram_split(X, A, P * Q, &S, &lper);
+    if ((int64_t)S * X * A > *part_peak) *part_peak = (int64_t)S * X * A;
+    if (!run) return NOP_OK;
+    const int ja = gram_ja(A);
+    const dim3 grid(S, (unsigned)ceil_div(X, GX), (unsigned)ceil_div(A, 16 * ja));
+    if (ja == 2)
+        k_gram_part<2><<<grid, THREADS, 0, s>>>(t, cc, part, P, X, A, Q, lper, S);
+    else if (ja == 3)
+        k_gram_part<3><<<grid, THREADS, 0, s>>>(t, cc, part, P, X, A, Q, lper, S);
+    else
+        k_gram_part<4><<<grid, THREADS, 0, s>>>(t, cc, part, P, X, A, Q, lper, S);
+    k_gram_sum<<<(unsigned)ceil_div((int64_t)X * A * 32, 256), 256, 0, s>>>(part, g, S, (int64_t)X * A);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? NOP_OK : cuda_fail(e, "tucker mode gram launch");
 }
@@ -206,11 +300,12 @@ struct Io {
     const float2* U[MAX_MODES];
     const float2 *core, *gw;
     float2 *g_core, *g_fac[MAX_MODES];
-    float2 *b[4], *cc, *part;  // workspace: 4 projection buffers, conj(core), gram partials
+    float2 *b[4], *cc, *part;  // workspace: 4 projection buffers, conj(core), gram split sums
 };
 
-// the whole computation (run) or its shapes only (!run: *peak = largest intermediate in elements)
-int32_t orchestrate(const Plan& pl, const Io& io, int64_t* peak, cudaStream_t s, bool run) {
+// the whole computation (run) or its shapes only (!run: *peak = largest intermediate, *part_peak = largest
+// set of gram split sums, in elements)
+int32_t orchestrate(const Plan& pl, const Io& io, int64_t* peak, int64_t* part_peak, cudaStream_t s, bool run) {
     const int n = pl.n;
     int left[MAX_MODES], right[MAX_MODES], nl = n / 2, nr = n - n / 2;
     for (int k = 0; k < nl; ++k) left[k] = k;
@@ -245,7 +340,7 @@ int32_t orchestrate(const Plan& pl, const Io& io, int64_t* peak, cudaStream_t s,
             if ((rc = project(pl, io.U, tk, &st, rest, m, b[0], b[1], dst, peak, s, run)) != NOP_OK) return rc;
             tk = dst;
         }
-        if (run && (rc = gram(tk, st, io.cc, k, (int)pl.r[k], io.part, io.g_fac[k], s)) != NOP_OK) return rc;
+        if ((rc = gram(tk, st, io.cc, k, (int)pl.r[k], io.part, io.g_fac[k], part_peak, s, run)) != NOP_OK) return rc;
     }
     return NOP_OK;
 }
@@ -254,21 +349,17 @@ struct Ws {
     size_t buf, cc, part, bytes;
 };
 
-Ws workspace(const Plan& pl) {
-    int64_t peak = 0, amax = 0, xmax = 0, rprod = 1;
+int32_t workspace(const Plan& pl, Ws* w) {
+    int64_t peak = 0, part_peak = 0, rprod = 1;
     Io none{};
-    orchestrate(pl, none, &peak, nullptr, false);
-    for (int k = 0; k < pl.n; ++k) {
-        amax = pl.r[k] > amax ? pl.r[k] : amax;
-        xmax = pl.d[k] > xmax ? pl.d[k] : xmax;
-        rprod *= pl.r[k];
-    }
-    Ws w{};
-    w.buf = up256((size_t)peak * sizeof(float2));
-    w.cc = up256((size_t)rprod * sizeof(float2));
-    w.part = up256((size_t)kGramSplits * xmax * amax * sizeof(float2));
-    w.bytes = 4 * w.buf + w.cc + w.part;
-    return w;
+    const int32_t rc = orchestrate(pl, none, &peak, &part_peak, nullptr, false);
+    if (rc != NOP_OK) return rc;
+    for (int k = 0; k < pl.n; ++k) rprod *= pl.r[k];
+    w->buf = up256((size_t)peak * sizeof(float2));
+    w->cc = up256((size_t)rprod * sizeof(float2));
+    w->part = up256((size_t)part_peak * sizeof(float2));
+    w->bytes = 4 * w->buf + w->cc + w->part;
+    return NOP_OK;
 }
 
 int32_t check(int32_t n, const int64_t* dims, const int64_t* ranks, Plan* pl) {
@@ -278,10 +369,10 @@ int32_t check(int32_t n, const int64_t* dims, const int64_t* ranks, Plan* pl) {
     int64_t total = 1;
     for (int k = 0; k < n; ++k) {
         if (dims[k] < 1 || ranks[k] < 1) return fail(NOP_E_INVALID, "mode sizes and ranks must be positive");
-        if (dims[k] > 65536 || ranks[k] > 65536)
-            return fail(NOP_E_UNSUPPORTED, "mode sizes and ranks above 65536 are not supported");
+        if (dims[k] > 65535 || ranks[k] > 65535)
+            return fail(NOP_E_UNSUPPORTED, "mode sizes and ranks above 65535 are not supported");
         total *= dims[k] > ranks[k] ? dims[k] : ranks[k];
-        if (total > (int64_t(1) << 40)) return fail(NOP_E_UNSUPPORTED, "the weight is too large");
+        if (total > (int64_t(1) << 35)) return fail(NOP_E_UNSUPPORTED, "the weight is too large");
         pl->d[k] = dims[k];
         pl->r[k] = ranks[k];
     }
@@ -300,7 +391,9 @@ int32_t nop_tucker_grads_workspace_size(int32_t n, const int64_t* dims, const in
     tg::Plan pl;
     int32_t rc = tg::check(n, dims, ranks, &pl);
     if (rc != NOP_OK) return rc;
-    *bytes = tg::workspace(pl).bytes;
+    tg::Ws w{};
+    if ((rc = tg::workspace(pl, &w)) != NOP_OK) return rc;
+    *bytes = w.bytes;
     return NOP_OK;
 }
 
@@ -314,7 +407,8 @@ int32_t nop_tucker_grads(int32_t n, const int64_t* dims, const int64_t* ranks, c
         return fail(NOP_E_INVALID, "core, factors, grad_w and the gradient outputs must be non-NULL");
     for (int k = 0; k < n; ++k)
         if (!factors[k] || !grad_factors[k]) return fail(NOP_E_INVALID, "a factor or factor gradient is NULL");
-    const tg::Ws w = tg::workspace(pl);
+    tg::Ws w{};
+    if ((rc = tg::workspace(pl, &w)) != NOP_OK) return rc;
     if (!workspace || workspace_bytes < w.bytes)
         return fail(NOP_E_WORKSPACE, "workspace missing or smaller than nop_tucker_grads_workspace_size");
     if ((uintptr_t)workspace % 256) return fail(NOP_E_ALIGNMENT, "workspace must be 256-byte aligned");
@@ -330,8 +424,8 @@ int32_t nop_tucker_grads(int32_t n, const int64_t* dims, const int64_t* ranks, c
     io.core = static_cast<const float2*>(core);
     io.gw = static_cast<const float2*>(grad_w);
     io.g_core = static_cast<float2*>(grad_core);
-    int64_t peak = 0;
-    return tg::orchestrate(pl, io, &peak, static_cast<cudaStream_t>(stream), true);
+    int64_t peak = 0, part_peak = 0;
+    return tg::orchestrate(pl, io, &peak, &part_peak, static_cast<cudaStream_t>(stream), true);
 }
 
 }  // extern "C"

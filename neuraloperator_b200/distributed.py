@@ -137,7 +137,8 @@ class SlabSpectralConv:
         _lib.check(_lib.library().nop_spectral_pack_weights(plan.handle, arr, len(ws), ctypes.c_void_p(packed.data_ptr()),
                                                             plan.packed_bytes, ctypes.c_void_p(workspace.data_ptr()),
                                                             plan.workspace_bytes, stream))
-        cache["slab_packed"] = (key, packed, list(weights))  # referenced: addresses cannot be recycled
+        # referenced (detached, so no autograd graph stays alive): addresses cannot be recycled
+        cache["slab_packed"] = (key, packed, [w.detach() for w in weights])
         return packed
 
     def stage_planes_fwd(self, x_slab: torch.Tensor, lay: SlabLayout) -> torch.Tensor:

@@ -101,8 +101,8 @@ def _packed_weights(plan, desc, ws, arr, dev, workspace, cache, stream, sources=
     packed = torch.empty(plan.packed_bytes, device=dev, dtype=torch.uint8)
     _lib.check(_lib.library().nop_spectral_pack_weights(plan.handle, arr, len(ws), _ptr(packed), plan.packed_bytes,
                                                         _ptr(workspace), plan.workspace_bytes, stream))
-    if cache is not None:
-        cache["packed"] = (key, packed, sources)
+    if cache is not None:  # detached: the storage stays referenced, no autograd graph is kept alive
+        cache["packed"] = (key, packed, [w.detach() for w in sources])
     return packed
 
 

@@ -28,7 +28,7 @@ def _needs_cuda():
 
 
 def _autograd(core, facs, gw):
-    leaves = [core.double().requires_grad_()] + [f.double().requires_grad_() for f in facs]
+    leaves = [core.to(torch.complex128).requires_grad_()] + [f.to(torch.complex128).requires_grad_() for f in facs]
     return torch.autograd.grad(_tucker_full(leaves[0], leaves[1:]), leaves, gw.to(torch.complex128))
 
 
