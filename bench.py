@@ -371,6 +371,9 @@ def run_model(args, world, rank, local):
     desc, cls, modes, hidden, cin, cout, grid, batch, kw, field = MODELS[args.config]
     if args.batch is not None:
         batch = args.batch
+    if args.grid is not None:  # reduced grid for small profiling cases (not a bench number)
+        grid = (args.grid,) * len(grid)
+        desc += f"_grid{args.grid}"
     slab = world > 1 and len(grid) == 3
     model = build_model(args.config, dev, args.precision)
     gbatch = batch if slab else batch * world
@@ -1148,6 +1151,8 @@ def main():
                     help="default c5 (FNO 3D, the largest single-GPU configuration) for --model fno, c2 for layer")
     ap.add_argument("--engine", choices=["auto", "fast", "generic"], default="auto")
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (default: the config's)")
+    ap.add_argument("--grid", type=int, default=None,
+                    help="--model fno: points per axis instead of the config's (small profiling cases only)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
