@@ -53,14 +53,12 @@ constexpr int MAX_GROUPS = 5;
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_LIMIT = 227 * 1024;
 
-__host__ __device__ inline int up8(int v) { return (v + 7) & ~7; }
-__host__ __device__ inline int up16(int v) { return (v + 15) & ~15; }
-__host__ __device__ inline int up1k(int v) { return (v + 1023) & ~1023; }
+__host__ __device__ constexpr int up8(int v) { return (v + 7) & ~7; }
+__host__ __device__ constexpr int up16(int v) { return (v + 15) & ~15; }
+__host__ __device__ constexpr int up1k(int v) { return (v + 1023) & ~1023; }
 
 struct Params {
     int64_t P, tiles, tps;          // points per sample, tiles, tiles per sample
-    int Cx, Cs, nd, Ch, Cy, Cp, Co; // real channel counts (Co: rows of W4)
-    int act0, act2, gate;
     int64_t sp[NOP_MAX_DIMS];       // spatial sizes of this call (row-major point index)
     int64_t goff[NOP_MAX_DIMS];     // index offset of the first point per axis (slabs)
     float glo[NOP_MAX_DIMS], gstep[NOP_MAX_DIMS];
@@ -86,6 +84,8 @@ struct Layout {
     int o_stash, stash_bytes;                  // per group: x stash (Cx rows), then s stash (Cs rows)
     int o_bar;
     int smem;
+    int Cx, Cs, nd, Ch, Cy, Cp, Co;  // real channel counts (Co: rows of W4)
+    int act0, act2, gate;            // activation after the skip stage / after fc2, soft-gating skip
 };
 
 __host__ __device__ inline uint32_t idesc_tf32(int N) {
@@ -262,56 +262,51 @@ __device__ void load_weight(char* sm, int off, const float* w, int rows, int col
 __device__ __forceinline__ float vec_or0(const float* v, int i, int n) { return (v && i < n) ? __ldg(v + i) : 0.f; }
 
 
-// Exact-form GELU, 0.5 v (1 + erf(v / sqrt 2)), with erf from the rational approximation of
-// Abramowitz & Stegun, Handbook of Mathematical Functions (1964), eq. 7.1.26 (after Hastings):
-//     erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),  t = 1 / (1 + p x),  x >= 0,
-// |error| <= 1.5e-7, odd extension for x < 0; the published p and a1..a5 below.  One reciprocal and
-// one exp2 on the special-function unit plus six FMAs: measured 1.57x the throughput of the erff form on
-// B200 (80 GELUs per point make it the kernel's largest instruction cost).  Evaluated in fp32 with the
-// hardware's approximate reciprocal and exp2, it differs from the erff form by at most 5.1e-7 (measured
-// over [-8, 8]); relative L2 against the exact GELU on N(0, 1) inputs is 9e-8.
+// Exact-form GELU, 0.5 v (1 + erf(v / sqrt 2)) = 0.5 (v + |v| erf(|v| / sqrt 2)) (erf is odd), with erf
+// from the rational approximation of Abramowitz & Stegun, Handbook of Mathematical Functions (1964),
+// eq. 7.1.26 (after Hastings):
+//     erf(x) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-x^2),  t = 1 / (1 + p x),  x >= 0,
+// |error| <= 1.5e-7; the published p and a1..a5 below.  It is evaluated on y = x sqrt(log2 e), so that
+// exp(-x^2) = exp2(-y^2) and t = 1 / (1 + (p / sqrt(log2 e)) y): one reciprocal and one exp2 on the
+// special-function unit, the rest FMAs; the odd extension needs no sign manipulation in this form.
+// Measured 1.57x the throughput of the erff form on B200 (80 GELUs per point make it the kernel's
+// largest instruction cost); against the exact GELU on N(0, 1) inputs the relative L2 error is ~1e-7.
+constexpr float kGeluY = 0.849321800288019f;    // sqrt(log2 e) / sqrt 2
+constexpr float kGeluP = 0.2727374808792225f;   // p / sqrt(log2 e), p = 0.3275911
+constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f, kA4 = -1.453152027f,
+                kA5 = 1.061405429f;
+
 __device__ __forceinline__ float gelu_fast(float v) {
-    const float x = v * 0.70710678118654752440f;
-    const float ax = __uint_as_float(__float_as_uint(x) & 0x7fffffffu);
-    float t;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
-    float poly = fmaf(t, 1.061405429f, -1.453152027f);
-    poly = fmaf(t, poly, 1.421413741f);
-    poly = fmaf(t, poly, -0.284496736f);
-    poly = fmaf(t, poly, 0.254829592f);
-    poly *= t;
-    float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-(ax * ax) * 1.4426950408889634f));
-    const float erf_x = __uint_as_float(__float_as_uint(fmaf(-poly, e, 1.0f)) | (__float_as_uint(x) & 0x80000000u));
-    const float h = 0.5f * v;
-    return fmaf(h, erf_x, h);
+    const float av = fabsf(v);
+    const float y = av * kGeluY;
+    float t, e;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(y, kGeluP, 1.0f)));
+    float ns = fmaf(t, -kA5, -kA4);  // -(a4 + t a5), ... : the negated polynomial
+    ns = fmaf(t, ns, -kA3);
+    ns = fmaf(t, ns, -kA2);
+    ns = fmaf(t, ns, -kA1);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-(y * y)));
+    const float erf_x = fmaf(t * e, ns, 1.0f);
+    return 0.5f * fmaf(av, erf_x, v);
 }
 
-// gelu_fast of two values with packed fp32x2 arithmetic (the same operations and roundings per lane:
-// the polynomial is evaluated with negated coefficients, which negates every intermediate exactly)
+// gelu_fast of two values with packed fp32x2 arithmetic (the same operations and roundings per lane)
 __device__ __forceinline__ float2 gelu_fast2(float2 v) {
-    const float2 x = __fmul2_rn(v, make_float2(0.70710678118654752440f, 0.70710678118654752440f));
-    const float2 ax = make_float2(__uint_as_float(__float_as_uint(x.x) & 0x7fffffffu),
-                                  __uint_as_float(__float_as_uint(x.y) & 0x7fffffffu));
-    const float2 d = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), ax, make_float2(1.0f, 1.0f));
-    float2 t;
+    const float2 av = make_float2(fabsf(v.x), fabsf(v.y));
+    const float2 y = __fmul2_rn(av, make_float2(kGeluY, kGeluY));
+    const float2 d = __ffma2_rn(y, make_float2(kGeluP, kGeluP), make_float2(1.0f, 1.0f));
+    float2 t, e;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.x) : "f"(d.x));
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.y) : "f"(d.y));
-    float2 q = __ffma2_rn(t, make_float2(-1.061405429f, -1.061405429f), make_float2(1.453152027f, 1.453152027f));
-    q = __ffma2_rn(t, q, make_float2(-1.421413741f, -1.421413741f));
-    q = __ffma2_rn(t, q, make_float2(0.284496736f, 0.284496736f));
-    q = __ffma2_rn(t, q, make_float2(-0.254829592f, -0.254829592f));
-    q = __fmul2_rn(q, t);  // -poly
-    const float2 arg = __fmul2_rn(__fmul2_rn(ax, ax), make_float2(-1.4426950408889634f, -1.4426950408889634f));
-    float2 e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
-    float2 r = __ffma2_rn(q, e, make_float2(1.0f, 1.0f));
-    // sign of x onto r (r = 1 - poly e >= 0)
-    r.x = __uint_as_float(__float_as_uint(r.x) | (__float_as_uint(x.x) & 0x80000000u));
-    r.y = __uint_as_float(__float_as_uint(r.y) | (__float_as_uint(x.y) & 0x80000000u));
-    const float2 h = __fmul2_rn(v, make_float2(0.5f, 0.5f));
-    return __ffma2_rn(h, r, h);
+    float2 ns = __ffma2_rn(t, make_float2(-kA5, -kA5), make_float2(-kA4, -kA4));
+    ns = __ffma2_rn(t, ns, make_float2(-kA3, -kA3));
+    ns = __ffma2_rn(t, ns, make_float2(-kA2, -kA2));
+    ns = __ffma2_rn(t, ns, make_float2(-kA1, -kA1));
+    const float2 sq = __fmul2_rn(y, y);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(-sq.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(-sq.y));
+    const float2 erf_x = __ffma2_rn(__fmul2_rn(t, e), ns, make_float2(1.0f, 1.0f));
+    return __fmul2_rn(__ffma2_rn(av, erf_x, v), make_float2(0.5f, 0.5f));
 }
 
 // GELU of 16 values in place (pairs)
@@ -344,10 +339,11 @@ __device__ __forceinline__ void add16(float (&v)[16], const float* __restrict__ 
 // Instantiated per group count G so each launch gets the registers its thread count allows (4 groups:
 // 128 per thread; 3: 168; 2 and 1: 255), which sets how many independent GELU chains the compiler keeps
 // in flight per thread.
-template <int G>
+template <int G, class LT>
 __global__ void __launch_bounds__(G * GT, 1)
-k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tms, Params p, Layout L,
+k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tms, Params p, Layout Lp,
         int* __restrict__ status) {
+    const auto L = LT::get(Lp);  // FixedLayout: every field a compile-time constant
     extern __shared__ __align__(1024) char sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = warp >> 2;                 // group
@@ -377,18 +373,19 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     // weights and vectors, once per CTA
-    const int K1r = p.Cs ? p.Cs : p.Cx + p.nd;
-    load_weight(sm, L.o_w0, p.w0, p.Cs, p.Cx, L.N0, L.Kx);
-    load_weight(sm, L.o_w1, p.w1, p.Ch, K1r, L.N1, L.K1);
-    if (!(L.tail && !p.Cp)) load_weight(sm, L.o_w2, p.w2, p.Cy, p.Ch, L.N2, L.N1);
-    load_weight(sm, L.o_w3, p.w3, p.Cp, p.Cy, L.N3, L.N2);
-    if (!L.tail) load_weight(sm, L.o_w4, p.w4, p.Co, p.Cp, L.N4, L.N3);
+    const int K1r = L.Cs ? L.Cs : L.Cx + L.nd;
+    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx);
+    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1);
+    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1);
+    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2);
+    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3);
     if (L.tail) {  // fp32 [4][Kt], rows past the outputs and columns past the hidden width zero
         float* wt = reinterpret_cast<float*>(sm + L.o_wt);
-        const float* src = p.Cp ? p.w4 : p.w2;
-        const int rows = p.Cp ? p.Co : p.Cy, cols = p.Cp ? p.Cp : p.Ch;
-        for (int e = threadIdx.x; e < 4 * L.Kt; e += blockDim.x) {
-            const int r = e / L.Kt, k = e % L.Kt;
+        const float* src = L.Cp ? p.w4 : p.w2;
+        const int rows = L.Cp ? L.Co : L.Cy, cols = L.Cp ? L.Cp : L.Ch;
+        const int kt = L.Kt > 0 ? L.Kt : 1;  // (Kt > 0 whenever tail is set)
+        for (int e = threadIdx.x; e < 4 * kt; e += blockDim.x) {
+            const int r = e / kt, k = e % kt;
             wt[e] = (r < rows && k < cols) ? __ldg(src + (int64_t)r * cols + k) : 0.f;
         }
     }
@@ -397,21 +394,21 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     float* vg = vb2 + L.N2;
     float* vb3 = vg + L.N2;
     float* vb4 = vb3 + L.N3;
-    for (int c = tid; c < L.N1; c += blockDim.x) vb1[c] = vec_or0(p.b1, c, p.Ch);
+    for (int c = tid; c < L.N1; c += blockDim.x) vb1[c] = vec_or0(p.b1, c, L.Ch);
     for (int c = tid; c < L.N2; c += blockDim.x) {
-        vb2[c] = vec_or0(p.b2, c, p.Cy) + (p.gate ? vec_or0(p.gb, c, p.Cy) : 0.f);
-        vg[c] = p.gate ? vec_or0(p.g, c, p.Cy) : 0.f;
+        vb2[c] = vec_or0(p.b2, c, L.Cy) + (L.gate ? vec_or0(p.gb, c, L.Cy) : 0.f);
+        vg[c] = L.gate ? vec_or0(p.g, c, L.Cy) : 0.f;
     }
-    for (int c = tid; c < L.N3; c += blockDim.x) vb3[c] = vec_or0(p.b3, c, p.Cp);
-    for (int c = tid; c < L.N4; c += blockDim.x) vb4[c] = vec_or0(p.b4, c, p.Co);
+    for (int c = tid; c < L.N3; c += blockDim.x) vb3[c] = vec_or0(p.b3, c, L.Cp);
+    for (int c = tid; c < L.N4; c += blockDim.x) vb4[c] = vec_or0(p.b4, c, L.Co);
     {  // zero the stash padding rows of every group (the tensor copies fill only the first Cx / Cs rows)
         const int xr = L.Kx > L.RX ? L.Kx : L.RX;
-        const int xpad = (xr - p.Cx) * TP, spad = (L.N0 - p.Cs) * TP;
+        const int xpad = (xr - L.Cx) * TP, spad = (L.N0 - L.Cs) * TP;
         for (int g = 0; g < L.groups; ++g) {
             float* xs = reinterpret_cast<float*>(sm + L.o_stash + g * L.stash_bytes);
             float* ss = xs + up1k(xr * TP * 4) / 4;
-            for (int e = tid; e < xpad; e += blockDim.x) xs[p.Cx * TP + e] = 0.f;
-            for (int e = tid; e < spad; e += blockDim.x) ss[p.Cs * TP + e] = 0.f;
+            for (int e = tid; e < xpad; e += blockDim.x) xs[L.Cx * TP + e] = 0.f;
+            for (int e = tid; e < spad; e += blockDim.x) ss[L.Cs * TP + e] = 0.f;
         }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // weight images -> tensor-core reads
@@ -431,7 +428,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const float* sst = xst + up1k(xrows * TP * 4) / 4;  // 1 KB aligned (tensor-copy destination)
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 > 0 && L.NC3 < L.N3;
     const int nch1 = L.N1 / L.NC1, nch3 = L.N3 ? L.N3 / L.NC3 : 0;
-    const uint32_t xbytes = (uint32_t)p.Cx * TP * 4, sbytes = (uint32_t)p.Cs * TP * 4;
+    const uint32_t xbytes = (uint32_t)L.Cx * TP * 4, sbytes = (uint32_t)L.Cs * TP * 4;
     const uint64_t pol = l2::evict_first();
     const uint64_t pol_x = L.gx ? l2::evict_normal() : pol;  // x must survive in L2 until the gate reads it
     const int bar_id = 1 + grp;
@@ -452,18 +449,18 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     auto issue_x = [&](int64_t tt) {
         const uint32_t b = (uint32_t)tt / tps;
         expect_tx(xfull, xbytes);
-        tma_load_2d(const_cast<float*>(xst), &tmx, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * p.Cx), xfull, pol_x);
+        tma_load_2d(const_cast<float*>(xst), &tmx, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * L.Cx), xfull, pol_x);
     };
     auto issue_s = [&](int64_t tt) {
         const uint32_t b = (uint32_t)tt / tps;
         expect_tx(sfull, sbytes);
-        tma_load_2d(const_cast<float*>(sst), &tms, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * p.Cs), sfull, pol);
+        tma_load_2d(const_cast<float*>(sst), &tms, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * L.Cs), sfull, pol);
     };
     int x_pending = 0, s_pending = 0;  // loads issued and not yet waited for (leader's count)
     if (leader && t < p.tiles) {
         issue_x(t);
         ++x_pending;
-        if (p.Cs) {
+        if (L.Cs) {
             issue_s(t);
             ++s_pending;
         }
@@ -510,11 +507,11 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         if (leader) --x_pending;
         group_bar(bar_id);  // the stash has landed (the leader waited)
         float crd[NOP_MAX_DIMS] = {0.f, 0.f, 0.f, 0.f};
-        if (p.nd) {
+        if (L.nd) {
             uint32_t idx = pnt;
 #pragma unroll
             for (int a = NOP_MAX_DIMS - 1; a >= 0; --a) {
-                if (a < p.nd) {
+                if (a < L.nd) {
                     const uint32_t n = (uint32_t)p.sp[a];
                     const uint32_t q = idx / n;
                     crd[a] = p.glo[a] + (float)((int64_t)(idx - q * n) + p.goff[a]) * p.gstep[a];
@@ -527,11 +524,11 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             const float* xc = xst + c0 * TP + pt;
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[j] = xc[j * TP];  // rows past Cx read the zeroed padding
-            if (p.nd) {  // grid channels Cx .. Cx + nd - 1 (lifting only)
+            if (L.nd) {  // grid channels Cx .. Cx + nd - 1 (lifting only)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const int a = c0 + j - p.Cx;
-                    if (a >= 0 && a < p.nd) v[j] = a == 0 ? crd[0] : a == 1 ? crd[1] : a == 2 ? crd[2] : crd[3];
+                    const int a = c0 + j - L.Cx;
+                    if (a >= 0 && a < L.nd) v[j] = a == 0 ? crd[0] : a == 1 ? crd[1] : a == 2 ? crd[2] : crd[3];
                 }
             }
             if (c0 < L.Kx) {
@@ -581,7 +578,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                     v[j] = u.x;
                     v[j + 1] = u.y;
                 }
-                if (p.act0) gelu16(v);
+                if (L.act0) gelu16(v);
                 st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -597,7 +594,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         }
 
         // ---- 3'. fc1 -> GELU -> fc2 with fc2 (<= 4 outputs) on CUDA cores: one epilogue, no round trip ----
-        float* const yb = p.y + ((int64_t)b * (L.N3 ? p.Co : p.Cy) * p.P + pnt);  // channel c at yb + c P
+        float* const yb = p.y + ((int64_t)b * (L.N3 ? L.Co : L.Cy) * p.P + pnt);  // channel c at yb + c P
         const float* wt = reinterpret_cast<const float*>(sm + L.o_wt);
         if (L.tail && !L.N3) {
             float2 acc[4] = {};
@@ -612,9 +609,9 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             if (valid) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    if (j < p.Cy) {
+                    if (j < L.Cy) {
                         const float o = acc[j].x + acc[j].y + vb2[j];
-                        __stcs(yb + (int64_t)j * p.P, p.act2 ? gelu_fast(o) : o);
+                        __stcs(yb + (int64_t)j * p.P, L.act2 ? gelu_fast(o) : o);
                     }
                 }
             }
@@ -652,16 +649,16 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         for (int c0 = 0; c0 < L.N2; c0 += 16) {
             float v[16], xr[16];
             if (L.gx) {  // x from L2 (coalesced: a warp reads 32 consecutive points of a channel)
-                const float* xg = p.x + ((int64_t)b * p.Cx + c0) * p.P + pnt;
+                const float* xg = p.x + ((int64_t)b * L.Cx + c0) * p.P + pnt;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) xr[j] = (valid && c0 + j < p.Cx) ? l2::ld(xg + (int64_t)j * p.P, pol) : 0.f;
+                for (int j = 0; j < 16; ++j) xr[j] = (valid && c0 + j < L.Cx) ? l2::ld(xg + (int64_t)j * p.P, pol) : 0.f;
             }
             tmem_ld16(tl + L.cD + c0, v);
-            if (p.gate && !L.gx) tmem_ld16(tl + L.cX + c0, xr);
+            if (L.gate && !L.gx) tmem_ld16(tl + L.cX + c0, xr);
             tmem_wait_ld(v);
-            if (p.gate && !L.gx) tmem_wait_ld(xr);
+            if (L.gate && !L.gx) tmem_wait_ld(xr);
             add16(v, vb2 + c0);
-            if (p.gate) {
+            if (L.gate) {
 #pragma unroll
                 for (int j = 0; j < 16; j += 4) {
                     const float4 gq = *reinterpret_cast<const float4*>(vg + c0 + j);
@@ -675,18 +672,18 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                     v[j + 3] = o1.y;
                 }
             }
-            if (p.act2) gelu16(v);
+            if (L.act2) gelu16(v);
             if (L.N3) {
                 st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
             } else if (valid) {
                 float* yc = yb + (int64_t)c0 * p.P;
-                if (c0 + 16 <= p.Cy) {
+                if (c0 + 16 <= L.Cy) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) __stcs(yc + (int64_t)j * p.P, v[j]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        if (c0 + j < p.Cy) __stcs(yc + (int64_t)j * p.P, v[j]);
+                        if (c0 + j < L.Cy) __stcs(yc + (int64_t)j * p.P, v[j]);
                 }
             }
         }
@@ -709,7 +706,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             if (valid) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    if (j < p.Co) __stcs(yb + (int64_t)j * p.P, acc[j].x + acc[j].y + vb4[j]);
+                    if (j < L.Co) __stcs(yb + (int64_t)j * p.P, acc[j].x + acc[j].y + vb4[j]);
             }
             continue;
         }
@@ -744,7 +741,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             if (valid) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    if (c0 + j < p.Co) __stcs(yb + (int64_t)(c0 + j) * p.P, v[j] + vb4[c0 + j]);
+                    if (c0 + j < L.Co) __stcs(yb + (int64_t)(c0 + j) * p.P, v[j] + vb4[c0 + j]);
             }
         }
     }
@@ -770,12 +767,27 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
 // host planner
 // ------------------------------------------------------------------------------------------------
 struct Sizes {
-    int Cx, Cs, nd, Ch, Cy, Cp, Co, gate;
+    int Cx, Cs, nd, Ch, Cy, Cp, Co, gate, act0, act2;
 };
 
-bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, Layout* out) {
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+// The layout of one chain for `groups` groups and chunk widths nc1 / nc3 (false when it does not fit).
+// constexpr: the layouts of the FNO configurations' chains are also computed at compile time, and a
+// kernel instantiated on one of them (FixedLayout) takes every size and offset as a constant.
+constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, Layout* out) {
     Layout L{};
     L.groups = groups;
+    L.Cx = z.Cx;
+    L.Cs = z.Cs;
+    L.nd = z.nd;
+    L.Ch = z.Ch;
+    L.Cy = z.Cy;
+    L.Cp = z.Cp;
+    L.Co = z.Co;
+    L.gate = z.gate;
+    L.act0 = z.act0;
+    L.act2 = z.act2;
     L.Kx = up8(z.Cx + (z.Cs ? 0 : z.nd));
     L.gx = (z.gate && gate_global) ? 1 : 0;
     L.RX = (z.gate && !gate_global) ? up16(z.Cx) : 0;
@@ -797,23 +809,21 @@ bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, 
     L.NC1 = nc1;
     L.NC3 = L.N3 ? nc3 : 0;
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 && L.NC3 < L.N3;
-    int ka = L.Kx;
-    auto mx = [](int& a, int b) { a = b > a ? b : a; };
-    mx(ka, L.N0);
-    if (!ch1 && !(L.tail && !z.Cp)) mx(ka, L.N1);  // h written as A (not when fc2 runs on CUDA cores)
-    if (L.N3) mx(ka, L.N2);
-    if (L.N3 && !ch3 && !L.tail) mx(ka, L.N3);
+    int ka = cmax(L.Kx, L.N0);
+    if (!ch1 && !(L.tail && !z.Cp)) ka = cmax(ka, L.N1);  // h written as A (not when fc2 runs on CUDA cores)
+    if (L.N3) ka = cmax(ka, L.N2);
+    if (L.N3 && !ch3 && !L.tail) ka = cmax(ka, L.N3);
     L.KA = up8(ka);
     int nd = L.N0;
-    if (!(L.tail && !z.Cp)) mx(nd, L.N2);
-    if (!L.tail) mx(nd, L.N4);
-    if (!ch1) mx(nd, L.N1);
-    if (L.N3 && !ch3) mx(nd, L.N3);
+    if (!(L.tail && !z.Cp)) nd = cmax(nd, L.N2);
+    if (!L.tail) nd = cmax(nd, L.N4);
+    if (!ch1) nd = cmax(nd, L.N1);
+    if (L.N3 && !ch3) nd = cmax(nd, L.N3);
     // temporary region: raw x (live until the gate) next to fc1's chunk regions; the projection's chunk
     // regions reuse it once the gate is done
     const int t1 = L.RX + (ch1 ? 3 * L.NC1 : 0);
     const int t3 = ch3 ? 3 * L.NC3 : 0;
-    const int tw = up16(t1 > t3 ? t1 : t3);
+    const int tw = up16(cmax(t1, t3));
     L.cX = 0;
     L.cC1 = L.RX;
     L.cH1 = L.RX + L.NC1;
@@ -824,21 +834,23 @@ bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, 
     L.cols = up16(L.cD + nd);
     if (L.cols * groups > TMEM_COLS) return false;
     int off = 0;
-    auto take = [&](int bytes) {
-        const int at = off;
-        off += up1k(bytes);
-        return at;
-    };
-    L.o_w0 = take(8 * L.N0 * L.Kx);
-    L.o_w1 = take(8 * L.N1 * L.K1);
-    L.o_w2 = take((L.tail && !z.Cp) ? 0 : 8 * L.N2 * L.N1);
-    L.o_w3 = take(8 * L.N3 * L.N2);
-    L.o_w4 = take(L.tail ? 0 : 8 * L.N4 * L.N3);
-    L.o_wt = take(L.tail ? 16 * L.Kt : 0);
-    L.o_vec = take(4 * (L.N1 + 2 * L.N2 + L.N3 + L.N4));
+    L.o_w0 = off;
+    off += up1k(8 * L.N0 * L.Kx);
+    L.o_w1 = off;
+    off += up1k(8 * L.N1 * L.K1);
+    L.o_w2 = off;
+    off += up1k((L.tail && !z.Cp) ? 0 : 8 * L.N2 * L.N1);
+    L.o_w3 = off;
+    off += up1k(8 * L.N3 * L.N2);
+    L.o_w4 = off;
+    off += up1k(L.tail ? 0 : 8 * L.N4 * L.N3);
+    L.o_wt = off;
+    off += up1k(L.tail ? 16 * L.Kt : 0);
+    L.o_vec = off;
+    off += up1k(4 * (L.N1 + 2 * L.N2 + L.N3 + L.N4));
     // per group: x stash padded to the rows stage 1 reads, s stash padded to N0 rows; the copies fill the
     // first Cx / Cs rows, the padding rows are zeroed once so the reads need no per-channel guard
-    L.stash_bytes = up1k((L.Kx > L.RX ? L.Kx : L.RX) * TP * 4) + up1k(L.N0 * TP * 4);
+    L.stash_bytes = up1k(cmax(L.Kx, L.RX) * TP * 4) + up1k(L.N0 * TP * 4);
     L.o_stash = off;
     off += groups * L.stash_bytes;
     L.o_bar = off;
@@ -852,23 +864,17 @@ bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, 
     return true;
 }
 
-// the layout with the most groups, then the widest chunks (fewest MMA round trips).  NOP_CHAIN_MAX_GROUPS
-// (1..4, read at every call) caps the group count, for A/B timing of fewer tiles in flight with wider
-// chunks against more tiles in flight with narrower ones.
-bool plan_layout(const Sizes& z, Layout* out) {
-    int max_groups = MAX_GROUPS;
-    if (const char* e = std::getenv("NOP_CHAIN_MAX_GROUPS")) {
-        const int v = std::atoi(e);
-        if (v >= 1 && v <= MAX_GROUPS) max_groups = v;
-    }
+// the layout with the most groups (at most max_groups), then the widest chunks (fewest MMA round trips);
+// the gate's x stays in tensor memory unless dropping it buys another group (it is then re-read from
+// L2, where the tile's copy left it)
+constexpr bool plan_layout_upto(const Sizes& z, int max_groups, Layout* out) {
     const int N1 = up16(z.Ch), N3 = z.Cp ? up16(z.Cp) : 16;
-    int opts1[4], n1 = 0, opts3[4], n3 = 0;
-    for (int c : {N1, 64, 32, 16})
-        if (c == N1 || (c < N1 && N1 % c == 0)) opts1[n1++] = c;
-    for (int c : {N3, 64, 32, 16})
-        if (c == N3 || (c < N3 && N3 % c == 0)) opts3[n3++] = c;
-    // the gate's x stays in tensor memory unless dropping it buys another group (it is then re-read
-    // from L2, where the tile's copy left it)
+    const int cand[3] = {64, 32, 16};
+    int opts1[4] = {N1, 0, 0, 0}, n1 = 1, opts3[4] = {N3, 0, 0, 0}, n3 = 1;
+    for (int i = 0; i < 3; ++i) {
+        if (cand[i] < N1 && N1 % cand[i] == 0) opts1[n1++] = cand[i];
+        if (cand[i] < N3 && N3 % cand[i] == 0) opts3[n3++] = cand[i];
+    }
     for (int groups = max_groups; groups >= 1; --groups)
         for (int gg = 0; gg < (z.gate ? 2 : 1); ++gg)
             for (int i = 0; i < n1; ++i)
@@ -876,6 +882,57 @@ bool plan_layout(const Sizes& z, Layout* out) {
                     if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, gg == 1, out)) return true;
     return false;
 }
+
+// plan_layout_upto with MAX_GROUPS, or the cap in NOP_CHAIN_MAX_GROUPS (1..5, read at every call) for
+// A/B timing of fewer tiles in flight with wider chunks against more tiles in flight with narrower ones
+bool plan_layout(const Sizes& z, Layout* out) {
+    int max_groups = MAX_GROUPS;
+    if (const char* e = std::getenv("NOP_CHAIN_MAX_GROUPS")) {
+        const int v = std::atoi(e);
+        if (v >= 1 && v <= MAX_GROUPS) max_groups = v;
+    }
+    return plan_layout_upto(z, max_groups, out);
+}
+
+constexpr Layout planned(const Sizes& z) {
+    Layout L{};
+    plan_layout_upto(z, MAX_GROUPS, &L);
+    return L;
+}
+
+// A layout known at compile time: every field a constant, so the kernel's loops over channels unroll
+// and its tensor- and shared-memory offsets fold into the instructions.  The chains of the FNO
+// configurations' models are instantiated this way; every other chain runs on the launch-time Layout.
+template <const Sizes& Z>
+struct FixedLayout {
+    static constexpr Layout kL = planned(Z);
+    static constexpr int Kx = kL.Kx, RX = kL.RX, gx = kL.gx, N0 = kL.N0, K1 = kL.K1, N1 = kL.N1, N2 = kL.N2,
+                         N3 = kL.N3, N4 = kL.N4, NC1 = kL.NC1, NC3 = kL.NC3, tail = kL.tail, Kt = kL.Kt,
+                         KA = kL.KA, cX = kL.cX, cC1 = kL.cC1, cH1 = kL.cH1, cC3 = kL.cC3, cH3 = kL.cH3,
+                         cA = kL.cA, cD = kL.cD, cols = kL.cols, groups = kL.groups, o_w0 = kL.o_w0,
+                         o_w1 = kL.o_w1, o_w2 = kL.o_w2, o_w3 = kL.o_w3, o_w4 = kL.o_w4, o_wt = kL.o_wt,
+                         o_vec = kL.o_vec, o_stash = kL.o_stash, stash_bytes = kL.stash_bytes, o_bar = kL.o_bar,
+                         smem = kL.smem, Cx = kL.Cx, Cs = kL.Cs, nd = kL.nd, Ch = kL.Ch, Cy = kL.Cy, Cp = kL.Cp,
+                         Co = kL.Co, act0 = kL.act0, act2 = kL.act2, gate = kL.gate;
+    __device__ static FixedLayout get(const Layout&) { return FixedLayout{}; }
+};
+
+// the launch-time layout
+struct LaunchLayout {
+    __device__ static const Layout& get(const Layout& l) { return l; }
+};
+
+// The FNO configurations' chains (hidden width 32: C1 / C5; 64: C2-C4): lifting with grid channels,
+// the inner blocks (skip stage, GELUs, gate), the last block with the projection fused.
+constexpr Sizes kLift3dH32{3, 0, 3, 64, 32, 0, 0, 0, 0, 0};
+constexpr Sizes kLift1dH32{1, 0, 1, 64, 32, 0, 0, 0, 0, 0};
+constexpr Sizes kLift2dH64{1, 0, 2, 128, 64, 0, 0, 0, 0, 0};
+constexpr Sizes kBlockH32{32, 32, 0, 16, 32, 0, 0, 1, 1, 1};
+constexpr Sizes kBlockH64{64, 64, 0, 32, 64, 0, 0, 1, 1, 1};
+constexpr Sizes kLastProj3H32{32, 32, 0, 16, 32, 64, 3, 1, 0, 0};
+constexpr Sizes kLastProj1H32{32, 32, 0, 16, 32, 64, 1, 1, 0, 0};
+constexpr Sizes kLastH64{64, 64, 0, 32, 64, 0, 0, 1, 0, 0};
+constexpr Sizes kProj1H64{64, 0, 0, 128, 1, 0, 0, 0, 0, 0};
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -932,6 +989,8 @@ int32_t check_desc(const nop_chain_desc* d, Sizes* z, int64_t* P) {
     z->Cp = d->proj_hidden;
     z->Co = d->proj_hidden ? d->proj_out : 0;
     z->gate = d->gate ? 1 : 0;
+    z->act0 = d->act_skip ? 1 : 0;
+    z->act2 = d->act_out ? 1 : 0;
     return NOP_OK;
 }
 
@@ -975,16 +1034,6 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
     p.P = P;
     p.tps = ceil_div(P, chain::TP);
     p.tiles = d->batch * p.tps;
-    p.Cx = z.Cx;
-    p.Cs = z.Cs;
-    p.nd = z.nd;
-    p.Ch = z.Ch;
-    p.Cy = z.Cy;
-    p.Cp = z.Cp;
-    p.Co = z.Co;
-    p.act0 = d->act_skip ? 1 : 0;
-    p.act2 = d->act_out ? 1 : 0;
-    p.gate = z.gate;
     for (int j = 0; j < NOP_MAX_DIMS; ++j) {
         p.sp[j] = j < d->ndim ? d->spatial[j] : 1;
         p.goff[j] = j < d->ndim ? d->grid_offset[j] : 0;
@@ -1027,12 +1076,32 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
         NOP_CUDA_TRY(cudaGetLastError());
         return NOP_OK;
     };
-    switch (L.groups) {
-        case 5: rc = launch(chain::k_chain<5>); break;
-        case 4: rc = launch(chain::k_chain<4>); break;
-        case 3: rc = launch(chain::k_chain<3>); break;
-        case 2: rc = launch(chain::k_chain<2>); break;
-        default: rc = launch(chain::k_chain<1>); break;
+    // a configuration layout compiled as constants when the planned layout is exactly it
+    bool fixed = false;
+    auto try_fixed = [&](auto tag) {
+        using F = decltype(tag);
+        if (fixed || std::memcmp(&L, &F::kL, sizeof(chain::Layout)) != 0) return;
+        fixed = true;
+        rc = launch(chain::k_chain<F::groups, F>);
+    };
+    try_fixed(chain::FixedLayout<chain::kBlockH32>{});
+    try_fixed(chain::FixedLayout<chain::kLift3dH32>{});
+    try_fixed(chain::FixedLayout<chain::kLastProj3H32>{});
+    try_fixed(chain::FixedLayout<chain::kLift1dH32>{});
+    try_fixed(chain::FixedLayout<chain::kLastProj1H32>{});
+    try_fixed(chain::FixedLayout<chain::kBlockH64>{});
+    try_fixed(chain::FixedLayout<chain::kLift2dH64>{});
+    try_fixed(chain::FixedLayout<chain::kLastH64>{});
+    try_fixed(chain::FixedLayout<chain::kProj1H64>{});
+    if (!fixed) {
+        using D = chain::LaunchLayout;
+        switch (L.groups) {
+            case 5: rc = launch(chain::k_chain<5, D>); break;
+            case 4: rc = launch(chain::k_chain<4, D>); break;
+            case 3: rc = launch(chain::k_chain<3, D>); break;
+            case 2: rc = launch(chain::k_chain<2, D>); break;
+            default: rc = launch(chain::k_chain<1, D>); break;
+        }
     }
     if (rc != NOP_OK) return rc;
     return NOP_OK;
