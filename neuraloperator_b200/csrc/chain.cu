@@ -86,6 +86,7 @@ struct Layout {
     int smem;
     int Cx, Cs, nd, Ch, Cy, Cp, Co;  // real channel counts (Co: rows of W4)
     int act0, act2, gate;            // activation after the skip stage / after fc2, soft-gating skip
+    int wide;                        // two MMAs per K step instead of three (see layer_mma)
 };
 
 __host__ __device__ inline uint32_t idesc_tf32(int N) {
@@ -207,15 +208,35 @@ __device__ __forceinline__ void mma_ts_acc(uint32_t d, uint32_t a, uint64_t b, u
 // both weight descriptors are built once and stepped through the K steps by adding to their address
 // field (shared-memory byte address / 16 in the low 14 bits; the images stay below 256 KB, so the add
 // never carries out of the field).
+// `wide`: the weight image holds, per chunk of N rows, the N hi rows followed by the N lo rows (2 Nfull
+// rows in all), and each K step is two MMAs instead of three: A_hi [W_hi | W_lo] into D columns
+// d .. d + 2N, then A_lo W_hi accumulated into d .. d + N.  The layer's result is then the sum of the two
+// column halves (ld_acc16), the same three products for two thirds of the MMA issue cost.
 __device__ __forceinline__ void layer_mma(uint32_t tb, int a, int lo_off, int K, uint32_t w_hi, uint32_t w_lo,
-                                          int Nfull, int row0, int ks0, int d, int N, bool acc) {
+                                          int Nfull, int row0, int ks0, int d, int N, bool acc, bool wide) {
+    const uint32_t td = tb + (uint32_t)d;
+    uint32_t ta = tb + (uint32_t)a;
+    const int nk = K / 8;
+    if (wide) {
+        const uint32_t id2 = idesc_tf32(2 * N), id1 = idesc_tf32(N);
+        const uint32_t boff = (uint32_t)(ks0 * 2 * Nfull * 32 + ((2 * row0) >> 3) * 256);
+        uint64_t b = tc::smem_desc(w_hi + boff);
+        const uint64_t step = (uint64_t)((2 * Nfull * 32) >> 4);
+        if (acc) mma_ts_acc(td, ta, b, id2);
+        else mma_ts(td, ta, b, id2, 0u);
+        mma_ts_acc(td, ta + (uint32_t)lo_off, b, id1);
+        for (int ks = 1; ks < nk; ++ks) {
+            b += step;
+            ta += 8;
+            mma_ts_acc(td, ta, b, id2);
+            mma_ts_acc(td, ta + (uint32_t)lo_off, b, id1);
+        }
+        return;
+    }
     const uint32_t idesc = idesc_tf32(N);
     const uint32_t boff = (uint32_t)(ks0 * Nfull * 32 + (row0 >> 3) * 256);
     uint64_t bh = tc::smem_desc(w_hi + boff), bl = tc::smem_desc(w_lo + boff);
     const uint64_t step = (uint64_t)((Nfull * 32) >> 4);
-    const uint32_t td = tb + (uint32_t)d;
-    uint32_t ta = tb + (uint32_t)a;
-    const int nk = K / 8;
     if (acc) mma_ts_acc(td, ta, bh, idesc);
     else mma_ts(td, ta, bh, idesc, 0u);
     mma_ts_acc(td, ta, bl, idesc);
@@ -227,6 +248,26 @@ __device__ __forceinline__ void layer_mma(uint32_t tb, int a, int lo_off, int K,
         mma_ts_acc(td, ta, bh, idesc);
         mma_ts_acc(td, ta, bl, idesc);
         mma_ts_acc(td, ta + (uint32_t)lo_off, bh, idesc);
+    }
+}
+
+// 16 accumulator columns col + c0 .. of a layer's result: with `half` > 0 (wide layers) the sum of the
+// two column halves, half columns apart
+__device__ __forceinline__ void ld_acc16(uint32_t col, int half, int c0, float (&v)[16]) {
+    tmem_ld16(col + (uint32_t)c0, v);
+    if (half) {
+        float w[16];
+        tmem_ld16(col + (uint32_t)(half + c0), w);
+        tmem_wait_ld(v);
+        tmem_wait_ld(w);
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const float2 q = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(w[j], w[j + 1]));
+            v[j] = q.x;
+            v[j + 1] = q.y;
+        }
+    } else {
+        tmem_wait_ld(v);
     }
 }
 
@@ -244,8 +285,10 @@ __device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
-// K-major hi / lo images of W [rows x cols] (row-major, out x in) padded with zeros to N x K
-__device__ void load_weight(char* sm, int off, const float* w, int rows, int cols, int N, int K) {
+// K-major hi / lo images of W [rows x cols] (row-major, out x in) padded with zeros to N x K: two N-row
+// images (hi, then lo), or with `wide` one 2N-row image whose chunks of C rows are hi rows followed by
+// the same rows' lo parts (layer_mma)
+__device__ void load_weight(char* sm, int off, const float* w, int rows, int cols, int N, int K, int C, bool wide) {
     if (N == 0) return;
     float* hi = reinterpret_cast<float*>(sm + off);
     float* lo = reinterpret_cast<float*>(sm + off + 4 * N * K);
@@ -253,9 +296,16 @@ __device__ void load_weight(char* sm, int off, const float* w, int rows, int col
         const int n = e / K, k = e % K;
         const float v = (n < rows && k < cols) ? __ldg(w + (int64_t)n * cols + k) : 0.f;
         const float h = tc::tf32_round(v);
-        const uint32_t o = kmaj_off(n, k, N) / 4;
-        hi[o] = h;
-        lo[o] = tc::tf32_round(v - h);
+        if (wide) {
+            const int r = (n / C) * 2 * C + n % C;
+            float* img = reinterpret_cast<float*>(sm + off);
+            img[kmaj_off(r, k, 2 * N) / 4] = h;
+            img[kmaj_off(r + C, k, 2 * N) / 4] = tc::tf32_round(v - h);
+        } else {
+            const uint32_t o = kmaj_off(n, k, N) / 4;
+            hi[o] = h;
+            lo[o] = tc::tf32_round(v - h);
+        }
     }
 }
 
@@ -374,11 +424,11 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     }
     // weights and vectors, once per CTA
     const int K1r = L.Cs ? L.Cs : L.Cx + L.nd;
-    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx);
-    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1);
-    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1);
-    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2);
-    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3);
+    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx, L.N0, L.wide);
+    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1, L.NC1, L.wide);
+    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1, L.N2, L.wide);
+    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2, L.NC3, L.wide);
+    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3, L.N4, L.wide);
     if (L.tail) {  // fp32 [4][Kt], rows past the outputs and columns past the hidden width zero
         float* wt = reinterpret_cast<float*>(sm + L.o_wt);
         const float* src = L.Cp ? p.w4 : p.w2;
@@ -557,9 +607,9 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 ++x_pending;
             }
             if (L.N0)
-                layer_mma(tb, L.cA, L.KA, L.Kx, s_w0, s_w0 + lo0, L.N0, 0, 0, L.cD, L.N0, false);
+                layer_mma(tb, L.cA, L.KA, L.Kx, s_w0, s_w0 + lo0, L.N0, 0, 0, L.cD, L.N0, false, L.wide);
             else
-                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false);
+                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false, L.wide);
         }
         commit_wait(L.N0 > 0);
 
@@ -567,8 +617,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         if (L.N0) {
             for (int c0 = 0; c0 < L.N0; c0 += 16) {
                 float v[16];
-                tmem_ld16(tl + L.cD + c0, v);
-                tmem_wait_ld(v);
+                ld_acc16(tl + L.cD, L.wide ? L.N0 : 0, c0, v);
 #pragma unroll
                 for (int j = 0; j < 16; j += 2) {
                     const int c = c0 + j;  // channels past Cs (padding) add 0
@@ -588,7 +637,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                     issue_s(nt);
                     ++s_pending;
                 }
-                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false);
+                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false, L.wide);
             }
             commit_wait(false);
         }
@@ -600,8 +649,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             float2 acc[4] = {};
             for (int c0 = 0; c0 < L.N1; c0 += 16) {
                 float v[16];
-                tmem_ld16(tl + L.cD + c0, v);
-                tmem_wait_ld(v);
+                ld_acc16(tl + L.cD, L.wide ? L.N1 : 0, c0, v);
                 add16(v, vb1 + c0);
                 gelu16(v);
                 tail_acc16(acc, wt, L.Kt, c0, v);
@@ -626,8 +674,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             const int dlo = ch1 ? L.NC1 : L.KA;
             for (int c0 = 0; c0 < L.NC1; c0 += 16) {
                 float v[16];
-                tmem_ld16(tl + src + c0, v);
-                tmem_wait_ld(v);
+                ld_acc16(tl + src, L.wide ? L.NC1 : 0, c0, v);
                 add16(v, vb1 + c * L.NC1 + c0);
                 gelu16(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
@@ -637,9 +684,9 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 break;
             }
             if (leader) {
-                layer_mma(tb, dst, dlo, L.NC1, s_w2, s_w2 + lo2, L.N2, 0, c * L.NC1 / 8, L.cD, L.N2, c > 0);
+                layer_mma(tb, dst, dlo, L.NC1, s_w2, s_w2 + lo2, L.N2, 0, c * L.NC1 / 8, L.cD, L.N2, c > 0, L.wide);
                 if (c + 1 < nch1)
-                    layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, (c + 1) * L.NC1, 0, L.cC1, L.NC1, false);
+                    layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, (c + 1) * L.NC1, 0, L.cC1, L.NC1, false, L.wide);
             }
             commit_wait(false);
         }
@@ -653,9 +700,8 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
 #pragma unroll
                 for (int j = 0; j < 16; ++j) xr[j] = (valid && c0 + j < L.Cx) ? l2::ld(xg + (int64_t)j * p.P, pol) : 0.f;
             }
-            tmem_ld16(tl + L.cD + c0, v);
             if (L.gate && !L.gx) tmem_ld16(tl + L.cX + c0, xr);
-            tmem_wait_ld(v);
+            ld_acc16(tl + L.cD, L.wide ? L.N2 : 0, c0, v);
             if (L.gate && !L.gx) tmem_wait_ld(xr);
             add16(v, vb2 + c0);
             if (L.gate) {
@@ -691,14 +737,13 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
 
         // ---- 5. projection: p = GELU(W3 y + b3) (chunks), out = W4 p + b4 ----
         if (!barrier_ok()) break;
-        if (leader) layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, 0, 0, ch3 ? L.cC3 : L.cD, L.NC3, false);
+        if (leader) layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, 0, 0, ch3 ? L.cC3 : L.cD, L.NC3, false, L.wide);
         commit_wait(false);
         if (L.tail) {  // out = W4 GELU(W3 y + b3) + b4 with W4 (<= 4 outputs) on CUDA cores
             float2 acc[4] = {};
             for (int c0 = 0; c0 < L.N3; c0 += 16) {
                 float v[16];
-                tmem_ld16(tl + L.cD + c0, v);
-                tmem_wait_ld(v);
+                ld_acc16(tl + L.cD, L.wide ? L.N3 : 0, c0, v);
                 add16(v, vb3 + c0);
                 gelu16(v);
                 tail_acc16(acc, wt, L.Kt, c0, v);
@@ -716,8 +761,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             const int dlo = ch3 ? L.NC3 : L.KA;
             for (int c0 = 0; c0 < L.NC3; c0 += 16) {
                 float v[16];
-                tmem_ld16(tl + src + c0, v);
-                tmem_wait_ld(v);
+                ld_acc16(tl + src, L.wide ? L.NC3 : 0, c0, v);
                 add16(v, vb3 + c * L.NC3 + c0);
                 gelu16(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
@@ -727,17 +771,16 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 break;
             }
             if (leader) {
-                layer_mma(tb, dst, dlo, L.NC3, s_w4, s_w4 + lo4, L.N4, 0, c * L.NC3 / 8, L.cD, L.N4, c > 0);
+                layer_mma(tb, dst, dlo, L.NC3, s_w4, s_w4 + lo4, L.N4, 0, c * L.NC3 / 8, L.cD, L.N4, c > 0, L.wide);
                 if (c + 1 < nch3)
-                    layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, (c + 1) * L.NC3, 0, L.cC3, L.NC3, false);
+                    layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, (c + 1) * L.NC3, 0, L.cC3, L.NC3, false, L.wide);
             }
             commit_wait(false);
         }
         if (broke) break;
         for (int c0 = 0; c0 < L.N4; c0 += 16) {
             float v[16];
-            tmem_ld16(tl + L.cD + c0, v);
-            tmem_wait_ld(v);
+            ld_acc16(tl + L.cD, L.wide ? L.N4 : 0, c0, v);
             if (valid) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -775,9 +818,10 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 // The layout of one chain for `groups` groups and chunk widths nc1 / nc3 (false when it does not fit).
 // constexpr: the layouts of the FNO configurations' chains are also computed at compile time, and a
 // kernel instantiated on one of them (FixedLayout) takes every size and offset as a constant.
-constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, Layout* out) {
+constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, bool wide, Layout* out) {
     Layout L{};
     L.groups = groups;
+    L.wide = wide ? 1 : 0;
     L.Cx = z.Cx;
     L.Cs = z.Cs;
     L.nd = z.nd;
@@ -809,6 +853,13 @@ constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gat
     L.NC1 = nc1;
     L.NC3 = L.N3 ? nc3 : 0;
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 && L.NC3 < L.N3;
+    const int dw = wide ? 2 : 1;  // accumulator columns per output channel
+    if (wide) {  // every MMA of 2 N columns within the instruction's N <= 256
+        const bool fc2_mma = !(L.tail && !z.Cp), fc4_mma = !L.tail;
+        if (2 * L.N0 > 256 || 2 * L.NC1 > 256 || (fc2_mma && 2 * L.N2 > 256) || 2 * L.NC3 > 256 ||
+            (fc4_mma && 2 * L.N4 > 256))
+            return false;
+    }
     int ka = cmax(L.Kx, L.N0);
     if (!ch1 && !(L.tail && !z.Cp)) ka = cmax(ka, L.N1);  // h written as A (not when fc2 runs on CUDA cores)
     if (L.N3) ka = cmax(ka, L.N2);
@@ -819,16 +870,17 @@ constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gat
     if (!L.tail) nd = cmax(nd, L.N4);
     if (!ch1) nd = cmax(nd, L.N1);
     if (L.N3 && !ch3) nd = cmax(nd, L.N3);
-    // temporary region: raw x (live until the gate) next to fc1's chunk regions; the projection's chunk
-    // regions reuse it once the gate is done
-    const int t1 = L.RX + (ch1 ? 3 * L.NC1 : 0);
-    const int t3 = ch3 ? 3 * L.NC3 : 0;
+    nd *= dw;
+    // temporary region: raw x (live until the gate) next to fc1's chunk regions (the chunk's accumulator,
+    // then its h as A hi | lo); the projection's chunk regions reuse it once the gate is done
+    const int t1 = L.RX + (ch1 ? (dw + 2) * L.NC1 : 0);
+    const int t3 = ch3 ? (dw + 2) * L.NC3 : 0;
     const int tw = up16(cmax(t1, t3));
     L.cX = 0;
     L.cC1 = L.RX;
-    L.cH1 = L.RX + L.NC1;
+    L.cH1 = L.RX + dw * L.NC1;
     L.cC3 = 0;
-    L.cH3 = L.NC3;
+    L.cH3 = dw * L.NC3;
     L.cA = tw;
     L.cD = L.cA + 2 * L.KA;
     L.cols = up16(L.cD + nd);
@@ -867,7 +919,7 @@ constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gat
 // the layout with the most groups (at most max_groups), then the widest chunks (fewest MMA round trips);
 // the gate's x stays in tensor memory unless dropping it buys another group (it is then re-read from
 // L2, where the tile's copy left it)
-constexpr bool plan_layout_upto(const Sizes& z, int max_groups, Layout* out) {
+constexpr bool plan_layout_upto(const Sizes& z, int max_groups, bool wide, Layout* out) {
     const int N1 = up16(z.Ch), N3 = z.Cp ? up16(z.Cp) : 16;
     const int cand[3] = {64, 32, 16};
     int opts1[4] = {N1, 0, 0, 0}, n1 = 1, opts3[4] = {N3, 0, 0, 0}, n3 = 1;
@@ -879,33 +931,54 @@ constexpr bool plan_layout_upto(const Sizes& z, int max_groups, Layout* out) {
         for (int gg = 0; gg < (z.gate ? 2 : 1); ++gg)
             for (int i = 0; i < n1; ++i)
                 for (int j = 0; j < (z.Cp ? n3 : 1); ++j)
-                    if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, gg == 1, out)) return true;
+                    if (layout_for(z, groups, opts1[i], z.Cp ? opts3[j] : 0, gg == 1, wide, out)) return true;
     return false;
 }
 
-// plan_layout_upto with MAX_GROUPS, or the cap in NOP_CHAIN_MAX_GROUPS (1..5, read at every call) for
-// A/B timing of fewer tiles in flight with wider chunks against more tiles in flight with narrower ones
+// The MMA form.  Wide (two MMAs per K step, layer_mma) doubles the accumulator columns, so it usually
+// costs tiles in flight; it is chosen when it keeps at least 4 groups and loses at most one: measured on
+// B200, the C5 block chain ran 4% faster wide with 4 groups than narrow with 5, while the lifting (3
+// groups against 5) and the last block with the projection (2 against 4) ran 23% and 28% slower wide,
+// and the width-64 chains (2 groups either way) 8-12% slower.  NOP_CHAIN_WIDE=0 / 1 forces the narrow /
+// wide form (read at every call, for A/B timing).
+constexpr bool plan_choice(const Sizes& z, int max_groups, int force_wide, Layout* out) {
+    Layout narrow{}, wide{};
+    const bool has_n = plan_layout_upto(z, max_groups, false, &narrow);
+    const bool has_w = plan_layout_upto(z, max_groups, true, &wide);
+    bool use_w = has_w && (!has_n || (wide.groups >= 4 && wide.groups + 1 >= narrow.groups));
+    if (force_wide == 0) use_w = false;
+    if (force_wide == 1 && has_w) use_w = true;
+    if (!use_w && !has_n) return false;
+    *out = use_w ? wide : narrow;
+    return true;
+}
+
+// plan_choice with MAX_GROUPS, or the cap in NOP_CHAIN_MAX_GROUPS (1..5, read at every call) for A/B
+// timing of fewer tiles in flight with wider chunks against more tiles in flight with narrower ones
 bool plan_layout(const Sizes& z, Layout* out) {
     int max_groups = MAX_GROUPS;
     if (const char* e = std::getenv("NOP_CHAIN_MAX_GROUPS")) {
         const int v = std::atoi(e);
         if (v >= 1 && v <= MAX_GROUPS) max_groups = v;
     }
-    return plan_layout_upto(z, max_groups, out);
+    int force = -1;
+    if (const char* e = std::getenv("NOP_CHAIN_WIDE")) force = e[0] == '0' ? 0 : 1;
+    return plan_choice(z, max_groups, force, out);
 }
 
-constexpr Layout planned(const Sizes& z) {
+constexpr Layout planned(const Sizes& z, int force_wide) {
     Layout L{};
-    plan_layout_upto(z, MAX_GROUPS, &L);
+    plan_choice(z, MAX_GROUPS, force_wide, &L);
     return L;
 }
 
-// A layout known at compile time: every field a constant, so the kernel's loops over channels unroll
-// and its tensor- and shared-memory offsets fold into the instructions.  The chains of the FNO
-// configurations' models are instantiated this way; every other chain runs on the launch-time Layout.
-template <const Sizes& Z>
+// A layout known at compile time (the planner's default choice for Z): every field a constant, so the
+// kernel's loops over channels unroll and its tensor- and shared-memory offsets fold into the
+// instructions.  The chains of the FNO configurations' models are instantiated this way; every other
+// chain (or a layout changed by the environment switches) runs on the launch-time Layout.
+template <const Sizes& Z, int W = -1>
 struct FixedLayout {
-    static constexpr Layout kL = planned(Z);
+    static constexpr Layout kL = planned(Z, W);
     static constexpr int Kx = kL.Kx, RX = kL.RX, gx = kL.gx, N0 = kL.N0, K1 = kL.K1, N1 = kL.N1, N2 = kL.N2,
                          N3 = kL.N3, N4 = kL.N4, NC1 = kL.NC1, NC3 = kL.NC3, tail = kL.tail, Kt = kL.Kt,
                          KA = kL.KA, cX = kL.cX, cC1 = kL.cC1, cH1 = kL.cH1, cC3 = kL.cC3, cH3 = kL.cH3,
@@ -913,7 +986,7 @@ struct FixedLayout {
                          o_w1 = kL.o_w1, o_w2 = kL.o_w2, o_w3 = kL.o_w3, o_w4 = kL.o_w4, o_wt = kL.o_wt,
                          o_vec = kL.o_vec, o_stash = kL.o_stash, stash_bytes = kL.stash_bytes, o_bar = kL.o_bar,
                          smem = kL.smem, Cx = kL.Cx, Cs = kL.Cs, nd = kL.nd, Ch = kL.Ch, Cy = kL.Cy, Cp = kL.Cp,
-                         Co = kL.Co, act0 = kL.act0, act2 = kL.act2, gate = kL.gate;
+                         Co = kL.Co, act0 = kL.act0, act2 = kL.act2, gate = kL.gate, wide = kL.wide;
     __device__ static FixedLayout get(const Layout&) { return FixedLayout{}; }
 };
 
