@@ -361,6 +361,51 @@ def instrumented_forward(model, x, spectral=None, grid_offset=None, grid_sizes=N
     return h, marks.spans(), [e.durations_ms() for e in spec]
 
 
+def pin_to_gpu_cpus(local):
+    """Restrict this process to the CPUs NVML reports as local to its GPU (its NUMA node), so the pinned
+    host buffers allocated next and the copy threads sit on the GPU's side of the socket.  Returns the
+    CPU count used, or None when NVML cannot tell."""
+    try:
+        import pynvml
+        props = torch.cuda.get_device_properties(local)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:  # noqa: BLE001
+        pass
+    return None
+
+
+def copy_ceiling_ms(x_host, y_dev, y_host, steps, world, stream):
+    """Per-step time of the e2e path's host traffic alone: x_host -> device and y_dev -> y_host as plain
+    cudaMemcpyAsync copies on two streams at once (every rank together), max over ranks."""
+    xd = torch.empty(tuple(x_host.shape), dtype=x_host.dtype, device=y_dev.device)
+    s_in, s_out = torch.cuda.Stream(y_dev.device), torch.cuda.Stream(y_dev.device)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        with torch.cuda.stream(s_in):
+            xd.copy_(x_host, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            y_host.copy_(y_dev, non_blocking=True)
+        stream.wait_stream(s_in)
+        stream.wait_stream(s_out)
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(a.elapsed_time(b) / steps, world)
+
+
 def run_model(args, world, rank, local):
     """FNO / TFNO forward (grid embedding + lifting, 4 FNO blocks, projection) at the configuration's full
     size.  N = 1: the whole batch on one GPU.  N > 1: the 3D configuration is slab-decomposed along x
@@ -449,8 +494,9 @@ def run_model(args, world, rank, local):
         del y_i
 
         # ---- end to end through the public API: pinned host input, pinned host output ----
-        ms_e2e, e2e_how, h2d, d2h = float("nan"), None, 0, 0
+        ms_e2e, e2e_how, h2d, d2h, ms_copy, numa = float("nan"), None, 0, 0, float("nan"), None
         if not args.no_e2e:
+            numa = pin_to_gpu_cpus(local)  # pinned buffers and copy threads on the GPU's own CPUs / node
             x_host = x.cpu().pin_memory()
             y_host = torch.empty(tuple(y.shape), dtype=torch.float32).pin_memory()
             # chunks of at least one sample and at most a quarter of the batch: a 256^3 sample (2 GB of
@@ -473,6 +519,7 @@ def run_model(args, world, rank, local):
             barrier(world)
             ms_e2e = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
             h2d, d2h = x_host.numel() * 4, y_host.numel() * 4
+            ms_copy = copy_ceiling_ms(x_host, y, y_host, e2e_steps, world, stream)
             e2e_how = (f"{'SlabFNO' if slab else cls}.forward_host: {batch // chunk} chunks of {chunk} sample(s) on 2 "
                        f"streams, pinned host buffers; output equal to the device forward: {ok_e2e}")
 
@@ -553,7 +600,14 @@ def run_model(args, world, rank, local):
         "kernels": klist,
         "instrumented_forward_matches_timed": same,
         "e2e": ({"value": gbatch / (ms_e2e / 1e3), "unit": "samples/s", "h2d_bytes_per_step": h2d,
-                 "d2h_bytes_per_step": d2h, "path": e2e_how} if not args.no_e2e else None),
+                 "d2h_bytes_per_step": d2h, "path": e2e_how,
+                 "copy_only": gbatch / (ms_copy / 1e3),
+                 "ceiling": min(gbatch / (ms_copy / 1e3), gbatch / (ms / 1e3)),
+                 "frac_of_ceiling": (gbatch / (ms_e2e / 1e3)) / min(gbatch / (ms_copy / 1e3), gbatch / (ms / 1e3)),
+                 "host_cpus": numa,
+                 "definition": "ceiling = min(device-resident forward, the same H2D and D2H bytes moved alone "
+                               "by cudaMemcpyAsync on two streams at once, every rank together, max over ranks)"}
+                if not args.no_e2e else None),
         "gpu_launches": launches * steps,
         "clocks": clocks.summary(),
     }
