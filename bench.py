@@ -499,9 +499,9 @@ def run_model(args, world, rank, local):
             numa = pin_to_gpu_cpus(local)  # pinned buffers and copy threads on the GPU's own CPUs / node
             x_host = x.cpu().pin_memory()
             y_host = torch.empty(tuple(y.shape), dtype=torch.float32).pin_memory()
-            # chunks of at least one sample and at most a quarter of the batch: a 256^3 sample (2 GB of
-            # activations per layer) fills the GPU alone, small 2D samples are grouped
-            chunk = max(1, batch // 4)
+            # eight chunks (at least one sample each) through the three-stage copy / forward / copy pipeline:
+            # only the first chunk's input copy and the last chunk's output copy are not hidden
+            chunk = max(1, batch // 8)
             host_call = (lambda: runner.forward_host(x_host, out=y_host, chunk=chunk, synchronize=False)) if slab else \
                 (lambda: model.forward_host(x_host, out=y_host, chunk=chunk, n_streams=2, synchronize=False))
             host_call()
@@ -520,8 +520,9 @@ def run_model(args, world, rank, local):
             ms_e2e = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
             h2d, d2h = x_host.numel() * 4, y_host.numel() * 4
             ms_copy = copy_ceiling_ms(x_host, y, y_host, e2e_steps, world, stream)
-            e2e_how = (f"{'SlabFNO' if slab else cls}.forward_host: {batch // chunk} chunks of {chunk} sample(s) on 2 "
-                       f"streams, pinned host buffers; output equal to the device forward: {ok_e2e}")
+            e2e_how = (f"{'SlabFNO' if slab else cls}.forward_host: {batch // chunk} chunks of {chunk} sample(s), "
+                       f"H2D / forward / D2H pipelined on three streams, pinned host buffers; output equal to the "
+                       f"device forward: {ok_e2e}")
 
         # ---- slab: rank 0 checks its planes against a single-GPU forward of the whole input ----
         check = None

@@ -21,6 +21,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib, ops
+from .utils import host_pipeline
 
 
 def shard_batch(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
@@ -260,8 +261,8 @@ class SlabFNO:
     def forward_host(self, x_slab: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: int = 1,
                      n_streams: int = 2, synchronize: bool = True) -> torch.Tensor:
         """``__call__`` on this rank's planes held in HOST memory, cut into chunks of ``chunk`` samples whose
-        copies in and out overlap the other chunks' kernels (every rank must make the same calls: the chunks'
-        all-to-alls pair up in order)."""
+        copies in and out overlap the other chunks' kernels (utils.host_pipeline; ``n_streams`` is ignored).
+        Every rank must make the same calls: the chunks' all-to-alls pair up in order."""
         if x_slab.is_cuda:
             raise ValueError("forward_host takes a host tensor")
         dev = next(self.model.parameters()).device
@@ -272,19 +273,7 @@ class SlabFNO:
         y = out if out is not None else torch.empty(y_shape, dtype=torch.float32, pin_memory=True)
         if y.is_cuda or tuple(y.shape) != y_shape or not y.is_contiguous():
             raise ValueError(f"out must be a contiguous host tensor of shape {y_shape}")
-        cur = torch.cuda.current_stream(dev)
-        if getattr(self, "_streams", None) is None or len(self._streams) != n_streams:
-            self._streams = [torch.cuda.Stream(dev) for _ in range(n_streams)]
-        for st in self._streams:
-            st.wait_stream(cur)
-        for k in range(batch // chunk):
-            st = self._streams[k % n_streams]
-            with torch.cuda.stream(st):
-                xd = x_slab[k * chunk:(k + 1) * chunk].to(dev, non_blocking=True)
-                yd = self(xd)
-                y[k * chunk:(k + 1) * chunk].copy_(yd, non_blocking=True)
-        for st in self._streams:
-            cur.wait_stream(st)
+        host_pipeline(self, x_slab, y, chunk, dev, self.__dict__.setdefault("_host_streams", {}))
         if synchronize:
-            cur.synchronize()
+            torch.cuda.current_stream(dev).synchronize()
         return y

@@ -21,7 +21,7 @@ from . import ops, pointwise
 from .fno_block import FNOBlocks
 from .layers import ChannelMLP, GridEmbeddingND
 from .spectral_convolution import SpectralConv
-from .utils import grad_needed
+from .utils import grad_needed, host_pipeline
 
 Number = Union[float, int]
 
@@ -179,8 +179,9 @@ class FNO(nn.Module):
     def forward_host(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, chunk: Optional[int] = None,
                      n_streams: int = 2, synchronize: bool = True) -> torch.Tensor:
         """``forward`` of a batch held in HOST memory: the batch is cut into chunks of ``chunk`` samples
-        and each chunk's host-to-device copy, forward and device-to-host copy run on one of ``n_streams``
-        streams, so the PCIe transfers of one chunk overlap the kernels of another.  ``x`` and ``out``
+        whose host-to-device copies, forwards and device-to-host copies run as a three-stage pipeline on
+        three streams (utils.host_pipeline), so the PCIe transfers in both directions overlap the kernels
+        (``n_streams`` is kept for compatibility and ignored).  ``x`` and ``out``
         are CPU tensors (page-locked for the overlap; the returned tensor is page-locked when ``out`` is
         None); the parameters stay on their CUDA device.  With ``synchronize=False`` the call returns once
         the work is queued on the device's current stream.  Inference only."""
@@ -197,24 +198,9 @@ class FNO(nn.Module):
         y = out if out is not None else torch.empty(y_shape, dtype=torch.float32, pin_memory=True)
         if y.is_cuda or tuple(y.shape) != y_shape or not y.is_contiguous():
             raise ValueError(f"out must be a contiguous host tensor of shape {y_shape}")
-        cur = torch.cuda.current_stream(dev)
-        streams = self.__dict__.setdefault("_nop_host_streams", {})
-        key = (dev.index, int(n_streams))
-        if key not in streams:
-            streams[key] = [torch.cuda.Stream(dev) for _ in range(int(n_streams))]
-        side = streams[key]
-        for st in side:
-            st.wait_stream(cur)
-        for k in range(batch // chunk):
-            st = side[k % len(side)]
-            with torch.cuda.stream(st):
-                xd = x[k * chunk:(k + 1) * chunk].to(dev, non_blocking=True)
-                yd = self(xd)
-                y[k * chunk:(k + 1) * chunk].copy_(yd, non_blocking=True)
-        for st in side:
-            cur.wait_stream(st)
+        host_pipeline(self, x, y, chunk, dev, self.__dict__.setdefault("_nop_host_streams", {}))
         if synchronize:
-            cur.synchronize()
+            torch.cuda.current_stream(dev).synchronize()
         return y
 
     @property

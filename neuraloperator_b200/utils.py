@@ -1,5 +1,5 @@
 """Host utilities mirroring neuralop.utils: scaling-factor validation, parameter count, and the test
-for whether autograd will record a call."""
+for whether autograd will record a call; the host-memory pipeline of the models' forward_host."""
 
 from __future__ import annotations
 
@@ -41,3 +41,46 @@ def grad_needed(x: torch.Tensor, module: torch.nn.Module) -> bool:
 def count_model_params(model) -> int:
     """Parameter count with complex entries counted twice (neuralop/utils.py:19-28)."""
     return sum(p.numel() * 2 if p.is_complex() else p.numel() for p in model.parameters())
+
+
+def host_pipeline(fn, x: torch.Tensor, y: torch.Tensor, chunk: int, dev: torch.device, streams: dict,
+                  n_buffers: int = 2) -> None:
+    """y[k] = fn(x[k]) for the chunks of ``chunk`` samples of the pinned host tensors x / y, as a
+    three-stage pipeline on three streams: host-to-device copies (running ahead by ``n_buffers`` chunks),
+    ``fn`` on the device copies, device-to-host copies.  Chunk k's input copy overlaps chunk k - 1's
+    kernels and chunk k - 2's output copy, so only the first input and the last output copy are not
+    hidden.  Work is queued on the device's current stream (the caller synchronises).  ``streams``
+    caches the three streams between calls."""
+    cur = torch.cuda.current_stream(dev)
+    key = (dev.index, "pipeline")
+    if key not in streams:
+        streams[key] = [torch.cuda.Stream(dev) for _ in range(3)]
+    s_in, s_fn, s_out = streams[key]
+    for st in (s_in, s_fn, s_out):
+        st.wait_stream(cur)
+    n = x.shape[0] // chunk
+    bufs = [torch.empty((chunk, *x.shape[1:]), dtype=x.dtype, device=dev) for _ in range(min(n_buffers, n))]
+    done_fn = []
+    for k in range(n):
+        b = bufs[k % len(bufs)]
+        with torch.cuda.stream(s_in):
+            if k >= len(bufs):
+                s_in.wait_event(done_fn[k - len(bufs)])  # the kernels reading this buffer are done
+            b.copy_(x[k * chunk:(k + 1) * chunk], non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(s_in)
+        with torch.cuda.stream(s_fn):
+            s_fn.wait_event(ready)
+            yd = fn(b)
+            ev = torch.cuda.Event()
+            ev.record(s_fn)
+            done_fn.append(ev)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev)
+            y[k * chunk:(k + 1) * chunk].copy_(yd, non_blocking=True)
+            yd.record_stream(s_out)
+    for b in bufs:
+        b.record_stream(s_in)
+        b.record_stream(s_fn)
+    for st in (s_in, s_fn, s_out):
+        cur.wait_stream(st)

@@ -130,3 +130,19 @@ def test_host_forward_argument_errors():
                                        ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(workspace.data_ptr()),
                                        size.value - 256, 2, None)
     assert rc == NOP_E_WORKSPACE
+
+
+@pytest.mark.parametrize("chunk", [1, 2, 3, 6])
+def test_fno_forward_host_matches_device(chunk):
+    """FNO.forward_host (three-stage copy / forward / copy pipeline over chunks of the batch) returns
+    exactly the device forward, for every chunk size, into a caller-owned pinned output."""
+    import neuraloperator_b200 as nb
+    torch.manual_seed(0)
+    model = nb.FNO(n_modes=(8, 8), in_channels=1, out_channels=1, hidden_channels=32, n_layers=4).cuda().eval()
+    x = torch.randn(6, 1, 64, 64)
+    with torch.no_grad():
+        ref = model(x.cuda()).cpu()
+        out = torch.full((6, 1, 64, 64), float("nan")).pin_memory()
+        y = model.forward_host(x.pin_memory(), out=out, chunk=chunk)
+    assert y.data_ptr() == out.data_ptr()
+    assert torch.equal(y, ref)
