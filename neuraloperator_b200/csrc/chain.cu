@@ -936,16 +936,19 @@ constexpr bool plan_layout_upto(const Sizes& z, int max_groups, bool wide, Layou
 }
 
 // The MMA form.  Wide (two MMAs per K step, layer_mma) doubles the accumulator columns, so it usually
-// costs tiles in flight; it is chosen when it keeps at least 4 groups and loses at most one: measured on
-// B200, the C5 block chain ran 4% faster wide with 4 groups than narrow with 5, while the lifting (3
-// groups against 5) and the last block with the projection (2 against 4) ran 23% and 28% slower wide,
-// and the width-64 chains (2 groups either way) 8-12% slower.  NOP_CHAIN_WIDE=0 / 1 forces the narrow /
-// wide form (read at every call, for A/B timing).
-constexpr bool plan_choice(const Sizes& z, int max_groups, int force_wide, Layout* out) {
+// costs tiles in flight; it is chosen for large problems when it keeps at least 4 groups and loses at
+// most one.  Measured on B200: the C5 block chain (1M tiles) ran 4% faster wide with 4 groups than narrow
+// with 5, while the C1 block chain (2048 tiles, 14 per SM) ran 54% slower wide (fewer tiles per round
+// leave a larger last round); the lifting (3 groups against 5) and the last block with the projection
+// (2 against 4) ran 23% and 28% slower wide, and the width-64 chains (2 groups either way) 8-12% slower.
+// NOP_CHAIN_WIDE=0 / 1 forces the narrow / wide form (read at every call, for A/B timing).
+constexpr int64_t kWideMinTiles = 148 * 64;
+
+constexpr bool plan_choice(const Sizes& z, int max_groups, int force_wide, int64_t tiles, Layout* out) {
     Layout narrow{}, wide{};
     const bool has_n = plan_layout_upto(z, max_groups, false, &narrow);
     const bool has_w = plan_layout_upto(z, max_groups, true, &wide);
-    bool use_w = has_w && (!has_n || (wide.groups >= 4 && wide.groups + 1 >= narrow.groups));
+    bool use_w = has_w && (!has_n || (tiles >= kWideMinTiles && wide.groups >= 4 && wide.groups + 1 >= narrow.groups));
     if (force_wide == 0) use_w = false;
     if (force_wide == 1 && has_w) use_w = true;
     if (!use_w && !has_n) return false;
@@ -955,7 +958,7 @@ constexpr bool plan_choice(const Sizes& z, int max_groups, int force_wide, Layou
 
 // plan_choice with MAX_GROUPS, or the cap in NOP_CHAIN_MAX_GROUPS (1..5, read at every call) for A/B
 // timing of fewer tiles in flight with wider chunks against more tiles in flight with narrower ones
-bool plan_layout(const Sizes& z, Layout* out) {
+bool plan_layout(const Sizes& z, int64_t tiles, Layout* out) {
     int max_groups = MAX_GROUPS;
     if (const char* e = std::getenv("NOP_CHAIN_MAX_GROUPS")) {
         const int v = std::atoi(e);
@@ -963,20 +966,21 @@ bool plan_layout(const Sizes& z, Layout* out) {
     }
     int force = -1;
     if (const char* e = std::getenv("NOP_CHAIN_WIDE")) force = e[0] == '0' ? 0 : 1;
-    return plan_choice(z, max_groups, force, out);
+    return plan_choice(z, max_groups, force, tiles, out);
 }
 
-constexpr Layout planned(const Sizes& z, int force_wide) {
+// the layout of Z in the given MMA form (falling back to narrow where no wide layout fits)
+constexpr Layout planned(const Sizes& z, int wide) {
     Layout L{};
-    plan_choice(z, MAX_GROUPS, force_wide, &L);
+    plan_choice(z, MAX_GROUPS, wide, 0, &L);
     return L;
 }
 
-// A layout known at compile time (the planner's default choice for Z): every field a constant, so the
+// A layout known at compile time (Z in MMA form W): every field a constant, so the
 // kernel's loops over channels unroll and its tensor- and shared-memory offsets fold into the
 // instructions.  The chains of the FNO configurations' models are instantiated this way; every other
 // chain (or a layout changed by the environment switches) runs on the launch-time Layout.
-template <const Sizes& Z, int W = -1>
+template <const Sizes& Z, int W>
 struct FixedLayout {
     static constexpr Layout kL = planned(Z, W);
     static constexpr int Kx = kL.Kx, RX = kL.RX, gx = kL.gx, N0 = kL.N0, K1 = kL.K1, N1 = kL.N1, N2 = kL.N2,
@@ -1080,7 +1084,7 @@ int32_t nop_chain_query(const nop_chain_desc* d, int32_t* groups) {
     int32_t rc = chain::check_desc(d, &z, &P);
     if (rc != NOP_OK) return rc;
     chain::Layout L;
-    if (!chain::plan_layout(z, &L))
+    if (!chain::plan_layout(z, d->batch * ceil_div(P, chain::TP), &L))
         return fail(NOP_E_UNSUPPORTED, "weights and tiles exceed the tensor or shared memory of a CTA");
     if (groups) *groups = L.groups;
     return NOP_OK;
@@ -1093,7 +1097,7 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
     if (rc != NOP_OK) return rc;
     if (!o) return fail(NOP_E_INVALID, "operands are NULL");
     chain::Layout L;
-    if (!chain::plan_layout(z, &L))
+    if (!chain::plan_layout(z, d->batch * ceil_div(P, chain::TP), &L))
         return fail(NOP_E_UNSUPPORTED, "weights and tiles exceed the tensor or shared memory of a CTA");
     if (d->batch == 0) return NOP_OK;
     if (!o->x || !o->w1 || !o->w2 || !o->y) return fail(NOP_E_INVALID, "x, w1, w2 and y must be non-NULL");
@@ -1157,15 +1161,16 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
         fixed = true;
         rc = launch(chain::k_chain<F::groups, F>);
     };
-    try_fixed(chain::FixedLayout<chain::kBlockH32>{});
-    try_fixed(chain::FixedLayout<chain::kLift3dH32>{});
-    try_fixed(chain::FixedLayout<chain::kLastProj3H32>{});
-    try_fixed(chain::FixedLayout<chain::kLift1dH32>{});
-    try_fixed(chain::FixedLayout<chain::kLastProj1H32>{});
-    try_fixed(chain::FixedLayout<chain::kBlockH64>{});
-    try_fixed(chain::FixedLayout<chain::kLift2dH64>{});
-    try_fixed(chain::FixedLayout<chain::kLastH64>{});
-    try_fixed(chain::FixedLayout<chain::kProj1H64>{});
+    try_fixed(chain::FixedLayout<chain::kBlockH32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLift3dH32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLastProj3H32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLift1dH32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLastProj1H32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kBlockH64, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLift2dH64, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLastH64, 0>{});
+    try_fixed(chain::FixedLayout<chain::kProj1H64, 0>{});
+    try_fixed(chain::FixedLayout<chain::kBlockH32, 1>{});  // the one chain the planner runs wide
     if (!fixed) {
         using D = chain::LaunchLayout;
         switch (L.groups) {

@@ -148,7 +148,7 @@ def test_chain_rejects_points_not_multiple_of_4():
 
 
 @pytest.mark.parametrize("name, kw, groups", [
-    ("block_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True), 4),
+    ("block_h32", dict(cx=32, hidden=16, cout=32, skip=32, gate=True), 5),
     ("block_h64", dict(cx=64, hidden=32, cout=64, skip=64, gate=True), 2),
     ("lifting_3d_h32", dict(cx=3, hidden=64, cout=32, grid=[(0.0, 1 / 256)] * 3), 5),
     ("lifting_2d_h64", dict(cx=1, hidden=128, cout=64, grid=[(0.0, 1 / 512)] * 2), 4),
@@ -163,12 +163,14 @@ def test_chain_planner_tiles_in_flight(name, kw, groups):
 
 
 def test_chain_planner_mma_form(monkeypatch):
-    """The C5 block chain runs in the wide MMA form (two MMAs per K step) with 4 tiles in flight; forced
-    narrow it keeps 5, and the lifting stays narrow with 5 (wide would leave 3)."""
+    """The C5 block chain (8 x 256^3 points) runs in the wide MMA form (two MMAs per K step) with 4 tiles
+    in flight; a small problem (2 x 64^3) and a forced-narrow one keep 5, and the lifting stays narrow
+    with 5 (wide would leave 3)."""
     from neuraloperator_b200 import pointwise
-    block = pointwise.make_desc(2, (64,) * 3, 32, 16, 32, skip=32, gate=True)
-    lifting = pointwise.make_desc(2, (64,) * 3, 3, 64, 32, grid=[(0.0, 1 / 256)] * 3)
-    assert pointwise.query(block) == 4 and pointwise.query(lifting) == 5
+    block = pointwise.make_desc(8, (256,) * 3, 32, 16, 32, skip=32, gate=True)
+    small = pointwise.make_desc(2, (64,) * 3, 32, 16, 32, skip=32, gate=True)
+    lifting = pointwise.make_desc(8, (256,) * 3, 3, 64, 32, grid=[(0.0, 1 / 256)] * 3)
+    assert pointwise.query(block) == 4 and pointwise.query(small) == 5 and pointwise.query(lifting) == 5
     monkeypatch.setenv("NOP_CHAIN_WIDE", "0")
     assert pointwise.query(block) == 5
     monkeypatch.setenv("NOP_CHAIN_WIDE", "1")
