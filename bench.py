@@ -499,9 +499,12 @@ def run_model(args, world, rank, local):
             numa = pin_to_gpu_cpus(local)  # pinned buffers and copy threads on the GPU's own CPUs / node
             x_host = x.cpu().pin_memory()
             y_host = torch.empty(tuple(y.shape), dtype=torch.float32).pin_memory()
-            # eight chunks (at least one sample each) through the three-stage copy / forward / copy pipeline:
-            # only the first chunk's input copy and the last chunk's output copy are not hidden
-            chunk = max(1, batch // 8)
+            # chunks through the three-stage copy / forward / copy pipeline (only the first chunk's input copy
+            # and the last chunk's output copy are not hidden): eight for samples with >= 256 MB of
+            # activations (the 3D config), four otherwise, where the forward's host-side launch time per
+            # chunk would otherwise exceed its kernels
+            per_sample = hidden * math.prod(grid) * 4
+            chunk = max(1, batch // (8 if per_sample >= (256 << 20) else 4))
             host_call = (lambda: runner.forward_host(x_host, out=y_host, chunk=chunk, synchronize=False)) if slab else \
                 (lambda: model.forward_host(x_host, out=y_host, chunk=chunk, n_streams=2, synchronize=False))
             host_call()
