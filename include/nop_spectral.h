@@ -285,6 +285,34 @@ typedef struct nop_chain_operands {
 int32_t nop_chain_query(const nop_chain_desc* desc, int32_t* groups);
 int32_t nop_chain_forward(const nop_chain_desc* desc, const nop_chain_operands* operands, void* stream);
 
+/* ---- backward of the chain (training) ---------------------------------------------------------
+ * Gradients of one chain call without the projection (proj_hidden = 0) given dL/dy: what torch autograd
+ * computes through the reference modules (linear skip, ChannelMLP with GELU, SoftGating, the GELUs,
+ * GridEmbeddingND's channels as inputs without a gradient).  The forward's intermediates are recomputed
+ * from x and s, in fp32 on CUDA cores; the weight and bias gradients are per-CTA sums over points added
+ * in a fixed order (deterministic).  Every output pointer may be NULL when that gradient is not wanted,
+ * except that the kernel always needs the operands' x, s (with skip), weights and dy.  dw* have the
+ * weights' shapes ([out, in]), db* / dg / dgb [channels]; dx [B, Cx, P], ds [B, Cs, P].  Outputs are
+ * overwritten, not accumulated.  Supported for channel counts <= 128 (nop_chain_backward_query). */
+typedef struct nop_chain_grads {
+    const float* dy;             /* dL/dy [B, out_channels, P] */
+    float* dx;
+    float* ds;
+    float* dw0;
+    float* dw1;
+    float* db1;
+    float* dw2;
+    float* db2;
+    float* dg;
+    float* dgb;
+} nop_chain_grads;
+
+/* NOP_OK when the backward takes this descriptor; *workspace_bytes (nullable) = the device workspace
+ * nop_chain_backward needs (256-byte aligned). */
+int32_t nop_chain_backward_query(const nop_chain_desc* desc, size_t* workspace_bytes);
+int32_t nop_chain_backward(const nop_chain_desc* desc, const nop_chain_operands* operands,
+                           const nop_chain_grads* grads, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- forward from host memory, copies overlapped with the kernels ---------------------------
  * The reference's SpectralConv.forward runs wherever its input lives; a serving caller that holds
  * inputs in host memory would copy the whole batch in, run, and copy the whole batch out, so the

@@ -32,7 +32,7 @@ EXPORTED_SYMBOLS = (
     "nop_spectral_forward_packed", "nop_set_launch_events", "nop_spectral_slab_plan_create",
     "nop_spectral_slab_info", "nop_spectral_slab_forward_planes", "nop_spectral_slab_modes",
     "nop_spectral_slab_inverse_planes", "nop_spectral_host_workspace_size", "nop_spectral_forward_host",
-    "nop_device_status", "nop_chain_query", "nop_chain_forward",
+    "nop_device_status", "nop_chain_query", "nop_chain_forward", "nop_chain_backward_query", "nop_chain_backward",
     "nop_spectral_spectrum_layout", "nop_spectral_forward_keep", "nop_spectral_weight_grad",
     "nop_spectral_weight_grad_workspace_size", "nop_spectral_pack_weights_adjoint",
     "nop_tucker_grads_workspace_size", "nop_tucker_grads",

@@ -109,11 +109,14 @@ class FNO(nn.Module):
         return (isinstance(mlp, ChannelMLP) and mlp.n_layers == 2 and mlp.dropout is None
                 and mlp.non_linearity is F.gelu)
 
-    def fused_plan(self, x, grid_sizes=None):
+    def fused_plan(self, x, grid_sizes=None, train_ok=True):
         """(grid, fuse_projection) when the fused forward takes x, else None.  ``grid_sizes``: the full
-        grid's sizes when x is a slab of it (the coordinate step follows the full grid)."""
+        grid's sizes when x is a slab of it (the coordinate step follows the full grid).  When autograd
+        records the call (``train_ok``), every chain must also fit the chain backward kernel and the
+        projection runs as its own chain call."""
         pe = self.positional_embedding
-        if not (x.is_cuda and x.dtype == torch.float32 and x.ndim == 2 + self.n_dim) or grad_needed(x, self):
+        train = grad_needed(x, self)
+        if not (x.is_cuda and x.dtype == torch.float32 and x.ndim == 2 + self.n_dim) or (train and not train_ok):
             return None
         if (pe is not None and not isinstance(pe, GridEmbeddingND)) or self.resolution_scaling_factor is not None:
             return None
@@ -125,16 +128,20 @@ class FNO(nn.Module):
         f1, f2 = self.lifting.fcs
         if self.lifting.in_channels != self.in_channels + (self.n_dim if pe is not None else 0):
             return None
-        if not pointwise.supported(batch, spatial, self.in_channels, f1.out_channels, f2.out_channels, grid=grid):
+        lift = (batch, spatial, self.in_channels, f1.out_channels, f2.out_channels)
+        if not pointwise.supported(*lift, grid=grid) or (train and not pointwise.backward_supported(*lift, grid=grid)):
             return None
         for i in range(self.n_layers):
-            if not (blocks._fusable(i, x, None) and blocks.chain_supported(i, batch, spatial)):
+            if not (blocks._fusable(i, x, None) and blocks.chain_supported(i, batch, spatial, backward=train)):
                 return None
         # the projection rides in the last block's kernel unless its weights would leave one tile in flight
-        fuse_proj = blocks.chain_supported(self.n_layers - 1, batch, spatial, proj=self.projection, min_groups=2)
+        # (or a gradient is recorded: the chain backward takes no projection)
+        fuse_proj = not train and blocks.chain_supported(self.n_layers - 1, batch, spatial, proj=self.projection,
+                                                         min_groups=2)
         if not fuse_proj:
             p1, p2 = self.projection.fcs
-            if not pointwise.supported(batch, spatial, self.hidden_channels, p1.out_channels, p2.out_channels):
+            proj = (batch, spatial, self.hidden_channels, p1.out_channels, p2.out_channels)
+            if not pointwise.supported(*proj) or (train and not pointwise.backward_supported(*proj)):
                 return None
         return grid, fuse_proj
 
@@ -144,7 +151,7 @@ class FNO(nn.Module):
         layer does not fit the fused kernels (the module path then runs).  ``spectral(index, conv, h)``
         replaces the blocks' spectral calls and ``grid_offset`` / ``grid_sizes`` place x in a larger grid
         (the slab-decomposed forward)."""
-        plan = self.fused_plan(x, grid_sizes)
+        plan = self.fused_plan(x, grid_sizes, train_ok=spectral is None)
         if plan is None:
             return None
         grid, fuse_proj = plan

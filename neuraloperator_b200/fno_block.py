@@ -105,7 +105,7 @@ class FNOBlocks(nn.Module):
         conv = self.convs[index]
         return (isinstance(conv, SpectralConv) and self.fno_skips is not None and self.fno_skip.lower() == "linear"
                 and self.stabilizer is None and self.non_linearity is F.gelu and output_shape is None
-                and conv.resolution_scaling_factor is None and x.is_cuda and not grad_needed(x, self))
+                and conv.resolution_scaling_factor is None and x.is_cuda)
 
     def _mlp_parts(self, index):
         """(ChannelMLP, soft-gating skip or None) of block `index` when they fit the chain kernel's form."""
@@ -118,10 +118,10 @@ class FNOBlocks(nn.Module):
             return None
         return mlp, sg
 
-    def chain_supported(self, index, batch, spatial, proj=None, min_groups=1) -> bool:
+    def chain_supported(self, index, batch, spatial, proj=None, min_groups=1, backward=False) -> bool:
         """Block `index` after its spectral convolution (and, with `proj`, the FNO projection ChannelMLP)
         fits one chain kernel call for an input of `batch` samples on a grid of `spatial` points, with at
-        least `min_groups` tiles in flight per SM."""
+        least `min_groups` tiles in flight per SM (and, with `backward`, the chain's backward kernel)."""
         parts = self._mlp_parts(index)
         if parts is None:
             return False
@@ -130,9 +130,11 @@ class FNOBlocks(nn.Module):
         kw = {}
         if proj is not None:
             kw = dict(proj_hidden=proj.fcs[0].out_channels, proj_out=proj.fcs[1].out_channels)
-        return pointwise.supported(batch, tuple(spatial), self.in_channels, mlp.hidden_channels, self.out_channels,
-                                   skip=self.out_channels, act_skip=not last, act_out=not last, gate=sg is not None,
-                                   min_groups=min_groups, **kw)
+        args = (batch, tuple(spatial), self.in_channels, mlp.hidden_channels, self.out_channels)
+        kw.update(skip=self.out_channels, act_skip=not last, act_out=not last, gate=sg is not None)
+        if backward and not pointwise.backward_supported(*args, **kw):
+            return False
+        return pointwise.supported(*args, min_groups=min_groups, **kw)
 
     def fused_block(self, x, index, spectral=None, proj=None):
         """Spectral convolution, then ONE chain kernel for the rest of the block: the linear skip added to
@@ -154,13 +156,13 @@ class FNOBlocks(nn.Module):
 
     def forward_with_postactivation(self, x, index=0, output_shape=None):
         if (self._fusable(index, x, output_shape) and x.dtype == torch.float32
-                and self.chain_supported(index, x.shape[0], x.shape[2:])):
+                and self.chain_supported(index, x.shape[0], x.shape[2:], backward=grad_needed(x, self))):
             return self.fused_block(x, index)
         last = index >= self.n_layers - 1
         if self.use_channel_mlp and self.channel_mlp_skips is not None:
             x_skip_mlp = self.channel_mlp_skips[index](x)
             x_skip_mlp = self.convs[index].transform(x_skip_mlp, output_shape=output_shape)
-        if self._fusable(index, x, output_shape):
+        if self._fusable(index, x, output_shape) and not grad_needed(x, self):  # the epilogue has no backward
             x_skip = self.fno_skips[index](x)
             x = self.convs[index](x, addend=x_skip, apply_gelu=not last)
         else:

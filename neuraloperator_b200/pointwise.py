@@ -53,9 +53,20 @@ class NopChainOperands(ctypes.Structure):
                 ("x", "s", "w0", "w1", "b1", "w2", "b2", "g", "gb", "w3", "b3", "w4", "b4", "y")]
 
 
+class NopChainGrads(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in
+                ("dy", "dx", "ds", "dw0", "dw1", "db1", "dw2", "db2", "dg", "dgb")]
+
+
 def _declare(lib):
     if getattr(lib, "_chain_declared", False):
         return
+    lib.nop_chain_backward_query.restype = ctypes.c_int32
+    lib.nop_chain_backward_query.argtypes = [ctypes.POINTER(NopChainDesc), ctypes.POINTER(ctypes.c_size_t)]
+    lib.nop_chain_backward.restype = ctypes.c_int32
+    lib.nop_chain_backward.argtypes = [ctypes.POINTER(NopChainDesc), ctypes.POINTER(NopChainOperands),
+                                       ctypes.POINTER(NopChainGrads), ctypes.c_void_p, ctypes.c_size_t,
+                                       ctypes.c_void_p]
     lib.nop_chain_query.restype = ctypes.c_int32
     lib.nop_chain_query.argtypes = [ctypes.POINTER(NopChainDesc), ctypes.POINTER(ctypes.c_int32)]
     lib.nop_chain_forward.restype = ctypes.c_int32
@@ -147,8 +158,13 @@ def chain(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: tor
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path)")
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in
                                        (x, s, w0, w1, b1, w2, b2, gate_w, gate_b, w3, b3, w4, b4)):
-        raise RuntimeError("the per-pixel chain kernel has no backward; call it under torch.no_grad() "
-                           "(the FNO modules use their torch layers whenever a gradient is needed)")
+        if w3 is not None or w4 is not None:
+            raise RuntimeError("the chain kernel's backward takes chains without the projection; run the "
+                               "projection as its own chain call when a gradient is needed")
+        if out is not None:
+            raise ValueError("out= is not supported when a gradient is recorded")
+        return _ChainFn.apply(x, s, w0, w1, b1, w2, b2, gate_w, gate_b,
+                              (bool(act_skip), bool(act_out), grid, grid_offset))
     if x.dtype != torch.float32:
         raise TypeError(f"expected float32 input, got {x.dtype}")
     x = x.contiguous()
@@ -180,3 +196,92 @@ def chain(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: tor
     with torch.cuda.device(x.device):
         _lib.check(lib.nop_chain_forward(ctypes.byref(d), ctypes.byref(ops), stream))
     return out
+
+
+def backward_supported(batch: int, spatial: Sequence[int], cx: int, hidden: int, cout: int, **kw) -> bool:
+    """Whether nop_chain_backward takes a chain of these sizes (no projection, channel counts <= 128)."""
+    if not 1 <= len(spatial) <= MAX_DIMS or kw.get("proj_hidden"):
+        return False
+    lib = _lib.library()
+    _declare(lib)
+    return lib.nop_chain_backward_query(ctypes.byref(make_desc(batch, spatial, cx, hidden, cout, **kw)), None) == \
+        _lib.NOP_OK
+
+
+def chain_backward(dy: torch.Tensor, x: torch.Tensor, w1, b1, w2, b2, *, s=None, w0=None, act_skip=False,
+                   act_out=False, gate_w=None, gate_b=None, grid=None, grid_offset=None, need=None):
+    """Gradients of one chain call (no projection) given dL/dy (nop_chain_backward): a dict with the keys
+    x, s, w0, w1, b1, w2, b2, g, gb (each [out, in] / [channels] / the activation's shape, None where not
+    applicable or not in ``need``)."""
+    x = x.detach().contiguous()
+    dy = dy.detach().contiguous().to(torch.float32)
+    spatial = tuple(x.shape[2:])
+    m0, m1, m2 = _mat(w0), _mat(w1), _mat(w2)
+    v1, v2, g, gb = _vec(b1), _vec(b2), _vec(gate_w), _vec(gate_b)
+    if s is not None:
+        s = s.detach().contiguous()
+    cy = m2.shape[0]
+    d = make_desc(x.shape[0], spatial, x.shape[1], m1.shape[0], cy, skip=0 if s is None else m0.shape[0],
+                  act_skip=act_skip, act_out=act_out, gate=g is not None, grid=grid, grid_offset=grid_offset)
+    want = set(need) if need is not None else {"x", "s", "w0", "w1", "b1", "w2", "b2", "g", "gb"}
+    dev = x.device
+    e = lambda *shape: torch.empty(shape, device=dev, dtype=torch.float32)  # noqa: E731
+    out = {
+        "x": e(*x.shape) if "x" in want else None,
+        "s": e(*s.shape) if s is not None and "s" in want else None,
+        "w0": e(*m0.shape) if m0 is not None and "w0" in want else None,
+        "w1": e(*m1.shape) if "w1" in want else None,
+        "b1": e(m1.shape[0]) if "b1" in want else None,
+        "w2": e(*m2.shape) if "w2" in want else None,
+        "b2": e(cy) if "b2" in want else None,
+        "g": e(cy) if g is not None and "g" in want else None,
+        "gb": e(cy) if gb is not None and "gb" in want else None,
+    }
+    ops = NopChainOperands()
+    for name, t in (("x", x), ("s", s), ("w0", m0), ("w1", m1), ("b1", v1), ("w2", m2), ("b2", v2), ("g", g),
+                    ("gb", gb)):
+        setattr(ops, name, None if t is None else t.data_ptr())
+    grads = NopChainGrads()
+    grads.dy = dy.data_ptr()
+    for name, key in (("dx", "x"), ("ds", "s"), ("dw0", "w0"), ("dw1", "w1"), ("db1", "b1"), ("dw2", "w2"),
+                      ("db2", "b2"), ("dg", "g"), ("dgb", "gb")):
+        t = out[key]
+        setattr(grads, name, None if t is None else t.data_ptr())
+    lib = _lib.library()
+    _declare(lib)
+    size = ctypes.c_size_t()
+    _lib.check(lib.nop_chain_backward_query(ctypes.byref(d), ctypes.byref(size)))
+    ws = torch.empty(max(int(size.value), 1), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(lib.nop_chain_backward(ctypes.byref(d), ctypes.byref(ops), ctypes.byref(grads),
+                                          ctypes.c_void_p(ws.data_ptr()), int(size.value), stream))
+    return out
+
+
+class _ChainFn(torch.autograd.Function):
+    """One chain call (no projection) under autograd: the forward is the tensor-core kernel, the backward
+    nop_chain_backward (the forward's intermediates recomputed from x and s)."""
+
+    @staticmethod
+    def forward(ctx, x, s, w0, w1, b1, w2, b2, gate_w, gate_b, cfg):
+        act_skip, act_out, grid, grid_offset = cfg
+        with torch.no_grad():
+            y = chain(x, w1, b1, w2, b2, s=s, w0=w0, act_skip=act_skip, act_out=act_out, gate_w=gate_w,
+                      gate_b=gate_b, grid=grid, grid_offset=grid_offset)
+        ctx.cfg = cfg
+        ctx.save_for_backward(x, s, w0, w1, b1, w2, b2, gate_w, gate_b)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, s, w0, w1, b1, w2, b2, gate_w, gate_b = ctx.saved_tensors
+        act_skip, act_out, grid, grid_offset = ctx.cfg
+        names = ("x", "s", "w0", "w1", "b1", "w2", "b2", "g", "gb")
+        need = [n for n, flag in zip(names, ctx.needs_input_grad[:9]) if flag]
+        g = chain_backward(gy, x, w1, b1, w2, b2, s=s, w0=w0, act_skip=act_skip, act_out=act_out, gate_w=gate_w,
+                           gate_b=gate_b, grid=grid, grid_offset=grid_offset, need=need)
+        res = []
+        for n, t in zip(names, (x, s, w0, w1, b1, w2, b2, gate_w, gate_b)):
+            res.append(None if g.get(n) is None or t is None else g[n].view(t.shape).to(t.dtype))
+        return (*res, None)
