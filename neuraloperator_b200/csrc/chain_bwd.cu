@@ -31,7 +31,8 @@
 namespace nop {
 namespace cbwd {
 
-constexpr int THREADS = 256;
+constexpr int THREADS = 512;
+constexpr int MAX_KB = 3;   // 4 x 4 weight-gradient blocks per thread (registers)
 constexpr int MAX_C = 128;  // channel counts per slot the backward takes
 constexpr int SMEM_LIMIT = 227 * 1024;
 
@@ -44,7 +45,7 @@ struct Dims {
     int act0, act2, gate, gbias, skip;
     int TP, ld;                        // points per tile, row stride (TP + 4)
     int oW0, oW1, oW2, oB1, oB2, oG, oGB;        // weights (padded, row-major [out][in]) and vectors
-    int oAcc, nAcc;                              // accumulators: dW0, dW1, dW2, db1, db2, dg
+    int nAcc;                                    // per-CTA sums: dW0, dW1, dW2, db1, db2, dg
     int aW0, aW1, aW2, aB1, aB2, aG;             // their offsets inside the accumulator block
     int oX, oU, oA0, oH, oG1, oDZ2;              // tiles ([rows][ld]); oU == oX when u is x itself
     int smem;                                    // bytes
@@ -108,11 +109,10 @@ __device__ __forceinline__ void act_gemm(const float* a, int am, int ak, const f
     }
 }
 
-// acc[m][n] += sum over the tile's points p of d[m][p] v[n][p] (d, v activation tiles of row stride ld),
-// for the 4 x 4 output block q (of M / 4 x N / 4 blocks); the accumulator row stride is N
-__device__ __forceinline__ void wgrad_block(const float* d, const float* v, int ld, int TP, int N, int q, float* acc) {
-    const int tn = N / 4;
-    const int m0 = (q / tn) * 4, n0 = (q % tn) * 4;
+// a[i][j] += sum over the tile's points p of d[m0 + i][p] v[n0 + j][p] (d, v activation tiles of row stride
+// ld): the 4 x 4 block (m0, n0) of a weight gradient
+__device__ __forceinline__ void wgrad_block(const float* d, const float* v, int ld, int TP, int m0, int n0,
+                                            float (&a)[16]) {
     float2 c[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -135,7 +135,32 @@ __device__ __forceinline__ void wgrad_block(const float* d, const float* v, int 
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[(m0 + i) * N + n0 + j] += c[i][j].x + c[i][j].y;
+        for (int j = 0; j < 4; ++j) a[i * 4 + j] += c[i][j].x + c[i][j].y;
+}
+
+// which weight gradient block q (of all three, dW0's first) is: the operand tiles, its (m0, n0), and its
+// first accumulator index (row stride N)
+struct WBlock {
+    int which, m0, n0, base, N;
+};
+
+__device__ __forceinline__ WBlock wblock(const Dims& D, int q) {
+    const int n0b = D.skip ? (D.pS / 4) * (D.pX / 4) : 0, n1b = (D.pH / 4) * (D.pK1 / 4);
+    WBlock w{};
+    int N, base;
+    if (q < n0b) {
+        w.which = 0, N = D.pX, base = D.aW0;
+    } else if ((q -= n0b) < n1b) {
+        w.which = 1, N = D.pK1, base = D.aW1;
+    } else {
+        q -= n1b;
+        w.which = 2, N = D.pH, base = D.aW2;
+    }
+    w.m0 = (q / (N / 4)) * 4;
+    w.n0 = (q % (N / 4)) * 4;
+    w.base = base;
+    w.N = N;
+    return w;
 }
 
 // sum over the tile's points of d[m][p] (and of d[m][p] v[m][p] when v is given)
@@ -172,7 +197,8 @@ __device__ void load_padded(float* dst, const float* w, int rows, int cols, int 
     }
 }
 
-__global__ void __launch_bounds__(THREADS) k_chain_bwd(Ptrs P, Dims D) {
+template <int KB>
+__global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, TP = D.TP, ld = D.ld;
     float* W0 = sm + D.oW0;
@@ -182,7 +208,6 @@ __global__ void __launch_bounds__(THREADS) k_chain_bwd(Ptrs P, Dims D) {
     float* vb2 = sm + D.oB2;
     float* vg = sm + D.oG;
     float* vgb = sm + D.oGB;
-    float* acc = sm + D.oAcc;
     float* X = sm + D.oX;
     float* U = sm + D.oU;
     float* A0 = sm + D.oA0;
@@ -196,15 +221,18 @@ __global__ void __launch_bounds__(THREADS) k_chain_bwd(Ptrs P, Dims D) {
     load_padded(vb2, P.b2, 1, D.Cy, 1, D.pY);
     load_padded(vg, D.gate ? P.g : nullptr, 1, D.Cy, 1, D.pY);
     load_padded(vgb, D.gbias ? P.gb : nullptr, 1, D.Cy, 1, D.pY);
-    for (int i = tid; i < D.nAcc; i += THREADS) acc[i] = 0.f;
+    float accw[KB][16];  // this thread's weight-gradient blocks tid, tid + THREADS, ...
+#pragma unroll
+    for (int k = 0; k < KB; ++k)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) accw[k][i] = 0.f;
+    float accv = 0.f;    // and its bias / gate entry (vector item tid)
     for (int i = D.oX + tid; i < D.smem / 4; i += THREADS) sm[i] = 0.f;  // tiles: padding rows stay zero
     __syncthreads();
 
     const int nq = TP / 4;
-    const int n0b = D.skip ? (D.pS / 4) * (D.pX / 4) : 0;
-    const int n1b = (D.pH / 4) * (D.pK1 / 4);
-    const int n2b = (D.pY / 4) * (D.pH / 4);
-    const int nwork = n0b + n1b + n2b + D.pH + D.pY + (D.gate ? D.pY : 0);
+    const int nblk = (D.skip ? (D.pS / 4) * (D.pX / 4) : 0) + (D.pH / 4) * (D.pK1 / 4) + (D.pY / 4) * (D.pH / 4);
+    const int nvec = D.pH + D.pY + (D.gate ? D.pY : 0);
     for (int64_t t = blockIdx.x; t < P.tiles; t += gridDim.x) {
         const int64_t b = t / P.tps;
         const int64_t p0 = (t - b * P.tps) * TP;
@@ -350,23 +378,35 @@ __global__ void __launch_bounds__(THREADS) k_chain_bwd(Ptrs P, Dims D) {
         }
 
         // ---- 7. weight and bias gradients over the tile's points (tiles only read from here on) ----
-        for (int q = tid; q < nwork; q += THREADS) {
-            int r = q;
-            if (r < n0b) { wgrad_block(A0, X, ld, TP, D.pX, r, acc + D.aW0); continue; }
-            r -= n0b;
-            if (r < n1b) { wgrad_block(G1, U, ld, TP, D.pK1, r, acc + D.aW1); continue; }
-            r -= n1b;
-            if (r < n2b) { wgrad_block(DZ2, H, ld, TP, D.pH, r, acc + D.aW2); continue; }
-            r -= n2b;
-            if (r < D.pH) { acc[D.aB1 + r] += row_sum(G1, nullptr, ld, TP, r); continue; }
-            r -= D.pH;
-            if (r < D.pY) { acc[D.aB2 + r] += row_sum(DZ2, nullptr, ld, TP, r); continue; }
-            r -= D.pY;
-            acc[D.aG + r] += row_sum(DZ2, X, ld, TP, r);
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const int q = tid + k * THREADS;
+            if (q >= nblk) break;
+            const WBlock w = wblock(D, q);
+            const float* dd = w.which == 0 ? A0 : w.which == 1 ? G1 : DZ2;
+            const float* vv = w.which == 0 ? X : w.which == 1 ? U : H;
+            wgrad_block(dd, vv, ld, TP, w.m0, w.n0, accw[k]);
+        }
+        if (tid < nvec) {
+            int r = tid;
+            if (r < D.pH) accv += row_sum(G1, nullptr, ld, TP, r);
+            else if ((r -= D.pH) < D.pY) accv += row_sum(DZ2, nullptr, ld, TP, r);
+            else accv += row_sum(DZ2, X, ld, TP, r - D.pY);
         }
         __syncthreads();  // the next tile overwrites the tiles
     }
-    for (int i = tid; i < D.nAcc; i += THREADS) P.part[(int64_t)blockIdx.x * D.nAcc + i] = acc[i];
+    float* part = P.part + (int64_t)blockIdx.x * D.nAcc;
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+        const int q = tid + k * THREADS;
+        if (q >= nblk) break;
+        const WBlock w = wblock(D, q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) part[w.base + (w.m0 + i) * w.N + w.n0 + j] = accw[k][i * 4 + j];
+    }
+    if (tid < nvec) part[D.aB1 + tid] = accv;  // db1, db2, dg are consecutive in the accumulator layout
 }
 
 // the gradients: per-CTA sums added in CTA order, unpadded into the callers' arrays
@@ -476,15 +516,15 @@ bool plan(const nop_chain_desc* d, Dims* out) {
     off += D.pY;
     D.oGB = off;
     off += D.pY;
-    D.oAcc = off;
     D.aW0 = 0;
     D.aW1 = D.aW0 + (D.skip ? D.pS * D.pX : 0);
     D.aW2 = D.aW1 + D.pH * D.pK1;
     D.aB1 = D.aW2 + D.pY * D.pH;
     D.aB2 = D.aB1 + D.pH;
     D.aG = D.aB2 + D.pY;
-    D.nAcc = D.aG + D.pY;
-    off += D.nAcc;
+    D.nAcc = D.aG + D.pY;  // the per-CTA sums' layout (held in registers in the kernel)
+    const int nblk = (D.skip ? (D.pS / 4) * (D.pX / 4) : 0) + (D.pH / 4) * (D.pK1 / 4) + (D.pY / 4) * (D.pH / 4);
+    if (nblk > MAX_KB * THREADS || D.pH + 2 * D.pY > THREADS) return false;
     const bool own_u = D.skip || D.nd > 0;
     const int rows = D.pX + (own_u ? D.pK1 : 0) + (D.skip ? D.pS : 0) + 2 * D.pH + D.pY;
     for (int tp = 128; tp >= 32; tp /= 2) {
@@ -580,8 +620,11 @@ int32_t nop_chain_backward(const nop_chain_desc* d, const nop_chain_operands* o,
     int dev = 0, sms = 148, per_sm = 1;
     NOP_CUDA_TRY(cudaGetDevice(&dev));
     NOP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    NOP_CUDA_TRY(cudaFuncSetAttribute(cbwd::k_chain_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, D.smem));
-    NOP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cbwd::k_chain_bwd, cbwd::THREADS, D.smem));
+    const int nblk = (D.skip ? (D.pS / 4) * (D.pX / 4) : 0) + (D.pH / 4) * (D.pK1 / 4) + (D.pY / 4) * (D.pH / 4);
+    const int kb = (int)ceil_div(nblk, cbwd::THREADS);
+    auto kernel = kb <= 1 ? cbwd::k_chain_bwd<1> : kb == 2 ? cbwd::k_chain_bwd<2> : cbwd::k_chain_bwd<3>;
+    NOP_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, D.smem));
+    NOP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, cbwd::THREADS, D.smem));
     int64_t ctas = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
     if (ctas > cbwd::MAX_CTAS) ctas = cbwd::MAX_CTAS;
     if (ctas > p.tiles) ctas = p.tiles;
@@ -591,7 +634,7 @@ int32_t nop_chain_backward(const nop_chain_desc* d, const nop_chain_operands* o,
         NOP_CUDA_TRY(cudaMemsetAsync(workspace, 0, (size_t)D.nAcc * sizeof(float), s));
         ctas = 1;
     } else {
-        cbwd::k_chain_bwd<<<(unsigned)ctas, cbwd::THREADS, D.smem, s>>>(p, D);
+        kernel<<<(unsigned)ctas, cbwd::THREADS, D.smem, s>>>(p, D);
         NOP_CUDA_TRY(cudaGetLastError());
     }
     cbwd::k_chain_bwd_reduce<<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(p.part, (int)ctas, D, outs);

@@ -17,6 +17,7 @@ callers keep the module path otherwise.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional, Sequence
 
 import torch
@@ -136,8 +137,9 @@ def supported(batch: int, spatial: Sequence[int], cx: int, hidden: int, cout: in
               **kw) -> bool:
     """Whether the kernel takes a chain of these sizes (channel counts <= 256, the weights and
     in-flight tiles fitting one CTA's tensor and shared memory, points per sample a multiple of 4) with
-    at least ``min_groups`` tiles in flight per SM."""
-    if not 1 <= len(spatial) <= MAX_DIMS:
+    at least ``min_groups`` tiles in flight per SM.  ``NOP_CHAIN=0`` in the environment (read at every
+    call) reports False, so the models run their module path (A/B timing)."""
+    if not 1 <= len(spatial) <= MAX_DIMS or os.environ.get("NOP_CHAIN") == "0":
         return False
     return query(make_desc(batch, spatial, cx, hidden, cout, **kw)) >= min_groups
 
