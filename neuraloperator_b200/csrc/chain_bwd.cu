@@ -92,14 +92,29 @@ __device__ __forceinline__ void act_gemm(const float* a, int am, int ak, const f
         for (int i = 0; i < 4; ++i) c[i][0] = c[i][1] = make_float2(0.f, 0.f);
         const float* bp = b + n0;
         const float* ap = a + m0 * am;
-#pragma unroll 4
-        for (int k = 0; k < K; ++k) {
-            const float4 bv = *reinterpret_cast<const float4*>(bp + k * ld);
+        for (int k = 0; k < K; k += 4) {  // K is a multiple of 4: 4 x 4 blocks of A and B per step
+            float av[4][4];  // av[kk][i] = A(m0 + i, k + kk)
+            if (am == 1) {   // W^T: rows m0 .. m0 + 3 are consecutive for each k
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float av = ap[i * am + k * ak];
-                c[i][0] = __ffma2_rn(make_float2(av, av), make_float2(bv.x, bv.y), c[i][0]);
-                c[i][1] = __ffma2_rn(make_float2(av, av), make_float2(bv.z, bv.w), c[i][1]);
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float4 v = *reinterpret_cast<const float4*>(ap + (k + kk) * ak);
+                    av[kk][0] = v.x, av[kk][1] = v.y, av[kk][2] = v.z, av[kk][3] = v.w;
+                }
+            } else {         // W: k .. k + 3 are consecutive in each row
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 v = *reinterpret_cast<const float4*>(ap + i * am + k);
+                    av[0][i] = v.x, av[1][i] = v.y, av[2][i] = v.z, av[3][i] = v.w;
+                }
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const float4 bv = *reinterpret_cast<const float4*>(bp + (k + kk) * ld);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    c[i][0] = __ffma2_rn(make_float2(av[kk][i], av[kk][i]), make_float2(bv.x, bv.y), c[i][0]);
+                    c[i][1] = __ffma2_rn(make_float2(av[kk][i], av[kk][i]), make_float2(bv.z, bv.w), c[i][1]);
+                }
             }
         }
         float4 r[4];
@@ -109,9 +124,10 @@ __device__ __forceinline__ void act_gemm(const float* a, int am, int ak, const f
     }
 }
 
-// a[i][j] += sum over the tile's points p of d[m0 + i][p] v[n0 + j][p] (d, v activation tiles of row stride
-// ld): the 4 x 4 block (m0, n0) of a weight gradient
-__device__ __forceinline__ void wgrad_block(const float* d, const float* v, int ld, int TP, int m0, int n0,
+// a[i][j] += sum over the tile's points p of d[m0 + i][p] v[nb + j nstep][p] (d, v activation tiles of row
+// stride ld): one 4 x 4 block of a weight gradient.  The four columns are nstep apart so that the threads
+// of a warp (consecutive nb) read consecutive rows of v: with ld / 4 odd those fall in distinct banks.
+__device__ __forceinline__ void wgrad_block(const float* d, const float* v, int ld, int TP, int m0, int nb, int nstep,
                                             float (&a)[16]) {
     float2 c[4][4];
 #pragma unroll
@@ -123,7 +139,7 @@ __device__ __forceinline__ void wgrad_block(const float* d, const float* v, int 
 #pragma unroll
         for (int i = 0; i < 4; ++i) dv[i] = *reinterpret_cast<const float4*>(d + (m0 + i) * ld + p);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) vv[j] = *reinterpret_cast<const float4*>(v + (n0 + j) * ld + p);
+        for (int j = 0; j < 4; ++j) vv[j] = *reinterpret_cast<const float4*>(v + (nb + j * nstep) * ld + p);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -138,10 +154,10 @@ __device__ __forceinline__ void wgrad_block(const float* d, const float* v, int 
         for (int j = 0; j < 4; ++j) a[i * 4 + j] += c[i][j].x + c[i][j].y;
 }
 
-// which weight gradient block q (of all three, dW0's first) is: the operand tiles, its (m0, n0), and its
-// first accumulator index (row stride N)
+// which weight gradient block q (of all three, dW0's first) is: the operand tiles, its rows m0 .. m0 + 3,
+// its columns nb + j N / 4 (j < 4), and its first accumulator index (row stride N)
 struct WBlock {
-    int which, m0, n0, base, N;
+    int which, m0, nb, base, N;
 };
 
 __device__ __forceinline__ WBlock wblock(const Dims& D, int q) {
@@ -157,7 +173,7 @@ __device__ __forceinline__ WBlock wblock(const Dims& D, int q) {
         w.which = 2, N = D.pH, base = D.aW2;
     }
     w.m0 = (q / (N / 4)) * 4;
-    w.n0 = (q % (N / 4)) * 4;
+    w.nb = q % (N / 4);
     w.base = base;
     w.N = N;
     return w;
@@ -385,7 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
             const WBlock w = wblock(D, q);
             const float* dd = w.which == 0 ? A0 : w.which == 1 ? G1 : DZ2;
             const float* vv = w.which == 0 ? X : w.which == 1 ? U : H;
-            wgrad_block(dd, vv, ld, TP, w.m0, w.n0, accw[k]);
+            wgrad_block(dd, vv, ld, TP, w.m0, w.nb, w.N / 4, accw[k]);
         }
         if (tid < nvec) {
             int r = tid;
@@ -404,7 +420,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) part[w.base + (w.m0 + i) * w.N + w.n0 + j] = accw[k][i * 4 + j];
+            for (int j = 0; j < 4; ++j) part[w.base + (w.m0 + i) * w.N + w.nb + j * (w.N / 4)] = accw[k][i * 4 + j];
     }
     if (tid < nvec) part[D.aB1 + tid] = accv;  // db1, db2, dg are consecutive in the accumulator layout
 }
