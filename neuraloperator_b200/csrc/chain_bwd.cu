@@ -263,6 +263,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
             const int c = e / nq, n = (e % nq) * 4;
             st4(DZ2 + c * ld + n, ld4_or0(P.dy + ((int64_t)b * D.Cy + c) * P.P + p0 + n, n < np));
         }
+        if (D.skip) {  // s into the act0' rows (the skip stage's epilogue reads it and writes act0' in place)
+            for (int e = tid; e < D.Cs * nq; e += THREADS) {
+                const int c = e / nq, n = (e % nq) * 4;
+                st4(A0 + c * ld + n, ld4_or0(P.s + ((int64_t)b * D.Cs + c) * P.P + p0 + n, n < np));
+            }
+        }
         if (!D.skip && D.nd) {
             for (int e = tid; e < D.Cx * nq; e += THREADS) {
                 const int c = e / nq, n = (e % nq) * 4;
@@ -289,7 +295,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int m = m0 + i;
-                    const float4 sv = ld4_or0(P.s + ((int64_t)b * D.Cs + m) * P.P + p0 + n0, m < D.Cs && n0 < np);
+                    const float4 sv = ld4(A0 + m * ld + n0);  // s (zero in padding rows and past np)
                     float u[4], sl[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
