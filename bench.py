@@ -406,6 +406,75 @@ def copy_ceiling_ms(x_host, y_dev, y_host, steps, world, stream):
     return max_over_ranks(a.elapsed_time(b) / steps, world)
 
 
+def run_model_train(args, world, rank, local):
+    """One FNO / TFNO training step at the configuration's full size: forward, MSE loss against a
+    synthetic target, loss.backward() and an Adam step (neuralop/training/trainer.py:629-700 per batch),
+    every rank its own batch (weak scaling, gradients not reduced: the data-parallel all-reduce is the
+    caller's).  The same step through the module path (torch Conv1d per-pixel layers, NOP_CHAIN=0) is
+    timed beside it."""
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    desc, cls, modes, hidden, cin, cout, grid, batch, kw, field = MODELS[args.config]
+    if args.batch is not None:
+        batch = args.batch
+    if args.grid is not None:
+        grid = (args.grid,) * len(grid)
+        desc += f"_grid{args.grid}"
+    model = build_model(args.config, dev, args.precision).train()
+    x = grf(batch, cin, grid, field, seed=1 + rank, device=dev)
+    target = grf(batch, cout, grid, field, seed=101 + rank, device=dev)
+    opt = torch.optim.Adam(model.parameters(), lr=1e-4)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        loss = torch.nn.functional.mse_loss(model(x), target)
+        loss.backward()
+        opt.step()
+        return loss
+
+    def timed(steps, warm):
+        for _ in range(warm):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            loss = step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / steps, world), float(loss)
+
+    fused = model.fused_plan(x) is not None
+    with ClockSampler(local) as clocks:
+        ms, loss_f = timed(args.steps, args.warmup)
+    os.environ["NOP_CHAIN"] = "0"
+    try:
+        ms_mod, loss_m = timed(max(3, args.steps // 2), 2)
+    except torch.OutOfMemoryError:
+        ms_mod, loss_m = float("nan"), float("nan")
+    finally:
+        os.environ.pop("NOP_CHAIN", None)
+    if rank != 0:
+        return
+    line = {
+        "metric": "FNO training step (forward + MSE loss + backward + Adam) samples/s", "value": world * batch / (ms / 1e3),
+        "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.precision == "fp32" else "f32 (bf16 contraction)",
+        "data": "synthetic (seeded Gaussian random fields as input and target; no dataset)",
+        "config": {"workload": desc + "_train", "model": cls, "global_batch": batch * world, "per_gpu_batch": batch,
+                   "grid": list(grid), "hidden_channels": hidden, "n_modes": list(modes), "launch": "eager",
+                   "fused_path": fused},
+        "module_path": {"samples_per_s": world * batch / (ms_mod / 1e3), "ms_per_step": ms_mod,
+                        "definition": "the same step with the per-pixel layers as torch Conv1d (NOP_CHAIN=0)"},
+        "loss_fused_vs_module": [loss_f, loss_m],
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_model(args, world, rank, local):
     """FNO / TFNO forward (grid embedding + lifting, 4 FNO blocks, projection) at the configuration's full
     size.  N = 1: the whole batch on one GPU.  N > 1: the 3D configuration is slab-decomposed along x
@@ -1245,7 +1314,9 @@ def main():
         cfg = (cfg[0], args.batch) + tuple(cfg[2:])
     world, rank, local = dist_setup()
     try:
-        if args.model == "fno":
+        if args.model == "fno" and args.pass_ == "train":
+            run_model_train(args, world, rank, local)
+        elif args.model == "fno":
             run_model(args, world, rank, local)
         elif args.pass_ == "train":
             run_train(args, cfg, world, rank, local)
