@@ -93,9 +93,10 @@ class SlabSpectralConv:
     all-to-alls on the current stream.
     """
 
-    def __init__(self, conv, group=None):
+    def __init__(self, conv, group=None, chunks: int = 2):
         self.conv = conv
         self.group = group
+        self.chunks = chunks  # batch chunks whose exchanges overlap the other chunks' transforms
         self._plans = {}
         self.exchange_events = None  # a list: (start, end) CUDA event pairs around each all-to-all
 
@@ -162,10 +163,12 @@ class SlabSpectralConv:
         return send2
 
     def stage_planes_inv(self, recv2: torch.Tensor, x_slab: torch.Tensor, lay: SlabLayout, addend=None,
-                         apply_gelu=False) -> torch.Tensor:
+                         apply_gelu=False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         plan, _, _ = self._plan(x_slab, lay)
-        y = torch.empty((x_slab.shape[0], self.conv.out_channels, *x_slab.shape[2:]), dtype=torch.float32,
-                        device=x_slab.device)
+        shape = (x_slab.shape[0], self.conv.out_channels, *x_slab.shape[2:])
+        if out is not None and (tuple(out.shape) != shape or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous tensor of shape {shape}")
+        y = out if out is not None else torch.empty(shape, dtype=torch.float32, device=x_slab.device)
         b = self.conv.bias
         b = None if b is None else b.detach().reshape(-1).to(x_slab.device, torch.float32).contiguous()
         a = None if addend is None else addend.detach().to(x_slab.device, torch.float32).contiguous()
@@ -190,6 +193,10 @@ class SlabSpectralConv:
 
     def __call__(self, x_slab: torch.Tensor, addend: Optional[torch.Tensor] = None, apply_gelu: bool = False):
         x_slab = x_slab.contiguous()
+        batch = x_slab.shape[0]
+        n = self.chunks
+        if self.exchange_events is None and n > 1 and batch >= n and batch % n == 0:
+            return self._pipelined(x_slab, n, addend, apply_gelu)
         lay = self.layout(x_slab)
         send1 = self.stage_planes_fwd(x_slab, lay)
         recv1 = torch.empty(sum(lay.recv1_split()), dtype=send1.dtype, device=send1.device)
@@ -198,6 +205,40 @@ class SlabSpectralConv:
         recv2 = torch.empty(sum(lay.recv2_split()), dtype=send2.dtype, device=send2.device)
         self._exchange(recv2, send2, lay.recv2_split(), lay.send2_split())
         return self.stage_planes_inv(recv2, x_slab, lay, addend=addend, apply_gelu=apply_gelu)
+
+    def _pipelined(self, x_slab, n, addend, apply_gelu):
+        """The forward in n batch chunks: chunk c's all-to-alls run asynchronously (NCCL's stream) while
+        the current stream transforms chunk c + 1, so the exchanges overlap the plane transforms and the
+        mode stage.  Every rank makes the same calls in the same order."""
+        cb = x_slab.shape[0] // n
+        xs = [x_slab[i * cb:(i + 1) * cb] for i in range(n)]
+        lay = self.layout(xs[0])
+        y = torch.empty((x_slab.shape[0], self.conv.out_channels, *x_slab.shape[2:]), dtype=torch.float32,
+                        device=x_slab.device)
+        keep, recv1, works = [], [], []
+        for xc in xs:
+            send1 = self.stage_planes_fwd(xc, lay)
+            r1 = torch.empty(sum(lay.recv1_split()), dtype=send1.dtype, device=send1.device)
+            works.append(dist.all_to_all_single(r1, send1, output_split_sizes=lay.recv1_split(),
+                                                input_split_sizes=lay.send1_split(), group=self.group,
+                                                async_op=True))
+            keep.append(send1)
+            recv1.append(r1)
+        recv2, works2 = [], []
+        for i, xc in enumerate(xs):
+            works[i].wait()
+            send2 = self.stage_modes(recv1[i], xc, lay)
+            r2 = torch.empty(sum(lay.recv2_split()), dtype=send2.dtype, device=send2.device)
+            works2.append(dist.all_to_all_single(r2, send2, output_split_sizes=lay.recv2_split(),
+                                                 input_split_sizes=lay.send2_split(), group=self.group,
+                                                 async_op=True))
+            keep.append(send2)
+            recv2.append(r2)
+        for i, xc in enumerate(xs):
+            works2[i].wait()
+            a = None if addend is None else addend[i * cb:(i + 1) * cb]
+            self.stage_planes_inv(recv2[i], xc, lay, addend=a, apply_gelu=apply_gelu, out=y[i * cb:(i + 1) * cb])
+        return y
 
     def launches(self, x_slab: torch.Tensor) -> int:
         """Kernel launches of this library per call (the two all-to-alls are NCCL's)."""

@@ -77,7 +77,7 @@ class EmulatedSlab(SlabSpectralConv):
         send2 = full.reshape(qc, B * Co, lay.world, nx, 8).permute(2, 0, 1, 3, 4)     # [dest][qc][BCo][nx][8]
         return _u8(send2.to(torch.complex64))
 
-    def stage_planes_inv(self, recv2, x_slab, lay, addend=None, apply_gelu=False):
+    def stage_planes_inv(self, recv2, x_slab, lay, addend=None, apply_gelu=False, out=None):
         geo = self._geo(x_slab, lay.world)
         B, _, nx, Ny, Nz = x_slab.shape
         Co = self.conv.out_channels
@@ -89,8 +89,11 @@ class EmulatedSlab(SlabSpectralConv):
         full = torch.fft.ifft(full, dim=-2, norm="forward")
         full[..., 0] = full[..., 0].real.to(full.dtype)
         y = torch.fft.irfft(full, n=Nz, dim=-1, norm="forward") * geo.inv_scale
-        y = y + self.conv.bias.detach().double()
-        return y.float()
+        y = (y + self.conv.bias.detach().double()).float()
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
 
 def _slab_worker(rank, world, port, result):
