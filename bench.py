@@ -574,6 +574,8 @@ def run_model(args, world, rank, local):
             # chunk would otherwise exceed its kernels
             per_sample = hidden * math.prod(grid) * 4
             chunk = max(1, batch // (8 if per_sample >= (256 << 20) else 4))
+            if slab:  # chunks of two samples: each chunk's spectral layers overlap their own two exchanges
+                chunk = 2 if batch % 2 == 0 else 1
             host_call = (lambda: runner.forward_host(x_host, out=y_host, chunk=chunk, synchronize=False)) if slab else \
                 (lambda: model.forward_host(x_host, out=y_host, chunk=chunk, n_streams=2, synchronize=False))
             host_call()
