@@ -504,7 +504,7 @@ int32_t check(const nop_chain_desc* d, int64_t* P) {
     return NOP_OK;
 }
 
-// the layout with the largest tile (128, 64 or 32 points) that fits a CTA's shared memory
+// the layout with the largest tile (256, 128, 64 or 32 points) that fits a CTA's shared memory
 bool plan(const nop_chain_desc* d, Dims* out) {
     Dims D{};
     D.Cx = d->x_channels;
@@ -549,7 +549,7 @@ bool plan(const nop_chain_desc* d, Dims* out) {
     if (nblk > MAX_KB * THREADS || D.pH + 2 * D.pY > THREADS) return false;
     const bool own_u = D.skip || D.nd > 0;
     const int rows = D.pX + (own_u ? D.pK1 : 0) + (D.skip ? D.pS : 0) + 2 * D.pH + D.pY;
-    for (int tp = 128; tp >= 32; tp /= 2) {
+    for (int tp = 256; tp >= 32; tp /= 2) {
         const int ld = tp + 4;
         const int bytes = 4 * (off + rows * ld);
         if (bytes > SMEM_LIMIT) continue;
