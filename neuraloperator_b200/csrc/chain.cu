@@ -87,6 +87,7 @@ struct Layout {
     int Cx, Cs, nd, Ch, Cy, Cp, Co;  // real channel counts (Co: rows of W4)
     int act0, act2, gate;            // activation after the skip stage / after fc2, soft-gating skip
     int wide;                        // two MMAs per K step instead of three (see layer_mma)
+    int gs;                          // 1: two x stash buffers per group, and the gate reads x from the stash
 };
 
 __host__ __device__ inline uint32_t idesc_tf32(int N) {
@@ -456,8 +457,10 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         const int xpad = (xr - L.Cx) * TP, spad = (L.N0 - L.Cs) * TP;
         for (int g = 0; g < L.groups; ++g) {
             float* xs = reinterpret_cast<float*>(sm + L.o_stash + g * L.stash_bytes);
-            float* ss = xs + up1k(xr * TP * 4) / 4;
+            float* ss = xs + (L.gs ? 2 : 1) * up1k(xr * TP * 4) / 4;
             for (int e = tid; e < xpad; e += blockDim.x) xs[L.Cx * TP + e] = 0.f;
+            if (L.gs)
+                for (int e = tid; e < xpad; e += blockDim.x) xs[up1k(xr * TP * 4) / 4 + L.Cx * TP + e] = 0.f;
             for (int e = tid; e < spad; e += blockDim.x) ss[L.Cs * TP + e] = 0.f;
         }
     }
@@ -473,14 +476,16 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const uint32_t s_w4 = tc::smem_u32(sm + L.o_w4);
     const uint32_t lo0 = 4u * L.N0 * L.Kx, lo1 = 4u * L.N1 * L.K1, lo2 = 4u * L.N2 * L.N1;
     const uint32_t lo3 = 4u * L.N3 * L.N2, lo4 = 4u * L.N4 * L.N3;
-    const float* xst = reinterpret_cast<const float*>(sm + L.o_stash + grp * L.stash_bytes);
+    const float* xst0 = reinterpret_cast<const float*>(sm + L.o_stash + grp * L.stash_bytes);
     const int xrows = L.Kx > L.RX ? L.Kx : L.RX;       // stash rows read in stage 1 (>= Cx)
-    const float* sst = xst + up1k(xrows * TP * 4) / 4;  // 1 KB aligned (tensor-copy destination)
+    const int xbuf = up1k(xrows * TP * 4) / 4;          // floats per x buffer (1 KB aligned)
+    const float* sst = xst0 + (L.gs ? 2 : 1) * xbuf;    // 1 KB aligned (tensor-copy destination)
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 > 0 && L.NC3 < L.N3;
     const int nch1 = L.N1 / L.NC1, nch3 = L.N3 ? L.N3 / L.NC3 : 0;
     const uint32_t xbytes = (uint32_t)L.Cx * TP * 4, sbytes = (uint32_t)L.Cs * TP * 4;
     const uint64_t pol = l2::evict_first();
-    const uint64_t pol_x = L.gx ? l2::evict_normal() : pol;  // x must survive in L2 until the gate reads it
+    // x must survive in L2 until the gate reads it, unless the gate reads the stash
+    const uint64_t pol_x = (L.gx && !L.gs) ? l2::evict_normal() : pol;
     const int bar_id = 1 + grp;
 
     auto give_up = [&]() {
@@ -496,10 +501,13 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const int64_t stride = (int64_t)gridDim.x * L.groups;
     int64_t t = (int64_t)blockIdx.x * L.groups + grp;
     const uint32_t tps = (uint32_t)p.tps;
-    auto issue_x = [&](int64_t tt) {
+    // the group's tiles alternate between the x buffers (one buffer without gs)
+    auto xbuf_of = [&](int it) { return xst0 + ((L.gs && (it & 1)) ? xbuf : 0); };
+    auto issue_x = [&](int64_t tt, int it) {
         const uint32_t b = (uint32_t)tt / tps;
         expect_tx(xfull, xbytes);
-        tma_load_2d(const_cast<float*>(xst), &tmx, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * L.Cx), xfull, pol_x);
+        tma_load_2d(const_cast<float*>(xbuf_of(it)), &tmx, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * L.Cx),
+                    xfull, pol_x);
     };
     auto issue_s = [&](int64_t tt) {
         const uint32_t b = (uint32_t)tt / tps;
@@ -507,8 +515,9 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         tma_load_2d(const_cast<float*>(sst), &tms, (int)(((uint32_t)tt - b * tps) * TP), (int)(b * L.Cs), sfull, pol);
     };
     int x_pending = 0, s_pending = 0;  // loads issued and not yet waited for (leader's count)
+    int it = 0;  // this group's tile count (selects the x buffer)
     if (leader && t < p.tiles) {
-        issue_x(t);
+        issue_x(t, 0);
         ++x_pending;
         if (L.Cs) {
             issue_s(t);
@@ -545,7 +554,8 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     };
 
-    for (; t < p.tiles && !stop; t += stride) {
+    for (; t < p.tiles && !stop; t += stride, ++it) {
+        const float* xst = xbuf_of(it);
         const uint32_t b = (uint32_t)t / tps;
         const uint32_t pnt = ((uint32_t)t - b * tps) * TP + pt;  // point index within the sample
         const bool valid = pnt < (uint32_t)p.P;
@@ -603,7 +613,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         if (!barrier_ok()) break;
         if (leader) {
             if (nt < p.tiles) {
-                issue_x(nt);
+                issue_x(nt, it + 1);
                 ++x_pending;
             }
             if (L.N0)
@@ -695,7 +705,10 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         // ---- 4. y = act(fc2 + b2 + g x + gb): store, or A of the projection ----
         for (int c0 = 0; c0 < L.N2; c0 += 16) {
             float v[16], xr[16];
-            if (L.gx) {  // x from L2 (coalesced: a warp reads 32 consecutive points of a channel)
+            if (L.gs) {  // x from this tile's stash buffer
+#pragma unroll
+                for (int j = 0; j < 16; ++j) xr[j] = c0 + j < L.Cx ? xst[(c0 + j) * TP + pt] : 0.f;
+            } else if (L.gx) {  // x from L2 (coalesced: a warp reads 32 consecutive points of a channel)
                 const float* xg = p.x + ((int64_t)b * L.Cx + c0) * p.P + pnt;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) xr[j] = (valid && c0 + j < L.Cx) ? l2::ld(xg + (int64_t)j * p.P, pol) : 0.f;
@@ -902,11 +915,16 @@ constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gat
     off += up1k(4 * (L.N1 + 2 * L.N2 + L.N3 + L.N4));
     // per group: x stash padded to the rows stage 1 reads, s stash padded to N0 rows; the copies fill the
     // first Cx / Cs rows, the padding rows are zeroed once so the reads need no per-channel guard
-    L.stash_bytes = up1k(cmax(L.Kx, L.RX) * TP * 4) + up1k(L.N0 * TP * 4);
+    // with the gate's x read back (gx), a second x buffer per group keeps the tile's x in shared memory
+    // until the gate while the next tile's x lands in the other one, when shared memory allows
+    const int xb = up1k(cmax(L.Kx, L.RX) * TP * 4), sb = up1k(L.N0 * TP * 4);
+    const int tail_bytes = 8 * (3 * groups + 1) + 8 + 4 * (1 + MAX_GROUPS);
+    L.gs = (L.gx && off + groups * (2 * xb + sb) + tail_bytes <= SMEM_LIMIT) ? 1 : 0;
+    L.stash_bytes = (L.gs ? 2 : 1) * xb + sb;
     L.o_stash = off;
     off += groups * L.stash_bytes;
     L.o_bar = off;
-    off += 8 * (3 * groups + 1) + 8 + 4 * (1 + MAX_GROUPS);
+    off += tail_bytes;
     L.smem = off;
     if (L.smem > SMEM_LIMIT) return false;
     // more than half an SM's shared memory: one CTA per SM, so a second CTA never waits in
@@ -990,7 +1008,7 @@ struct FixedLayout {
                          o_w1 = kL.o_w1, o_w2 = kL.o_w2, o_w3 = kL.o_w3, o_w4 = kL.o_w4, o_wt = kL.o_wt,
                          o_vec = kL.o_vec, o_stash = kL.o_stash, stash_bytes = kL.stash_bytes, o_bar = kL.o_bar,
                          smem = kL.smem, Cx = kL.Cx, Cs = kL.Cs, nd = kL.nd, Ch = kL.Ch, Cy = kL.Cy, Cp = kL.Cp,
-                         Co = kL.Co, act0 = kL.act0, act2 = kL.act2, gate = kL.gate, wide = kL.wide;
+                         Co = kL.Co, act0 = kL.act0, act2 = kL.act2, gate = kL.gate, wide = kL.wide, gs = kL.gs;
     __device__ static FixedLayout get(const Layout&) { return FixedLayout{}; }
 };
 
