@@ -52,9 +52,9 @@ TRAFFIC = {
     # profiles/contraction_tma_c2_full.md: full-size capture of the contraction (one launch)
     ("c2", "contraction"): 207.854080e6 + 10.398976e6,
     # profiles/chain_c5_small_full.md: 128^3 batch-1 capture x 64 (the chain's traffic grows with the points)
-    ("c5", "chain_block"): 64 * (538.103040e6 + 214.885120e6),
-    ("c5", "chain_lifting"): 64 * (25.213184e6 + 208.536320e6),
-    ("c5", "chain_last_block_projection"): 64 * (536.959744e6 + 17.336064e6),
+    ("c5", "chain_block"): 64 * (536.928256e6 + 225.449984e6),
+    ("c5", "chain_lifting"): 64 * (25.228032e6 + 208.604928e6),
+    ("c5", "chain_last_block_projection"): 64 * (536.945408e6 + 16.902400e6),
 }
 
 # name -> (description, batch, Ci, Co, grid, n_modes, factorization)
