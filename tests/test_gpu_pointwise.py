@@ -180,3 +180,16 @@ def test_fused_fno_matches_module_path(monkeypatch):
         assert rel_l2(y_fused, y_modules) <= TOL
     finally:
         torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def test_chain_large_block_wide_form_with_stash_gate():
+    """A C5-shaped block chain large enough (16384 tiles) for the planner's wide MMA form with the gate
+    reading x from the two-buffer shared-memory stash, against the float64 reference."""
+    case = ("block_h32_3d_large", 1, (128, 128, 128), 32, 16, 32, True, None, True, False, True, None)
+    assert pointwise.query(pointwise.make_desc(1, (128, 128, 128), 32, 16, 32, skip=32, act_skip=True,
+                                               act_out=True, gate=True)) == 4  # the wide form
+    ops = _operands(case)
+    y = _run(case, ops)
+    y_ref = _expect(case, ops)
+    assert rel_l2(y.cpu(), y_ref) <= TOL
+    assert _lib.device_status() == 0
