@@ -19,20 +19,22 @@
 // MMAs by the three-pass split: each operand value v = hi + lo (hi = tf32(v), lo = tf32(v - hi)) and
 // D = A_hi W_hi + A_hi W_lo + A_lo W_hi in fp32 (the dropped lo * lo term is below 2^-22 relative).
 //
-// Work split: a CTA (one per SM, persistent) holds up to four independent groups of 128 threads; group
+// Work split: a CTA (one per SM, persistent) holds up to five independent groups of 128 threads; group
 // g walks its own tiles and issues its own MMAs (one elected thread), so the epilogue arithmetic of one
 // group runs while the MMAs and loads of the others are in flight.  Per tile a group:
 //   1. waits for its x tile (TMA box {128 points, Cx channels} -> stash [c][p]) and writes A = x
-//      (+ grid coordinates) and, for the gate, the raw x into tensor memory; the stash is free: the
-//      next tile's x load is issued;
+//      (+ grid coordinates) and, for the gate, the raw x into tensor memory -- or keeps the tile's x in
+//      its stash buffer (two buffers per group) or re-reads it from L2 when tensor memory is short; the
+//      next tile's x load is issued (into the other buffer);
 //   2. skip stage: MMA, wait; u = act(acc + s) -> A (the s stash is free: the next tile's s load);
 //   3. fc1 / fc2: MMA(s), wait; h = GELU(acc + b1) -> A; MMA, wait.  A wide hidden layer runs in chunks
 //      of NC channels: chunk c's fc2 MMA and chunk c + 1's fc1 MMA are issued together;
 //   4. y = act(acc + b2 + g x + gb): stored (coalesced: a warp writes 32 consecutive points of a
 //      channel), or written as A of the projection, which repeats step 3 and stores its output.
-// Tensor memory per group: the raw-x region (gate), the chunk regions, A (hi | lo) and the accumulator;
-// the host planner picks the group count and chunk widths that fit 512 columns and 227 KB of shared
-// memory.  Every wait is bounded: on expiry the kernel records NOP_DEVICE_MMA_TIMEOUT in the status
+// Tensor memory per group: the raw-x region (gate), the chunk regions, A (hi | lo) and the accumulator
+// (twice as wide in the wide MMA form, layer_mma); the host planner (constexpr, so the FNO
+// configurations' layouts are also compiled as constants: FixedLayout) picks the group count, the MMA
+// form and the chunk widths that fit 512 columns and 227 KB of shared memory.  Every wait is bounded: on expiry the kernel records NOP_DEVICE_MMA_TIMEOUT in the status
 // word, every group leaves its loop at the next group barrier, issued MMAs and loads are drained
 // (bounded) and the tensor memory is freed.
 #include <cuda.h>
