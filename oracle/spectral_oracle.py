@@ -339,12 +339,19 @@ def grid_embedding(x: torch.Tensor, boundaries=None) -> torch.Tensor:
     return torch.cat((x, *grids), dim=1)
 
 
+def _conv1x1(h: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """A kernel-size-1 Conv1d ([out, in, 1] weight) on h [B, in, L] as a matrix product: the same sums as
+    F.conv1d, through BLAS (conv1d's CPU kernels crashed on lines of 2^24 points in one environment)."""
+    out = torch.matmul(w.reshape(w.shape[0], -1), h)
+    return out if b is None else out + b.reshape(1, -1, 1)
+
+
 def channel_mlp(x: torch.Tensor, layers, non_linearity=F.gelu) -> torch.Tensor:
     """``ChannelMLP.forward`` (channel_mlp.py:82-119): 1x1 Conv1d layers with GELU between."""
     size = list(x.shape)
     h = x.reshape(size[0], size[1], -1) if x.ndim > 3 else x
     for i, (w, b) in enumerate(layers):
-        h = F.conv1d(h, w, b)
+        h = _conv1x1(h, w, b)
         if i < len(layers) - 1:
             h = non_linearity(h)
     if x.ndim > 3:
@@ -361,7 +368,7 @@ def skip(x: torch.Tensor, kind: Optional[str], weight) -> torch.Tensor:
         return weight * x
     if kind == "linear":
         size = list(x.shape)
-        h = F.conv1d(x.reshape(size[0], size[1], -1), weight)
+        h = _conv1x1(x.reshape(size[0], size[1], -1), weight)
         return h.reshape(size[0], weight.shape[0], *size[2:])
     raise ValueError(kind)
 
