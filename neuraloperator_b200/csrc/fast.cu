@@ -671,8 +671,14 @@ int32_t mix_stage(const Plan& p, const float2* Xh, const char* packed, float2* Y
 // planes per CTA of the 256 x 256 inverse plane kernel: two, so each CTA prefetches one plane's
 // spectrum across planes, once the grid still fills the 2 CTAs x SMs slots several times over
 // (measured on B200 with 4096 planes: 1 -> 307 us, 2 -> 301 us, 3 -> 322 us, 4 -> 302 us)
+// planes per CTA of the 256 x 256 inverse: two from 8 planes per SM; persistent (two CTAs per SM, every
+// CTA the same number of planes, the twiddle tables built once per CTA) from 64 planes per SM.  Measured
+// on B200: the C5 layer's inverse (65536 planes) 3.69 -> 3.56 ms persistent, while the C2 layer's
+// (4096 planes, 14 per CTA persistent) ran 261 -> 275 us, so it keeps two per CTA.
 inline int planes_per_cta(const Plan& p, int64_t planes) {
-    return planes >= 8 * (int64_t)p.sm_count ? 2 : 1;
+    const int64_t sms = p.sm_count;
+    if (planes >= 64 * sms) return (int)((planes + 2 * sms - 1) / (2 * sms));
+    return planes >= 8 * sms ? 2 : 1;
 }
 
 inline unsigned plane_ctas(const Plan& p, int64_t planes) {
