@@ -402,7 +402,11 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     const int grp = warp >> 2;                 // group
     const int quad = warp & 3;                 // tensor-memory lane quadrant of this warp
     const int pt = quad * 32 + lane;           // this thread's point in the tile (= its lane)
-    const bool leader = (tid & (GT - 1)) == 0;
+    // the thread that waits on the group's barriers and issues its copies and MMAs: lane 0 of the group's
+    // warp grp % 4, so the groups' leaders sit on different SM sub-partitions (an MMA costs its issuing
+    // warp tens of cycles; with every leader on sub-partition 0, one scheduler carried all of them and the
+    // C5 lifting took 10.9 ms instead of 9.7, the block chain 11.4 instead of 11.0)
+    const bool leader = (tid & (GT - 1)) == 32 * (grp & 3);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.o_bar);
     uint64_t* mbar = bars + 3 * grp;           // MMA completion of this group
     uint64_t* xfull = mbar + 1;                // x stash landed

@@ -78,6 +78,8 @@ CASES = [
     ("projection", 2, (64, 64), 64, 128, 1, False, None, False, False, False, None),
     ("odd_channels_gate_bias_partial_tile", 3, (3, 124), 7, 5, 7, True, None, True, True, True, None),
     ("no_gate", 2, (40, 36), 24, 40, 24, True, None, False, False, True, None),
+    # lifting with a hidden width that is not a multiple of 16 (40 -> 48 columns), a partial last tile
+    ("lifting_odd_partial_tile", 3, (3, 124), 2, 40, 24, False, ((0.0, 1.0), (-1.0, 1.0)), False, False, True, None),
 ]
 
 
@@ -188,6 +190,22 @@ def test_chain_large_block_wide_form_with_stash_gate():
     case = ("block_h32_3d_large", 1, (128, 128, 128), 32, 16, 32, True, None, True, False, True, None)
     assert pointwise.query(pointwise.make_desc(1, (128, 128, 128), 32, 16, 32, skip=32, act_skip=True,
                                                act_out=True, gate=True)) == 4  # the wide form
+    ops = _operands(case)
+    y = _run(case, ops)
+    y_ref = _expect(case, ops)
+    assert rel_l2(y.cpu(), y_ref) <= TOL
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("wide", ["0", "1"])
+def test_chain_lifting_many_tiles_per_group(monkeypatch, wide):
+    """The C5 lifting shape (3 channels + 3 grid channels -> 64 -> 32) over 4096 tiles, several per group
+    (the barrier phases and x-stash reuse carry across tiles), in both MMA forms, against the float64
+    reference."""
+    monkeypatch.setenv("NOP_CHAIN_WIDE", wide)
+    case = ("lifting_3d_many_tiles", 2, (64, 64, 64), 3, 64, 32, False, ((0.0, 1.0),) * 3, False, False, False, None)
+    assert pointwise.query(pointwise.make_desc(2, (64, 64, 64), 3, 64, 32, grid=[(0.0, 1 / 64)] * 3)) == \
+        (5 if wide == "0" else 3)
     ops = _operands(case)
     y = _run(case, ops)
     y_ref = _expect(case, ops)
