@@ -291,14 +291,16 @@ __device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
 
 // K-major hi / lo images of W [rows x cols] (row-major, out x in) padded with zeros to N x K: two N-row
 // images (hi, then lo), or with `wide` one 2N-row image whose chunks of C rows are hi rows followed by
-// the same rows' lo parts (layer_mma)
-__device__ void load_weight(char* sm, int off, const float* w, int rows, int cols, int N, int K, int C, bool wide) {
+// the same rows' lo parts (layer_mma); the weights are multiplied by `scale` (1, or 0.5 for a layer whose
+// input is a GELU computed without its final halving)
+__device__ void load_weight(char* sm, int off, const float* w, int rows, int cols, int N, int K, int C, bool wide,
+                            float scale) {
     if (N == 0) return;
     float* hi = reinterpret_cast<float*>(sm + off);
     float* lo = reinterpret_cast<float*>(sm + off + 4 * N * K);
     for (int e = threadIdx.x; e < N * K; e += blockDim.x) {
         const int n = e / K, k = e % K;
-        const float v = (n < rows && k < cols) ? __ldg(w + (int64_t)n * cols + k) : 0.f;
+        const float v = (n < rows && k < cols) ? scale * __ldg(w + (int64_t)n * cols + k) : 0.f;
         const float h = tc::tf32_round(v);
         if (wide) {
             const int r = (n / C) * 2 * C + n % C;
@@ -344,7 +346,11 @@ __device__ __forceinline__ float gelu_fast(float v) {
     return 0.5f * fmaf(av, erf_x, v);
 }
 
-// gelu_fast of two values with packed fp32x2 arithmetic (the same operations and roundings per lane)
+// gelu_fast of two values with packed fp32x2 arithmetic (the same operations and roundings per lane).
+// kHalf = false returns 2 GELU(v) (the final halving left out): where the GELU feeds a layer of the
+// chain, its weights are halved instead (exact, and exact through the tf32 split: the results are
+// bit-identical), saving a multiply per pair.
+template <bool kHalf = true>
 __device__ __forceinline__ float2 gelu_fast2(float2 v) {
     const float2 av = make_float2(fabsf(v.x), fabsf(v.y));
     const float2 y = __fmul2_rn(av, make_float2(kGeluY, kGeluY));
@@ -360,14 +366,16 @@ __device__ __forceinline__ float2 gelu_fast2(float2 v) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(-sq.x));
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(-sq.y));
     const float2 erf_x = __ffma2_rn(__fmul2_rn(t, e), ns, make_float2(1.0f, 1.0f));
-    return __fmul2_rn(__ffma2_rn(av, erf_x, v), make_float2(0.5f, 0.5f));
+    const float2 g2 = __ffma2_rn(av, erf_x, v);
+    return kHalf ? __fmul2_rn(g2, make_float2(0.5f, 0.5f)) : g2;
 }
 
-// GELU of 16 values in place (pairs)
+// GELU of 16 values in place (pairs); kHalf = false: 2 GELU (gelu_fast2)
+template <bool kHalf = true>
 __device__ __forceinline__ void gelu16(float (&v)[16]) {
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
-        const float2 g = gelu_fast2(make_float2(v[j], v[j + 1]));
+        const float2 g = gelu_fast2<kHalf>(make_float2(v[j], v[j + 1]));
         v[j] = g.x;
         v[j + 1] = g.y;
     }
@@ -432,11 +440,12 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     }
     // weights and vectors, once per CTA
     const int K1r = L.Cs ? L.Cs : L.Cx + L.nd;
-    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx, L.N0, L.wide);
-    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1, L.NC1, L.wide);
-    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1, L.N2, L.wide);
-    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2, L.NC3, L.wide);
-    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3, L.N4, L.wide);
+    // a layer fed by a GELU takes half weights (the GELU is evaluated without its final halving)
+    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx, L.N0, L.wide, 1.f);
+    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1, L.NC1, L.wide, (L.Cs && L.act0) ? 0.5f : 1.f);
+    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1, L.N2, L.wide, 0.5f);
+    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2, L.NC3, L.wide, L.act2 ? 0.5f : 1.f);
+    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3, L.N4, L.wide, 0.5f);
     if (L.tail) {  // fp32 [4][Kt], rows past the outputs and columns past the hidden width zero
         float* wt = reinterpret_cast<float*>(sm + L.o_wt);
         const float* src = L.Cp ? p.w4 : p.w2;
@@ -444,7 +453,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         const int kt = L.Kt > 0 ? L.Kt : 1;  // (Kt > 0 whenever tail is set)
         for (int e = threadIdx.x; e < 4 * kt; e += blockDim.x) {
             const int r = e / kt, k = e % kt;
-            wt[e] = (r < rows && k < cols) ? __ldg(src + (int64_t)r * cols + k) : 0.f;
+            wt[e] = (r < rows && k < cols) ? 0.5f * __ldg(src + (int64_t)r * cols + k) : 0.f;  // GELU-fed
         }
     }
     float* vb1 = reinterpret_cast<float*>(sm + L.o_vec);
@@ -644,7 +653,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                     v[j] = u.x;
                     v[j + 1] = u.y;
                 }
-                if (L.act0) gelu16(v);
+                if (L.act0) gelu16<false>(v);
                 st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -668,7 +677,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 float v[16];
                 ld_acc16(tl + L.cD, L.wide ? L.N1 : 0, c0, v);
                 add16(v, vb1 + c0);
-                gelu16(v);
+                gelu16<false>(v);
                 tail_acc16(acc, wt, L.Kt, c0, v);
             }
             if (valid) {
@@ -693,7 +702,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 float v[16];
                 ld_acc16(tl + src, L.wide ? L.NC1 : 0, c0, v);
                 add16(v, vb1 + c * L.NC1 + c0);
-                gelu16(v);
+                gelu16<false>(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
             }
             if (!barrier_ok()) {
@@ -738,7 +747,17 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                     v[j + 3] = o1.y;
                 }
             }
-            if (L.act2) gelu16(v);
+            if (L.act2) {
+                gelu16<false>(v);
+                if (!L.N3) {  // stored: halve here (with the projection, W3 takes half weights)
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2) {
+                        const float2 h = __fmul2_rn(make_float2(v[j], v[j + 1]), make_float2(0.5f, 0.5f));
+                        v[j] = h.x;
+                        v[j + 1] = h.y;
+                    }
+                }
+            }
             if (L.N3) {
                 st_split16(tl + L.cA + c0, tl + L.cA + L.KA + c0, v);
             } else if (valid) {
@@ -765,7 +784,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 float v[16];
                 ld_acc16(tl + L.cD, L.wide ? L.N3 : 0, c0, v);
                 add16(v, vb3 + c0);
-                gelu16(v);
+                gelu16<false>(v);
                 tail_acc16(acc, wt, L.Kt, c0, v);
             }
             if (valid) {
@@ -783,7 +802,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 float v[16];
                 ld_acc16(tl + src, L.wide ? L.NC3 : 0, c0, v);
                 add16(v, vb3 + c * L.NC3 + c0);
-                gelu16(v);
+                gelu16<false>(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
             }
             if (!barrier_ok()) {
