@@ -52,9 +52,9 @@ TRAFFIC = {
     # profiles/contraction_tma_c2_full.md: full-size capture of the contraction (one launch)
     ("c2", "contraction"): 207.854080e6 + 10.398976e6,
     # profiles/chain_c5_small_full.md: 128^3 batch-1 capture x 64 (the chain's traffic grows with the points)
-    ("c5", "chain_block"): 64 * (536.928256e6 + 225.449984e6),
-    ("c5", "chain_lifting"): 64 * (25.228032e6 + 208.604928e6),
-    ("c5", "chain_last_block_projection"): 64 * (536.945408e6 + 16.902400e6),
+    ("c5", "chain_block"): 64 * (537.109760e6 + 227.285760e6),
+    ("c5", "chain_lifting"): 64 * (25.244928e6 + 209.326080e6),
+    ("c5", "chain_last_block_projection"): 64 * (537.034240e6 + 17.639168e6),
 }
 
 # name -> (description, batch, Ci, Co, grid, n_modes, factorization)
