@@ -70,6 +70,8 @@ struct Params {
     float* y;
 };
 
+constexpr int kW0 = 1, kW1 = 2, kW2 = 4, kW3 = 8, kW4 = 16, kWAll = 31;  // Layout::wide bits
+
 struct Layout {
     int Kx;                          // A columns written from x (+ grid channels)
     int RX;                          // raw-x columns (gate) or 0
@@ -89,7 +91,8 @@ struct Layout {
     int smem;
     int Cx, Cs, nd, Ch, Cy, Cp, Co;  // real channel counts (Co: rows of W4)
     int act0, act2, gate;            // activation after the skip stage / after fc2, soft-gating skip
-    int wide;                        // two MMAs per K step instead of three (see layer_mma)
+    int wide;                        // layers in the wide MMA form (two MMAs per K step instead of three,
+                                     // layer_mma): bit k for W_k (kW0 .. kW4)
     int gs;                          // 1: two x stash buffers per group, and the gate reads x from the stash
 };
 
@@ -441,11 +444,11 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
     // weights and vectors, once per CTA
     const int K1r = L.Cs ? L.Cs : L.Cx + L.nd;
     // a layer fed by a GELU takes half weights (the GELU is evaluated without its final halving)
-    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx, L.N0, L.wide, 1.f);
-    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1, L.NC1, L.wide, (L.Cs && L.act0) ? 0.5f : 1.f);
-    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1, L.N2, L.wide, 0.5f);
-    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2, L.NC3, L.wide, L.act2 ? 0.5f : 1.f);
-    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3, L.N4, L.wide, 0.5f);
+    load_weight(sm, L.o_w0, p.w0, L.Cs, L.Cx, L.N0, L.Kx, L.N0, L.wide & kW0, 1.f);
+    load_weight(sm, L.o_w1, p.w1, L.Ch, K1r, L.N1, L.K1, L.NC1, L.wide & kW1, (L.Cs && L.act0) ? 0.5f : 1.f);
+    if (!(L.tail && !L.Cp)) load_weight(sm, L.o_w2, p.w2, L.Cy, L.Ch, L.N2, L.N1, L.N2, L.wide & kW2, 0.5f);
+    load_weight(sm, L.o_w3, p.w3, L.Cp, L.Cy, L.N3, L.N2, L.NC3, L.wide & kW3, L.act2 ? 0.5f : 1.f);
+    if (!L.tail) load_weight(sm, L.o_w4, p.w4, L.Co, L.Cp, L.N4, L.N3, L.N4, L.wide & kW4, 0.5f);
     if (L.tail) {  // fp32 [4][Kt], rows past the outputs and columns past the hidden width zero
         float* wt = reinterpret_cast<float*>(sm + L.o_wt);
         const float* src = L.Cp ? p.w4 : p.w2;
@@ -633,9 +636,9 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 ++x_pending;
             }
             if (L.N0)
-                layer_mma(tb, L.cA, L.KA, L.Kx, s_w0, s_w0 + lo0, L.N0, 0, 0, L.cD, L.N0, false, L.wide);
+                layer_mma(tb, L.cA, L.KA, L.Kx, s_w0, s_w0 + lo0, L.N0, 0, 0, L.cD, L.N0, false, L.wide & kW0);
             else
-                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false, L.wide);
+                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false, L.wide & kW1);
         }
         commit_wait(L.N0 > 0);
 
@@ -643,7 +646,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
         if (L.N0) {
             for (int c0 = 0; c0 < L.N0; c0 += 16) {
                 float v[16];
-                ld_acc16(tl + L.cD, L.wide ? L.N0 : 0, c0, v);
+                ld_acc16(tl + L.cD, (L.wide & kW0) ? L.N0 : 0, c0, v);
 #pragma unroll
                 for (int j = 0; j < 16; j += 2) {
                     const int c = c0 + j;  // channels past Cs (padding) add 0
@@ -663,7 +666,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                     issue_s(nt);
                     ++s_pending;
                 }
-                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false, L.wide);
+                layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, 0, 0, ch1 ? L.cC1 : L.cD, L.NC1, false, L.wide & kW1);
             }
             commit_wait(false);
         }
@@ -675,7 +678,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             float2 acc[4] = {};
             for (int c0 = 0; c0 < L.N1; c0 += 16) {
                 float v[16];
-                ld_acc16(tl + L.cD, L.wide ? L.N1 : 0, c0, v);
+                ld_acc16(tl + L.cD, (L.wide & kW1) ? L.N1 : 0, c0, v);
                 add16(v, vb1 + c0);
                 gelu16<false>(v);
                 tail_acc16(acc, wt, L.Kt, c0, v);
@@ -700,7 +703,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             const int dlo = ch1 ? L.NC1 : L.KA;
             for (int c0 = 0; c0 < L.NC1; c0 += 16) {
                 float v[16];
-                ld_acc16(tl + src, L.wide ? L.NC1 : 0, c0, v);
+                ld_acc16(tl + src, (L.wide & kW1) ? L.NC1 : 0, c0, v);
                 add16(v, vb1 + c * L.NC1 + c0);
                 gelu16<false>(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
@@ -710,9 +713,9 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 break;
             }
             if (leader) {
-                layer_mma(tb, dst, dlo, L.NC1, s_w2, s_w2 + lo2, L.N2, 0, c * L.NC1 / 8, L.cD, L.N2, c > 0, L.wide);
+                layer_mma(tb, dst, dlo, L.NC1, s_w2, s_w2 + lo2, L.N2, 0, c * L.NC1 / 8, L.cD, L.N2, c > 0, L.wide & kW2);
                 if (c + 1 < nch1)
-                    layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, (c + 1) * L.NC1, 0, L.cC1, L.NC1, false, L.wide);
+                    layer_mma(tb, L.cA, L.KA, L.K1, s_w1, s_w1 + lo1, L.N1, (c + 1) * L.NC1, 0, L.cC1, L.NC1, false, L.wide & kW1);
             }
             commit_wait(false);
         }
@@ -730,7 +733,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 for (int j = 0; j < 16; ++j) xr[j] = (valid && c0 + j < L.Cx) ? l2::ld(xg + (int64_t)j * p.P, pol) : 0.f;
             }
             if (L.gate && !L.gx) tmem_ld16(tl + L.cX + c0, xr);
-            ld_acc16(tl + L.cD, L.wide ? L.N2 : 0, c0, v);
+            ld_acc16(tl + L.cD, (L.wide & kW2) ? L.N2 : 0, c0, v);
             if (L.gate && !L.gx) tmem_wait_ld(xr);
             add16(v, vb2 + c0);
             if (L.gate) {
@@ -776,13 +779,13 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
 
         // ---- 5. projection: p = GELU(W3 y + b3) (chunks), out = W4 p + b4 ----
         if (!barrier_ok()) break;
-        if (leader) layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, 0, 0, ch3 ? L.cC3 : L.cD, L.NC3, false, L.wide);
+        if (leader) layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, 0, 0, ch3 ? L.cC3 : L.cD, L.NC3, false, L.wide & kW3);
         commit_wait(false);
         if (L.tail) {  // out = W4 GELU(W3 y + b3) + b4 with W4 (<= 4 outputs) on CUDA cores
             float2 acc[4] = {};
             for (int c0 = 0; c0 < L.N3; c0 += 16) {
                 float v[16];
-                ld_acc16(tl + L.cD, L.wide ? L.N3 : 0, c0, v);
+                ld_acc16(tl + L.cD, (L.wide & kW3) ? L.N3 : 0, c0, v);
                 add16(v, vb3 + c0);
                 gelu16<false>(v);
                 tail_acc16(acc, wt, L.Kt, c0, v);
@@ -800,7 +803,7 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             const int dlo = ch3 ? L.NC3 : L.KA;
             for (int c0 = 0; c0 < L.NC3; c0 += 16) {
                 float v[16];
-                ld_acc16(tl + src, L.wide ? L.NC3 : 0, c0, v);
+                ld_acc16(tl + src, (L.wide & kW3) ? L.NC3 : 0, c0, v);
                 add16(v, vb3 + c * L.NC3 + c0);
                 gelu16<false>(v);
                 st_split16(tl + dst + c0, tl + dst + dlo + c0, v);
@@ -810,16 +813,16 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
                 break;
             }
             if (leader) {
-                layer_mma(tb, dst, dlo, L.NC3, s_w4, s_w4 + lo4, L.N4, 0, c * L.NC3 / 8, L.cD, L.N4, c > 0, L.wide);
+                layer_mma(tb, dst, dlo, L.NC3, s_w4, s_w4 + lo4, L.N4, 0, c * L.NC3 / 8, L.cD, L.N4, c > 0, L.wide & kW4);
                 if (c + 1 < nch3)
-                    layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, (c + 1) * L.NC3, 0, L.cC3, L.NC3, false, L.wide);
+                    layer_mma(tb, L.cA, L.KA, L.N2, s_w3, s_w3 + lo3, L.N3, (c + 1) * L.NC3, 0, L.cC3, L.NC3, false, L.wide & kW3);
             }
             commit_wait(false);
         }
         if (broke) break;
         for (int c0 = 0; c0 < L.N4; c0 += 16) {
             float v[16];
-            ld_acc16(tl + L.cD, L.wide ? L.N4 : 0, c0, v);
+            ld_acc16(tl + L.cD, (L.wide & kW4) ? L.N4 : 0, c0, v);
             if (valid) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -857,10 +860,10 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 // The layout of one chain for `groups` groups and chunk widths nc1 / nc3 (false when it does not fit).
 // constexpr: the layouts of the FNO configurations' chains are also computed at compile time, and a
 // kernel instantiated on one of them (FixedLayout) takes every size and offset as a constant.
-constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, bool wide, Layout* out) {
+// `wide`: the layers in the wide MMA form (Layout::wide bits).
+constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gate_global, int wide, Layout* out) {
     Layout L{};
     L.groups = groups;
-    L.wide = wide ? 1 : 0;
     L.Cx = z.Cx;
     L.Cs = z.Cs;
     L.nd = z.nd;
@@ -892,34 +895,38 @@ constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gat
     L.NC1 = nc1;
     L.NC3 = L.N3 ? nc3 : 0;
     const bool ch1 = L.NC1 < L.N1, ch3 = L.N3 && L.NC3 < L.N3;
-    const int dw = wide ? 2 : 1;  // accumulator columns per output channel
-    if (wide) {  // every MMA of 2 N columns within the instruction's N <= 256
-        const bool fc2_mma = !(L.tail && !z.Cp), fc4_mma = !L.tail;
-        if (2 * L.N0 > 256 || 2 * L.NC1 > 256 || (fc2_mma && 2 * L.N2 > 256) || 2 * L.NC3 > 256 ||
-            (fc4_mma && 2 * L.N4 > 256))
-            return false;
-    }
+    const bool fc2_mma = !(L.tail && !z.Cp), fc4_mma = !L.tail;
+    // only the layers present are wide; each wide MMA of 2 N columns stays within N <= 256
+    if (!L.N0) wide &= ~kW0;
+    if (!fc2_mma) wide &= ~kW2;
+    if (!L.N3) wide &= ~kW3;
+    if (!L.N4 || !fc4_mma) wide &= ~kW4;
+    L.wide = wide;
+    // accumulator columns per output channel of each layer
+    const int dw0 = (wide & kW0) ? 2 : 1, dw1 = (wide & kW1) ? 2 : 1, dw2 = (wide & kW2) ? 2 : 1,
+              dw3 = (wide & kW3) ? 2 : 1, dw4 = (wide & kW4) ? 2 : 1;
+    if (dw0 * L.N0 > 256 || dw1 * L.NC1 > 256 || dw2 * L.N2 > 256 || dw3 * L.NC3 > 256 || dw4 * L.N4 > 256)
+        return false;
     int ka = cmax(L.Kx, L.N0);
     if (!ch1 && !(L.tail && !z.Cp)) ka = cmax(ka, L.N1);  // h written as A (not when fc2 runs on CUDA cores)
     if (L.N3) ka = cmax(ka, L.N2);
     if (L.N3 && !ch3 && !L.tail) ka = cmax(ka, L.N3);
     L.KA = up8(ka);
-    int nd = L.N0;
-    if (!(L.tail && !z.Cp)) nd = cmax(nd, L.N2);
-    if (!L.tail) nd = cmax(nd, L.N4);
-    if (!ch1) nd = cmax(nd, L.N1);
-    if (L.N3 && !ch3) nd = cmax(nd, L.N3);
-    nd *= dw;
+    int nd = dw0 * L.N0;
+    if (fc2_mma) nd = cmax(nd, dw2 * L.N2);
+    if (fc4_mma) nd = cmax(nd, dw4 * L.N4);
+    if (!ch1) nd = cmax(nd, dw1 * L.N1);
+    if (L.N3 && !ch3) nd = cmax(nd, dw3 * L.N3);
     // temporary region: raw x (live until the gate) next to fc1's chunk regions (the chunk's accumulator,
     // then its h as A hi | lo); the projection's chunk regions reuse it once the gate is done
-    const int t1 = L.RX + (ch1 ? (dw + 2) * L.NC1 : 0);
-    const int t3 = ch3 ? (dw + 2) * L.NC3 : 0;
+    const int t1 = L.RX + (ch1 ? (dw1 + 2) * L.NC1 : 0);
+    const int t3 = ch3 ? (dw3 + 2) * L.NC3 : 0;
     const int tw = up16(cmax(t1, t3));
     L.cX = 0;
     L.cC1 = L.RX;
-    L.cH1 = L.RX + dw * L.NC1;
+    L.cH1 = L.RX + dw1 * L.NC1;
     L.cC3 = 0;
-    L.cH3 = dw * L.NC3;
+    L.cH3 = dw3 * L.NC3;
     L.cA = tw;
     L.cD = L.cA + 2 * L.KA;
     L.cols = up16(L.cD + nd);
@@ -963,7 +970,7 @@ constexpr bool layout_for(const Sizes& z, int groups, int nc1, int nc3, bool gat
 // the layout with the most groups (at most max_groups), then the widest chunks (fewest MMA round trips);
 // the gate's x stays in tensor memory unless dropping it buys another group (it is then re-read from
 // L2, where the tile's copy left it)
-constexpr bool plan_layout_upto(const Sizes& z, int max_groups, bool wide, Layout* out) {
+constexpr bool plan_layout_upto(const Sizes& z, int max_groups, int wide, Layout* out) {
     const int N1 = up16(z.Ch), N3 = z.Cp ? up16(z.Cp) : 16;
     const int cand[3] = {64, 32, 16};
     int opts1[4] = {N1, 0, 0, 0}, n1 = 1, opts3[4] = {N3, 0, 0, 0}, n3 = 1;
@@ -985,18 +992,26 @@ constexpr bool plan_layout_upto(const Sizes& z, int max_groups, bool wide, Layou
 // with 5, while the C1 block chain (2048 tiles, 14 per SM) ran 54% slower wide (fewer tiles per round
 // leave a larger last round); the lifting (3 groups against 5) and the last block with the projection
 // (2 against 4) ran 23% and 28% slower wide, and the width-64 chains (2 groups either way) 8-12% slower.
-// NOP_CHAIN_WIDE=0 / 1 forces the narrow / wide form (read at every call, for A/B timing).
+// With a projection, a third form keeps the projection's layers narrow and makes the block's layers
+// (skip, fc1, fc2) wide: the projection's 64-column accumulator bounds the tensor memory either way, so
+// it costs no group; it is taken whenever it keeps the narrow form's group count (the C5 last block with
+// the projection: 42 -> 32 MMAs per tile, 14.7 -> 14.0 ms on a box held at 1750 MHz).
+// NOP_CHAIN_WIDE=0 / 1 / 2 forces the narrow / wide / block-wide form (read at every call, for A/B timing).
 constexpr int64_t kWideMinTiles = 148 * 64;
+constexpr int kWBlock = kW0 | kW1 | kW2;
 
 constexpr bool plan_choice(const Sizes& z, int max_groups, int force_wide, int64_t tiles, Layout* out) {
-    Layout narrow{}, wide{};
-    const bool has_n = plan_layout_upto(z, max_groups, false, &narrow);
-    const bool has_w = plan_layout_upto(z, max_groups, true, &wide);
+    Layout narrow{}, wide{}, mixed{};
+    const bool has_n = plan_layout_upto(z, max_groups, 0, &narrow);
+    const bool has_w = plan_layout_upto(z, max_groups, kWAll, &wide);
+    const bool has_m = z.Cp && plan_layout_upto(z, max_groups, kWBlock, &mixed);
     bool use_w = has_w && (!has_n || (tiles >= kWideMinTiles && wide.groups >= 4 && wide.groups + 1 >= narrow.groups));
-    if (force_wide == 0) use_w = false;
-    if (force_wide == 1 && has_w) use_w = true;
-    if (!use_w && !has_n) return false;
-    *out = use_w ? wide : narrow;
+    bool use_m = !use_w && has_m && (!has_n || mixed.groups >= narrow.groups);
+    if (force_wide == 0) use_w = use_m = false;
+    if (force_wide == 1 && has_w) use_w = true, use_m = false;
+    if (force_wide == 2 && has_m) use_m = true, use_w = false;
+    if (!use_w && !use_m && !has_n) return false;
+    *out = use_w ? wide : use_m ? mixed : narrow;
     return true;
 }
 
@@ -1009,11 +1024,12 @@ bool plan_layout(const Sizes& z, int64_t tiles, Layout* out) {
         if (v >= 1 && v <= MAX_GROUPS) max_groups = v;
     }
     int force = -1;
-    if (const char* e = std::getenv("NOP_CHAIN_WIDE")) force = e[0] == '0' ? 0 : 1;
+    if (const char* e = std::getenv("NOP_CHAIN_WIDE")) force = e[0] == '0' ? 0 : e[0] == '2' ? 2 : 1;
     return plan_choice(z, max_groups, force, tiles, out);
 }
 
-// the layout of Z in the given MMA form (falling back to narrow where no wide layout fits)
+// the layout of Z in the given MMA form (0 narrow, 1 wide, 2 block-wide; falling back to narrow where
+// the form does not fit)
 constexpr Layout planned(const Sizes& z, int wide) {
     Layout L{};
     plan_choice(z, MAX_GROUPS, wide, 0, &L);
@@ -1207,14 +1223,15 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
     };
     try_fixed(chain::FixedLayout<chain::kBlockH32, 0>{});
     try_fixed(chain::FixedLayout<chain::kLift3dH32, 0>{});
-    try_fixed(chain::FixedLayout<chain::kLastProj3H32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLastProj3H32, 2>{});
     try_fixed(chain::FixedLayout<chain::kLift1dH32, 0>{});
-    try_fixed(chain::FixedLayout<chain::kLastProj1H32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kLastProj1H32, 2>{});
     try_fixed(chain::FixedLayout<chain::kBlockH64, 0>{});
     try_fixed(chain::FixedLayout<chain::kLift2dH64, 0>{});
     try_fixed(chain::FixedLayout<chain::kLastH64, 0>{});
     try_fixed(chain::FixedLayout<chain::kProj1H64, 0>{});
-    try_fixed(chain::FixedLayout<chain::kBlockH32, 1>{});  // the one chain the planner runs wide
+    try_fixed(chain::FixedLayout<chain::kBlockH32, 1>{});  // the chain the planner runs wide
+    try_fixed(chain::FixedLayout<chain::kLastProj3H32, 0>{});  // the narrow form (NOP_CHAIN_WIDE=0)
     if (!fixed) {
         using D = chain::LaunchLayout;
         switch (L.groups) {
