@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c5]
 
-Default workload: the whole FNO forward (BASELINE.json's metric, "FNO fwd samples/s") on the largest
+Default workload: the whole FNO forward (the headline metric, "FNO fwd samples/s") on the largest
 configuration that fits one GPU, configs[4]: FNO 3D, 256^3 grid, batch 8, hidden 32, n_modes (32, 32, 32),
 3 input (+3 grid) and 3 output channels, fp32.  Input: three seeded periodic Gaussian random fields
 with covariance (-Lap + 16 I)^-2 (no dataset); weights: the reference initialisers, seed 0.
@@ -43,15 +43,15 @@ METRIC = "FNO fwd samples/s/GPU at 1–8 B200; spectral block % of HBM/tensor ro
 HBM_FALLBACK_GBS = 6533.2  # measured copy bandwidth on this pool (MEASURED_PEAKS.json at round start)
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures summarised under
-# profiles/ (small-batch capture scaled to the full batch; traffic grows with the number of planes)
+# (small-batch capture scaled to the full batch; traffic grows with the number of planes)
 TRAFFIC = {
-    # profiles/spectral_block_c2_b8_full.md: batch-8 capture x 8 (reads + writes during the kernel; the
+    # `ncu --set full` of the C2 block at batch 8, x 8 (reads + writes during the kernel; the
     # plane kernels' traffic grows with the number of planes)
     ("c2", "plane_inv"): 8 * (8.701952e6 + 79.316992e6),
     ("c2", "plane_fwd"): 8 * (134.246144e6 + 4.028928e6),
-    # profiles/contraction_tma_c2_full.md: full-size capture of the contraction (one launch)
+    # full-size capture of the C2 contraction (one launch)
     ("c2", "contraction"): 207.854080e6 + 10.398976e6,
-    # profiles/chain_c5_small_full.md: 128^3 batch-1 capture x 64 (the chain's traffic grows with the points)
+    # C5 model at 128^3, batch 1: capture x 64 (the chain's traffic grows with the points)
     ("c5", "chain_block"): 64 * (537.109760e6 + 227.285760e6),
     ("c5", "chain_lifting"): 64 * (25.244928e6 + 209.326080e6),
     ("c5", "chain_last_block_projection"): 64 * (537.034240e6 + 17.639168e6),
@@ -215,11 +215,11 @@ def capture_graph(fn, stream):
 
 
 # ---------------------------------------------------------------------------------------------------
-# Full FNO / TFNO forward (the headline: BASELINE.json's metric is FNO forward samples/s)
+# Full FNO / TFNO forward (the headline metric: FNO forward samples/s)
 # ---------------------------------------------------------------------------------------------------
 # name -> (workload, class, n_modes, hidden, in, out, grid, batch, kwargs, input field)
-# The input fields are seeded periodic Gaussian random fields with the covariances BASELINE.json gives
-# for each configuration (no dataset is available): (scale, tau^2, alpha) of s^2 (-Lap + tau^2 I)^-alpha,
+# The input fields are seeded periodic Gaussian random fields with each benchmark configuration's
+# covariance (no dataset is available): (scale, tau^2, alpha) of s^2 (-Lap + tau^2 I)^-alpha,
 # plus the Darcy threshold to {3, 12}.
 MODELS = {
     "c1": ("fno2d_darcy", "FNO", (16, 16), 32, 1, 1, (128, 128), 16, {}, (1.0, 9.0, 2.0, "darcy")),

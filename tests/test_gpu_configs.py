@@ -1,12 +1,12 @@
 """Parity at the benchmark configurations' own sizes: the CUDA path against the oracle.
 
 The golden vectors (test_gpu_parity.py) pin the CUDA path to the reference's own outputs on small
-shapes; here every configuration of BASELINE.json runs at its full batch, channel count and grid, so
+shapes; here every benchmark configuration (C1-C5) runs at its full batch, channel count and grid, so
 the kernel instantiations the benchmark times (the C2 contraction at 64 x 64 channels, the Tucker
 chain at C4's ranks on 512^2, the 3D plane kernels at 256^3, the per-pixel chain kernel at hidden
 widths 32 and 64) are the ones checked.  Batch rows are independent, so the oracle -- the reference's
 forward restated on the CPU (oracle/spectral_oracle.py) -- runs on the first few samples and the
-CUDA output's rows for them are compared.  Tolerances: relative L2 <= 1e-5 with
+CUDA output's rows for them are compared.  Tolerances (the benchmark's stated bars): relative L2 <= 1e-5 with
 the fp32 contraction, <= 2e-2 with the bf16 contraction.
 """
 
