@@ -24,6 +24,7 @@
 // result does not depend on scheduling.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <string>
 
 #include "nop_internal.cuh"
@@ -35,6 +36,7 @@ constexpr int THREADS = 512;
 constexpr int MAX_KB = 3;   // 4 x 4 weight-gradient blocks per thread (registers)
 constexpr int MAX_C = 128;  // channel counts per slot the backward takes
 constexpr int SMEM_LIMIT = 227 * 1024;
+constexpr int SMEM_HALF = 113 * 1024;  // two CTAs per SM (228 KB, 1 KB reserved per CTA)
 
 __host__ __device__ constexpr int up4(int v) { return (v + 3) & ~3; }
 
@@ -44,6 +46,7 @@ struct Dims {
     int pX, pS, pK1, pH, pY;           // padded to multiples of 4
     int act0, act2, gate, gbias, skip;
     int TP, ld;                        // points per tile, row stride (TP + 4)
+    int nt;                            // threads per CTA (256: two CTAs per SM; 512)
     int oW0, oW1, oW2, oB1, oB2, oG, oGB;        // weights (padded, row-major [out][in]) and vectors
     int nAcc;                                    // per-CTA sums: dW0, dW1, dW2, db1, db2, dg
     int aW0, aW1, aW2, aB1, aB2, aG;             // their offsets inside the accumulator block
@@ -85,7 +88,7 @@ template <class Epi>
 __device__ __forceinline__ void act_gemm(const float* a, int am, int ak, const float* b, int ld, int M, int K, int TP,
                                          Epi epi) {
     const int tn = TP / 4, tiles = (M / 4) * tn;
-    for (int q = threadIdx.x; q < tiles; q += THREADS) {
+    for (int q = threadIdx.x; q < tiles; q += blockDim.x) {
         const int m0 = (q / tn) * 4, n0 = (q % tn) * 4;
         float2 c[4][2];
 #pragma unroll
@@ -207,14 +210,16 @@ __device__ __forceinline__ float comp(const float4& v, int j) { return j == 0 ? 
 
 // padded row-major copy of W [rows x cols] into [R][C] (zeros outside)
 __device__ void load_padded(float* dst, const float* w, int rows, int cols, int R, int C) {
-    for (int e = threadIdx.x; e < R * C; e += THREADS) {
+    for (int e = threadIdx.x; e < R * C; e += blockDim.x) {
         const int r = e / C, c = e % C;
         dst[e] = (w && r < rows && c < cols) ? __ldg(w + (int64_t)r * cols + c) : 0.f;
     }
 }
 
-template <int KB>
-__global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
+// NT threads per CTA: 256 with tiles small enough for two CTAs per SM (one CTA's tile loads and
+// barrier waits then overlap the other's arithmetic), 512 where the channels need the larger CTA
+template <int KB, int NT>
+__global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_chain_bwd(Ptrs P, Dims D) {
     extern __shared__ __align__(16) float sm[];
     const int tid = threadIdx.x, TP = D.TP, ld = D.ld;
     float* W0 = sm + D.oW0;
@@ -237,13 +242,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
     load_padded(vb2, P.b2, 1, D.Cy, 1, D.pY);
     load_padded(vg, D.gate ? P.g : nullptr, 1, D.Cy, 1, D.pY);
     load_padded(vgb, D.gbias ? P.gb : nullptr, 1, D.Cy, 1, D.pY);
-    float accw[KB][16];  // this thread's weight-gradient blocks tid, tid + THREADS, ...
+    float accw[KB][16];  // this thread's weight-gradient blocks tid, tid + NT, ...
 #pragma unroll
     for (int k = 0; k < KB; ++k)
 #pragma unroll
         for (int i = 0; i < 16; ++i) accw[k][i] = 0.f;
     float accv = 0.f;    // and its bias / gate entry (vector item tid)
-    for (int i = D.oX + tid; i < D.smem / 4; i += THREADS) sm[i] = 0.f;  // tiles: padding rows stay zero
+    for (int i = D.oX + tid; i < D.smem / 4; i += NT) sm[i] = 0.f;  // tiles: padding rows stay zero
     __syncthreads();
 
     const int nq = TP / 4;
@@ -255,26 +260,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
         const int np = (int)(P.P - p0 < TP ? P.P - p0 : TP);  // valid points (a multiple of 4)
 
         // ---- 0. x, dy (and the grid channels of the lifting) -> tiles; points past np read as zero ----
-        for (int e = tid; e < D.Cx * nq; e += THREADS) {
+        for (int e = tid; e < D.Cx * nq; e += NT) {
             const int c = e / nq, n = (e % nq) * 4;
             st4(X + c * ld + n, ld4_or0(P.x + ((int64_t)b * D.Cx + c) * P.P + p0 + n, n < np));
         }
-        for (int e = tid; e < D.Cy * nq; e += THREADS) {
+        for (int e = tid; e < D.Cy * nq; e += NT) {
             const int c = e / nq, n = (e % nq) * 4;
             st4(DZ2 + c * ld + n, ld4_or0(P.dy + ((int64_t)b * D.Cy + c) * P.P + p0 + n, n < np));
         }
         if (D.skip) {  // s into the act0' rows (the skip stage's epilogue reads it and writes act0' in place)
-            for (int e = tid; e < D.Cs * nq; e += THREADS) {
+            for (int e = tid; e < D.Cs * nq; e += NT) {
                 const int c = e / nq, n = (e % nq) * 4;
                 st4(A0 + c * ld + n, ld4_or0(P.s + ((int64_t)b * D.Cs + c) * P.P + p0 + n, n < np));
             }
         }
         if (!D.skip && D.nd) {
-            for (int e = tid; e < D.Cx * nq; e += THREADS) {
+            for (int e = tid; e < D.Cx * nq; e += NT) {
                 const int c = e / nq, n = (e % nq) * 4;
                 st4(U + c * ld + n, ld4_or0(P.x + ((int64_t)b * D.Cx + c) * P.P + p0 + n, n < np));
             }
-            for (int n = tid; n < TP; n += THREADS) {
+            for (int n = tid; n < TP; n += NT) {
                 float crd[NOP_MAX_DIMS] = {0.f, 0.f, 0.f, 0.f};
                 if (n < np) {
                     int64_t idx = p0 + n;
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
         // ---- 7. weight and bias gradients over the tile's points (tiles only read from here on) ----
 #pragma unroll
         for (int k = 0; k < KB; ++k) {
-            const int q = tid + k * THREADS;
+            const int q = tid + k * NT;
             if (q >= nblk) break;
             const WBlock w = wblock(D, q);
             const float* dd = w.which == 0 ? A0 : w.which == 1 ? G1 : DZ2;
@@ -420,7 +425,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_chain_bwd(Ptrs P, Dims D) {
     float* part = P.part + (int64_t)blockIdx.x * D.nAcc;
 #pragma unroll
     for (int k = 0; k < KB; ++k) {
-        const int q = tid + k * THREADS;
+        const int q = tid + k * NT;
         if (q >= nblk) break;
         const WBlock w = wblock(D, q);
 #pragma unroll
@@ -546,13 +551,23 @@ bool plan(const nop_chain_desc* d, Dims* out) {
     D.aG = D.aB2 + D.pY;
     D.nAcc = D.aG + D.pY;  // the per-CTA sums' layout (held in registers in the kernel)
     const int nblk = (D.skip ? (D.pS / 4) * (D.pX / 4) : 0) + (D.pH / 4) * (D.pK1 / 4) + (D.pY / 4) * (D.pH / 4);
-    if (nblk > MAX_KB * THREADS || D.pH + 2 * D.pY > THREADS) return false;
+    const int nvec = D.pH + 2 * D.pY;
+    if (nblk > MAX_KB * THREADS || nvec > THREADS) return false;
     const bool own_u = D.skip || D.nd > 0;
     const int rows = D.pX + (own_u ? D.pK1 : 0) + (D.skip ? D.pS : 0) + 2 * D.pH + D.pY;
-    for (int tp = 256; tp >= 32; tp /= 2) {
+    // two CTAs of 256 threads per SM when the weight-gradient blocks and vector entries fit 256 threads
+    // and a tile of at least 64 points fits half the SM's shared memory (measured on B200, C5 training:
+    // one CTA of 512 threads spent its time in barrier and global-load stalls, issue 34-42% active);
+    // else one CTA of 512 threads with the largest tile.  NOP_CHAIN_BWD_NT=512 forces the latter (read
+    // at every call, for A/B timing).
+    const char* e = std::getenv("NOP_CHAIN_BWD_NT");
+    const bool small_ok = nblk <= MAX_KB * 256 && nvec <= 256 && !(e && std::atoi(e) == 512);
+    for (int pass = small_ok ? 0 : 1; pass < 2; ++pass)
+    for (int tp = 256; tp >= (pass == 0 ? 64 : 32); tp /= 2) {
         const int ld = tp + 4;
         const int bytes = 4 * (off + rows * ld);
-        if (bytes > SMEM_LIMIT) continue;
+        if (bytes > (pass == 0 ? SMEM_HALF : SMEM_LIMIT)) continue;
+        D.nt = pass == 0 ? 256 : THREADS;
         D.TP = tp;
         D.ld = ld;
         int o = off;
@@ -643,10 +658,12 @@ int32_t nop_chain_backward(const nop_chain_desc* d, const nop_chain_operands* o,
     NOP_CUDA_TRY(cudaGetDevice(&dev));
     NOP_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int nblk = (D.skip ? (D.pS / 4) * (D.pX / 4) : 0) + (D.pH / 4) * (D.pK1 / 4) + (D.pY / 4) * (D.pH / 4);
-    const int kb = (int)ceil_div(nblk, cbwd::THREADS);
-    auto kernel = kb <= 1 ? cbwd::k_chain_bwd<1> : kb == 2 ? cbwd::k_chain_bwd<2> : cbwd::k_chain_bwd<3>;
+    const int kb = (int)ceil_div(nblk, D.nt);
+    void (*kernel)(cbwd::Ptrs, cbwd::Dims) =
+        D.nt == 256 ? (kb <= 1 ? cbwd::k_chain_bwd<1, 256> : kb == 2 ? cbwd::k_chain_bwd<2, 256> : cbwd::k_chain_bwd<3, 256>)
+                    : (kb <= 1 ? cbwd::k_chain_bwd<1, 512> : kb == 2 ? cbwd::k_chain_bwd<2, 512> : cbwd::k_chain_bwd<3, 512>);
     NOP_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, D.smem));
-    NOP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, cbwd::THREADS, D.smem));
+    NOP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, D.nt, D.smem));
     int64_t ctas = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
     if (ctas > cbwd::MAX_CTAS) ctas = cbwd::MAX_CTAS;
     if (ctas > p.tiles) ctas = p.tiles;
@@ -656,7 +673,7 @@ int32_t nop_chain_backward(const nop_chain_desc* d, const nop_chain_operands* o,
         NOP_CUDA_TRY(cudaMemsetAsync(workspace, 0, (size_t)D.nAcc * sizeof(float), s));
         ctas = 1;
     } else {
-        kernel<<<(unsigned)ctas, cbwd::THREADS, D.smem, s>>>(p, D);
+        kernel<<<(unsigned)ctas, D.nt, D.smem, s>>>(p, D);
         NOP_CUDA_TRY(cudaGetLastError());
     }
     cbwd::k_chain_bwd_reduce<<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(p.part, (int)ctas, D, outs);
