@@ -1073,6 +1073,10 @@ constexpr Sizes kLastProj3H32{32, 32, 0, 16, 32, 64, 3, 1, 0, 0};
 constexpr Sizes kLastProj1H32{32, 32, 0, 16, 32, 64, 1, 1, 0, 0};
 constexpr Sizes kLastH64{64, 64, 0, 32, 64, 0, 0, 1, 0, 0};
 constexpr Sizes kProj1H64{64, 0, 0, 128, 1, 0, 0, 0, 0, 0};
+// training keeps the projection apart (its backward is a chain of its own): the last block without the
+// output GELU, and the projection
+constexpr Sizes kLastH32{32, 32, 0, 16, 32, 0, 0, 1, 1, 0};
+constexpr Sizes kProj3H32{32, 0, 0, 64, 3, 0, 0, 0, 0, 0};
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1235,6 +1239,9 @@ int32_t nop_chain_forward(const nop_chain_desc* d, const nop_chain_operands* o, 
     try_fixed(chain::FixedLayout<chain::kProj1H64, 0>{});
     try_fixed(chain::FixedLayout<chain::kBlockH32, 1>{});  // the chain the planner runs wide
     try_fixed(chain::FixedLayout<chain::kLastProj3H32, 0>{});  // the narrow form (NOP_CHAIN_WIDE=0)
+    try_fixed(chain::FixedLayout<chain::kLastH32, 1>{});
+    try_fixed(chain::FixedLayout<chain::kLastH32, 0>{});
+    try_fixed(chain::FixedLayout<chain::kProj3H32, 0>{});
     if (!fixed) {
         using D = chain::LaunchLayout;
         switch (L.groups) {
