@@ -259,22 +259,28 @@ __global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_chain_bwd(Ptrs P, Dim
         const int64_t p0 = (t - b * P.tps) * TP;
         const int np = (int)(P.P - p0 < TP ? P.P - p0 : TP);  // valid points (a multiple of 4)
 
-        // ---- 0. x, dy (and the grid channels of the lifting) -> tiles; points past np read as zero ----
+        // ---- 0. x, dy (and the grid channels of the lifting) -> tiles; points past np read as zero.  The
+        // copy loops are unrolled so that several 16-byte loads per thread are in flight before their
+        // shared-memory stores (the stores cannot alias the global loads) ----
+#pragma unroll 4
         for (int e = tid; e < D.Cx * nq; e += NT) {
             const int c = e / nq, n = (e % nq) * 4;
             st4(X + c * ld + n, ld4_or0(P.x + ((int64_t)b * D.Cx + c) * P.P + p0 + n, n < np));
         }
+#pragma unroll 4
         for (int e = tid; e < D.Cy * nq; e += NT) {
             const int c = e / nq, n = (e % nq) * 4;
             st4(DZ2 + c * ld + n, ld4_or0(P.dy + ((int64_t)b * D.Cy + c) * P.P + p0 + n, n < np));
         }
         if (D.skip) {  // s into the act0' rows (the skip stage's epilogue reads it and writes act0' in place)
+#pragma unroll 4
             for (int e = tid; e < D.Cs * nq; e += NT) {
                 const int c = e / nq, n = (e % nq) * 4;
                 st4(A0 + c * ld + n, ld4_or0(P.s + ((int64_t)b * D.Cs + c) * P.P + p0 + n, n < np));
             }
         }
         if (!D.skip && D.nd) {
+#pragma unroll 4
             for (int e = tid; e < D.Cx * nq; e += NT) {
                 const int c = e / nq, n = (e % nq) * 4;
                 st4(U + c * ld + n, ld4_or0(P.x + ((int64_t)b * D.Cx + c) * P.P + p0 + n, n < np));
