@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(MD_THREADS) k_mode_dot(const float2* __restric
     for (int n0 = 0; n0 < N; n0 += NCH) {
         const int nc = N - n0 < NCH ? N - n0 : NCH;
         __syncthreads();
+#pragma unroll 4  // several loads in flight before their shared-memory stores
         for (int e = threadIdx.x; e < nc * RB; e += MD_THREADS) {
             const int n = e / RB, j = e % RB;
             const float2 v = r0 + j < R ? u[(int64_t)(n0 + n) * R + r0 + j] : make_float2(0.f, 0.f);
@@ -127,11 +128,13 @@ __global__ void __launch_bounds__(THREADS) k_gram_part(const float2* __restrict_
             off_c[threadIdx.x] = l < le ? pp * A * Q + qq : -1;
         }
         __syncthreads();
+#pragma unroll 4  // several loads in flight before their shared-memory stores
         for (int e = threadIdx.x; e < LC * GX; e += THREADS) {
             const int li = lfast ? e % LC : e / GX, xi = lfast ? e / LC : e % GX;
             const int64_t o = off_t[li];
             ts[li][xi] = o >= 0 && x0 + xi < X ? t[o + (int64_t)(x0 + xi) * Q] : make_float2(0.f, 0.f);
         }
+#pragma unroll 4
         for (int e = threadIdx.x; e < LC * AT; e += THREADS) {
             const int li = lfast ? e % LC : e / AT, ai = lfast ? e / LC : e % AT;
             const int64_t o = off_c[li];
