@@ -420,8 +420,10 @@ __global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_chain_bwd(Ptrs P, Dim
             const float* vv = w.which == 0 ? X : w.which == 1 ? U : H;
             wgrad_block(dd, vv, ld, TP, w.m0, w.nb, w.N / 4, accw[k]);
         }
-        if (tid < nvec) {
-            int r = tid;
+        // the vector entries on the last threads, idle in the weight-gradient blocks above when nblk + nvec
+        // <= NT (entry r on thread NT - nvec + r)
+        if (tid >= NT - nvec) {
+            int r = tid - (NT - nvec);
             if (r < D.pH) accv += row_sum(G1, nullptr, ld, TP, r);
             else if ((r -= D.pH) < D.pY) accv += row_sum(DZ2, nullptr, ld, TP, r);
             else accv += row_sum(DZ2, X, ld, TP, r - D.pY);
@@ -439,7 +441,8 @@ __global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_chain_bwd(Ptrs P, Dim
 #pragma unroll
             for (int j = 0; j < 4; ++j) part[w.base + (w.m0 + i) * w.N + w.nb + j * (w.N / 4)] = accw[k][i * 4 + j];
     }
-    if (tid < nvec) part[D.aB1 + tid] = accv;  // db1, db2, dg are consecutive in the accumulator layout
+    if (tid >= NT - nvec)
+        part[D.aB1 + tid - (NT - nvec)] = accv;  // db1, db2, dg are consecutive in the accumulator layout
 }
 
 // the gradients: per-CTA sums added in CTA order, unpadded into the callers' arrays
