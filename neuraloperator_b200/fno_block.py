@@ -142,7 +142,18 @@ class FNOBlocks(nn.Module):
         `proj` (a ChannelMLP), the FNO's projection on the block output.  ``spectral(index, conv, x)``
         replaces the spectral call (the slab-decomposed path passes its own)."""
         conv = self.convs[index]
-        s = conv(x) if spectral is None else spectral(index, conv, x)
+        relay = None
+        if spectral is None and proj is None and type(conv) is SpectralConv and grad_needed(x, self):
+            # x's two gradients (through the spectral convolution and through the chain's skip and gate)
+            # leave the spectral backward's last kernel as one tensor (pointwise.GradRelay)
+            relay = pointwise.GradRelay()
+            conv.__dict__["_nop_grad_relay"] = relay
+        try:
+            s = conv(x) if spectral is None else spectral(index, conv, x)
+        finally:
+            unused = conv.__dict__.pop("_nop_grad_relay", None) is not None
+        if relay is not None and (unused or not s.requires_grad or s.grad_fn is None):
+            relay = None  # the spectral call took no relay or recorded no backward: the chain returns dL/dx
         mlp, sg = self._mlp_parts(index)
         last = index >= self.n_layers - 1
         kw = {}
@@ -152,7 +163,7 @@ class FNOBlocks(nn.Module):
         return pointwise.chain(x, mlp.fcs[0].weight, mlp.fcs[0].bias, mlp.fcs[1].weight, mlp.fcs[1].bias, s=s,
                                w0=self.fno_skips[index].conv.weight, act_skip=not last, act_out=not last,
                                gate_w=sg.weight if sg is not None else None,
-                               gate_b=sg.bias if sg is not None else None, **kw)
+                               gate_b=sg.bias if sg is not None else None, grad_relay=relay, **kw)
 
     def forward_with_postactivation(self, x, index=0, output_shape=None):
         if (self._fusable(index, x, output_shape) and x.dtype == torch.float32

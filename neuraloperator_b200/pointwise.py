@@ -153,9 +153,10 @@ def chain(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: tor
           act_skip: bool = False, act_out: bool = False, gate_w: Optional[torch.Tensor] = None,
           gate_b: Optional[torch.Tensor] = None, grid=None, grid_offset=None, w3: Optional[torch.Tensor] = None,
           b3: Optional[torch.Tensor] = None, w4: Optional[torch.Tensor] = None, b4: Optional[torch.Tensor] = None,
-          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+          out: Optional[torch.Tensor] = None, grad_relay: Optional["GradRelay"] = None) -> torch.Tensor:
     """One chain call on x's device and current stream (see the module docstring); returns y (or the
-    projection's output when w3 / w4 are given).  ``gate_w`` switches on the soft-gating skip of x."""
+    projection's output when w3 / w4 are given).  ``gate_w`` switches on the soft-gating skip of x.
+    ``grad_relay``: under autograd, dL/dx is handed to that relay instead of returned (GradRelay)."""
     if not x.is_cuda:
         raise RuntimeError("neuraloperator_b200 runs on CUDA devices only (there is no CPU path)")
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in
@@ -166,7 +167,7 @@ def chain(x: torch.Tensor, w1: torch.Tensor, b1: Optional[torch.Tensor], w2: tor
         if out is not None:
             raise ValueError("out= is not supported when a gradient is recorded")
         return _ChainFn.apply(x, s, w0, w1, b1, w2, b2, gate_w, gate_b,
-                              (bool(act_skip), bool(act_out), grid, grid_offset))
+                              (bool(act_skip), bool(act_out), grid, grid_offset, grad_relay))
     if x.dtype != torch.float32:
         raise TypeError(f"expected float32 input, got {x.dtype}")
     x = x.contiguous()
@@ -267,7 +268,7 @@ class _ChainFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, s, w0, w1, b1, w2, b2, gate_w, gate_b, cfg):
-        act_skip, act_out, grid, grid_offset = cfg
+        act_skip, act_out, grid, grid_offset, _ = cfg
         with torch.no_grad():
             y = chain(x, w1, b1, w2, b2, s=s, w0=w0, act_skip=act_skip, act_out=act_out, gate_w=gate_w,
                       gate_b=gate_b, grid=grid, grid_offset=grid_offset)
@@ -278,7 +279,7 @@ class _ChainFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gy):
         x, s, w0, w1, b1, w2, b2, gate_w, gate_b = ctx.saved_tensors
-        act_skip, act_out, grid, grid_offset = ctx.cfg
+        act_skip, act_out, grid, grid_offset, relay = ctx.cfg
         names = ("x", "s", "w0", "w1", "b1", "w2", "b2", "g", "gb")
         need = [n for n, flag in zip(names, ctx.needs_input_grad[:9]) if flag]
         g = chain_backward(gy, x, w1, b1, w2, b2, s=s, w0=w0, act_skip=act_skip, act_out=act_out, gate_w=gate_w,
@@ -286,4 +287,29 @@ class _ChainFn(torch.autograd.Function):
         res = []
         for n, t in zip(names, (x, s, w0, w1, b1, w2, b2, gate_w, gate_b)):
             res.append(None if g.get(n) is None or t is None else g[n].view(t.shape).to(t.dtype))
+        if relay is not None and res[0] is not None:
+            relay.put(res[0])
+            res[0] = None
         return (*res, None)
+
+
+class GradRelay:
+    """Hands dL/dx of one FNO block's chain call to the backward of the block's spectral convolution,
+    which reads the same x and adds it in the epilogue of its dL/dx kernel: the two gradients of x then
+    leave one kernel as one tensor, instead of autograd adding them in a separate pass over x.
+
+    The spectral convolution's output feeds only the chain call, so its backward always runs after the
+    chain's (it needs dL/ds); the chain then reports no gradient for x and the spectral backward's dL/dx
+    is the whole of it."""
+
+    __slots__ = ("grad",)
+
+    def __init__(self):
+        self.grad = None
+
+    def put(self, g: torch.Tensor):
+        self.grad = g
+
+    def take(self) -> Optional[torch.Tensor]:
+        g, self.grad = self.grad, None
+        return g

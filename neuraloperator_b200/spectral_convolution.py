@@ -58,6 +58,7 @@ class _Call:
         self.ranks = tuple(ranks)
         self.apply_gelu = apply_gelu
         self.train = train
+        self.relay = None  # GradRelay of a fused FNO block: dL/dx of the block's chain call, added in backward
 
     def forward(self, x, weights, bias, addend, keep_spectrum=False):
         m = self.module
@@ -67,8 +68,9 @@ class _Call:
                                     apply_gelu=self.apply_gelu, precision=m.contraction_precision, engine=m.engine,
                                     cache=cache, keep_spectrum=keep_spectrum)
 
-    def backward(self, gy, weights, spec, need_x: bool, need_w: bool, need_b: bool):
-        """(dL/dx, [dL/d weight operand], dL/dbias [Co]) for dL/dy = gy; entries not needed are None."""
+    def backward(self, gy, weights, spec, need_x: bool, need_w: bool, need_b: bool, addend=None):
+        """(dL/dx, [dL/d weight operand], dL/dbias [Co]) for dL/dy = gy; entries not needed are None.
+        ``addend`` (x's shape) is added to dL/dx in the adjoint forward's last kernel."""
         m = self.module
         gy = gy.contiguous()
         adj_geo = adjoint_geometry(self.geo)
@@ -83,7 +85,7 @@ class _Call:
         gx, gspec = ops.spectral_forward(gy, adj_geo, adj_ws, out_channels=m.in_channels,
                                          weight_kind=self.kind, ranks=adj_ranks, separable=m.separable,
                                          precision=m.contraction_precision, engine=m.engine, keep_spectrum=True,
-                                         packed=packed)
+                                         packed=packed, addend=addend if need_x else None)
         lead = (m.in_channels,) if m.separable else (m.in_channels, m.out_channels)
         gw, gb = ops.weight_grad(spec, gspec, lead + tuple(self.geo.kept) if need_w else None,
                                  m.out_channels if need_b else 0)
@@ -126,7 +128,10 @@ class _SpectralFn(torch.autograd.Function):
         need_x, need_b, need_a = ctx.needs_input_grad[:3]
         need_w = any(ctx.needs_input_grad[4:])
         need_b = bool(need_b and ctx.bias_shape is not None)
-        gx, gws, gb = ctx.call.backward(gy, weights, ctx.spec, need_x, need_w, need_b)
+        # a fused FNO block's chain call hands its dL/dx here (the same x), so both gradients of x leave
+        # the adjoint forward's last kernel as one tensor instead of autograd adding them in another pass
+        relay = ctx.call.relay.take() if ctx.call.relay is not None else None
+        gx, gws, gb = ctx.call.backward(gy, weights, ctx.spec, need_x, need_w, need_b, addend=relay)
         if gb is not None:
             gb = gb.view(ctx.bias_shape)
         ga = gy if need_a else None
@@ -267,6 +272,10 @@ class SpectralConv(BaseSpectralConv):
             raise NotImplementedError("backward of a SpectralConv that resamples its output is not implemented; "
                                       "run it under torch.no_grad()")
         call = _Call(self, geo, kind, ranks, apply_gelu, train)
+        # set by FNOBlocks.fused_block for this one call (pointwise.GradRelay); taken here so that a later
+        # call of the module never sees it
+        call.relay = self.__dict__.pop("_nop_grad_relay", None) if train else None
+        self.__dict__.pop("_nop_grad_relay", None)
         return _SpectralFn.apply(x, bias, addend, call, *weights)
 
     @torch.no_grad()

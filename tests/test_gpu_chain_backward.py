@@ -86,14 +86,17 @@ def test_fno_training_step_fused_matches_module_path(monkeypatch):
     try:
         torch.manual_seed(0)
         model = nb.FNO(n_modes=(12, 12), in_channels=1, out_channels=1, hidden_channels=32, n_layers=4).cuda()
-        x = torch.randn(3, 1, 64, 64, device="cuda")
+        x = torch.randn(3, 1, 64, 64, device="cuda", requires_grad=True)
         target = torch.randn(3, 1, 64, 64, device="cuda")
 
         def step():
             model.zero_grad(set_to_none=True)
+            x.grad = None
             loss = ((model(x) - target) ** 2).mean()
             loss.backward()
-            return loss.item(), {n: p.grad.clone() for n, p in model.named_parameters()}
+            grads = {n: p.grad.clone() for n, p in model.named_parameters()}
+            grads["input"] = x.grad.clone()  # through every block's two gradient paths of its input
+            return loss.item(), grads
 
         assert model.fused_plan(x) is not None  # a gradient is recorded: the fused path must take it
         loss_f, g_f = step()
