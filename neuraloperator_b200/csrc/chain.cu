@@ -613,13 +613,10 @@ k_chain(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtenso
             if (c0 < L.Kx) {
                 uint32_t h[8], l[8];
 #pragma unroll
-                for (int j = 0; j < 8; j += 2) {
-                    const float2 hv = make_float2(tf32_hi(v[j]), tf32_hi(v[j + 1]));
-                    const float2 lv = __ffma2_rn(hv, make_float2(-1.0f, -1.0f), make_float2(v[j], v[j + 1]));  // exact
-                    h[j] = __float_as_uint(hv.x);
-                    h[j + 1] = __float_as_uint(hv.y);
-                    l[j] = __float_as_uint(lv.x);
-                    l[j + 1] = __float_as_uint(lv.y);
+                for (int j = 0; j < 8; ++j) {  // scalar: pairing these stash values costs more moves than it saves
+                    const float hv = tf32_hi(v[j]);
+                    h[j] = __float_as_uint(hv);
+                    l[j] = __float_as_uint(v[j] - hv);
                 }
                 tmem_st8(tl + L.cA + c0, h);
                 tmem_st8(tl + L.cA + L.KA + c0, l);
