@@ -177,6 +177,23 @@ def test_chain_planner_mma_form(monkeypatch):
     assert pointwise.query(lifting) == 3
 
 
+def test_chain_planner_block_wide_form(monkeypatch):
+    """With the projection fused, the C5 last block runs its block layers wide and the projection narrow:
+    that keeps the narrow form's 4 tiles in flight (all layers wide would leave 2).  The chains of the
+    training forward (the last block without its output GELU, the projection on its own) plan 4 each."""
+    from neuraloperator_b200 import pointwise
+    last_proj = pointwise.make_desc(8, (256,) * 3, 32, 16, 32, skip=32, act_skip=True, gate=True, proj_hidden=64,
+                                    proj_out=3)
+    last = pointwise.make_desc(2, (256,) * 3, 32, 16, 32, skip=32, act_skip=True, gate=True)
+    proj = pointwise.make_desc(2, (256,) * 3, 32, 64, 3)
+    assert pointwise.query(last_proj) == 4 and pointwise.query(last) == 4 and pointwise.query(proj) == 4
+    for form, groups in (("0", 4), ("1", 2), ("2", 4)):
+        monkeypatch.setenv("NOP_CHAIN_WIDE", form)
+        assert pointwise.query(last_proj) == groups, form
+    monkeypatch.setenv("NOP_CHAIN_WIDE", "2")  # no projection, no block-wide form: the planner's own choice
+    assert pointwise.query(last) == 4
+
+
 def test_tucker_grads_host_checks():
     """Workspace sizing and argument checks of nop_tucker_grads run on the host (no device call)."""
     lib = _lib.library()
