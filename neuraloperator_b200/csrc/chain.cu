@@ -996,7 +996,8 @@ constexpr bool plan_layout_upto(const Sizes& z, int max_groups, int wide, Layout
 // (skip, fc1, fc2) wide: the projection's 64-column accumulator bounds the tensor memory either way, so
 // it costs no group; it is taken whenever it keeps the narrow form's group count (the C5 last block with
 // the projection: 42 -> 32 MMAs per tile, 14.7 -> 14.0 ms on a box held at 1750 MHz).
-// NOP_CHAIN_WIDE=0 / 1 / 2 forces the narrow / wide / block-wide form (read at every call, for A/B timing).
+// NOP_CHAIN_WIDE=0 / 1 / 2 forces the narrow / wide / block-wide form (read at every call, for A/B timing;
+// 2 only where a projection is fused, other chains keep the choice above).
 constexpr int64_t kWideMinTiles = 148 * 64;
 constexpr int kWBlock = kW0 | kW1 | kW2;
 
